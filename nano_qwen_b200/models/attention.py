@@ -1,0 +1,128 @@
+"""Grouped-query attention with QK-RMSNorm and RoPE (Qwen3).
+
+Parameters and names follow the reference (q_proj/k_proj/v_proj/o_proj,
+q_norm/k_norm; reference: model/attention.py:49-80).  Execution differs:
+
+* training / full-sequence path: one GEMM over the contiguous q|k|v weight,
+  then ``ops.attention_core`` (fused QK-norm + RoPE + flash attention), then
+  o_proj;
+* cached path (prefill and decode): positions continue from the cache length
+  (the reference restarts RoPE at 0 on each decode step,
+  reference: eval/generate.py:126-135 with model/rope.py:123-126) and
+  prefill is causal (the reference runs cached prefill without a mask,
+  model/attention.py:113).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from ..config import ModelConfig
+from .kv_cache import KVCache
+from .layers import Linear, RMSNorm, fused_linear
+from .rope import RotaryEmbedding
+
+
+class Attention(nn.Module):
+    def __init__(self, config: ModelConfig, layer_idx: int = 0):
+        super().__init__()
+        self.config = config
+        self.layer_idx = layer_idx
+        self.hidden_size = config.hidden_size
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads
+        self.head_dim = config.head_dim
+        self.num_kv_groups = config.num_kv_groups
+        b = config.attention_bias
+        self.q_proj = Linear(self.hidden_size, self.num_heads * self.head_dim, b)
+        self.k_proj = Linear(self.hidden_size, self.num_kv_heads * self.head_dim, b)
+        self.v_proj = Linear(self.hidden_size, self.num_kv_heads * self.head_dim, b)
+        self.o_proj = Linear(self.num_heads * self.head_dim, self.hidden_size, b)
+        self.qk_norm = config.qk_norm
+        if self.qk_norm:
+            self.q_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+            self.k_norm = RMSNorm(self.head_dim, eps=config.rms_norm_eps)
+        self.rotary_emb = RotaryEmbedding(self.head_dim, config.max_position_embeddings,
+                                          config.rope_theta, config.rope_scaling)
+        # Tensor-parallel attention runs local heads only (set by parallel.tensor_parallel).
+        self.tp_heads = None
+
+    def fusion_groups(self):
+        return [["q_proj.weight", "k_proj.weight", "v_proj.weight"]]
+
+    def _heads(self):
+        if self.tp_heads is not None:
+            return self.tp_heads
+        return self.num_heads, self.num_kv_heads
+
+    def forward(self, hidden_states: torch.Tensor, position_ids: Optional[torch.Tensor] = None,
+                attention_mask: Optional[torch.Tensor] = None,
+                kv_cache: Optional[KVCache] = None) -> torch.Tensor:
+        B, S, _ = hidden_states.shape
+        Hq, Hk = self._heads()
+        D = self.head_dim
+        dtype = hidden_states.dtype
+        qkv = fused_linear(hidden_states, [self.q_proj, self.k_proj, self.v_proj], dtype)
+        qw = self.q_norm.weight if self.qk_norm else None
+        kw = self.k_norm.weight if self.qk_norm else None
+        cos, sin = self.rotary_emb.cos_cached, self.rotary_emb.sin_cached
+        eps = self.config.rms_norm_eps
+        if kv_cache is None and attention_mask is None:
+            o = ops.attention_core(qkv, qw, kw, cos, sin, position_ids, Hq, Hk, D, eps,
+                                   causal=True)
+        else:
+            o = self._attend_general(qkv, qw, kw, cos, sin, position_ids, attention_mask,
+                                     kv_cache, B, S, Hq, Hk, D, eps)
+        return fused_linear(o, [self.o_proj], dtype)
+
+    def _attend_general(self, qkv, qw, kw, cos, sin, position_ids, attention_mask, kv_cache,
+                        B, S, Hq, Hk, D, eps):
+        q, k, v = qkv.split([Hq * D, Hk * D, Hk * D], dim=-1)
+        q = q.reshape(B, S, Hq, D)
+        k = k.reshape(B, S, Hk, D)
+        v = v.reshape(B, S, Hk, D)
+        past = kv_cache.seq_len if kv_cache is not None else 0
+        if position_ids is None:
+            position_ids = (torch.arange(S, device=q.device) + past).unsqueeze(0).expand(B, S)
+        q, k = ops.rope_qk(q, k, qw, kw, cos, sin, position_ids, eps)
+        if kv_cache is not None:
+            k_all, v_all = kv_cache.append(k, v)
+        else:
+            k_all, v_all = k, v
+        if attention_mask is not None:
+            o = _masked_attention(q, k_all, v_all, attention_mask, past)
+        elif q.is_cuda:
+            kb, vb = (kv_cache.buffers() if kv_cache is not None else (k_all, v_all))
+            n = torch.full((B,), past + S, dtype=torch.int32, device=q.device)
+            start = torch.full((B,), past, dtype=torch.int32, device=q.device)
+            o = ops.decode_attention(q, kb, vb, n, start)
+        else:
+            o = ops.reference.attention(q, k_all, v_all, causal=True, q_offset=past)
+        return o.reshape(B, S, Hq * D)
+
+
+def _masked_attention(q, k, v, attention_mask, past):
+    """Causal attention plus a key-padding / additive mask (general path)."""
+    import math
+    B, Sq, Hq, D = q.shape
+    Sk, Hk = k.shape[1], k.shape[2]
+    g = Hq // Hk
+    qf = q.float().reshape(B, Sq, Hk, g, D)
+    s = torch.einsum("bqhgd,bkhd->bhgqk", qf, k.float()) / math.sqrt(D)
+    causal = torch.arange(Sk, device=q.device)[None, :] > (torch.arange(Sq, device=q.device)[:, None] + past)
+    s = s.masked_fill(causal, float("-inf"))
+    m = attention_mask
+    if m.dtype == torch.bool or m.dtype in (torch.int32, torch.int64):
+        if m.dim() == 2:  # [B, Sk] key padding, 1 = keep
+            s = s.masked_fill(~m.bool()[:, None, None, None, :], float("-inf"))
+        else:
+            s = s.masked_fill(~m.bool().reshape(B, 1, 1, Sq, Sk), float("-inf"))
+    else:
+        s = s + m.float().reshape(B, 1, 1, Sq, Sk) if m.dim() == 4 else s + m.float()
+    p = torch.softmax(s, dim=-1).nan_to_num(0.0)
+    o = torch.einsum("bhgqk,bkhd->bqhgd", p, v.float())
+    return o.reshape(B, Sq, Hq, D).to(q.dtype)

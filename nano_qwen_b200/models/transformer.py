@@ -1,0 +1,169 @@
+"""Qwen3 decoder: blocks and the full causal language model.
+
+Public API and parameter names match the reference (``Qwen3Model.forward(
+input_ids, position_ids, attention_mask, kv_caches, labels) -> {"logits",
+"loss", "aux_loss", "hidden_states"}``; reference: model/transformer.py:77-162),
+with labels aligned to ``input_ids`` and the model doing the shift.
+
+Execution plan on B200: the residual stream stays fp32 and every residual add
+is fused into the following RMSNorm kernel (the model loop carries
+``(resid, pending_delta)`` between blocks); the loss is the fused lm_head +
+vocab-chunked cross-entropy, so the [T, V] logits are only produced when a
+caller asks for them (``return_logits`` / ``logits_to_keep``).
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.utils.checkpoint as ckpt
+
+from .. import ops
+from ..config import ModelConfig
+from .attention import Attention
+from .ffn import build_ffn
+from .kv_cache import KVCache
+from .layers import Linear, RMSNorm, fused_linear
+from .moe import MoELayer
+
+
+class TokenEmbedding(nn.Module):
+    """reference: model/embedding.py:9-16 (parameter ``embed_tokens.weight``)."""
+
+    def __init__(self, config: ModelConfig):
+        super().__init__()
+        self.embed_tokens = nn.Embedding(config.vocab_size, config.hidden_size)
+        self.hidden_size = config.hidden_size
+
+    def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        return ops.embedding(input_ids, self.embed_tokens.weight)
+
+
+class TransformerBlock(nn.Module):
+    def __init__(self, config: ModelConfig, layer_idx: int = 0):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.config = config
+        self.input_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.attention = Attention(config, layer_idx)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self._use_moe = config.layer_is_moe(layer_idx)
+        self.feed_forward = MoELayer(config) if self._use_moe else build_ffn(config)
+
+    def forward_fused(self, resid: torch.Tensor, delta: Optional[torch.Tensor],
+                      position_ids=None, attention_mask=None, kv_cache=None):
+        """(resid, pending delta) -> (resid, new delta, aux).  resid is fp32."""
+        eps = self.config.rms_norm_eps
+        resid, x = ops.add_rms_norm(resid, delta, self.input_layernorm.weight, eps)
+        a = self.attention(x, position_ids, attention_mask, kv_cache)
+        resid, x = ops.add_rms_norm(resid, a, self.post_attention_layernorm.weight, eps)
+        if self._use_moe:
+            f, aux = self.feed_forward(x)
+        else:
+            f, aux = self.feed_forward(x), None
+        return resid, f, aux
+
+    def forward(self, hidden_states, position_ids=None, attention_mask=None, kv_cache=None):
+        """Reference-compatible: returns (hidden_states, aux_loss)."""
+        resid, f, aux = self.forward_fused(hidden_states.float() if hidden_states.is_cuda
+                                           else hidden_states, None, position_ids,
+                                           attention_mask, kv_cache)
+        return resid + f.to(resid.dtype), aux
+
+
+class Qwen3Model(nn.Module):
+    def __init__(self, config: ModelConfig):
+        super().__init__()
+        self.config = config
+        self.embed = TokenEmbedding(config)
+        self.layers = nn.ModuleList([TransformerBlock(config, i)
+                                     for i in range(config.num_hidden_layers)])
+        self.norm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.lm_head = Linear(config.hidden_size, config.vocab_size, bias=False)
+        if config.tie_word_embeddings:
+            self.lm_head.weight = self.embed.embed_tokens.weight
+        self.gradient_checkpointing = config.gradient_checkpointing
+        self.reset_parameters()
+
+    # ------------------------------------------------------------------ init
+    @torch.no_grad()
+    def reset_parameters(self, generator: Optional[torch.Generator] = None) -> None:
+        """Normal(0, initializer_range) for every linear/embedding weight, zeros
+        for biases, ones for norms (reference: model/transformer.py:98-105)."""
+        std = self.config.initializer_range
+        for m in self.modules():
+            if isinstance(m, (Linear, nn.Linear)):
+                m.weight.normal_(0.0, std, generator=generator)
+                if m.bias is not None:
+                    m.bias.zero_()
+            elif isinstance(m, nn.Embedding):
+                m.weight.normal_(0.0, std, generator=generator)
+
+    # --------------------------------------------------------------- forward
+    def lm_head_ref(self, dtype):
+        return ops.weight_ref([self.lm_head.weight], dtype)
+
+    def compute_dtype(self, device: torch.device) -> torch.dtype:
+        return torch.bfloat16 if device.type == "cuda" else self.embed.embed_tokens.weight.dtype
+
+    def hidden(self, input_ids: torch.Tensor, position_ids=None, attention_mask=None,
+               kv_caches: Optional[List[KVCache]] = None, inputs_embeds=None):
+        """Runs embed + blocks + final norm; returns (normed hidden [B,S,H], aux_total, n_moe)."""
+        resid = self.embed(input_ids) if inputs_embeds is None else inputs_embeds
+        delta = None
+        aux_total = None
+        n_moe = 0
+        use_ckpt = self.gradient_checkpointing and self.training and torch.is_grad_enabled()
+        for i, layer in enumerate(self.layers):
+            cache = kv_caches[i] if kv_caches is not None else None
+            if use_ckpt and cache is None:
+                resid, delta, aux = ckpt.checkpoint(layer.forward_fused, resid, delta,
+                                                    position_ids, attention_mask, None,
+                                                    use_reentrant=False)
+            else:
+                resid, delta, aux = layer.forward_fused(resid, delta, position_ids,
+                                                        attention_mask, cache)
+            if aux is not None:
+                aux_total = aux if aux_total is None else aux_total + aux
+                n_moe += 1
+        _, x = ops.add_rms_norm(resid, delta, self.norm.weight, self.config.rms_norm_eps)
+        return x, aux_total, n_moe
+
+    def forward(self, input_ids: torch.Tensor, position_ids: Optional[torch.Tensor] = None,
+                attention_mask: Optional[torch.Tensor] = None,
+                kv_caches: Optional[List[KVCache]] = None, labels: Optional[torch.Tensor] = None,
+                return_logits: Optional[bool] = None, logits_to_keep: int = 0,
+                inputs_embeds: Optional[torch.Tensor] = None) -> dict:
+        x, aux_total, n_moe = self.hidden(input_ids, position_ids, attention_mask, kv_caches,
+                                          inputs_embeds)
+        dtype = x.dtype
+        if return_logits is None:
+            return_logits = labels is None
+        logits = None
+        if return_logits:
+            xs = x[:, -logits_to_keep:] if logits_to_keep else x
+            logits = ops.linear(xs, self.lm_head_ref(dtype))
+        loss = None
+        if labels is not None:
+            targets = shift_targets(labels)
+            loss = ops.linear_cross_entropy(x, self.lm_head_ref(dtype), targets)
+            if n_moe > 0:
+                loss = loss + self.config.router_aux_loss_coef * (aux_total / n_moe)
+        aux_out = None
+        if n_moe > 0:
+            aux_out = aux_total
+        return {"logits": logits, "loss": loss, "aux_loss": aux_out, "hidden_states": x}
+
+    @torch.no_grad()
+    def count_parameters(self) -> dict:
+        total = sum(p.numel() for p in self.parameters())
+        trainable = sum(p.numel() for p in self.parameters() if p.requires_grad)
+        return {"total": total, "trainable": trainable}
+
+
+def shift_targets(labels: torch.Tensor) -> torch.Tensor:
+    """targets[:, t] = labels[:, t+1]; the last position is ignored (-100)."""
+    pad = torch.full_like(labels[..., :1], -100)
+    return torch.cat([labels[..., 1:], pad], dim=-1)

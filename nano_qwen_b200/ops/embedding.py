@@ -1,0 +1,43 @@
+"""Token embedding gather / scatter-add.
+
+The forward gathers fp32 rows from the master table (so the residual stream
+starts in fp32, exactly like the reference's fp32 ``nn.Embedding`` output,
+reference: model/embedding.py:15); the backward scatter-adds fp32 row
+gradients into the table's gradient buffer with vectorised atomics.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from ._ext import ext
+from .common import grad_buffer
+
+
+class _EmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, weight):
+        ids_c = ids.reshape(-1).contiguous()
+        out = ext().embedding_fwd(ids_c, weight)
+        ctx.save_for_backward(ids_c, weight)
+        return out.view(*ids.shape, weight.shape[1])
+
+    @staticmethod
+    def backward(ctx, dout):
+        ids_c, weight = ctx.saved_tensors
+        if weight.requires_grad:
+            d2 = dout.reshape(-1, dout.shape[-1])
+            if d2.dtype != torch.float32 or not d2.is_contiguous():
+                d2 = d2.float().contiguous()
+            ext().embedding_bwd(ids_c, d2, grad_buffer(weight))
+        return None, None
+
+
+def embedding(ids: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    if ids.is_cuda:
+        if torch.is_grad_enabled() and weight.requires_grad:
+            return _EmbeddingFn.apply(ids, weight)
+        return ext().embedding_fwd(ids.reshape(-1).contiguous(), weight).view(
+            *ids.shape, weight.shape[1])
+    return F.embedding(ids, weight)

@@ -1,0 +1,91 @@
+"""Training engine: model + flat store + data parallelism + fused optimizer.
+
+One ``train_step`` runs the gradient-accumulation micro-steps, the gradient
+reduction, fused clipping and the fused AdamW update and returns device
+tensors (loss, grad norm, aux loss) so the loop never blocks on the host; the
+caller reads them back when it logs.  This replaces the inner loops of the
+reference's trainers (reference: training/pretrain.py:158-215,
+training/sft.py:197-240), which called ``loss.item()`` every micro-step.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Iterable, List, Optional
+
+import torch
+import torch.nn as nn
+
+from ..parallel.comm import get_world_size
+from ..parallel.data_parallel import DataParallel
+from ..runtime.flat_params import ALIGN
+from .optimizer import attach_param_store, build_optimizer
+from .scheduler import build_scheduler
+
+
+class TrainEngine:
+    def __init__(self, model: nn.Module, training_config: dict, device: torch.device,
+                 dp_mode: Optional[str] = None, dp_group=None):
+        self.model = model.to(device)
+        self.device = device
+        self.cfg = training_config
+        world = get_world_size(dp_group)
+        dist_cfg = training_config.get("distributed", {}) or {}
+        if dp_mode is None:
+            dp_mode = "shard" if dist_cfg.get("fsdp_enabled", True) else "replicate"
+        self.store = attach_param_store(self.model, pad_multiple=ALIGN * max(1, world))
+        self.dp = DataParallel(self.store, mode=dp_mode, group=dp_group) if world > 1 else None
+        if self.dp is not None:
+            self.dp.broadcast_params(0)
+        opt = training_config.get("optimizer", {}) or {}
+        self.optimizer = build_optimizer(
+            self.model, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),
+            beta1=opt.get("beta1", 0.9), beta2=opt.get("beta2", 0.95), eps=opt.get("eps", 1e-8),
+            fused=True, store=self.store, shard=self.dp.shard if self.dp is not None else None)
+        sch = training_config.get("scheduler", {}) or {}
+        self.scheduler = build_scheduler(self.optimizer, scheduler_type=sch.get("type", "cosine"),
+                                         warmup_steps=sch.get("warmup_steps", 2000),
+                                         total_steps=sch.get("total_steps", 100000),
+                                         min_lr=opt.get("min_lr"),
+                                         stable_steps=sch.get("stable_steps",
+                                                              int(0.8 * sch.get("total_steps", 100000))))
+        self.grad_clip = opt.get("grad_clip", 1.0)
+        self.dtype = getattr(torch, (training_config.get("precision", {}) or {}).get("dtype", "bfloat16"))
+
+    # ----------------------------------------------------------------- step
+    def forward_backward(self, batch: Dict[str, torch.Tensor], scale: float):
+        out = self.model(input_ids=batch["input_ids"], labels=batch["labels"])
+        loss = out["loss"] * scale
+        loss.backward()
+        aux = out.get("aux_loss")
+        return loss.detach(), (aux.detach() * scale if aux is not None else None)
+
+    def train_step(self, micro_batches: List[Dict[str, torch.Tensor]], loss_fn=None) -> dict:
+        self.model.train()
+        self.store.zero_grad()
+        n = len(micro_batches)
+        loss_sum = torch.zeros((), dtype=torch.float32, device=self.device)
+        aux_sum = None
+        for mb in micro_batches:
+            if loss_fn is not None:
+                loss = loss_fn(self.model, mb) / n
+                loss.backward()
+                l, a = loss.detach(), None
+            else:
+                l, a = self.forward_backward(mb, 1.0 / n)
+            loss_sum += l.float()
+            if a is not None:
+                aux_sum = a.float() if aux_sum is None else aux_sum + a.float()
+        if self.dp is not None:
+            self.dp.sync_grads()
+        reduce = self.dp.norm_sq_reduce if self.dp is not None else None
+        gnorm = self.optimizer.clip_grad_norm_(self.grad_clip, reduce)
+        self.optimizer.step()
+        if self.dp is not None:
+            self.dp.gather_params()
+        self.scheduler.step()
+        return {"loss": loss_sum, "grad_norm": gnorm, "aux_loss": aux_sum}
+
+    def state_for_save(self):
+        if self.dp is not None:
+            self.dp.gather_master()
+        return self.model, self.optimizer, self.scheduler
