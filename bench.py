@@ -1,0 +1,436 @@
+"""Headline benchmark: train tokens/s (device-timed, max over ranks) + MFU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+Multi-GPU: launched by ``torch.distributed.run --nproc-per-node N``; each rank
+reads RANK/LOCAL_RANK/WORLD_SIZE from the environment and uses NCCL.
+
+Default config = the reference's functional headline path: Qwen3-1.7B-shaped
+dense model (28 layers, hidden 2048, 16 Q / 8 KV heads, head_dim 128,
+intermediate 6144, vocab 151936, tied embeddings), per-GPU batch 4 x 4096
+uniform-random token ids, random-init weights, bf16 compute, AdamW with grad
+clipping, data parallel over N GPUs (weak scaling).  ``--impl reference`` runs
+the unmodified reference (``baseline/_ref``) through its own public API: its
+``Qwen3Model`` + ``build_optimizer`` + ``build_scheduler`` under bf16 autocast
+with ``clip_grad_norm_``, and for N>1 its ``ParallelismManager`` (FSDP2).
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
+``torch.cuda.synchronize()`` on both sides, timed with CUDA events on the
+launching stream; the per-step time is the max over ranks.  The step's working
+set (3.4 GB of bf16 weights, tens of GB of activations) is far larger than the
+126 MB L2, so no L2 flush is needed.  SM clocks and throttle reasons are
+sampled with nvidia-smi during the timed region.  The end-to-end number ("e2e")
+repeats the measurement through the public training API with, every step, a
+pinned host->device copy of the step's token ids/labels and a device->host read
+of the loss and grad norm, timed by the host clock.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+BASELINE_METRIC = "train tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; MFU"
+
+CONFIGS = {
+    # name: (model kwargs, per-GPU micro batch, seq, parallel label)
+    "qwen3-1.7b": (dict(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16,
+                        num_key_value_heads=8, head_dim=128, intermediate_size=6144,
+                        vocab_size=151936, max_position_embeddings=4096, rope_theta=1e6,
+                        qk_norm=True, tie_word_embeddings=True), 4, 4096, "dp"),
+    "debug": (dict(hidden_size=512, num_hidden_layers=8, num_attention_heads=8, num_key_value_heads=2,
+                   head_dim=64, intermediate_size=1408, vocab_size=32000, max_position_embeddings=2048,
+                   rope_theta=1e6, qk_norm=True, tie_word_embeddings=True), 4, 256, "dp"),
+    "debug-moe": (dict(hidden_size=512, num_hidden_layers=8, num_attention_heads=8, num_key_value_heads=2,
+                       head_dim=64, intermediate_size=1408, vocab_size=32000,
+                       max_position_embeddings=2048, rope_theta=1e6, qk_norm=True,
+                       tie_word_embeddings=True, num_experts=64, num_experts_per_tok=8,
+                       moe_intermediate_size=256, router_aux_loss_coef=0.001), 8, 2048, "dp"),
+}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", default="qwen3-1.7b", choices=sorted(CONFIGS))
+    p.add_argument("--e2e-steps", type=int, default=None)
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        def pump():
+            for line in self.proc.stdout:
+                self.lines.append(line.strip())
+        self.thread = threading.Thread(target=pump, daemon=True)
+        self.thread.start()
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(self.REASONS, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ common
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def maybe_init_pg(world, local):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+
+def max_over_ranks(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return x
+
+
+def barrier():
+    import torch
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier(device_ids=[torch.cuda.current_device()])
+
+
+def flops_per_token(mk: dict, seq: int) -> float:
+    h = mk["hidden_size"]
+    L = mk["num_hidden_layers"]
+    qd = mk["num_attention_heads"] * mk["head_dim"]
+    kvd = mk["num_key_value_heads"] * mk["head_dim"]
+    attn = h * qd * 2 + 2 * h * kvd
+    if mk.get("num_experts"):
+        ffn = mk["num_experts_per_tok"] * 3 * h * mk["moe_intermediate_size"] + h * mk["num_experts"]
+    else:
+        ffn = 3 * h * mk["intermediate_size"]
+    n_active = L * (attn + ffn) + mk["vocab_size"] * h
+    return 6.0 * n_active + 12.0 * L * qd * (seq / 2)
+
+
+def measured_peak() -> float:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]) * 1e12
+    except Exception:
+        return 1.59e15
+
+
+def synthetic_batches(n, B, S, V, device, seed=1234, pinned=False):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        ids = torch.randint(0, V, (B, S), generator=g)
+        if pinned:
+            ids = ids.pin_memory()
+        elif device is not None:
+            ids = ids.to(device)
+        out.append(ids)
+    return out
+
+
+def timed_loop(step_fn, inputs, K, W, local):
+    """Warm-up W, then K device-timed steps; returns ms/step (max over ranks) and clocks."""
+    import torch
+    for i in range(W):
+        step_fn(inputs[i % len(inputs)])
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(K):
+        step_fn(inputs[i % len(inputs)])
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / K
+    return max_over_ranks(ms), clocks
+
+
+# ------------------------------------------------------------- our engine
+def run_ours(args, world, rank, local):
+    import torch
+    sys.path.insert(0, ROOT)
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.parallel.comm import init_distributed
+    from nano_qwen_b200.training.engine import TrainEngine
+
+    mk, B, S, par = CONFIGS[args.config]
+    init_distributed()
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    cfg = ModelConfig(**mk)
+    with torch.device(dev):
+        model = Qwen3Model(cfg)
+    tcfg = {"optimizer": {"lr": 3e-4, "weight_decay": 0.1, "grad_clip": 1.0},
+            "scheduler": {"type": "cosine", "warmup_steps": 100, "total_steps": 100000},
+            "distributed": {"fsdp_enabled": True}}
+    eng = TrainEngine(model, tcfg, dev)
+    del model
+    inputs = synthetic_batches(4, B, S, cfg.vocab_size, dev, seed=1234 + rank)
+
+    def step(ids):
+        eng.train_step([{"input_ids": ids, "labels": ids}])
+
+    ext().error_flag_clear()
+    ms, clocks = timed_loop(step, inputs, args.steps, args.warmup, local)
+    err = ext().error_flag_read()
+    launches = count_launches(step, inputs[0])
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e_ours(eng, args, B, S, cfg.vocab_size, dev, rank)
+    return ms, clocks, {"kernel_error_flag": err, "gpu_launches_per_step": launches}, e2e
+
+
+def count_launches(step_fn, ids):
+    """Kernels of this repository (namespace nq::) launched by one training step,
+    counted with the CUDA profiler on an extra, untimed step."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn(ids)
+        torch.cuda.synchronize()
+    ours = total = 0
+    for ev in prof.events():
+        if ev.device_type is not None and str(ev.device_type).endswith("CUDA"):
+            total += 1
+            if "nq::" in ev.name:
+                ours += 1
+    return {"ours": ours, "all": total}
+
+
+def run_e2e_ours(eng, args, B, S, V, dev, rank):
+    import torch
+    K = args.e2e_steps or args.steps
+    host = synthetic_batches(2, B, S, V, None, seed=99 + rank, pinned=True)
+    losses = []
+
+    def one(i):
+        ids = host[i % len(host)].to(dev, non_blocking=True)
+        out = eng.train_step([{"input_ids": ids, "labels": ids}])
+        stats = torch.stack([out["loss"], out["grad_norm"]]).cpu()
+        losses.append(float(stats[0]))
+
+    for i in range(2):
+        one(i)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(K):
+        one(i)
+    torch.cuda.synchronize()
+    dt = max_over_ranks((time.perf_counter() - t0) / K)
+    return {"s_per_step": dt, "h2d": B * S * 8, "d2h": 8,
+            "last_loss": losses[-1]}
+
+
+# -------------------------------------------------------- reference arm
+def run_reference(args, world, rank, local):
+    import torch
+    import torch.nn as nn
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "model")):
+        raise FileNotFoundError("baseline/_ref is missing")
+    sys.path.insert(0, ref)
+    from model.config import ModelConfig as RC  # noqa: E402  (reference code)
+    from model.transformer import Qwen3Model as RM
+    from training.optimizer import build_optimizer
+    from training.scheduler import build_scheduler
+
+    mk, B, S, par = CONFIGS[args.config]
+    rk = dict(mk)
+    torch.manual_seed(0)
+    model = RM(RC(**rk))
+    dev = torch.device("cuda", local)
+    model = model.to(dev)
+    if world > 1:
+        from distributed.parallel import ParallelConfig, ParallelismManager
+        pm = ParallelismManager(ParallelConfig(dp_size=-1, fsdp_enabled=True, dtype="bfloat16"))
+        model = pm.apply_parallelism(model)
+    opt = build_optimizer(model, lr=3e-4, weight_decay=0.1, fused=True)
+    sched = build_scheduler(opt, scheduler_type="cosine", warmup_steps=100, total_steps=100000)
+    inputs = synthetic_batches(4, B, S, mk["vocab_size"], dev, seed=1234 + rank)
+
+    def step(ids):
+        opt.zero_grad()
+        with torch.amp.autocast("cuda", dtype=torch.bfloat16):
+            out = model(input_ids=ids, labels=ids)
+            loss = out["loss"]
+        loss.backward()
+        loss.item()  # the reference loop reads the loss every micro-step
+        nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        sched.step()
+
+    ms, clocks = timed_loop(step, inputs, args.steps, args.warmup, local)
+    e2e = None
+    if not args.no_e2e:
+        host = synthetic_batches(2, B, S, mk["vocab_size"], None, seed=99 + rank, pinned=True)
+        for i in range(2):
+            step(host[i].to(dev, non_blocking=True))
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        K = args.e2e_steps or args.steps
+        for i in range(K):
+            ids = host[i % 2].to(dev, non_blocking=True)
+            opt.zero_grad()
+            with torch.amp.autocast("cuda", dtype=torch.bfloat16):
+                out = model(input_ids=ids, labels=ids)
+                loss = out["loss"]
+            loss.backward()
+            gn = nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+            opt.step()
+            sched.step()
+            torch.stack([loss.detach().float(), gn.float() if torch.is_tensor(gn) else loss.detach().float()]).cpu()
+        torch.cuda.synchronize()
+        e2e = {"s_per_step": max_over_ranks((time.perf_counter() - t0) / K), "h2d": B * S * 8, "d2h": 8}
+    return ms, clocks, {}, e2e
+
+
+# --------------------------------------------------------------------- main
+def main():
+    args = parse()
+    import torch
+    world, rank, local = dist_setup()
+    if args.gpus != world and world == 1 and args.gpus > 1:
+        print(json.dumps({"error": "launch N>1 with torch.distributed.run"}))
+        return 2
+    mk, B, S, par = CONFIGS[args.config]
+    try:
+        if args.impl == "reference":
+            maybe_init_pg(world, local)
+            ms, clocks, extra, e2e = run_reference(args, world, rank, local)
+        else:
+            ms, clocks, extra, e2e = run_ours(args, world, rank, local)
+    except FileNotFoundError as e:
+        if rank == 0:
+            print(json.dumps({"impl": args.impl, "unavailable": str(e)}))
+        return 0
+    tokens_per_step = B * S * world
+    value = tokens_per_step / (ms / 1e3)
+    fpt = flops_per_token(mk, S)
+    mfu = value * fpt / (measured_peak() * world)
+    line = {
+        "metric": BASELINE_METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic uniform-random token ids, random-init weights",
+        "config": {"model": f"{args.config} (Qwen3-1.7B shape: L28 h2048 16Q/8KV hd128 I6144 V151936 tied)"
+                   if args.config == "qwen3-1.7b" else args.config,
+                   "global_batch": B * world, "seq_len": S,
+                   "parallelism": f"dp{world}" + (" (ZeRO-2 sharded AdamW)" if args.impl == "ours" and world > 1
+                                                  else (" (FSDP2)" if world > 1 else "")),
+                   "l2": "no flush: per-step working set (weights + activations) >> 126 MB L2"},
+        "mfu": round(mfu, 4),
+        "flops_per_token": fpt,
+        "clocks": clocks,
+    }
+    if args.impl == "reference":
+        line["impl"] = "reference"
+    else:
+        line["impl"] = "ours"
+        line["gpu_launches"] = extra["gpu_launches_per_step"]["ours"] * args.steps
+        line["launches_per_step"] = extra["gpu_launches_per_step"]
+        line["kernel_error_flag"] = extra["kernel_error_flag"]
+    if e2e is not None:
+        line["e2e"] = {"value": round(tokens_per_step / e2e["s_per_step"], 1), "unit": "tokens/s",
+                       "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

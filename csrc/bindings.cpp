@@ -1,0 +1,110 @@
+// Python bindings of the sm_100a kernel library (module nano_qwen_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace nq {
+// gemm.cu
+torch::Tensor gemm_nt(torch::Tensor A, torch::Tensor B);
+void gemm_nt_out(torch::Tensor A, torch::Tensor B, torch::Tensor C);
+torch::Tensor gemm_nn(torch::Tensor A, torch::Tensor B);
+void gemm_nn_out(torch::Tensor A, torch::Tensor B, torch::Tensor C);
+void gemm_tn_acc(torch::Tensor A, torch::Tensor B, torch::Tensor C);
+torch::Tensor grouped_gemm_nt(torch::Tensor X, torch::Tensor W, torch::Tensor offsets);
+torch::Tensor grouped_gemm_nn(torch::Tensor dY, torch::Tensor W, torch::Tensor offsets);
+void grouped_gemm_tn_acc(torch::Tensor dY, torch::Tensor X, torch::Tensor dW, torch::Tensor offsets);
+// norm.cu
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor, c10::optional<torch::Tensor>, torch::Tensor, double);
+std::vector<torch::Tensor> add_rmsnorm_bwd(torch::Tensor, c10::optional<torch::Tensor>, torch::Tensor,
+                                           torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>);
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor, torch::Tensor, double, c10::ScalarType);
+torch::Tensor rmsnorm_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>);
+std::vector<torch::Tensor> layernorm_fwd(torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>, double, c10::ScalarType);
+torch::Tensor layernorm_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+                            c10::optional<torch::Tensor>, c10::optional<torch::Tensor>);
+// rope.cu
+std::vector<torch::Tensor> qknorm_rope_fwd(torch::Tensor, c10::optional<torch::Tensor>, c10::optional<torch::Tensor>,
+                                           torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>, int64_t,
+                                           int64_t, int64_t, int64_t, int64_t, double);
+void qknorm_rope_bwd(torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>, c10::optional<torch::Tensor>,
+                     torch::Tensor, torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>, torch::Tensor,
+                     c10::optional<torch::Tensor>, c10::optional<torch::Tensor>, int64_t, int64_t, int64_t,
+                     int64_t, int64_t);
+// attention
+std::vector<torch::Tensor> attn_fwd(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
+torch::Tensor attn_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+                       int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
+torch::Tensor decode_attn(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, double);
+// elementwise.cu
+int64_t error_flag_read();
+void error_flag_clear();
+torch::Tensor swiglu_fwd(torch::Tensor);
+torch::Tensor swiglu_bwd(torch::Tensor, torch::Tensor);
+torch::Tensor gelu_fwd(torch::Tensor);
+torch::Tensor gelu_bwd(torch::Tensor, torch::Tensor);
+void scale_inplace(torch::Tensor, torch::Tensor);
+void axpy_(torch::Tensor, torch::Tensor, torch::Tensor);
+torch::Tensor embedding_fwd(torch::Tensor, torch::Tensor);
+void embedding_bwd(torch::Tensor, torch::Tensor, torch::Tensor);
+torch::Tensor ce_count_valid(torch::Tensor);
+void ce_fused_chunk(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, bool);
+void ce_lse_chunk(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor);
+void ce_grad_chunk(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor);
+torch::Tensor sum_squares(torch::Tensor);
+void adamw_flat(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+                int64_t, int64_t, int64_t, double, double, double, double, double, double, double, double);
+// moe.cu
+std::vector<torch::Tensor> router_fwd(torch::Tensor, int64_t, bool);
+torch::Tensor router_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, bool);
+std::vector<torch::Tensor> moe_plan(torch::Tensor, int64_t, int64_t, int64_t);
+torch::Tensor moe_gather(torch::Tensor, torch::Tensor);
+torch::Tensor moe_combine(torch::Tensor, torch::Tensor, torch::Tensor);
+std::vector<torch::Tensor> moe_combine_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor);
+torch::Tensor moe_scatter_add(torch::Tensor, torch::Tensor, int64_t);
+}  // namespace nq
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nano_qwen_b200 sm_100a kernels";
+  m.def("gemm_nt", &nq::gemm_nt, "C = A @ B^T (bf16, tcgen05)");
+  m.def("gemm_nt_out", &nq::gemm_nt_out);
+  m.def("gemm_nn", &nq::gemm_nn, "C = A @ B (bf16, tcgen05)");
+  m.def("gemm_nn_out", &nq::gemm_nn_out);
+  m.def("gemm_tn_acc", &nq::gemm_tn_acc, "C(fp32) += A^T @ B (tcgen05)");
+  m.def("grouped_gemm_nt", &nq::grouped_gemm_nt);
+  m.def("grouped_gemm_nn", &nq::grouped_gemm_nn);
+  m.def("grouped_gemm_tn_acc", &nq::grouped_gemm_tn_acc);
+  m.def("add_rmsnorm_fwd", &nq::add_rmsnorm_fwd);
+  m.def("add_rmsnorm_bwd", &nq::add_rmsnorm_bwd);
+  m.def("rmsnorm_fwd", &nq::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &nq::rmsnorm_bwd);
+  m.def("layernorm_fwd", &nq::layernorm_fwd);
+  m.def("layernorm_bwd", &nq::layernorm_bwd);
+  m.def("qknorm_rope_fwd", &nq::qknorm_rope_fwd);
+  m.def("qknorm_rope_bwd", &nq::qknorm_rope_bwd);
+  m.def("attn_fwd", &nq::attn_fwd);
+  m.def("attn_bwd", &nq::attn_bwd);
+  m.def("decode_attn", &nq::decode_attn);
+  m.def("error_flag_read", &nq::error_flag_read);
+  m.def("error_flag_clear", &nq::error_flag_clear);
+  m.def("swiglu_fwd", &nq::swiglu_fwd);
+  m.def("swiglu_bwd", &nq::swiglu_bwd);
+  m.def("gelu_fwd", &nq::gelu_fwd);
+  m.def("gelu_bwd", &nq::gelu_bwd);
+  m.def("scale_inplace", &nq::scale_inplace);
+  m.def("axpy_", &nq::axpy_);
+  m.def("embedding_fwd", &nq::embedding_fwd);
+  m.def("embedding_bwd", &nq::embedding_bwd);
+  m.def("ce_count_valid", &nq::ce_count_valid);
+  m.def("ce_fused_chunk", &nq::ce_fused_chunk);
+  m.def("ce_lse_chunk", &nq::ce_lse_chunk);
+  m.def("ce_grad_chunk", &nq::ce_grad_chunk);
+  m.def("sum_squares", &nq::sum_squares);
+  m.def("adamw_flat", &nq::adamw_flat);
+  m.def("router_fwd", &nq::router_fwd);
+  m.def("router_bwd", &nq::router_bwd);
+  m.def("moe_plan", &nq::moe_plan);
+  m.def("moe_gather", &nq::moe_gather);
+  m.def("moe_combine", &nq::moe_combine);
+  m.def("moe_combine_bwd", &nq::moe_combine_bwd);
+  m.def("moe_scatter_add", &nq::moe_scatter_add);
+}

@@ -1,0 +1,452 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   C[M,N] = A * B^T with A, B either K-major or MN-major in global memory:
+//     fwd    : A = X  [M,K] (K-major),   B = W [N,K] (K-major)      -> C bf16
+//     dgrad  : A = dY [M,N'] (K-major),  B = W [N',K'] (MN-major)   -> C bf16
+//     wgrad  : A = dY [T,N'] (MN-major), B = X [T,K'] (MN-major)    -> C fp32 +=
+//   and grouped (mixture-of-experts) variants where groups split M (one
+//   weight per group) or K (one fp32 output per group).
+//
+// CTA = 6 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
+// warp 1 (one elected thread) issues tcgen05.mma 128xBNx16 into one of two TMEM
+// accumulators, warps 2-5 drain the other accumulator (tcgen05.ld -> registers
+// -> global) so the epilogue of tile i overlaps the main loop of tile i+1.  One
+// CTA per SM walks the tile list with a grid stride; tiles are rasterised in
+// bands of 8 M-tiles for L2 reuse of B.
+#include "sm100.cuh"
+#include "tmap.h"
+
+namespace nq {
+
+constexpr int GBM = 128;
+constexpr int GBK = 64;
+constexpr int kGemmThreads = 192;
+constexpr int kMaxGroups = 256;
+
+enum GroupMode : int { kGroupNone = 0, kGroupM = 1, kGroupK = 2 };
+enum EpiMode : int { kEpiBF16 = 0, kEpiAccF32 = 1 };
+
+struct GemmArgs {
+  int M, N, K;
+  void* C;
+  int64_t ldc;
+  int group_mode;
+  int num_groups;
+  const int* offsets;       // [num_groups+1], rows (group M) or k-rows (group K)
+  int64_t c_group_stride;   // group K: elements between the groups' outputs
+  int b_group_rows;         // group M: rows of B per group in the tensor map's row space
+  int* err;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = GBM * GBK * 2;
+  static constexpr int kBBytes = BN * GBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOff = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOff + 1024 + 4 * (kMaxGroups + 1) + 1024;  // + align slack
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
+  const int band_tiles = 8 * tiles_n;
+  const int band = t / band_tiles;
+  const int r = t - band * band_tiles;
+  const int m_base = band * 8;
+  const int bm = min(8, tiles_m - m_base);
+  mt = m_base + r % bm;
+  nt = r / bm;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmArgs args) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* s_off = reinterpret_cast<int*>(smem + L::kBarOff + 1024);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* err = args.err;
+
+  const int tiles_n = (args.N + BN - 1) / BN;
+  int tiles_m, total_tiles;
+  if (args.group_mode == kGroupM) {
+    tiles_m = 0;  // computed below from offsets
+  }
+  if (args.group_mode != kGroupNone) {
+    for (int i = threadIdx.x; i <= args.num_groups; i += blockDim.x) s_off[i] = args.offsets[i];
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (args.group_mode == kGroupM) {
+    tiles_m = s_off[args.num_groups] / GBM;
+    total_tiles = tiles_m * tiles_n;
+  } else if (args.group_mode == kGroupK) {
+    tiles_m = (args.M + GBM - 1) / GBM;
+    total_tiles = args.num_groups * tiles_m * tiles_n;
+  } else {
+    tiles_m = (args.M + GBM - 1) / GBM;
+    total_tiles = tiles_m * tiles_n;
+  }
+  const int per_group = tiles_m * tiles_n;
+
+  // Decode tile t -> (m0, n0, group, k range in elements).
+  auto decode = [&](int t, int& m0, int& n0, int& g, int& kb, int& ke) {
+    int tt = t;
+    g = 0;
+    if (args.group_mode == kGroupK) {
+      g = t / per_group;
+      tt = t - g * per_group;
+    }
+    int mt, nt;
+    tile_coords(tt, tiles_m, tiles_n, mt, nt);
+    m0 = mt * GBM;
+    n0 = nt * BN;
+    if (args.group_mode == kGroupM) {
+      int lo = 0, hi = args.num_groups - 1;
+      while (lo < hi) {  // last group with s_off[g] <= m0
+        int mid = (lo + hi + 1) >> 1;
+        if (s_off[mid] <= m0) lo = mid; else hi = mid - 1;
+      }
+      g = lo;
+    }
+    if (args.group_mode == kGroupK) {
+      kb = s_off[g];
+      ke = s_off[g + 1];
+    } else {
+      kb = 0;
+      ke = args.K;
+    }
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int m0, n0, g, kb, ke;
+        decode(t, m0, n0, g, kb, ke);
+        const int b_row_off = (args.group_mode == kGroupM) ? g * args.b_group_rows : 0;
+        for (int k0 = kb; k0 < ke; k0 += GBK) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTimeoutProducer)) { ok = false; break; }
+          uint8_t* sA = smem + stage * L::kStageBytes;
+          uint8_t* sB = sA + L::kABytes;
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < GBM / 64; ++j) tma_load_2d(sA + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(sB, &tmB, &full[stage], k0, b_row_off + n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sB + j * 8192, &tmB, &full[stage], n0 + 64 * j, b_row_off + k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: wait (bounded) until every issued load has landed before exiting.
+      if (!ok) {
+        for (int s = 0; s < STAGES; ++s) {
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(&full[s], 0) && !mbar_try_wait(&full[s], 1)) {
+            if (globaltimer() - t0 > 100000000ull) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16(GBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        int m0, n0, g, kb, ke;
+        decode(t, m0, n0, g, kb, ke);
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        uint32_t acc = 0;
+        for (int k0 = kb; k0 < ke; k0 += GBK) {
+          if (!mbar_wait(&full[stage], phase, err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < GBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                     : sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                     : sdesc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, acc);
+            acc = 1;
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        if (acc) umma_commit(&tfull[buf]);
+        else mbar_arrive(&tfull[buf]);  // empty K range: nothing accumulated
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      int m0, n0, g, kb, ke;
+      decode(t, m0, n0, g, kb, ke);
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&tfull[buf], use & 1, err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const int m_limit = (args.group_mode == kGroupM) ? s_off[args.num_groups] : args.M;
+      const bool row_ok = row < m_limit;
+      const bool has_acc = ke > kb;
+      if (has_acc) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + c, r);
+          tmem_wait_ld();
+          const int col = n0 + c;
+          if (!row_ok || col >= args.N) continue;
+          const int ncols = min(32, args.N - col);
+          if (EPI == kEpiBF16) {
+            __nv_bfloat16* Cp = reinterpret_cast<__nv_bfloat16*>(args.C) + static_cast<int64_t>(row) * args.ldc + col;
+            if (ncols == 32 && (reinterpret_cast<uintptr_t>(Cp) & 15) == 0) {
+              uint4* dst = reinterpret_cast<uint4*>(Cp);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 v;
+                v.x = pack_bf16(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1]));
+                v.y = pack_bf16(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3]));
+                v.z = pack_bf16(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5]));
+                v.w = pack_bf16(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7]));
+                dst[q] = v;
+              }
+            } else {
+              for (int j = 0; j < ncols; ++j) Cp[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+            }
+          } else {
+            float* Cp = reinterpret_cast<float*>(args.C) + static_cast<int64_t>(g) * args.c_group_stride +
+                        static_cast<int64_t>(row) * args.ldc + col;
+            if (ncols == 32 && (reinterpret_cast<uintptr_t>(Cp) & 15) == 0) {
+              float4* p4 = reinterpret_cast<float4*>(Cp);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 v = p4[q];
+                v.x += __uint_as_float(r[q * 4 + 0]);
+                v.y += __uint_as_float(r[q * 4 + 1]);
+                v.z += __uint_as_float(r[q * 4 + 2]);
+                v.w += __uint_as_float(r[q * 4 + 3]);
+                p4[q] = v;
+              }
+            } else {
+              for (int j = 0; j < ncols; ++j) Cp[j] += __uint_as_float(r[j]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ----------------------------------------------------------------------- host
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                        int max_tiles, cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    attr_set = true;
+  }
+  int grid = std::min(num_sms(), std::max(1, max_tiles));
+  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, a);
+  NQ_CHECK_CUDA(cudaGetLastError());
+}
+
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+
+static GemmArgs base_args(int M, int N, int K, void* C, int64_t ldc) {
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.C = C; a.ldc = ldc;
+  a.group_mode = kGroupNone; a.num_groups = 1; a.offsets = nullptr;
+  a.c_group_stride = 0; a.b_group_rows = 0; a.err = error_flag_ptr();
+  return a;
+}
+
+static inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+// C[M,N] (bf16) = A[M,K] @ B[N,K]^T
+void gemm_nt_out(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
+  check_bf16(A, "A"); check_bf16(B, "B"); check_bf16(C, "C");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_nt: shape mismatch");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm_nt: inner dim must be contiguous");
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "gemm_nt: C shape");
+  if (M == 0 || N == 0) return;
+  if (K == 0) { C.zero_(); return; }
+  c10::cuda::CUDAGuard g(A.device());
+  auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, GBM);
+  auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, kBN);
+  auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
+  launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
+                                                    at::cuda::getCurrentCUDAStream());
+}
+
+torch::Tensor gemm_nt(torch::Tensor A, torch::Tensor B) {
+  auto C = torch::empty({A.size(0), B.size(0)}, A.options());
+  gemm_nt_out(A, B, C);
+  return C;
+}
+
+// C[M,N] (bf16) = A[M,K] @ B[K,N]
+void gemm_nn_out(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
+  check_bf16(A, "A"); check_bf16(B, "B"); check_bf16(C, "C");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(0), "gemm_nn: shape mismatch");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm_nn: inner dim must be contiguous");
+  const int M = A.size(0), K = A.size(1), N = B.size(1);
+  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "gemm_nn: C shape");
+  if (M == 0 || N == 0) return;
+  if (K == 0) { C.zero_(); return; }
+  c10::cuda::CUDAGuard g(A.device());
+  auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, GBM);
+  auto tb = make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, 64);
+  auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
+  launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
+                                                   at::cuda::getCurrentCUDAStream());
+}
+
+torch::Tensor gemm_nn(torch::Tensor A, torch::Tensor B) {
+  auto C = torch::empty({A.size(0), B.size(1)}, A.options());
+  gemm_nn_out(A, B, C);
+  return C;
+}
+
+// C[M,N] (fp32) += A[K,M]^T @ B[K,N]
+void gemm_tn_acc(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
+  check_bf16(A, "A"); check_bf16(B, "B");
+  TORCH_CHECK(C.scalar_type() == torch::kFloat32 && C.is_cuda(), "gemm_tn_acc: C must be fp32 CUDA");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(0) == B.size(0), "gemm_tn_acc: shape mismatch");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm_tn_acc: inner dim must be contiguous");
+  const int K = A.size(0), M = A.size(1), N = B.size(1);
+  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "gemm_tn_acc: C shape");
+  if (M == 0 || N == 0 || K == 0) return;
+  c10::cuda::CUDAGuard g(A.device());
+  auto ta = make_tmap_2d_bf16(A.data_ptr(), K, M, A.stride(0), 64, 64);
+  auto tb = make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, 64);
+  auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
+  launch_gemm<kBN, kStages, true, true, kEpiAccF32>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
+                                                    at::cuda::getCurrentCUDAStream());
+}
+
+// ------------------------------------------------------------- grouped GEMMs
+// X [R, K] rows grouped by `offsets` (multiples of 128), W [G, N, K]:
+//   out[r, :] = X[r, :] @ W[g(r)]^T
+torch::Tensor grouped_gemm_nt(torch::Tensor X, torch::Tensor W, torch::Tensor offsets) {
+  check_bf16(X, "X"); check_bf16(W, "W");
+  TORCH_CHECK(W.dim() == 3 && X.size(1) == W.size(2) && W.is_contiguous() && X.is_contiguous(), "grouped_gemm_nt: shapes");
+  TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() == W.size(0) + 1, "offsets");
+  const int G = W.size(0), N = W.size(1), K = W.size(2), R = X.size(0);
+  TORCH_CHECK(G <= kMaxGroups, "too many groups");
+  auto C = torch::empty({R, N}, X.options());
+  if (R == 0) return C;
+  c10::cuda::CUDAGuard gd(X.device());
+  auto ta = make_tmap_2d_bf16(X.data_ptr(), R, K, K, 64, GBM);
+  auto tb = make_tmap_2d_bf16(W.data_ptr(), static_cast<int64_t>(G) * N, K, K, 64, kBN);
+  auto a = base_args(R, N, K, C.data_ptr(), N);
+  a.group_mode = kGroupM; a.num_groups = G; a.offsets = offsets.data_ptr<int>(); a.b_group_rows = N;
+  launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, cdiv(R, GBM) * cdiv(N, kBN),
+                                                    at::cuda::getCurrentCUDAStream());
+  return C;
+}
+
+// dY [R, N] grouped rows, W [G, N, K]: out[r, :] = dY[r, :] @ W[g(r)]   ([R, K])
+torch::Tensor grouped_gemm_nn(torch::Tensor dY, torch::Tensor W, torch::Tensor offsets) {
+  check_bf16(dY, "dY"); check_bf16(W, "W");
+  TORCH_CHECK(W.dim() == 3 && dY.size(1) == W.size(1) && W.is_contiguous() && dY.is_contiguous(), "grouped_gemm_nn: shapes");
+  const int G = W.size(0), N = W.size(1), K = W.size(2), R = dY.size(0);
+  TORCH_CHECK(N % 64 == 0, "grouped_gemm_nn: per-group reduction extent must be a multiple of 64");
+  auto C = torch::empty({R, K}, dY.options());
+  if (R == 0) return C;
+  c10::cuda::CUDAGuard gd(dY.device());
+  auto ta = make_tmap_2d_bf16(dY.data_ptr(), R, N, N, 64, GBM);
+  auto tb = make_tmap_2d_bf16(W.data_ptr(), static_cast<int64_t>(G) * N, K, K, 64, 64);
+  auto a = base_args(R, K, N, C.data_ptr(), K);
+  a.group_mode = kGroupM; a.num_groups = G; a.offsets = offsets.data_ptr<int>(); a.b_group_rows = N;
+  launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, cdiv(R, GBM) * cdiv(K, kBN),
+                                                   at::cuda::getCurrentCUDAStream());
+  return C;
+}
+
+// dW[g] (fp32 [N, K]) += dY[rows of g]^T @ X[rows of g]
+void grouped_gemm_tn_acc(torch::Tensor dY, torch::Tensor X, torch::Tensor dW, torch::Tensor offsets) {
+  check_bf16(dY, "dY"); check_bf16(X, "X");
+  TORCH_CHECK(dW.scalar_type() == torch::kFloat32 && dW.dim() == 3 && dW.is_contiguous(), "dW");
+  const int G = dW.size(0), N = dW.size(1), K = dW.size(2), R = dY.size(0);
+  TORCH_CHECK(dY.size(1) == N && X.size(1) == K && X.size(0) == R, "grouped_gemm_tn_acc: shapes");
+  if (R == 0) return;
+  c10::cuda::CUDAGuard gd(dY.device());
+  auto ta = make_tmap_2d_bf16(dY.data_ptr(), R, N, N, 64, 64);
+  auto tb = make_tmap_2d_bf16(X.data_ptr(), R, K, K, 64, 64);
+  auto a = base_args(N, K, 0, dW.data_ptr(), K);
+  a.group_mode = kGroupK; a.num_groups = G; a.offsets = offsets.data_ptr<int>();
+  a.c_group_stride = static_cast<int64_t>(N) * K;
+  launch_gemm<kBN, kStages, true, true, kEpiAccF32>(ta, tb, a, G * cdiv(N, GBM) * cdiv(K, kBN),
+                                                    at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace nq

@@ -81,25 +81,31 @@ class Attention(nn.Module):
 
     def _attend_general(self, qkv, qw, kw, cos, sin, position_ids, attention_mask, kv_cache,
                         B, S, Hq, Hk, D, eps):
-        q, k, v = qkv.split([Hq * D, Hk * D, Hk * D], dim=-1)
-        q = q.reshape(B, S, Hq, D)
-        k = k.reshape(B, S, Hk, D)
-        v = v.reshape(B, S, Hk, D)
         past = kv_cache.seq_len if kv_cache is not None else 0
         if position_ids is None:
-            position_ids = (torch.arange(S, device=q.device) + past).unsqueeze(0).expand(B, S)
-        q, k = ops.rope_qk(q, k, qw, kw, cos, sin, position_ids, eps)
+            position_ids = (torch.arange(S, device=qkv.device) + past).unsqueeze(0).expand(B, S)
+        q, k, v = ops.rope_qk(qkv, Hq, Hk, D, qw, kw, cos, sin, position_ids, eps)
         if kv_cache is not None:
             k_all, v_all = kv_cache.append(k, v)
         else:
             k_all, v_all = k, v
         if attention_mask is not None:
             o = _masked_attention(q, k_all, v_all, attention_mask, past)
+        elif q.is_cuda and past == 0:
+            # prefill into an empty cache: the flash-attention kernel on the prompt
+            o = ops.attention_core(qkv, qw, kw, cos, sin, position_ids, Hq, Hk, D, eps,
+                                   causal=True).view(B, S, Hq, D)
         elif q.is_cuda:
             kb, vb = (kv_cache.buffers() if kv_cache is not None else (k_all, v_all))
-            n = torch.full((B,), past + S, dtype=torch.int32, device=q.device)
-            start = torch.full((B,), past, dtype=torch.int32, device=q.device)
-            o = ops.decode_attention(q, kb, vb, n, start)
+            # the decode kernel holds at most 32 (q-head, row) pairs per kv head
+            rows = max(1, 32 // (Hq // Hk))
+            outs = []
+            for s0 in range(0, S, rows):
+                s1 = min(S, s0 + rows)
+                n = torch.full((B,), past + s1, dtype=torch.int32, device=q.device)
+                start = torch.full((B,), past + s0, dtype=torch.int32, device=q.device)
+                outs.append(ops.decode_attention(q[:, s0:s1].contiguous(), kb, vb, n, start))
+            o = outs[0] if len(outs) == 1 else torch.cat(outs, 1)
         else:
             o = ops.reference.attention(q, k_all, v_all, causal=True, q_offset=past)
         return o.reshape(B, S, Hq * D)

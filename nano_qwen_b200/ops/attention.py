@@ -89,13 +89,29 @@ def attention_core(qkv: torch.Tensor, q_w: Optional[torch.Tensor], k_w: Optional
     return o.reshape(B, S, Hq * D)
 
 
-def rope_qk(q: torch.Tensor, k: torch.Tensor, q_w, k_w, cos, sin, position_ids, eps):
-    """QK-norm + RoPE for the decode path (no autograd).  q [B,S,Hq,D]."""
-    B, S = q.shape[:2]
-    if q.is_cuda:
-        return ext().qknorm_rope_pair(q, k, q_w, k_w, cos, sin, position_ids, float(eps))
+def rope_qk(qkv: torch.Tensor, num_heads: int, num_kv_heads: int, head_dim: int, q_w, k_w,
+            cos, sin, position_ids, eps):
+    """QK-norm + RoPE at explicit positions for the cached path (no autograd).
+
+    qkv [B, S, (Hq+2Hk)*D] -> q [B,S,Hq,D], k [B,S,Hk,D], v [B,S,Hk,D].
+    """
+    B, S, _ = qkv.shape
+    Hq, Hk, D = num_heads, num_kv_heads, head_dim
+    if qkv.is_cuda:
+        qkv2 = qkv.reshape(B * S, -1).contiguous()
+        qk, _ = ext().qknorm_rope_fwd(qkv2, q_w, k_w, cos, sin, position_ids, B, S, Hq, Hk, D,
+                                      float(eps))
+        q = qk[:, :Hq * D].reshape(B, S, Hq, D)
+        k = qk[:, Hq * D:].reshape(B, S, Hk, D)
+        v = qkv2[:, (Hq + Hk) * D:].reshape(B, S, Hk, D)
+        return q, k, v
+    q, k, v = qkv.split([Hq * D, Hk * D, Hk * D], dim=-1)
+    q = q.reshape(B, S, Hq, D)
+    k = k.reshape(B, S, Hk, D)
+    v = v.reshape(B, S, Hk, D)
     c, s = _rope_tables(cos, sin, position_ids, B, S)
-    return ref.qk_norm_rope(q, k, q_w, k_w, c, s, eps)
+    q, k = ref.qk_norm_rope(q, k, q_w, k_w, c, s, eps)
+    return q, k, v
 
 
 def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

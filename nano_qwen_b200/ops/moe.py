@@ -96,9 +96,9 @@ class _MoEFFNFn(torch.autograd.Function):
         k = idx.shape[1]
         # slot_of [N,k] int32: row of each (token, slot) pair in the expert-sorted
         # buffer, -1 when dropped; offsets [E+1] int32: aligned start row per expert.
-        slot_of, offsets = E.moe_plan(idx, num_experts, capacity, PAD)
-        rows_cap = N * k + num_experts * PAD
-        xp = E.moe_gather(x, slot_of, rows_cap)
+        # src_of [N*k + E*PAD] int32: source token of each buffer row (-1 = zero row).
+        slot_of, offsets, src_of = E.moe_plan(idx, num_experts, capacity, PAD)
+        xp = E.moe_gather(x, src_of)
         Wgu = w_gu.compute.view(num_experts, 2 * inter, H)
         Wd = w_d.compute.view(num_experts, H, inter)
         gu = E.grouped_gemm_nt(xp, Wgu, offsets)
