@@ -1,43 +1,45 @@
-// Causal / non-causal GQA flash attention for sm_100a (tcgen05 + TMEM + TMA).
+// Causal / non-causal GQA flash attention forward for sm_100a
+// (tcgen05 + TMEM + TMA).
 //
 // Layout: q|k rows [T, (Hq+Hk)*D] and v inside the packed q|k|v rows
 // [T, (Hq+2Hk)*D] (T = B*S, token-major), so no head transposes exist anywhere.
 // GQA is native: q head h reads kv head h / (Hq/Hk).
 //
-// Forward CTA (one (batch, q-head, 128-query block)), 6 warps:
-//   warp 0   : TMA producer: Q once, then K_j / V_j into a 2-stage ring;
-//   warp 1   : MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
-//              S buffers, O += P_{j-1} V_{j-1} into the TMEM O accumulator,
-//              software-pipelined so softmax(j) overlaps P V (j-1);
-//   warps 2-5: softmax warpgroup, thread = query row = TMEM lane: reads S_j,
-//              masks, exponentiates (exp2 domain), writes bf16 P into a 128B-
-//              swizzled SMEM tile (the A operand of P V), and rescales O in
-//              TMEM only when the running max grows by more than 2^8 (exact:
-//              the final O / l uses the same reference max).
-// Output: bf16 O [T, Hq*D] and fp32 log-sum-exp [B, Hq, S].
+// CTA = (batch, q-head, 256 queries) = two 128-row query tiles, 12 warps:
+//   warp 0     : TMA producer: Q0/Q1 once, then K_j / V_j into a 2-stage ring;
+//   warp 1     : MMA issuer (one thread).  Per key block j and tile t it issues
+//                O_t += P_t(j-1) V(j-1)   (A operand P read from TMEM)
+//                S_t  = Q_t K_j^T         (into the same TMEM columns P used)
+//                so the tensor core alternates between the two tiles while the
+//                other tile's softmax runs;
+//   warps 4-7  : softmax warpgroup for tile 0, warps 8-11 for tile 1; thread =
+//                query row = TMEM lane.  Reads S (fp32), masks, exponentiates
+//                in the exp2 domain with tree reductions, writes P as packed
+//                bf16 back into TMEM over S, and rescales O in TMEM only when
+//                the running max grew by more than 2^8 (exact: the final O / l
+//                uses the same reference max).
+// TMEM: S/P tile 0 cols [0,128), tile 1 [128,256), O tile 0 [256,256+D),
+// O tile 1 [384,384+D).  Outputs bf16 O [T, Hq*D] and fp32 LSE [B, Hq, S].
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
 
 namespace nq {
 
-constexpr int ABM = 128;      // queries per CTA
-constexpr int ABN = 128;      // keys per block
-constexpr int kAttnThreads = 192;
-constexpr int kKVStages = 2;
+constexpr int ABM = 128;        // queries per tile
+constexpr int ABN = 128;        // keys per block
+constexpr int kTilesPerCta = 2;
+constexpr int kAttnThreads = 384;
 constexpr float kRescaleThresh = 8.0f;  // log2 units
 
 template <int D>
 struct AttnFwdSmem {
-  static constexpr int kQBytes = ABM * D * 2;
-  static constexpr int kKBytes = ABN * D * 2;
-  static constexpr int kVBytes = ABN * D * 2;
-  static constexpr int kPBytes = ABM * ABN * 2;
+  static constexpr int kQBytes = ABM * D * 2;   // per tile
+  static constexpr int kKVBytes = ABN * D * 2;  // K or V per stage
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQBytes;
-  static constexpr int kVOff = kKOff + kKVStages * kKBytes;
-  static constexpr int kPOff = kVOff + kKVStages * kVBytes;
-  static constexpr int kBarOff = kPOff + kPBytes;
+  static constexpr int kKOff = kQOff + kTilesPerCta * kQBytes;
+  static constexpr int kVOff = kKOff + 2 * kKVBytes;
+  static constexpr int kBarOff = kVOff + 2 * kKVBytes;
   static constexpr int kBytes = kBarOff + 256 + 1024;
 };
 
@@ -48,25 +50,52 @@ struct AttnArgs {
   __nv_bfloat16* O;  // [T, Hq*D]
   float* lse;        // [B, Hq, S]
   int* err;
+  unsigned long long* dbg;  // optional per-event timestamps of CTA 0 (profiling aid)
 };
 
-// Write one row of 128 bf16 values (given as fp32) into a K-major SW128 tile
-// made of 64-column regions of ABM rows (region stride ABM*128 bytes).
-__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, int col0, const float* v,
-                                                int nrows_region) {
-  // col0 is a multiple of 8; writes 8 values (one 16-byte unit)
-  const int region = col0 >> 6;
-  const int unit = (col0 & 63) >> 3;
-  uint8_t* base = tile + region * nrows_region * 128 + row * 128 + ((unit ^ (row & 7)) << 4);
-  uint4 u;
-  u.x = pack_bf16(v[0], v[1]);
-  u.y = pack_bf16(v[2], v[3]);
-  u.z = pack_bf16(v[4], v[5]);
-  u.w = pack_bf16(v[6], v[7]);
-  *reinterpret_cast<uint4*>(base) = u;
+#define NQ_TS(slot)                                                         \
+  do {                                                                      \
+    if (args.dbg != nullptr && blockIdx.x == 0) args.dbg[(slot)] = globaltimer(); \
+  } while (0)
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32"
+      " [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 
-template <int D>
+// Hardware 2^x (MUFU), relative error ~2^-22; ample for bf16 probabilities.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x on the FMA pipe, used for a share of the softmax exponentials so the
+// MUFU unit is not the only bottleneck.  x = n + f with n = round(x) obtained by
+// the 1.5*2^23 rounding trick and f in [-0.5, 0.5]; 2^f is a cubic fitted in
+// this repository by iteratively reweighted least squares for minimum max
+// relative error on [-0.5, 0.5] (max relative error 7.5e-5); 2^n is applied by
+// adding n to the exponent field (the low bits of the rounded value hold n).
+// Inputs below -126 are clamped (result ~1e-38, i.e. zero for softmax).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = x + 12582912.0f;
+  const float f = x - (t - 12582912.0f);
+  float p = fmaf(0.05517150089f, f, 0.24261096120f);
+  p = fmaf(p, f, 0.69326096773f);
+  p = fmaf(p, f, 0.99992805719f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+template <int D, int MODE>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmV,
                     const AttnArgs args) {
@@ -77,16 +106,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sQ = smem + L::kQOff;
   uint8_t* sK = smem + L::kKOff;
   uint8_t* sV = smem + L::kVOff;
-  uint8_t* sP = smem + L::kPOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* v_full = bars + 3;   // [2]
-  uint64_t* kv_empty = bars + 5; // [2]
-  uint64_t* s_full = bars + 7;   // [2]
-  uint64_t* s_free = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* pv_done = bars + 12;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;    // [2] per tile
+  uint64_t* p_full = bars + 9;    // [2] per tile (P written, S consumed)
+  uint64_t* o_done = bars + 11;   // [2] per tile: PV(j) complete
+  uint64_t* turn = bars + 15;     // [2] softmax ping-pong: turn[t] = tile t may exponentiate
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = threadIdx.x >> 5;
@@ -94,16 +122,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   int* err = args.err;
 
   const int S = args.S;
-  const int n_mblk = (S + ABM - 1) / ABM;
-  // Heaviest (last) query blocks first for causal load balance.
-  const int mb = n_mblk - 1 - (blockIdx.x % n_mblk);
+  constexpr int CTA_M = ABM * kTilesPerCta;
+  const int n_mblk = (S + CTA_M - 1) / CTA_M;
+  const int mb = n_mblk - 1 - (blockIdx.x % n_mblk);  // heaviest first
   const int bh = blockIdx.x / n_mblk;
   const int b = bh / args.Hq;
   const int h = bh - b * args.Hq;
   const int hk = h / (args.Hq / args.Hk);
-  const int q0 = mb * ABM;               // first query (within the sequence)
-  const int tok0 = b * S;                // first token of the sequence
-  const int n_kblk = args.causal ? min((q0 + ABM + ABN - 1) / ABN, (S + ABN - 1) / ABN)
+  const int q0 = mb * CTA_M;
+  const int tok0 = b * S;
+  const int n_kblk = args.causal ? min((q0 + CTA_M + ABN - 1) / ABN, (S + ABN - 1) / ABN)
                                  : (S + ABN - 1) / ABN;
 
   if (warp == 0 && lane == 0) {
@@ -113,10 +141,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 4);
+      mbar_init(&p_full[s], 4);
+      mbar_init(&o_done[s], 1);
+      mbar_init(&turn[s], 4);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmQK);
     tma_prefetch_desc(&tmV);
@@ -129,27 +157,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;          // two S buffers: cols [0,128), [128,256)
-  const uint32_t tO = tmem + 256;    // O accumulator: cols [256, 256+D)
 
   if (warp == 0) {
     if (elect_one()) {
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, L::kQBytes);
+      mbar_arrive_expect_tx(q_full, kTilesPerCta * L::kQBytes);
 #pragma unroll
-      for (int c = 0; c < KCH; ++c) tma_load_3d(sQ + c * ABM * 128, &tmQK, q_full, c * 64, h, tok0 + q0);
+      for (int t = 0; t < kTilesPerCta; ++t)
+#pragma unroll
+        for (int c = 0; c < KCH; ++c)
+          tma_load_3d(sQ + t * L::kQBytes + c * ABM * 128, &tmQK, q_full, c * 64, h, tok0 + q0 + t * ABM);
       for (int j = 0; j < n_kblk && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&kv_empty[st], ph ^ 1, err, kErrTimeoutProducer)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[st], L::kKBytes);
+        NQ_TS(8 * j + 0);
+        mbar_arrive_expect_tx(&k_full[st], L::kKVBytes);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-          tma_load_3d(sK + st * L::kKBytes + c * ABN * 128, &tmQK, &k_full[st], c * 64, args.Hq + hk, tok0 + j * ABN);
-        mbar_arrive_expect_tx(&v_full[st], L::kVBytes);
+          tma_load_3d(sK + st * L::kKVBytes + c * ABN * 128, &tmQK, &k_full[st], c * 64, args.Hq + hk, tok0 + j * ABN);
+        mbar_arrive_expect_tx(&v_full[st], L::kKVBytes);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-          tma_load_3d(sV + st * L::kVBytes + c * ABN * 128, &tmV, &v_full[st], c * 64, args.Hq + args.Hk + hk, tok0 + j * ABN);
+          tma_load_3d(sV + st * L::kKVBytes + c * ABN * 128, &tmV, &v_full[st], c * 64, args.Hq + args.Hk + hk, tok0 + j * ABN);
       }
     }
   } else if (warp == 1) {
@@ -159,138 +189,172 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = mbar_wait(q_full, 0, err, kErrTimeoutMma);
       tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ);
-      auto issue_pv = [&](int jj) -> bool {
-        const int st = jj & 1;
-        if (!mbar_wait(p_full, jj & 1, err, kErrTimeoutMma)) return false;
-        if (!mbar_wait(&v_full[st], (jj >> 1) & 1, err, kErrTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP);
-        const uint32_t v_addr = smem_u32(sV + st * L::kVBytes);
-#pragma unroll
-        for (int kk = 0; kk < ABN / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * (ABM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, ABN * 128, 1024);
-          umma_bf16(tO, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
-        return true;
-      };
-      for (int j = 0; j < n_kblk && ok; ++j) {
+      // iteration j issues, per tile: PV(j-1) then QK(j); after the loop, PV(n-1).
+      for (int j = 0; j <= n_kblk && ok; ++j) {
         const int st = j & 1;
-        const int sb = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
-        if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, err, kErrTimeoutMma)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + st * L::kKBytes);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(q_addr + (kk >> 2) * (ABM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * (ABN * 128) + (kk & 3) * 32, 16, 1024);
-          umma_bf16(tS + sb * ABN, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        const int pst = (j - 1) & 1;
+        if (j < n_kblk) {
+          if (!mbar_wait(&k_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
+          NQ_TS(8 * j + 1);
         }
-        umma_commit(&s_full[sb]);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        if (j > 0) {
+          if (!mbar_wait(&v_full[pst], ((j - 1) >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
+        }
+#pragma unroll
+        for (int t = 0; t < kTilesPerCta; ++t) {
+          const uint32_t tS = tmem + t * ABN;
+          const uint32_t tO = tmem + 256 + t * 128;
+          if (j > 0) {
+            // P_t(j-1) is ready once its softmax finished
+            if (!mbar_wait(&p_full[t], (j - 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
+            NQ_TS(8 * j + 2 + t);
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(sV + pst * L::kKVBytes);
+#pragma unroll
+            for (int kk = 0; kk < ABN / 16; ++kk) {
+              const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, ABN * 128, 1024);
+              umma_bf16_ts(tO, tS + kk * 8, bd, idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&o_done[t]);
+          }
+          if (j < n_kblk) {
+            const uint32_t k_addr = smem_u32(sK + st * L::kKVBytes);
+            const uint32_t qa = q_addr + t * L::kQBytes;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * (ABM * 128) + (kk & 3) * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * (ABN * 128) + (kk & 3) * 32, 16, 1024);
+              umma_bf16(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&s_full[t]);
+          }
+        }
+        if (!ok) break;
+        if (j > 0) umma_commit(&kv_empty[pst]);  // K(j-1) and V(j-1) no longer read
       }
-      if (ok) issue_pv(n_kblk - 1);
     }
-  } else {
-    // -------------------------------------------------------- softmax WG
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------- softmax WGs
+    const int t = (warp - 4) >> 2;          // tile
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // row within the tile == TMEM lane
-    const int qi = q0 + r;              // query position within the sequence
+    const int r = quarter * 32 + lane;      // row in tile == TMEM lane
+    const int qi = q0 + t * ABM + r;        // query position in the sequence
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    float m_ref = -INFINITY;  // reference max (log2 domain, scaled)
+    const uint32_t tS = tmem + t * ABN + lane_base;
+    const uint32_t tO = tmem + 256 + t * 128 + lane_base;
+    float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kblk; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t], j & 1, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      if (threadIdx.x % 128 == 0) NQ_TS(8 * j + 4 + 2 * t);
       tc_fence_after();
-      float s[ABN];
-#pragma unroll
-      for (int c = 0; c < ABN; c += 32) {
-        uint32_t u[32];
-        tmem_ld32(tS + lane_base + sb * ABN + c, u);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(u[i]) * args.scale_log2;
+      // Ping-pong: tile 0 exponentiates block j after tile 1 finished block j-1,
+      // tile 1 after tile 0 finished block j, so the two tiles' MUFU phases
+      // alternate and each overlaps the other tile's MMAs.
+      if (t == 0 ? j > 0 : true) {
+        const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
+        if (!mbar_wait(&turn[t], par, err, kErrTimeoutSoftmax)) { ok = false; break; }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
+      uint32_t u[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, u[c]);
+      tmem_wait_ld();
+      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 0);
       const int k0 = j * ABN;
-      const bool need_mask = (args.causal && k0 + ABN - 1 > q0) || (k0 + ABN > S);
-      float mx = -INFINITY;
+      const bool need_mask = (args.causal && k0 + ABN - 1 > q0 + t * ABM) || (k0 + ABN > S);
+      // Raw scores stay in registers; the scale (> 0) is applied to the max and
+      // folded into the exponent's FFMA.
       if (need_mask) {
 #pragma unroll
-        for (int i = 0; i < ABN; ++i) {
-          const int kj = k0 + i;
-          if (kj >= S || (args.causal && kj > qi)) s[i] = -INFINITY;
-          mx = fmaxf(mx, s[i]);
-        }
-      } else {
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < ABN; ++i) mx = fmaxf(mx, s[i]);
+          for (int i = 0; i < 32; ++i) {
+            const int kj = k0 + c * 32 + i;
+            if (kj >= S || (args.causal && kj > qi)) u[c][i] = 0xff800000u;  // -inf
+          }
       }
-      // Lazy rescale: move the reference max only when it grew by > 2^8.
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(u[c][i]));
+      const float sl2 = args.scale_log2;
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
+      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 1);
       const bool grow = mx > m_ref + kRescaleThresh;
       const float m_new = grow ? mx : m_ref;
-      const float alpha = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - m_new);
-      float rowsum = 0.f;
       const bool dead = (m_new == -INFINITY);
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      // P overwrites the first 64 columns of this tile's S region as packed bf16
+      // pairs.  PV(j-1) read the previous P before QK(j) wrote S (MMAs of one
+      // issuing thread execute in order), so the columns are free already.
 #pragma unroll
-      for (int i = 0; i < ABN; ++i) {
-        s[i] = dead ? 0.f : exp2f(s[i] - m_new);
-        rowsum += s[i];
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float x0 = fmaf(__uint_as_float(u[c][i]), sl2, -m_new);
+          const float x1 = fmaf(__uint_as_float(u[c][i + 1]), sl2, -m_new);
+          // MODE 1: one exponential in four runs on the FMA pipe (exp2_poly).
+          const float p0 = dead ? 0.f : ex2_approx(x0);
+          const float p1 = dead ? 0.f : ((MODE == 1 && (i & 2)) ? exp2_poly(x1) : ex2_approx(x1));
+          sum4[(i >> 1) & 3] += p0 + p1;
+          pk[i >> 1] = pack_bf16(p0, p1);
+        }
+        tmem_st16(tS + c * 16, pk);
       }
-      // P buffer and O are busy until the previous P V completes.
+      const float rowsum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&turn[t ^ 1]);
+      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 2);
+      // O and the P columns are busy until PV(j-1) of this tile completes.
       if (j > 0) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, err, kErrTimeoutSoftmax)) { ok = false; break; }
+        if (!mbar_wait(&o_done[t], (j - 1) & 1, err, kErrTimeoutSoftmax)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, grow && m_ref != -INFINITY)) {
-          const float a = grow ? alpha : 1.f;
+          const float a = (grow && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
 #pragma unroll
-          for (int c = 0; c < D; c += 16) {
-            uint32_t u[16];
-            tmem_ld16(tO + lane_base + c, u);
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(tO + c, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * a);
-            tmem_st16(tO + lane_base + c, u);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
+            tmem_st32(tO + c, o);
           }
-          tmem_wait_st();
         }
       }
-      l = l * (grow ? alpha : 1.f) + rowsum;
+      const float alpha = (m_ref == -INFINITY) ? 0.f : (grow ? exp2f(m_ref - m_new) : 1.f);
+      l = l * alpha + rowsum;
       m_ref = m_new;
-#pragma unroll
-      for (int c = 0; c < ABN; c += 8) store_row_sw128(sP, r, c, &s[c], ABM);
-      fence_proxy_async();
+      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 3);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (threadIdx.x % 128 == 0) NQ_TS(8 * j + 5 + 2 * t);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // --------------------------------------------------------- epilogue
-    if (ok && mbar_wait(pv_done, (n_kblk - 1) & 1, err, kErrTimeoutSoftmax)) {
+    if (ok && n_kblk > 0 && mbar_wait(&o_done[t], (n_kblk - 1) & 1, err, kErrTimeoutSoftmax)) {
       tc_fence_after();
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const bool row_ok = qi < S;
       __nv_bfloat16* orow = args.O + (static_cast<int64_t>(tok0 + qi) * args.Hq + h) * D;
 #pragma unroll
       for (int c = 0; c < D; c += 32) {
-        uint32_t u[32];
-        tmem_ld32(tO + lane_base + c, u);
+        uint32_t o[32];
+        tmem_ld32(tO + c, o);
         tmem_wait_ld();
         if (row_ok) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 v;
-            v.x = pack_bf16(__uint_as_float(u[q * 8 + 0]) * inv_l, __uint_as_float(u[q * 8 + 1]) * inv_l);
-            v.y = pack_bf16(__uint_as_float(u[q * 8 + 2]) * inv_l, __uint_as_float(u[q * 8 + 3]) * inv_l);
-            v.z = pack_bf16(__uint_as_float(u[q * 8 + 4]) * inv_l, __uint_as_float(u[q * 8 + 5]) * inv_l);
-            v.w = pack_bf16(__uint_as_float(u[q * 8 + 6]) * inv_l, __uint_as_float(u[q * 8 + 7]) * inv_l);
+            v.x = pack_bf16(__uint_as_float(o[q * 8 + 0]) * inv_l, __uint_as_float(o[q * 8 + 1]) * inv_l);
+            v.y = pack_bf16(__uint_as_float(o[q * 8 + 2]) * inv_l, __uint_as_float(o[q * 8 + 3]) * inv_l);
+            v.z = pack_bf16(__uint_as_float(o[q * 8 + 4]) * inv_l, __uint_as_float(o[q * 8 + 5]) * inv_l);
+            v.w = pack_bf16(__uint_as_float(o[q * 8 + 6]) * inv_l, __uint_as_float(o[q * 8 + 7]) * inv_l);
             dst[q] = v;
           }
         }
@@ -311,9 +375,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // --------------------------------------------------------------------- host
-template <int D>
+template <int D, int MODE = 0>
 static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, torch::Tensor& o,
-                            torch::Tensor& lse, int B, int S, int Hq, int Hk, bool causal, float scale) {
+                            torch::Tensor& lse, int B, int S, int Hq, int Hk, bool causal, float scale,
+                            unsigned long long* dbg = nullptr) {
   using L = AttnFwdSmem<D>;
   const int64_t T = static_cast<int64_t>(B) * S;
   auto tq = make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, ABM);
@@ -325,13 +390,14 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
   a.O = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   a.lse = lse.data_ptr<float>();
   a.err = error_flag_ptr();
-  auto kern = attn_fwd_kernel<D>;
+  a.dbg = dbg;
+  auto kern = attn_fwd_kernel<D, MODE>;
   static bool attr = false;
   if (!attr) {
     NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     attr = true;
   }
-  const int grid = B * Hq * ((S + ABM - 1) / ABM);
+  const int grid = B * Hq * ((S + ABM * kTilesPerCta - 1) / (ABM * kTilesPerCta));
   kern<<<grid, kAttnThreads, L::kBytes, at::cuda::getCurrentCUDAStream()>>>(tq, tv, a);
   NQ_CHECK_CUDA(cudaGetLastError());
 }
@@ -350,6 +416,22 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qk, torch::Tensor qkv, int64_t
   else if (D == 64) launch_attn_fwd<64>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale);
   else TORCH_CHECK(false, "attn_fwd: head_dim must be 64 or 128");
   return {o, lse};
+}
+
+// Same as attn_fwd, plus globaltimer stamps of pipeline events of CTA 0
+// (8 slots per key block: load issue, K ready, P0 ready, P1 ready, S0 ready,
+// P0 written, S1 ready, P1 written).  Profiling aid only.
+std::vector<torch::Tensor> attn_fwd_timeline(torch::Tensor qk, torch::Tensor qkv, int64_t B, int64_t S,
+                                             int64_t Hq, int64_t Hk, int64_t D, bool causal, double scale,
+                                             int64_t mode) {
+  c10::cuda::CUDAGuard g(qk.device());
+  auto o = torch::empty({B * S, Hq * D}, qk.options());
+  auto lse = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
+  auto ts = torch::zeros({8192}, qk.options().dtype(torch::kInt64));
+  auto* p = reinterpret_cast<unsigned long long*>(ts.data_ptr<int64_t>());
+  if (mode == 1) launch_attn_fwd<128, 1>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
+  else launch_attn_fwd<128, 0>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
+  return {o, lse, ts};
 }
 
 }  // namespace nq

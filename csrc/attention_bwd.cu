@@ -1,15 +1,27 @@
 // Flash-attention backward for sm_100a (tcgen05 + TMEM + TMA).
 //
-// CTA = (batch, kv-head, 128-key block).  K and V stay resident in shared
-// memory; the CTA walks every q-head of its GQA group and every query block
-// that can see its keys (causal), and for each one issues five tcgen05 GEMMs:
-//   S^T  = K Q^T,  dP^T = V dO^T          (TMEM; thread = key row)
-//   P^T  = exp(S^T * scale - lse),  dS^T = P^T (dP^T - delta) * scale  (bf16 -> SMEM)
-//   dV  += P^T dO,  dK += dS^T Q          (TMEM accumulators for the whole walk)
-//   dQ_i = dS K                           (TMEM, then vector atomics into fp32 dQ)
-// The dS^T tile written K-major for dK is read MN-major as the A operand of dQ
-// (same 128B-swizzled bytes), so no transpose pass exists.  delta = rowsum(dO*O)
-// comes from a small pre-pass kernel that also zeroes the dQ accumulator.
+// CTA = (batch, kv-head, 128-key block), 12 warps.  K and V stay resident in
+// shared memory; the CTA walks every q-head of its GQA group and every query
+// block that can see its keys (causal).  Per (q-head, query block) it issues
+//   S^T  = K Q^T        -> TMEM cols [0,128)     (thread = key row)
+//   dP^T = V dO^T       -> TMEM cols [128,256)
+//   compute: P^T = exp2(S^T*scale*log2e - lse*log2e) written back into TMEM as
+//            packed bf16 over S^T; dS^T = P^T (dP^T - delta) * scale written to a
+//            128B-swizzled shared tile
+//   dV  += P^T dO       (A operand P^T read from TMEM)   TMEM [384,512)
+//   dK  += dS^T Q                                        TMEM [256,384)
+//   dQ_i = dS K         -> TMEM cols [128,256) (over dP^T, already consumed);
+//          the dS^T tile written K-major for dK is read MN-major as dQ's A
+//          operand (same swizzled bytes), so there is no transpose pass.
+// Warp 0 streams Q/dO through a 2-deep ring, warp 1 issues the MMAs, warps 4-7
+// and 8-11 are two compute warpgroups that split every tile's 128 columns
+// (q columns for P/dS, head-dim columns for dQ/dK/dV).  dQ_i is staged (fp32,
+// 128B-swizzled) in iteration i's Q/dO buffers once its MMAs are done, and warp 2
+// adds it into an fp32 buffer with TMA bulk reductions
+// (cp.reduce.async.bulk.tensor .add) off the compute warps' critical path; the
+// producer reuses the buffers after that reduction has read them.  Warp 3
+// prefetches the next iteration's lse / delta.  The fp32 dq buffer is zeroed by
+// the pre-pass kernel, which also computes delta = rowsum(dO * O).
 // Outputs: dq|dk fp32 [T, (Hq+Hk)*D]; dv bf16 written into the v slot of dqkv.
 #include "common.cuh"
 #include "sm100.cuh"
@@ -19,21 +31,20 @@ namespace nq {
 
 constexpr int BKN = 128;  // keys per CTA
 constexpr int BQM = 128;  // queries per iteration
-constexpr int kBwdThreads = 192;
+constexpr int kBwdThreads = 384;
 
 template <int D>
 struct AttnBwdSmem {
   static constexpr int kTile = 128 * D * 2;  // K, V, Q, dO tiles
-  static constexpr int kPT = BKN * BQM * 2;
+  static constexpr int kDS = BKN * BQM * 2;
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kTile;
-  static constexpr int kQOff = kVOff + kTile;
-  static constexpr int kDOOff = kQOff + kTile;
-  static constexpr int kPTOff = kDOOff + kTile;
-  static constexpr int kDSOff = kPTOff + kPT;
-  static constexpr int kLseOff = kDSOff + kPT;          // 128 floats lse (log2 domain), 128 delta
+  static constexpr int kQOff = kVOff + kTile;        // [2]
+  static constexpr int kDOOff = kQOff + 2 * kTile;    // [2]
+  static constexpr int kDSOff = kDOOff + 2 * kTile;
+  static constexpr int kLseOff = kDSOff + kDS;        // 128 lse (log2 units) + 128 delta
   static constexpr int kBarOff = kLseOff + 2 * BQM * 4;
-  static constexpr int kBytes = kBarOff + 256 + 1024;
+  static constexpr int kBytes = kBarOff + 128 + 1024;
 };
 
 struct AttnBwdArgs {
@@ -46,7 +57,19 @@ struct AttnBwdArgs {
   float* dqk;         // [T, (Hq+Hk)*D] fp32: dq accumulated by atomics, dk written
   __nv_bfloat16* dqkv;  // [T, (Hq+2Hk)*D]: dv written into the v slot
   int* err;
+  unsigned long long* dbg;  // optional event timestamps of CTA 0 (profiling aid)
 };
+
+#define NQ_BTS(slot)                                                              \
+  do {                                                                            \
+    if (args.dbg != nullptr && blockIdx.x == 0) args.dbg[(slot)] = globaltimer(); \
+  } while (0)
+
+__device__ __forceinline__ float bwd_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ void store8_sw128(uint8_t* tile, int row, int col0, const float* v) {
   const int region = col0 >> 6;
@@ -60,12 +83,13 @@ __device__ __forceinline__ void store8_sw128(uint8_t* tile, int row, int col0, c
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-__device__ __forceinline__ void wg_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void wg_sync(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
 
 template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmV,
-                    const __grid_constant__ CUtensorMap tmDO, const AttnBwdArgs args) {
+                    const __grid_constant__ CUtensorMap tmDO, const __grid_constant__ CUtensorMap tmDQ,
+                    const AttnBwdArgs args) {
   using L = AttnBwdSmem<D>;
   constexpr int KCH = D / 64;
   extern __shared__ uint8_t smem_raw[];
@@ -74,28 +98,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = smem + L::kVOff;
   uint8_t* sQ = smem + L::kQOff;
   uint8_t* sDO = smem + L::kDOOff;
-  uint8_t* sPT = smem + L::kPTOff;
   uint8_t* sDS = smem + L::kDSOff;
   float* sLse = reinterpret_cast<float*>(smem + L::kLseOff);
   float* sDelta = sLse + BQM;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* s_full = bars + 3;    // S^T and dP^T ready
-  uint64_t* pt_full = bars + 4;   // P^T / dS^T written (and S^T/dP^T consumed)
-  uint64_t* pt_free = bars + 5;   // MMAs reading P^T / dS^T done
-  uint64_t* dq_full = bars + 6;
-  uint64_t* st_free = bars + 7;   // dQ read out of TMEM
-  uint64_t* acc_done = bars + 8;  // final dK / dV
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;     // S^T and dP^T ready
+  uint64_t* pt_full = bars + 6;    // P^T (TMEM) / dS^T (SMEM) written; S^T, dP^T consumed (8 warps)
+  uint64_t* dq_full = bars + 7;    // dQ_i in TMEM; dS^T smem free again
+  uint64_t* dq_free = bars + 8;    // dQ_i drained (8 warps)
+  uint64_t* acc_done = bars + 9;   // final dK / dV
+  uint64_t* staged = bars + 10;    // dQ_i staged in the Q/dO buffer of iteration i (8 warps)
+  uint64_t* qdo_rel = bars + 11;   // [2] bulk reduce finished reading the staged dQ
+  uint64_t* lse_rdy = bars + 13;   // lse/delta of the next iteration in shared memory
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = args.err;
   const int S = args.S;
   const int n_kblk = (S + BKN - 1) / BKN;
-  const int nb = blockIdx.x % n_kblk;
+  const int nb = blockIdx.x % n_kblk;  // causal: low key blocks carry the most work, start them first
   const int bk = blockIdx.x / n_kblk;
   const int b = bk / args.Hk;
   const int hk = bk - b * args.Hk;
@@ -108,11 +133,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int n_iter = G * iters_per_head;
 
   if (warp == 0 && lane == 0) {
-    for (int i = 0; i < 10; ++i) mbar_init(&bars[i], (i == 4 || i == 7) ? 4u : 1u);  // pt_full, st_free: 4 warps
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(pt_full, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 8);
+    mbar_init(acc_done, 1);
+    mbar_init(staged, 8);
+    mbar_init(&qdo_rel[0], 1);
+    mbar_init(&qdo_rel[1], 1);
+    mbar_init(lse_rdy, 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmQK);
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -122,8 +161,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tST = tmem;         // S^T, later dQ
-  const uint32_t tDP = tmem + 128;   // dP^T
+  const uint32_t tST = tmem;         // S^T, then P^T (bf16 packed in cols [0,64))
+  const uint32_t tDP = tmem + 128;   // dP^T, then dQ
   const uint32_t tDK = tmem + 256;
   const uint32_t tDV = tmem + 384;
 
@@ -144,12 +183,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int it = 0; it < n_iter; ++it) {
         int hq, mb;
         iter_coords(it, hq, mb);
-        if (!mbar_wait(qdo_empty, (it & 1) ^ 1, err, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * L::kTile);
+        const int bf = it & 1;
+        // buffer bf is reused once iteration it-2's MMAs and its dQ reduction are done
+        if (!mbar_wait(&qdo_empty[bf], ((it >> 1) & 1) ^ 1, err, kErrTimeoutProducer)) break;
+        if (!mbar_wait(&qdo_rel[bf], ((it >> 1) & 1) ^ 1, err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&qdo_full[bf], 2 * L::kTile);
 #pragma unroll
         for (int c = 0; c < KCH; ++c) {
-          tma_load_3d(sQ + c * 128 * 128, &tmQK, qdo_full, c * 64, hq, tok0 + mb * BQM);
-          tma_load_3d(sDO + c * 128 * 128, &tmDO, qdo_full, c * 64, hq, tok0 + mb * BQM);
+          tma_load_3d(sQ + bf * L::kTile + c * 128 * 128, &tmQK, &qdo_full[bf], c * 64, hq, tok0 + mb * BQM);
+          tma_load_3d(sDO + bf * L::kTile + c * 128 * 128, &tmDO, &qdo_full[bf], c * 64, hq, tok0 + mb * BQM);
         }
       }
     }
@@ -159,115 +201,196 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t id_kv = idesc_bf16(BKN, D, false, true);     // P^T dO, dS^T Q
       constexpr uint32_t id_q = idesc_bf16(BQM, D, true, true);       // dS K
       bool ok = mbar_wait(kv_full, 0, err, kErrTimeoutMma);
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
-      const uint32_t aPT = smem_u32(sPT), aDS = smem_u32(sDS);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aDS = smem_u32(sDS);
       for (int it = 0; it < n_iter && ok; ++it) {
-        const uint32_t ph = it & 1;
-        if (!mbar_wait(qdo_full, ph, err, kErrTimeoutMma)) { ok = false; break; }
-        if (!mbar_wait(st_free, ph ^ 1, err, kErrTimeoutMma)) { ok = false; break; }
+        const int bf = it & 1;
+        const uint32_t aQ = smem_u32(sQ + bf * L::kTile), aDO = smem_u32(sDO + bf * L::kTile);
+        if (!mbar_wait(&qdo_full[bf], (it >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
+        NQ_BTS(8 * it + 0);
         tc_fence_after();
+        // S^T (tST is free: P^T(it-1) was read by dV(it-1), issued earlier on this thread)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
           umma_bf16(tST, sdesc_sw128(aK + off, 16, 1024), sdesc_sw128(aQ + off, 16, 1024), id_s, kk > 0);
+        }
+        // dP^T overwrites dQ(it-1): wait until the compute warps drained it
+        if (!mbar_wait(dq_free, (it & 1) ^ 1, err, kErrTimeoutMma)) { ok = false; break; }
+        NQ_BTS(8 * it + 1);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
           umma_bf16(tDP, sdesc_sw128(aV + off, 16, 1024), sdesc_sw128(aDO + off, 16, 1024), id_s, kk > 0);
         }
         umma_commit(s_full);
-        if (!mbar_wait(pt_full, ph, err, kErrTimeoutMma)) { ok = false; break; }
+        if (!mbar_wait(pt_full, it & 1, err, kErrTimeoutMma)) { ok = false; break; }
+        NQ_BTS(8 * it + 2);
         tc_fence_after();
-        // dV += P^T dO ; dK += dS^T Q   (K = queries)
 #pragma unroll
         for (int kk = 0; kk < BQM / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-          const uint32_t boff = kk * 2048;
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16(tDV, sdesc_sw128(aPT + aoff, 16, 1024), sdesc_sw128(aDO + boff, 128 * 128, 1024), id_kv, acc);
-          umma_bf16(tDK, sdesc_sw128(aDS + aoff, 16, 1024), sdesc_sw128(aQ + boff, 128 * 128, 1024), id_kv, acc);
+          // dV += P^T dO : A = P^T from TMEM (K = queries), B = dO MN-major
+          umma_bf16_ts(tDV, tST + kk * 8, sdesc_sw128(aDO + kk * 2048, 128 * 128, 1024), id_kv, acc);
+          // dK += dS^T Q : A = dS^T smem K-major, B = Q MN-major
+          umma_bf16(tDK, sdesc_sw128(aDS + (kk >> 2) * (128 * 128) + (kk & 3) * 32, 16, 1024),
+                    sdesc_sw128(aQ + kk * 2048, 128 * 128, 1024), id_kv, acc);
         }
-        // dQ = dS K   (M = queries, K = keys): A = dS^T tile read MN-major, B = K read MN-major
+        // dQ = dS K (M = queries, K = keys): A = dS^T tile read MN-major, B = K MN-major
 #pragma unroll
         for (int kk = 0; kk < BKN / 16; ++kk) {
-          umma_bf16(tST, sdesc_sw128(aDS + kk * 2048, 128 * 128, 1024),
+          umma_bf16(tDP, sdesc_sw128(aDS + kk * 2048, 128 * 128, 1024),
                     sdesc_sw128(aK + kk * 2048, 128 * 128, 1024), id_q, kk > 0);
         }
         umma_commit(dq_full);
-        umma_commit(qdo_empty);
-        umma_commit(pt_free);
+        umma_commit(&qdo_empty[bf]);
       }
       if (ok) umma_commit(acc_done);
     }
-  } else {
-    // ------------------------------------------------------- compute WG
+  } else if (warp == 2) {
+    // ------------------------------------------------ dQ bulk-reduce issuer
+    if (elect_one()) {
+      for (int it = 0; it < n_iter; ++it) {
+        int hq, mb;
+        iter_coords(it, hq, mb);
+        const int bf = it & 1;
+        if (!mbar_wait(staged, it & 1, err, kErrTimeoutDrain)) break;
+#pragma unroll
+        for (int bx = 0; bx < D / 32; ++bx) {
+          const uint8_t* src = (D == 128) ? ((bx < 2 ? sQ : sDO) + bf * L::kTile + (bx & 1) * (128 * 128))
+                                          : ((bx == 0 ? sQ : sDO) + bf * L::kTile);
+          tma_reduce_add_3d(&tmDQ, src, 32 * bx, hq, tok0 + mb * BQM);
+        }
+        bulk_commit();
+        bulk_wait_read_all();
+        mbar_arrive(&qdo_rel[bf]);
+      }
+      bulk_wait_all();
+    }
+  } else if (warp == 3) {
+    // ------------------------------------- lse / delta prefetch (per iteration)
+    for (int it = 0; it < n_iter; ++it) {
+      int hq, mb;
+      iter_coords(it, hq, mb);
+      // the previous iteration's P/dS phase is the only reader of these values
+      if (it > 0 && !mbar_wait(pt_full, (it - 1) & 1, err, kErrTimeoutDrain)) break;
+      const int q0 = mb * BQM;
+#pragma unroll
+      for (int e = 0; e < BQM / 32; ++e) {
+        const int ql = e * 32 + lane;
+        const int q = q0 + ql;
+        const int64_t idx = (static_cast<int64_t>(b) * args.Hq + hq) * S + q;
+        sLse[ql] = (q < S) ? args.lse[idx] * 1.4426950408889634f : INFINITY;
+        sDelta[ql] = (q < S) ? args.delta[idx] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(lse_rdy);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------- compute WGs
+    const int wg = (warp - 4) >> 2;     // column half
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const int tid = threadIdx.x - 64;  // 0..127
+    const int r = quarter * 32 + lane;  // TMEM lane: key row (P/dS phase) or query row (dQ phase)
+    const int tid = (warp - 4) * 32 + lane - wg * 128;  // 0..127 within the WG
+    const int col0 = wg * 64;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int kj = k0 + r;             // this thread's key position
+    const int kj = k0 + r;              // this thread's key position
     bool ok = true;
     for (int it = 0; it < n_iter; ++it) {
       int hq, mb;
       iter_coords(it, hq, mb);
       const uint32_t ph = it & 1;
       const int q0 = mb * BQM;
-      // per-query lse (log2 domain) and delta into shared memory
-      {
-        const int q = q0 + tid;
-        const int64_t idx = (static_cast<int64_t>(b) * args.Hq + hq) * S + q;
-        sLse[tid] = (q < S) ? args.lse[idx] * 1.4426950408889634f : INFINITY;
-        sDelta[tid] = (q < S) ? args.delta[idx] : 0.f;
-      }
-      wg_sync();
+      if (!mbar_wait(lse_rdy, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       if (!mbar_wait(s_full, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 3);
       tc_fence_after();
-      // previous iteration's MMAs must be done reading sPT / sDS
-      if (!mbar_wait(pt_free, ph ^ 1, err, kErrTimeoutSoftmax)) { ok = false; break; }
-#pragma unroll 1
-      for (int c = 0; c < BQM; c += 32) {
-        uint32_t us[32], ud[32];
-        tmem_ld32(tST + lane_base + c, us);
-        tmem_ld32(tDP + lane_base + c, ud);
-        tmem_wait_ld();
+      const bool need_mask = (args.causal && k0 + BKN - 1 > q0) || (q0 + BQM > S) || (k0 + BKN > S);
+      uint32_t us2[2][32], ud2[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld32(tST + lane_base + col0 + 32 * c, us2[c]);
+        tmem_ld32(tDP + lane_base + col0 + 32 * c, ud2[c]);
+      }
+      tmem_wait_ld();
+      // P^T of the second column half lands in TMEM columns the first half is
+      // still reading as S^T: both compute warpgroups finish loading first.
+      asm volatile("bar.sync 3, 256;" ::: "memory");
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
+        const uint32_t* us = us2[c >> 5];
+        const uint32_t* ud = ud2[c >> 5];
         float p[32], ds[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qi = q0 + c + i;
-          const bool masked = (qi >= S) || (kj >= S) || (args.causal && kj > qi);
-          const float pv = masked ? 0.f : exp2f(__uint_as_float(us[i]) * args.scale_log2 - sLse[c + i]);
-          p[i] = pv;
-          ds[i] = pv * (__uint_as_float(ud[i]) - sDelta[c + i]) * args.scale;
-        }
+        for (int i = 0; i < 32; i += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(sLse + col0 + c + i);
+          const float4 d4 = *reinterpret_cast<const float4*>(sDelta + col0 + c + i);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+          const float dl[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          store8_sw128(sPT, r, c + i, &p[i]);
-          store8_sw128(sDS, r, c + i, &ds[i]);
+          for (int e = 0; e < 4; ++e) {
+            const float pv = bwd_ex2(fmaf(__uint_as_float(us[i + e]), args.scale_log2, -lv[e]));
+            p[i + e] = pv;
+            ds[i + e] = pv * (__uint_as_float(ud[i + e]) - dl[e]) * args.scale;
+          }
         }
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int qi = q0 + col0 + c + i;
+            const bool m = (qi >= S) || (kj >= S) || (args.causal && kj > qi);
+            p[i] = m ? 0.f : p[i];
+            ds[i] = m ? 0.f : ds[i];
+          }
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(p[2 * i], p[2 * i + 1]);
+        // P^T as packed bf16 over the first 64 columns of the S^T region:
+        // query column q lands in TMEM column q / 2.
+        tmem_st16(tST + lane_base + (col0 + c) / 2, pk);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) store8_sw128(sDS, r, col0 + c + i, &ds[i]);
       }
+      tmem_wait_st();
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 4);
       if (lane == 0) mbar_arrive(pt_full);
-      // dQ tile (thread = query row r) -> atomics into fp32 dq
+      // dQ drain: TMEM -> fp32 staging in the dS tile (free once the dQ MMA
+      // completed, which dq_full implies) -> TMA bulk reduce-add into the fp32 dq
+      // buffer.  Rounds of 64 head-dim columns; each warpgroup stages one
+      // 128-row x 32-column box (128B-swizzled, bank-conflict free).
       if (!mbar_wait(dq_full, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 5);
       tc_fence_after();
-      const int qrow = q0 + r;
-      float* dq = args.dqk + (static_cast<int64_t>(tok0 + qrow) * (args.Hq + args.Hk) + hq) * D;
-#pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
-        uint32_t u[32];
-        tmem_ld32(tST + lane_base + c, u);
-        tmem_wait_ld();
-        if (qrow < S) {
+      {
+        const int bf = it & 1;
+        uint32_t u[D / 64][32];
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            atomicAdd(reinterpret_cast<float4*>(dq + c + i),
-                      make_float4(__uint_as_float(u[i]), __uint_as_float(u[i + 1]),
-                                  __uint_as_float(u[i + 2]), __uint_as_float(u[i + 3])));
-          }
+        for (int hh = 0; hh < D / 64; ++hh) tmem_ld32(tDP + lane_base + 64 * hh + 32 * wg, u[hh]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);  // TMEM region free for the next dP^T
+        // dQ box (hh, wg) = 128 rows x 32 fp32 columns, 128B-swizzled, into the
+        // Q/dO buffer of this iteration (all of this iteration's MMAs are done).
+#pragma unroll
+        for (int hh = 0; hh < D / 64; ++hh) {
+          const int bx = 2 * hh + wg;
+          uint8_t* box = (D == 128) ? ((bx < 2 ? sQ : sDO) + bf * L::kTile + (bx & 1) * (128 * 128))
+                                    : ((bx == 0 ? sQ : sDO) + bf * L::kTile);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4*>(box + r * 128 + ((q ^ (r & 7)) << 4)) =
+                make_uint4(u[hh][4 * q], u[hh][4 * q + 1], u[hh][4 * q + 2], u[hh][4 * q + 3]);
         }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(staged);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(st_free);
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 6);
     }
     // ------------------------------------------------------- dK / dV out
     if (ok && n_iter > 0 && mbar_wait(acc_done, 0, err, kErrTimeoutSoftmax)) {
@@ -275,17 +398,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const bool row_ok = kj < S;
       float* dk = args.dqk + (static_cast<int64_t>(tok0 + kj) * (args.Hq + args.Hk) + args.Hq + hk) * D;
       __nv_bfloat16* dv = args.dqkv + (static_cast<int64_t>(tok0 + kj) * (args.Hq + 2 * args.Hk) + args.Hq + args.Hk + hk) * D;
-#pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
+#pragma unroll
+      for (int c = 0; c < D / 2; c += 32) {
+        const int cc = (D / 2) * wg + c;
         uint32_t uk[32], uv[32];
-        tmem_ld32(tDK + lane_base + c, uk);
-        tmem_ld32(tDV + lane_base + c, uv);
+        tmem_ld32(tDK + lane_base + cc, uk);
+        tmem_ld32(tDV + lane_base + cc, uv);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dk + c + i) = make_float4(__uint_as_float(uk[i]), __uint_as_float(uk[i + 1]),
-                                                               __uint_as_float(uk[i + 2]), __uint_as_float(uk[i + 3]));
+            *reinterpret_cast<float4*>(dk + cc + i) = make_float4(__uint_as_float(uk[i]), __uint_as_float(uk[i + 1]),
+                                                                __uint_as_float(uk[i + 2]), __uint_as_float(uk[i + 3]));
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 v;
@@ -293,16 +417,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             v.y = pack_bf16(__uint_as_float(uv[q * 8 + 2]), __uint_as_float(uv[q * 8 + 3]));
             v.z = pack_bf16(__uint_as_float(uv[q * 8 + 4]), __uint_as_float(uv[q * 8 + 5]));
             v.w = pack_bf16(__uint_as_float(uv[q * 8 + 6]), __uint_as_float(uv[q * 8 + 7]));
-            reinterpret_cast<uint4*>(dv + c)[q] = v;
+            reinterpret_cast<uint4*>(dv + cc)[q] = v;
           }
         }
-      }
-    } else if (n_iter == 0) {
-      // no query can see these keys: zero gradients
-      if (kj < S) {
-        float* dk = args.dqk + (static_cast<int64_t>(tok0 + kj) * (args.Hq + args.Hk) + args.Hq + hk) * D;
-        __nv_bfloat16* dv = args.dqkv + (static_cast<int64_t>(tok0 + kj) * (args.Hq + 2 * args.Hk) + args.Hq + args.Hk + hk) * D;
-        for (int c = 0; c < D; ++c) { dk[c] = 0.f; dv[c] = __float2bfloat16_rn(0.f); }
       }
     }
   }
@@ -347,8 +464,10 @@ __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dO, const 
 template <int D>
 static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tensor& qk, const torch::Tensor& qkv,
                                      const torch::Tensor& O, const torch::Tensor& lse, torch::Tensor& dqkv,
-                                     int B, int S, int Hq, int Hk, bool causal, float scale) {
+                                     int B, int S, int Hq, int Hk, bool causal, float scale,
+                                     unsigned long long* dbg = nullptr) {
   using L = AttnBwdSmem<D>;
+  static_assert(L::kBytes <= 232448, "attention backward shared memory budget");
   const int64_t T = static_cast<int64_t>(B) * S;
   auto dqk = torch::empty({T, (int64_t)(Hq + Hk) * D}, qk.options().dtype(torch::kFloat32));
   auto delta = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
@@ -364,6 +483,7 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
   auto tq = make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, 128);
   auto tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, 128);
   auto tdo = make_tmap_3d_bf16(dO.data_ptr(), D, Hq, T, D, (int64_t)Hq * D, 64, 1, 128);
+  auto tdq = make_tmap_3d_f32(dqk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 32, 1, 128);
   AttnBwdArgs a;
   a.B = B; a.S = S; a.Hq = Hq; a.Hk = Hk;
   a.scale = scale;
@@ -374,6 +494,7 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
   a.dqk = dqk.data_ptr<float>();
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.err = error_flag_ptr();
+  a.dbg = dbg;
   auto kern = attn_bwd_kernel<D>;
   static bool attr = false;
   if (!attr) {
@@ -381,7 +502,7 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
     attr = true;
   }
   const int grid = B * Hk * ((S + BKN - 1) / BKN);
-  kern<<<grid, kBwdThreads, L::kBytes, st>>>(tq, tv, tdo, a);
+  kern<<<grid, kBwdThreads, L::kBytes, st>>>(tq, tv, tdo, tdq, a);
   NQ_CHECK_CUDA(cudaGetLastError());
   return dqk;
 }
@@ -397,6 +518,20 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qk, torch::Tensor qkv, to
   if (D == 64) return launch_attn_bwd<64>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale);
   TORCH_CHECK(false, "attn_bwd: head_dim must be 64 or 128");
   return torch::Tensor();
+}
+
+// attn_bwd plus globaltimer stamps of CTA 0's pipeline events (8 per
+// iteration: Q/dO ready, dQ drained, P/dS ready (MMA view), S ready, P/dS
+// written, dQ ready, dQ drained (compute view)).  Profiling aid only.
+std::vector<torch::Tensor> attn_bwd_timeline(torch::Tensor dO, torch::Tensor qk, torch::Tensor qkv,
+                                             torch::Tensor O, torch::Tensor lse, torch::Tensor dqkv,
+                                             int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
+                                             bool causal, double scale) {
+  c10::cuda::CUDAGuard g(qk.device());
+  auto ts = torch::zeros({16384}, qk.options().dtype(torch::kInt64));
+  auto* p = reinterpret_cast<unsigned long long*>(ts.data_ptr<int64_t>());
+  auto dqk = launch_attn_bwd<128>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale, p);
+  return {dqk, ts};
 }
 
 }  // namespace nq

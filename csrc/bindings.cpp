@@ -32,8 +32,11 @@ void qknorm_rope_bwd(torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>,
                      int64_t, int64_t);
 // attention
 std::vector<torch::Tensor> attn_fwd(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
+std::vector<torch::Tensor> attn_fwd_timeline(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double, int64_t);
 torch::Tensor attn_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
                        int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
+std::vector<torch::Tensor> attn_bwd_timeline(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+                                             torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
 torch::Tensor decode_attn(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, double);
 // elementwise.cu
 int64_t error_flag_read();
@@ -83,6 +86,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qknorm_rope_bwd", &nq::qknorm_rope_bwd);
   m.def("attn_fwd", &nq::attn_fwd);
   m.def("attn_bwd", &nq::attn_bwd);
+  m.def("attn_fwd_timeline", &nq::attn_fwd_timeline);
+  m.def("attn_bwd_timeline", &nq::attn_bwd_timeline);
   m.def("decode_attn", &nq::decode_attn);
   m.def("error_flag_read", &nq::error_flag_read);
   m.def("error_flag_clear", &nq::error_flag_clear);

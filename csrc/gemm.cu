@@ -265,7 +265,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 dst[q] = v;
               }
             } else {
-              for (int j = 0; j < ncols; ++j) Cp[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) Cp[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
             }
           } else {
             float* Cp = reinterpret_cast<float*>(args.C) + static_cast<int64_t>(g) * args.c_group_stride +
@@ -282,7 +284,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 p4[q] = v;
               }
             } else {
-              for (int j = 0; j < ncols; ++j) Cp[j] += __uint_as_float(r[j]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) Cp[j] += __uint_as_float(r[j]);
             }
           }
         }

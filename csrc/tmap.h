@@ -73,6 +73,26 @@ inline CUtensorMap make_tmap_3d_bf16(const void* base, int64_t d0, int64_t d1, i
   return m;
 }
 
+// 3-D fp32 tensor map (used as the destination of TMA bulk reductions).
+inline CUtensorMap make_tmap_3d_f32(const void* base, int64_t d0, int64_t d1, int64_t d2,
+                                    int64_t s1_elems, int64_t s2_elems, int b0, int b1, int b2,
+                                    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1),
+                        static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(s1_elems) * 4,
+                           static_cast<cuuint64_t>(s2_elems) * 4};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(b0), static_cast<cuuint32_t>(b1),
+                       static_cast<cuuint32_t>(b2)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base not 16B aligned");
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled(3d f32) failed: " + std::to_string(r));
+  return m;
+}
+
 inline int num_sms() {
   static int n = -1;
   if (n < 0) {
