@@ -2,9 +2,11 @@
 //
 // One CTA of 256 threads owns a row at a time and walks rows with a grid
 // stride; each thread keeps its 8*NCH elements in registers (vectorised 16-byte
-// loads).  Weight gradients are reduced per CTA in registers and flushed with
-// one atomicAdd per element per CTA, so the backward needs no [rows, H] partial
-// buffer (the reference Triton kernel wrote one, kernels/rmsnorm.py:43-104).
+// loads).  Weight gradients are reduced per CTA in registers (over all of the
+// CTA's rows), written as one row per CTA of a small [CTAs, H] buffer, and
+// summed into the gradient by ``colsum_add_kernel`` -- deterministic and free
+// of same-address atomics (the reference's Triton kernel wrote a [rows, H]
+// partial buffer instead, kernels/rmsnorm.py:43-104).
 #include "common.cuh"
 #include "tmap.h"
 
@@ -117,13 +119,11 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_bwd_kernel(
       }
     }
   }
-  if (dw != nullptr) {
+  if (dw != nullptr) {  // this CTA's row of the [gridDim.x, H] partial buffer
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * kNormThreads + threadIdx.x) * 8;
-      if (col < H)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) atomicAdd(dw + col + i, dwacc[c][i]);
+      if (col < H) st8(dw + static_cast<int64_t>(blockIdx.x) * H + col, dwacc[c]);
     }
   }
 }
@@ -211,13 +211,11 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
       }
     }
   }
-  if (dw != nullptr) {
+  if (dw != nullptr) {  // this CTA's row of the [gridDim.x, H] partial buffer
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * kNormThreads + threadIdx.x) * 8;
-      if (col < H)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) atomicAdd(dw + col + i, dwacc[c][i]);
+      if (col < H) st8(dw + static_cast<int64_t>(blockIdx.x) * H + col, dwacc[c]);
     }
   }
 }
@@ -322,17 +320,46 @@ __global__ void __launch_bounds__(kNormThreads) layernorm_bwd_kernel(
   for (int c = 0; c < NCH; ++c) {
     const int col = (c * kNormThreads + threadIdx.x) * 8;
     if (col < H) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (dw != nullptr) atomicAdd(dw + col + i, dwacc[c][i]);
-        if (db != nullptr) atomicAdd(db + col + i, dbacc[c][i]);
-      }
+      if (dw != nullptr) st8(dw + static_cast<int64_t>(blockIdx.x) * H + col, dwacc[c]);
+      if (db != nullptr) st8(db + static_cast<int64_t>(blockIdx.x) * H + col, dbacc[c]);
     }
   }
 }
 
 // --------------------------------------------------------------------- host
 static int norm_grid(int T) { return std::max(1, std::min(T, num_sms() * 8)); }
+
+// out[c] += sum_b part[b, c]; grid (ceil(H/32), splits), block (32, 8).
+__global__ void __launch_bounds__(256) colsum_add_kernel(const float* __restrict__ part, int G, int H,
+                                                         float* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int col = blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (col < H)
+    for (int b = blockIdx.y * 8 + threadIdx.y; b < G; b += 8 * gridDim.y)
+      s += part[static_cast<int64_t>(b) * H + col];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && col < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int y = 0; y < 8; ++y) t += red[y][threadIdx.x];
+    if (gridDim.y == 1) out[col] += t; else atomicAdd(out + col, t);
+  }
+}
+
+// Partial weight-gradient buffer for a backward launch with `grid` CTAs.
+static torch::Tensor wgrad_partial(const torch::Tensor& like, int grid, int H) {
+  return torch::empty({grid, H}, like.options().dtype(torch::kFloat32));
+}
+
+static void colsum_add(const torch::Tensor& part, float* out, cudaStream_t st) {
+  const int G = part.size(0), H = part.size(1);
+  const int cb = (H + 31) / 32;
+  const int splits = std::max(1, std::min(G / 64, (2 * num_sms() + cb - 1) / cb));
+  colsum_add_kernel<<<dim3(cb, splits), dim3(32, 8), 0, st>>>(part.data_ptr<float>(), G, H, out);
+  NQ_CHECK_CUDA(cudaGetLastError());
+}
 static int nch_for(int H) {
   TORCH_CHECK(H % 8 == 0, "norm: hidden size must be a multiple of 8");
   int n = (H / 8 + kNormThreads - 1) / kNormThreads;
@@ -388,12 +415,17 @@ std::vector<torch::Tensor> add_rmsnorm_bwd(torch::Tensor dy, c10::optional<torch
   float* dwp = (dw.has_value() && dw->defined()) ? dw->data_ptr<float>() : nullptr;
   if (T == 0) return {dx, dxb};
   auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = norm_grid(T);
+  torch::Tensor part;
+  if (dwp != nullptr) part = wgrad_partial(h, grid, H);
   NQ_NCH_DISPATCH(nch_for(H),
-    add_rmsnorm_bwd_kernel<NCH><<<norm_grid(T), kNormThreads, 0, st>>>(
+    add_rmsnorm_bwd_kernel<NCH><<<grid, kNormThreads, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(dy.contiguous().data_ptr()), dhp, h.data_ptr<float>(),
         w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr<float>(),
-        reinterpret_cast<__nv_bfloat16*>(dxb.data_ptr()), dwp, T, H));
+        reinterpret_cast<__nv_bfloat16*>(dxb.data_ptr()),
+        dwp != nullptr ? part.data_ptr<float>() : nullptr, T, H));
   NQ_CHECK_CUDA(cudaGetLastError());
+  if (dwp != nullptr) colsum_add(part, dwp, st);
   return {dx, dxb};
 }
 
@@ -430,16 +462,21 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
   if (T == 0) return dx;
   auto dyc = dy.to(x.scalar_type()).contiguous();
   auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = norm_grid(T);
+  torch::Tensor part;
+  if (dwp != nullptr) part = wgrad_partial(x, grid, H);
+  float* pp = dwp != nullptr ? part.data_ptr<float>() : nullptr;
   NQ_NCH_DISPATCH(nch_for(H),
     if (x.scalar_type() == torch::kBFloat16)
-      rmsnorm_bwd_kernel<NCH, __nv_bfloat16><<<norm_grid(T), kNormThreads, 0, st>>>(
+      rmsnorm_bwd_kernel<NCH, __nv_bfloat16><<<grid, kNormThreads, 0, st>>>(
           reinterpret_cast<const __nv_bfloat16*>(dyc.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-          w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr<float>(), dwp, T, H);
+          w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr<float>(), pp, T, H);
     else
-      rmsnorm_bwd_kernel<NCH, float><<<norm_grid(T), kNormThreads, 0, st>>>(
+      rmsnorm_bwd_kernel<NCH, float><<<grid, kNormThreads, 0, st>>>(
           dyc.data_ptr<float>(), x.data_ptr<float>(), w.data_ptr<float>(), rstd.data_ptr<float>(),
-          dx.data_ptr<float>(), dwp, T, H));
+          dx.data_ptr<float>(), pp, T, H));
   NQ_CHECK_CUDA(cudaGetLastError());
+  if (dwp != nullptr) colsum_add(part, dwp, st);
   return dx;
 }
 
@@ -479,16 +516,24 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
   float* dbp = (db.has_value() && db->defined()) ? db->data_ptr<float>() : nullptr;
   auto dyc = dy.to(x.scalar_type()).contiguous();
   auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = norm_grid(T);
+  torch::Tensor pw, pb;
+  if (dwp != nullptr) pw = wgrad_partial(x, grid, H);
+  if (dbp != nullptr) pb = wgrad_partial(x, grid, H);
+  float* pwp = dwp != nullptr ? pw.data_ptr<float>() : nullptr;
+  float* pbp = dbp != nullptr ? pb.data_ptr<float>() : nullptr;
   NQ_NCH_DISPATCH(nch_for(H),
     if (x.scalar_type() == torch::kBFloat16)
-      layernorm_bwd_kernel<NCH, __nv_bfloat16><<<norm_grid(T), kNormThreads, 0, st>>>(
+      layernorm_bwd_kernel<NCH, __nv_bfloat16><<<grid, kNormThreads, 0, st>>>(
           reinterpret_cast<const __nv_bfloat16*>(dyc.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-          w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr<float>(), dwp, dbp, T, H);
+          w.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr<float>(), pwp, pbp, T, H);
     else
-      layernorm_bwd_kernel<NCH, float><<<norm_grid(T), kNormThreads, 0, st>>>(
+      layernorm_bwd_kernel<NCH, float><<<grid, kNormThreads, 0, st>>>(
           dyc.data_ptr<float>(), x.data_ptr<float>(), w.data_ptr<float>(), mean.data_ptr<float>(),
-          rstd.data_ptr<float>(), dx.data_ptr<float>(), dwp, dbp, T, H));
+          rstd.data_ptr<float>(), dx.data_ptr<float>(), pwp, pbp, T, H));
   NQ_CHECK_CUDA(cudaGetLastError());
+  if (dwp != nullptr) colsum_add(pw, dwp, st);
+  if (dbp != nullptr) colsum_add(pb, dbp, st);
   return dx;
 }
 

@@ -61,7 +61,9 @@ class Attention(nn.Module):
 
     def forward(self, hidden_states: torch.Tensor, position_ids: Optional[torch.Tensor] = None,
                 attention_mask: Optional[torch.Tensor] = None,
-                kv_cache: Optional[KVCache] = None) -> torch.Tensor:
+                kv_cache: Optional[KVCache] = None, rope=None) -> torch.Tensor:
+        """``rope`` = optional (cos, sin) per-token tables [B*S, D/2] (multimodal
+        RoPE); they replace the 1-D position tables for this call."""
         B, S, _ = hidden_states.shape
         Hq, Hk = self._heads()
         D = self.head_dim
@@ -70,14 +72,33 @@ class Attention(nn.Module):
         qw = self.q_norm.weight if self.qk_norm else None
         kw = self.k_norm.weight if self.qk_norm else None
         cos, sin = self.rotary_emb.cos_cached, self.rotary_emb.sin_cached
+        if rope is not None:
+            cos, sin = rope
+            position_ids = torch.arange(B * S, device=qkv.device).view(B, S)
         eps = self.config.rms_norm_eps
-        if kv_cache is None and attention_mask is None:
+        cp = getattr(self, "cp_group", None)
+        if cp is not None and kv_cache is None:
+            o = self._attend_cp(qkv, qw, kw, cos, sin, position_ids, B, S, Hq, Hk, D, eps, cp)
+        elif kv_cache is None and attention_mask is None:
             o = ops.attention_core(qkv, qw, kw, cos, sin, position_ids, Hq, Hk, D, eps,
                                    causal=True)
         else:
             o = self._attend_general(qkv, qw, kw, cos, sin, position_ids, attention_mask,
                                      kv_cache, B, S, Hq, Hk, D, eps)
         return fused_linear(o, [self.o_proj], dtype)
+
+    def _attend_cp(self, qkv, qw, kw, cos, sin, position_ids, B, S, Hq, Hk, D, eps, group):
+        """Context-parallel attention: local queries against the group's keys
+        (``parallel.context_parallel.cp_attention``); positions are global."""
+        from ..parallel.context_parallel import cp_attention
+        q, k, v = qkv.split([Hq * D, Hk * D, Hk * D], dim=-1)
+        q = q.reshape(B, S, Hq, D)
+        k = k.reshape(B, S, Hk, D)
+        v = v.reshape(B, S, Hk, D)
+        pos = position_ids.expand(B, S)
+        q, k = ops.reference.qk_norm_rope(q, k, qw, kw, cos[pos], sin[pos], eps)
+        o = cp_attention(q, k, v, pos, group)
+        return o.reshape(B, S, Hq * D)
 
     def _attend_general(self, qkv, qw, kw, cos, sin, position_ids, attention_mask, kv_cache,
                         B, S, Hq, Hk, D, eps):

@@ -35,14 +35,25 @@ def compute_dtype_of(x: torch.Tensor) -> torch.dtype:
 
 
 def fused_linear(x: torch.Tensor, linears: Sequence[Linear], dtype: torch.dtype) -> torch.Tensor:
-    """One GEMM over the concatenated weights of ``linears`` (rows stacked)."""
+    """One GEMM over the concatenated weights of ``linears`` (rows stacked).
+
+    Tensor-parallel layers (``tp_mode`` set by ``parallel.tensor_parallel``)
+    gather their input (column-parallel) or reduce their output (row-parallel).
+    """
     wref = ops.weight_ref([l.weight for l in linears], dtype)
     bias = None
     if linears[0].bias is not None:
         bias = torch.cat([l.bias for l in linears]) if len(linears) > 1 else linears[0].bias
     if x.dtype != dtype:
         x = x.to(dtype)
-    return ops.linear(x, wref, bias)
+    mode = getattr(linears[0], "tp_mode", None)
+    if mode is None:
+        return ops.linear(x, wref, bias)
+    from ..parallel.tensor_parallel import tp_input, tp_output
+    if mode == "col":
+        return ops.linear(tp_input(x, linears[0]), wref, bias)
+    y = tp_output(ops.linear(x, wref), linears[0])
+    return y + bias.to(y.dtype) if bias is not None else y
 
 
 class RMSNorm(nn.Module):

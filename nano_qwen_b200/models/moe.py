@@ -31,10 +31,16 @@ class TopKRouter(nn.Module):
         self.norm_topk_prob = config.norm_topk_prob
         self.aux_loss_coef = config.router_aux_loss_coef
         self.gate = Linear(config.hidden_size, config.num_experts, bias=False)
+        # < 1 under tensor parallelism: every TP rank routes the same tokens, so
+        # each contributes 1/tp of the router's gradient (summed over TP later).
+        self.grad_scale = 1.0
 
     def forward(self, hidden_states: torch.Tensor):
         """Returns (weights fp32 [N,k], indices int32 [N,k], counts [E], prob_sum [E])."""
         logits = fused_linear(hidden_states, [self.gate], hidden_states.dtype)
+        if self.grad_scale != 1.0:
+            from ..parallel.tensor_parallel import scale_grad
+            logits = scale_grad(logits, self.grad_scale)
         return ops.route(logits, self.top_k, self.norm_topk_prob)
 
 
@@ -66,9 +72,10 @@ class MoELayer(nn.Module):
 
     def fusion_groups(self):
         gu = []
-        for e in range(self.num_experts):
+        n = len(self.experts)  # E, or E/ep under expert parallelism
+        for e in range(n):
             gu += [f"experts.{e}.ffn.gate_proj.weight", f"experts.{e}.ffn.up_proj.weight"]
-        down = [f"experts.{e}.ffn.down_proj.weight" for e in range(self.num_experts)]
+        down = [f"experts.{e}.ffn.down_proj.weight" for e in range(n)]
         return [gu, down]
 
     def expert_weight_refs(self, dtype):
@@ -84,6 +91,17 @@ class MoELayer(nn.Module):
         return int(self.capacity_factor * num_tokens * self.top_k / self.num_experts)
 
     def forward(self, hidden_states: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        tp = getattr(self, "tp_group", None)
+        if tp is not None:
+            # experts are sharded along the intermediate dim: all tokens in, partial sums out
+            from ..parallel.tensor_parallel import _CopyToTP, gather_seq, scatter_seq, tp_output
+            x_in = gather_seq(hidden_states, tp) if self.tp_sp else _CopyToTP.apply(hidden_states, tp)
+            out, aux = self._forward_local(x_in)
+            out = scatter_seq(out, tp) if self.tp_sp else tp_output_allreduce(out, tp)
+            return out, aux
+        return self._forward_local(hidden_states)
+
+    def _forward_local(self, hidden_states: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
         N = x.shape[0]
@@ -100,6 +118,11 @@ class MoELayer(nn.Module):
             out = ops.moe_ffn(x, weights, idx, w_gu, w_d, self.num_experts, self.inter,
                               self.capacity(N))
         return out.view(shape), aux
+
+
+def tp_output_allreduce(y, group):
+    from ..parallel.tensor_parallel import _AllReduce
+    return _AllReduce.apply(y, group)
 
 
 class GlobalBatchLoadBalancer:

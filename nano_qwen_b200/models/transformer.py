@@ -53,11 +53,11 @@ class TransformerBlock(nn.Module):
         self.feed_forward = MoELayer(config) if self._use_moe else build_ffn(config)
 
     def forward_fused(self, resid: torch.Tensor, delta: Optional[torch.Tensor],
-                      position_ids=None, attention_mask=None, kv_cache=None):
+                      position_ids=None, attention_mask=None, kv_cache=None, rope=None):
         """(resid, pending delta) -> (resid, new delta, aux).  resid is fp32."""
         eps = self.config.rms_norm_eps
         resid, x = ops.add_rms_norm(resid, delta, self.input_layernorm.weight, eps)
-        a = self.attention(x, position_ids, attention_mask, kv_cache)
+        a = self.attention(x, position_ids, attention_mask, kv_cache, rope)
         resid, x = ops.add_rms_norm(resid, a, self.post_attention_layernorm.weight, eps)
         if self._use_moe:
             f, aux = self.feed_forward(x)
@@ -85,6 +85,9 @@ class Qwen3Model(nn.Module):
         if config.tie_word_embeddings:
             self.lm_head.weight = self.embed.embed_tokens.weight
         self.gradient_checkpointing = config.gradient_checkpointing
+        # Set by parallel.tensor_parallel: the residual stream is sequence-sharded.
+        self.sp_group = None
+        self.tp_group = None
         self.reset_parameters()
 
     # ------------------------------------------------------------------ init
@@ -109,9 +112,21 @@ class Qwen3Model(nn.Module):
         return torch.bfloat16 if device.type == "cuda" else self.embed.embed_tokens.weight.dtype
 
     def hidden(self, input_ids: torch.Tensor, position_ids=None, attention_mask=None,
-               kv_caches: Optional[List[KVCache]] = None, inputs_embeds=None):
+               kv_caches: Optional[List[KVCache]] = None, inputs_embeds=None, rope=None):
         """Runs embed + blocks + final norm; returns (normed hidden [B,S,H], aux_total, n_moe)."""
-        resid = self.embed(input_ids) if inputs_embeds is None else inputs_embeds
+        if self.sp_group is not None:
+            # sequence parallel: this rank's slice only (embedding rows are looked
+            # up for the local tokens, so their gradient is partial over TP)
+            import torch.distributed as dist
+
+            from ..parallel.tensor_parallel import scale_grad, split_dim, split_seq
+            if inputs_embeds is None:
+                resid = self.embed(split_dim(input_ids, 1, self.sp_group))
+            else:
+                resid = split_seq(scale_grad(inputs_embeds, 1.0 / dist.get_world_size(self.sp_group)),
+                                  self.sp_group)
+        else:
+            resid = self.embed(input_ids) if inputs_embeds is None else inputs_embeds
         delta = None
         aux_total = None
         n_moe = 0
@@ -120,11 +135,11 @@ class Qwen3Model(nn.Module):
             cache = kv_caches[i] if kv_caches is not None else None
             if use_ckpt and cache is None:
                 resid, delta, aux = ckpt.checkpoint(layer.forward_fused, resid, delta,
-                                                    position_ids, attention_mask, None,
+                                                    position_ids, attention_mask, None, rope,
                                                     use_reentrant=False)
             else:
                 resid, delta, aux = layer.forward_fused(resid, delta, position_ids,
-                                                        attention_mask, cache)
+                                                        attention_mask, cache, rope)
             if aux is not None:
                 aux_total = aux if aux_total is None else aux_total + aux
                 n_moe += 1
@@ -136,6 +151,9 @@ class Qwen3Model(nn.Module):
                 kv_caches: Optional[List[KVCache]] = None, labels: Optional[torch.Tensor] = None,
                 return_logits: Optional[bool] = None, logits_to_keep: int = 0,
                 inputs_embeds: Optional[torch.Tensor] = None) -> dict:
+        if getattr(self, "cp_group", None) is not None and kv_caches is None:
+            return self._forward_cp(input_ids, position_ids, labels, return_logits,
+                                    logits_to_keep, inputs_embeds)
         x, aux_total, n_moe = self.hidden(input_ids, position_ids, attention_mask, kv_caches,
                                           inputs_embeds)
         dtype = x.dtype
@@ -143,12 +161,19 @@ class Qwen3Model(nn.Module):
             return_logits = labels is None
         logits = None
         if return_logits:
-            xs = x[:, -logits_to_keep:] if logits_to_keep else x
+            xf = x
+            if self.sp_group is not None:
+                from ..parallel.tensor_parallel import all_gather_dim
+                xf = all_gather_dim(x, 1, self.sp_group)
+            xs = xf[:, -logits_to_keep:] if logits_to_keep else xf
             logits = ops.linear(xs, self.lm_head_ref(dtype))
         loss = None
         if labels is not None:
             targets = shift_targets(labels)
-            loss = ops.linear_cross_entropy(x, self.lm_head_ref(dtype), targets)
+            if self.sp_group is None:
+                loss = ops.linear_cross_entropy(x, self.lm_head_ref(dtype), targets)
+            else:
+                loss = _sp_loss(x, self.lm_head_ref(dtype), targets, self.sp_group)
             if n_moe > 0:
                 loss = loss + self.config.router_aux_loss_coef * (aux_total / n_moe)
         aux_out = None
@@ -156,11 +181,71 @@ class Qwen3Model(nn.Module):
             aux_out = aux_total
         return {"logits": logits, "loss": loss, "aux_loss": aux_out, "hidden_states": x}
 
+    def _forward_cp(self, input_ids, position_ids, labels, return_logits, logits_to_keep,
+                    inputs_embeds):
+        """Context-parallel forward: this rank runs its zigzag share of the
+        sequence (``parallel.context_parallel``); the loss is the global mean."""
+        import torch.distributed as dist
+
+        from ..parallel.context_parallel import cp_loss, zigzag_indices
+        from ..parallel.tensor_parallel import all_gather_dim
+        if self.sp_group is not None:
+            raise NotImplementedError("context parallelism with sequence parallelism")
+        grp = self.cp_group
+        ws, r = dist.get_world_size(grp), dist.get_rank(grp)
+        src = input_ids if input_ids is not None else inputs_embeds
+        B, S = src.shape[0], src.shape[1]
+        dev = src.device
+        idx = zigzag_indices(S, ws, r, dev)
+        pos = (torch.arange(S, device=dev).unsqueeze(0).expand(B, S) if position_ids is None
+               else position_ids.expand(B, S))
+        x, aux_total, n_moe = self.hidden(
+            input_ids[:, idx] if input_ids is not None else None, pos[:, idx], None, None,
+            inputs_embeds[:, idx] if inputs_embeds is not None else None)
+        dtype = x.dtype
+        if return_logits is None:
+            return_logits = labels is None
+        logits = None
+        if return_logits:
+            order = torch.cat([zigzag_indices(S, ws, q, dev) for q in range(ws)])
+            xg = all_gather_dim(x, 1, grp)
+            xf = torch.empty_like(xg)
+            xf[:, order] = xg
+            xs = xf[:, -logits_to_keep:] if logits_to_keep else xf
+            logits = ops.linear(xs, self.lm_head_ref(dtype))
+        loss = None
+        if labels is not None:
+            t = shift_targets(labels)[:, idx].contiguous()
+            n_local = (t != -100).sum().float()
+            n_global = n_local.clone()
+            dist.all_reduce(n_global, group=grp)
+            part = ops.linear_cross_entropy(x, self.lm_head_ref(dtype), t) * \
+                (n_local / n_global.clamp(min=1))
+            loss = cp_loss(part, grp)
+            if n_moe > 0:
+                loss = loss + self.config.router_aux_loss_coef * (aux_total / n_moe)
+        return {"logits": logits, "loss": loss, "aux_loss": aux_total if n_moe > 0 else None,
+                "hidden_states": x}
+
     @torch.no_grad()
     def count_parameters(self) -> dict:
         total = sum(p.numel() for p in self.parameters())
         trainable = sum(p.numel() for p in self.parameters() if p.requires_grad)
         return {"total": total, "trainable": trainable}
+
+
+def _sp_loss(x, wref, targets, group):
+    """Global mean CE when each rank holds a sequence slice: local sum / global
+    count, summed over the group (forward all-reduce, identity backward)."""
+    import torch.distributed as dist
+
+    from ..parallel.tensor_parallel import _AllReduce, split_dim
+    t = split_dim(targets, 1, group)
+    n_local = (t != -100).sum().float()
+    n_global = n_local.clone()
+    dist.all_reduce(n_global, group=group)
+    part = ops.linear_cross_entropy(x, wref, t) * (n_local / n_global.clamp(min=1))
+    return _AllReduce.apply(part, group)
 
 
 def shift_targets(labels: torch.Tensor) -> torch.Tensor:

@@ -11,7 +11,7 @@ from ._ext import available as native_available
 from ._ext import ext
 from .attention import attention_core, decode_attention, full_attention, rope_qk
 from .embedding import embedding
-from .linear import WeightRef, linear, weight_ref
+from .linear import WeightRef, dense, linear, weight_ref
 from .loss import linear_cross_entropy, token_logprobs
 from .mlp import swiglu_packed
 from .moe import aux_loss_from_stats, moe_ffn, route

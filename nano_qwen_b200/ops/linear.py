@@ -129,6 +129,39 @@ class _LinearFn(torch.autograd.Function):
         return (dx, None) + (None,) * len(wref.anchors)
 
 
+class _DenseFn(torch.autograd.Function):
+    """y = x W^T with both inputs ordinary autograd tensors (the weight gradient
+    is returned, not accumulated in place); for weights derived by other ops."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        ctx.save_for_backward(x2, w)
+        ctx.in_shape = x.shape
+        y = ext().gemm_nt(x2, w.contiguous())
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        E = ext()
+        dx = E.gemm_nn(dy2, w.contiguous()).view(ctx.in_shape) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+            E.gemm_tn_acc(dy2, x2, dw)
+            dw = dw.to(w.dtype)
+        return dx, dw
+
+
+def dense(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """x @ w^T through the tcgen05 GEMM with standard autograd semantics."""
+    if x.is_cuda:
+        return _DenseFn.apply(x, w)
+    return x @ w.t()
+
+
 def linear(x: torch.Tensor, wref: WeightRef, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     if torch.is_grad_enabled() and (x.requires_grad or wref.requires_grad):
         y = _LinearFn.apply(x, wref, *wref.anchors)

@@ -1,0 +1,173 @@
+"""Context parallelism: the sequence is split over the CP group.
+
+Layout: the sequence is cut into 2*cp equal chunks and rank r holds chunks r
+and 2*cp-1-r ("zigzag"), so every rank gets the same amount of causal work.
+Tokens keep their global positions (RoPE and the causal mask use them).
+
+Attention: each rank projects q/k/v for its own tokens, all-gathers k and v
+(and their positions) over the group -- with GQA the k|v rows are a quarter of
+the q rows or less, and over NVSwitch the gather is one collective -- and
+attends its queries to every key whose position is not after the query's.  The
+backward of the gather is a reduce-scatter of dk/dv.  Gradients of the
+replicated parameters are partial sums over the group; ``cp_loss`` scales the
+backward by cp so that the engine's gradient average over the (dp x cp) group
+yields the data-parallel mean of the full-sequence gradient.
+
+The reference's ring attention (reference: distributed/context_parallel.py:52-136)
+is also provided under its name, with a correct source rank per ring step (the
+reference receives from rank-1 but masks as if the chunk came from rank+1).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .tensor_parallel import all_gather_dim, reduce_scatter_dim
+
+
+def zigzag_indices(seq_len: int, cp: int, rank: int, device=None) -> torch.Tensor:
+    """Global positions held by ``rank`` (chunks rank and 2cp-1-rank)."""
+    if seq_len % (2 * cp):
+        raise ValueError(f"seq_len={seq_len} must divide by 2*cp_size={2 * cp}")
+    c = seq_len // (2 * cp)
+    a = torch.arange(rank * c, (rank + 1) * c, device=device)
+    b = torch.arange((2 * cp - 1 - rank) * c, (2 * cp - rank) * c, device=device)
+    return torch.cat([a, b])
+
+
+def split_sequence(hidden_states: torch.Tensor, cp_rank: int, cp_size: int) -> torch.Tensor:
+    """Contiguous split along dim 1 (reference API:
+    distributed/context_parallel.py:17)."""
+    S = hidden_states.shape[1]
+    assert S % cp_size == 0, f"seq_len={S} not divisible by cp_size={cp_size}"
+    c = S // cp_size
+    return hidden_states[:, cp_rank * c:(cp_rank + 1) * c].contiguous()
+
+
+def gather_sequence(local_hidden: torch.Tensor, cp_group=None) -> torch.Tensor:
+    """All-gather contiguous chunks back to the full sequence (reference API:
+    distributed/context_parallel.py:38)."""
+    if cp_group is None or dist.get_world_size(cp_group) <= 1:
+        return local_hidden
+    return all_gather_dim(local_hidden, 1, cp_group)
+
+
+class _GatherKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return all_gather_dim(x, 1, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        return reduce_scatter_dim(g.contiguous(), 1, ctx.group), None
+
+
+class _CPLoss(torch.autograd.Function):
+    """Forward: sum of the per-rank partial losses.  Backward: cp * grad, see
+    the module docstring."""
+
+    @staticmethod
+    def forward(ctx, part, group):
+        ctx.ws = dist.get_world_size(group)
+        out = part.clone()
+        dist.all_reduce(out, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        return g * ctx.ws, None
+
+
+def cp_loss(part: torch.Tensor, group) -> torch.Tensor:
+    return _CPLoss.apply(part, group)
+
+
+def cp_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: torch.Tensor,
+                 group, scale: Optional[float] = None) -> torch.Tensor:
+    """q [B,Sl,Hq,D], k/v [B,Sl,Hk,D] local; pos [B,Sl] global positions.
+
+    Returns [B,Sl,Hq,D]: causal attention over the whole sequence by position.
+    """
+    B, Sl, Hq, D = q.shape
+    Hk = k.shape[2]
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    kf = _GatherKV.apply(k, group)
+    vf = _GatherKV.apply(v, group)
+    pk = all_gather_dim(pos, 1, group)                       # [B, S]
+    keep = pk[:, None, :] <= pos[:, :, None]                 # [B, Sl, S]
+    g = Hq // Hk
+    if g > 1:
+        kf = kf.repeat_interleave(g, dim=2)
+        vf = vf.repeat_interleave(g, dim=2)
+    o = F.scaled_dot_product_attention(q.transpose(1, 2), kf.transpose(1, 2), vf.transpose(1, 2),
+                                       attn_mask=keep[:, None], scale=scale)
+    return o.transpose(1, 2)
+
+
+def apply_context_parallel(model: nn.Module, cp_group, cp_ranks=None) -> nn.Module:
+    """Mark a Qwen3Model (or the LM of a VL model) for context parallelism."""
+    from ..models.attention import Attention
+    lm = getattr(model, "language_model", model)
+    lm.cp_group = cp_group
+    for m in lm.modules():
+        if isinstance(m, Attention):
+            m.cp_group = cp_group
+    return model
+
+
+class RingAttention(nn.Module):
+    """Ring attention over contiguous sequence chunks (reference API:
+    distributed/context_parallel.py:52).  q/k/v are [B,H,S_local,D]; K/V blocks
+    travel one hop per step while the local block is attended; partial results
+    are merged with their log-sum-exp.  Differentiable through autograd of the
+    per-step math (the p2p exchange itself is treated as constant, as in the
+    reference); the model's CP path uses ``cp_attention``."""
+
+    def __init__(self, cp_group=None):
+        super().__init__()
+        self.cp_group = cp_group
+        self.cp_size = dist.get_world_size(cp_group) if cp_group is not None else 1
+        self.cp_rank = dist.get_rank(cp_group) if cp_group is not None else 0
+
+    def forward(self, q, k, v, causal: bool = True):
+        if self.cp_size <= 1:
+            return F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        B, H, S, D = q.shape
+        scale = 1.0 / math.sqrt(D)
+        ranks = dist.get_process_group_ranks(self.cp_group)
+        nxt = ranks[(self.cp_rank + 1) % self.cp_size]
+        prv = ranks[(self.cp_rank - 1) % self.cp_size]
+        out = torch.zeros(B, H, S, D, dtype=torch.float32, device=q.device)
+        lse = torch.full((B, H, S, 1), float("-inf"), device=q.device)
+        kc, vc = k.contiguous(), v.contiguous()
+        for step in range(self.cp_size):
+            src = (self.cp_rank - step) % self.cp_size   # owner of the block held now
+            if step < self.cp_size - 1:
+                kr, vr = torch.empty_like(kc), torch.empty_like(vc)
+                ops = [dist.P2POp(dist.isend, kc, nxt, self.cp_group),
+                       dist.P2POp(dist.isend, vc, nxt, self.cp_group),
+                       dist.P2POp(dist.irecv, kr, prv, self.cp_group),
+                       dist.P2POp(dist.irecv, vr, prv, self.cp_group)]
+                reqs = dist.batch_isend_irecv(ops)
+            if not (causal and src > self.cp_rank):
+                s = torch.matmul(q.float(), kc.float().transpose(-2, -1)) * scale
+                if causal and src == self.cp_rank:
+                    m = torch.triu(torch.ones(S, S, dtype=torch.bool, device=q.device), 1)
+                    s = s.masked_fill(m, float("-inf"))
+                blk_lse = torch.logsumexp(s, -1, keepdim=True)
+                blk = torch.matmul(torch.exp(s - blk_lse), vc.float())
+                new = torch.logaddexp(lse, blk_lse)
+                out = out * torch.exp(lse - new) + blk * torch.exp(blk_lse - new)
+                lse = new
+            if step < self.cp_size - 1:
+                for r in reqs:
+                    r.wait()
+                kc, vc = kr, vr
+        return out.to(q.dtype)

@@ -4,9 +4,7 @@ Two modes, both operating on slices of the ``FlatParamStore`` buffers (no
 packing copies):
 
 * ``replicate``: every rank keeps full weights/optimizer state; gradients are
-  averaged with bucketed all-reduces.  Buckets are issued from a backward hook
-  as soon as a block's gradients are final, on a side stream, so the
-  reductions overlap the rest of the backward pass.
+  averaged with bucketed all-reduces after the backward pass.
 * ``shard`` (default; the role FSDP2 plays in the reference,
   reference: distributed/fsdp.py:44-75): gradients are reduce-scattered so each
   rank owns 1/N of the flat buffer, the fused AdamW kernel updates only that
@@ -39,11 +37,29 @@ def shard_bounds(numel: int, world: int, rank: int) -> Tuple[int, int]:
     return b, e
 
 
+def _src(group) -> int:
+    """Global rank of the group's first member (``dist.broadcast`` takes a
+    global rank)."""
+    return dist.get_global_rank(group, 0) if group is not None else 0
+
+
 class DataParallel:
+    """``expert_group``: ranks that hold the same experts under expert
+    parallelism (one per EP block).  The store's expert span is summed over it
+    and divided by the data-parallel world, which equals the data-parallel mean
+    of the full-batch expert gradient (each EP rank's expert gradient already
+    sums the tokens of its whole EP block).  Expert parallelism uses the
+    replicate mode."""
+
     def __init__(self, store: FlatParamStore, mode: str = "shard", group=None,
-                 bucket_mb: float = 256.0):
+                 bucket_mb: float = 256.0, expert_group=None):
         self.store = store
         self.group = group
+        xb, xe = getattr(store, "expert_span", (0, 0))
+        self.expert_span = (xb, xe) if xe > xb else None
+        self.expert_group = expert_group
+        if self.expert_span is not None and mode == "shard":
+            mode = "replicate"
         self.mode = mode
         self.world = get_world_size(group)
         self.rank = get_rank(group)
@@ -74,8 +90,15 @@ class DataParallel:
             return
         g = self.store.grad
         if self.mode == "replicate":
-            for s in range(0, g.numel(), self.bucket_elems):
-                dist.all_reduce(g[s:s + self.bucket_elems], op=dist.ReduceOp.AVG, group=self.group)
+            for b, e in self._dense_ranges(g.numel()):
+                for s in range(b, e, self.bucket_elems):
+                    dist.all_reduce(g[s:min(e, s + self.bucket_elems)], op=dist.ReduceOp.AVG,
+                                    group=self.group)
+            if self.expert_span is not None:
+                xb, xe = self.expert_span
+                if self.expert_group is not None and get_world_size(self.expert_group) > 1:
+                    dist.all_reduce(g[xb:xe], group=self.expert_group)
+                g[xb:xe].mul_(1.0 / self.world)
             return
         gp = self._padded(g, "_grad_pad")
         out = gp[self.rank * self.per:(self.rank + 1) * self.per]
@@ -83,6 +106,12 @@ class DataParallel:
         if gp.data_ptr() != g.data_ptr():
             b, e = self.shard
             g[b:e].copy_(gp[b:e])
+
+    def _dense_ranges(self, n: int):
+        if self.expert_span is None:
+            return [(0, n)]
+        xb, xe = self.expert_span
+        return [(0, xb), (xe, n)]
 
     def norm_sq_reduce(self, sq: torch.Tensor) -> torch.Tensor:
         """Sum a per-rank squared norm (shard mode) over the group."""
@@ -124,5 +153,17 @@ class DataParallel:
         """Make every rank start from rank ``src``'s weights."""
         if self.world == 1:
             return
-        dist.broadcast(self.store.master, src=src, group=self.group)
+        m = self.store.master
+        if self.expert_span is None:
+            dist.broadcast(m, src=_src(self.group), group=self.group)
+        else:
+            for b, e in self._dense_ranges(m.numel()):
+                t = m[b:e].clone()
+                dist.broadcast(t, src=_src(self.group), group=self.group)
+                m[b:e].copy_(t)
+            if self.expert_group is not None and get_world_size(self.expert_group) > 1:
+                xb, xe = self.expert_span
+                t = m[xb:xe].clone()
+                dist.broadcast(t, src=_src(self.expert_group), group=self.expert_group)
+                m[xb:xe].copy_(t)
         self.store.refresh_compute()

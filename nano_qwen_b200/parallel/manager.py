@@ -1,0 +1,162 @@
+"""N-D parallelism orchestrator.
+
+``ParallelConfig`` keeps the reference's fields (reference:
+distributed/parallel.py:26-35).  ``ParallelismManager`` lays ranks out on a
+(pp, dp, cp, tp) grid, tp fastest (tensor-parallel ranks share an NVSwitch
+domain and exchange the most bytes), and creates one process group per axis;
+expert-parallel groups are carved out of the data-parallel axis in contiguous
+blocks of ``ep_size``.  ``apply_parallelism`` applies TP(+SP) -> EP -> CP -> PP
+and returns the model; data parallelism / FSDP-style sharding is applied by the
+training engine on the flat parameter store (``parallel.data_parallel``).
+
+Differences from the reference: every axis is functional (its TP crashed on a
+head-count view, EP exchanged only counts, PP/CP were never used; SURVEY of
+distributed/*), the world-size check includes ep and cp, and SFT/GRPO/DPO take
+the same config as pretraining.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from .comm import get_rank, get_world_size, init_distributed, is_dist
+
+
+@dataclass
+class ParallelConfig:
+    dp_size: int = -1
+    tp_size: int = 1
+    pp_size: int = 1
+    ep_size: int = 1
+    cp_size: int = 1
+    fsdp_enabled: bool = True
+    dtype: str = "bfloat16"
+    reshard_after_forward: bool = True
+    sequence_parallel: bool = True
+    pp_microbatches: int = 4
+
+
+def grid_coords(rank: int, tp: int, cp: int, dp: int, pp: int) -> Dict[str, int]:
+    return {"tp": rank % tp, "cp": (rank // tp) % cp, "dp": (rank // (tp * cp)) % dp,
+            "pp": rank // (tp * cp * dp)}
+
+
+def axis_groups(world: int, tp: int, cp: int, dp: int, pp: int, axis: str) -> List[List[int]]:
+    """All rank lists that vary only along ``axis``."""
+    seen, out = set(), []
+    for r in range(world):
+        c = grid_coords(r, tp, cp, dp, pp)
+        key = tuple(v for k, v in c.items() if k != axis)
+        if key in seen:
+            continue
+        seen.add(key)
+        ranks = [q for q in range(world)
+                 if tuple(v for k, v in grid_coords(q, tp, cp, dp, pp).items() if k != axis) == key]
+        out.append(sorted(ranks, key=lambda q: grid_coords(q, tp, cp, dp, pp)[axis]))
+    return out
+
+
+class ParallelismManager:
+    def __init__(self, config: ParallelConfig):
+        self.config = config
+        self.rank, self.world_size = init_distributed()
+        c = config
+        if c.dp_size <= 0:
+            c.dp_size = max(1, self.world_size // (c.tp_size * c.pp_size * c.cp_size))
+        total = c.dp_size * c.tp_size * c.pp_size * c.cp_size
+        if total != self.world_size:
+            raise ValueError(f"dp({c.dp_size})*tp({c.tp_size})*pp({c.pp_size})*cp({c.cp_size})="
+                             f"{total} != world_size({self.world_size})")
+        if c.dp_size % c.ep_size != 0:
+            raise ValueError(f"ep_size ({c.ep_size}) must divide dp_size ({c.dp_size})")
+        self.coords = grid_coords(self.rank, c.tp_size, c.cp_size, c.dp_size, c.pp_size)
+        self.groups: Dict[str, Optional[dist.ProcessGroup]] = {}
+        self.ranks: Dict[str, List[int]] = {}
+        for axis, size in (("tp", c.tp_size), ("cp", c.cp_size), ("dp", c.dp_size), ("pp", c.pp_size)):
+            self._make_axis(axis, size)
+        self._make_dp_cp()
+        self._make_ep()
+        self.mesh = None
+
+    def _make_axis(self, axis: str, size: int) -> None:
+        c = self.config
+        mine = [self.rank]
+        grp = None
+        for ranks in axis_groups(self.world_size, c.tp_size, c.cp_size, c.dp_size, c.pp_size, axis):
+            g = dist.new_group(ranks) if (is_dist() and size > 1) else None
+            if self.rank in ranks:
+                mine, grp = ranks, g
+        self.ranks[axis] = mine
+        self.groups[axis] = grp
+
+    def _make_dp_cp(self) -> None:
+        """Gradient-averaging group: ranks that differ only in dp and cp."""
+        c = self.config
+        if c.cp_size == 1:
+            self.groups["dp_cp"], self.ranks["dp_cp"] = self.groups["dp"], self.ranks["dp"]
+            return
+        seen = {}
+        for r in range(self.world_size):
+            co = grid_coords(r, c.tp_size, c.cp_size, c.dp_size, c.pp_size)
+            seen.setdefault((co["tp"], co["pp"]), []).append(r)
+        self.groups["dp_cp"], self.ranks["dp_cp"] = None, [self.rank]
+        for key in sorted(seen):
+            ranks = seen[key]
+            g = dist.new_group(ranks) if is_dist() else None
+            if self.rank in ranks:
+                self.groups["dp_cp"], self.ranks["dp_cp"] = g, ranks
+
+    def _make_ep(self) -> None:
+        """EP blocks of ``ep_size`` consecutive dp ranks, and the
+        expert-data-parallel groups (same position in every block)."""
+        c = self.config
+        dp_ranks = axis_groups(self.world_size, c.tp_size, c.cp_size, c.dp_size, c.pp_size, "dp")
+        self.groups["ep"] = None
+        self.ranks["ep"] = [self.rank]
+        self.groups["edp"] = None
+        self.ranks["edp"] = [self.rank]
+        for ranks in dp_ranks:
+            for s in range(0, len(ranks), c.ep_size):
+                blk = ranks[s:s + c.ep_size]
+                g = dist.new_group(blk) if (is_dist() and c.ep_size > 1) else None
+                if self.rank in blk:
+                    self.ranks["ep"], self.groups["ep"] = blk, g
+        if c.ep_size == 1:
+            return
+        for ranks in dp_ranks:
+            for j in range(c.ep_size):
+                same = ranks[j::c.ep_size]
+                g = dist.new_group(same) if (is_dist() and len(same) > 1) else None
+                if self.rank in same:
+                    self.ranks["edp"], self.groups["edp"] = same, g
+
+    # --------------------------------------------------------------- apply
+    def apply_parallelism(self, model: nn.Module) -> nn.Module:
+        c = self.config
+        if c.tp_size > 1:
+            from .tensor_parallel import apply_tensor_parallel
+            apply_tensor_parallel(model, self.groups["tp"], sequence_parallel=c.sequence_parallel)
+        if c.ep_size > 1:
+            from .expert_parallel import apply_expert_parallel
+            apply_expert_parallel(model, self.groups["ep"])
+        if c.cp_size > 1:
+            from .context_parallel import apply_context_parallel
+            apply_context_parallel(model, self.groups["cp"], self.ranks["cp"])
+        if c.pp_size > 1:
+            from .pipeline_parallel import apply_pipeline_parallel
+            model = apply_pipeline_parallel(model, self.groups["pp"], self.ranks["pp"],
+                                            c.pp_microbatches)
+        return model
+
+    @property
+    def dp_group(self):
+        return self.groups.get("dp")
+
+    @property
+    def tp_group(self):
+        return self.groups.get("tp")

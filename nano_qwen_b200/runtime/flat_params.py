@@ -71,6 +71,12 @@ class FlatParamStore:
             groups = [g for g in groups if all(p.requires_grad for _, p in g)]
         decay = [g for g in groups if not no_decay_rule(g[0][0], g[0][1])]
         nodecay = [g for g in groups if no_decay_rule(g[0][0], g[0][1])]
+        # Expert-parallel-local parameters (different experts on every EP rank)
+        # form one contiguous span at the end of the decay region, so data
+        # parallelism can reduce them over their own group.
+        dense_decay = [g for g in decay if not getattr(g[0][1], "_ep_local", False)]
+        expert_decay = [g for g in decay if getattr(g[0][1], "_ep_local", False)]
+        decay = dense_decay + expert_decay
         ordered = decay + nodecay
         dev = device or next(model.parameters()).device
         self.device = dev
@@ -81,9 +87,14 @@ class FlatParamStore:
         self.decay_begin = 0
         self.decay_end = 0
         self.group_spans: List[Tuple[int, int]] = []
+        self.expert_span = (0, 0)
         for gi, grp in enumerate(ordered):
             off = (off + ALIGN - 1) // ALIGN * ALIGN
+            if gi == len(dense_decay) and expert_decay:
+                self.expert_span = (off, 0)
             if gi == len(decay):
+                if expert_decay:
+                    self.expert_span = (self.expert_span[0], off)
                 self.decay_end = off
             g0 = off
             for n, p in grp:
@@ -94,6 +105,8 @@ class FlatParamStore:
             self.group_spans.append((g0, off))
         if len(decay) == len(ordered):
             self.decay_end = off
+            if expert_decay:
+                self.expert_span = (self.expert_span[0], off)
         # Padding to a multiple of (ALIGN * data-parallel world) lets reduce-scatter and
         # all-gather run on equal-size shards of the buffers themselves.
         pad = max(ALIGN, int(pad_multiple))

@@ -23,19 +23,33 @@ from .scheduler import build_scheduler
 
 
 class TrainEngine:
+    """``parallel``: an optional ``ParallelismManager`` whose model has already
+    been through ``apply_parallelism``; its groups then drive the gradient
+    reductions (data parallel over dp x cp, replicated-parameter sums over TP,
+    expert spans over the expert-data-parallel group, norms over PP)."""
+
     def __init__(self, model: nn.Module, training_config: dict, device: torch.device,
-                 dp_mode: Optional[str] = None, dp_group=None):
+                 dp_mode: Optional[str] = None, dp_group=None, parallel=None):
         self.model = model.to(device)
         self.device = device
         self.cfg = training_config
+        self.parallel = parallel
+        self.tp_group = self.pp_group = expert_group = None
+        if parallel is not None:
+            dp_group = parallel.groups.get("dp_cp") or parallel.groups.get("dp")
+            self.tp_group = parallel.groups.get("tp")
+            self.pp_group = parallel.groups.get("pp")
+            expert_group = parallel.groups.get("edp")
         world = get_world_size(dp_group)
         dist_cfg = training_config.get("distributed", {}) or {}
         if dp_mode is None:
             dp_mode = "shard" if dist_cfg.get("fsdp_enabled", True) else "replicate"
         self.store = attach_param_store(self.model, pad_multiple=ALIGN * max(1, world))
-        self.dp = DataParallel(self.store, mode=dp_mode, group=dp_group) if world > 1 else None
+        self.dp = (DataParallel(self.store, mode=dp_mode, group=dp_group, expert_group=expert_group)
+                   if world > 1 else None)
         if self.dp is not None:
             self.dp.broadcast_params(0)
+        self._dups = self._duplicated_params()
         opt = training_config.get("optimizer", {}) or {}
         self.optimizer = build_optimizer(
             self.model, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),
@@ -65,25 +79,66 @@ class TrainEngine:
         n = len(micro_batches)
         loss_sum = torch.zeros((), dtype=torch.float32, device=self.device)
         aux_sum = None
-        for mb in micro_batches:
-            if loss_fn is not None:
-                loss = loss_fn(self.model, mb) / n
-                loss.backward()
-                l, a = loss.detach(), None
-            else:
-                l, a = self.forward_backward(mb, 1.0 / n)
-            loss_sum += l.float()
-            if a is not None:
-                aux_sum = a.float() if aux_sum is None else aux_sum + a.float()
+        if hasattr(self.model, "pipeline_forward_backward") and loss_fn is None:
+            loss_sum, aux_sum = self.model.pipeline_forward_backward(micro_batches)
+        else:
+            for mb in micro_batches:
+                if loss_fn is not None:
+                    loss = loss_fn(self.model, mb) / n
+                    loss.backward()
+                    l, a = loss.detach(), None
+                else:
+                    l, a = self.forward_backward(mb, 1.0 / n)
+                loss_sum += l.float()
+                if a is not None:
+                    aux_sum = a.float() if aux_sum is None else aux_sum + a.float()
+        if self.tp_group is not None:
+            from ..parallel.tensor_parallel import sync_replicated_grads
+            sync_replicated_grads(self.model, self.tp_group)
         if self.dp is not None:
             self.dp.sync_grads()
-        reduce = self.dp.norm_sq_reduce if self.dp is not None else None
-        gnorm = self.optimizer.clip_grad_norm_(self.grad_clip, reduce)
+        gnorm = self.optimizer.clip_grad_norm_(self.grad_clip, self._norm_sq_reduce)
         self.optimizer.step()
         if self.dp is not None:
             self.dp.gather_params()
         self.scheduler.step()
         return {"loss": loss_sum, "grad_norm": gnorm, "aux_loss": aux_sum}
+
+    # ------------------------------------------------------- grad norm
+    def _duplicated_params(self):
+        """Parameters whose gradient also exists on another model-parallel rank
+        and must count once in the global norm: replicated parameters on TP
+        ranks other than 0, the tied lm_head copy on the last PP stage."""
+        import torch.distributed as dist
+        dups = []
+        if self.tp_group is not None and dist.get_world_size(self.tp_group) > 1 \
+                and dist.get_rank(self.tp_group) != 0:
+            dups += [p for p in self.model.parameters() if not getattr(p, "_tp_sharded", False)]
+        if hasattr(self.model, "duplicated_params"):
+            dups += list(self.model.duplicated_params())
+        seen, out = set(), []
+        for p in dups:
+            if id(p) not in seen and id(p) in self.store.offsets:
+                seen.add(id(p))
+                out.append(p)
+        return out
+
+    def _norm_sq_reduce(self, sq: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+        if self._dups:
+            b, e = self.optimizer.shard
+            for p in self._dups:
+                o = self.store.offsets[id(p)]
+                lo, hi = max(b, o), min(e, o + p.numel())
+                if hi > lo:
+                    sq = sq - self.store.grad[lo:hi].double().pow(2).sum().float()
+        if self.dp is not None:
+            sq = self.dp.norm_sq_reduce(sq)
+        for g in (self.tp_group, self.pp_group):
+            if g is not None and dist.get_world_size(g) > 1:
+                sq = sq.clone()
+                dist.all_reduce(sq, group=g)
+        return sq
 
     def state_for_save(self):
         if self.dp is not None:
