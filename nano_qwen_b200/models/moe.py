@@ -31,16 +31,14 @@ class TopKRouter(nn.Module):
         self.norm_topk_prob = config.norm_topk_prob
         self.aux_loss_coef = config.router_aux_loss_coef
         self.gate = Linear(config.hidden_size, config.num_experts, bias=False)
-        # < 1 under tensor parallelism: every TP rank routes the same tokens, so
-        # each contributes 1/tp of the router's gradient (summed over TP later).
+        # < 1 under tensor parallelism: every TP rank computes the same aux loss
+        # from the same tokens, so each back-propagates 1/tp of it (the router
+        # gradients are summed over TP afterwards).
         self.grad_scale = 1.0
 
     def forward(self, hidden_states: torch.Tensor):
         """Returns (weights fp32 [N,k], indices int32 [N,k], counts [E], prob_sum [E])."""
         logits = fused_linear(hidden_states, [self.gate], hidden_states.dtype)
-        if self.grad_scale != 1.0:
-            from ..parallel.tensor_parallel import scale_grad
-            logits = scale_grad(logits, self.grad_scale)
         return ops.route(logits, self.top_k, self.norm_topk_prob)
 
 
@@ -111,6 +109,9 @@ class MoELayer(nn.Module):
             gcounts, gtokens = self.global_stats_fn(counts, N)
         aux = ops.aux_loss_from_stats(counts, prob_sum, N, self.top_k, self.num_experts,
                                       gcounts, gtokens)
+        if self.router.grad_scale != 1.0:
+            from ..parallel.tensor_parallel import scale_grad
+            aux = scale_grad(aux, self.router.grad_scale)
         if self.ep is not None:
             out = self.ep(self, x, weights, idx)
         else:

@@ -141,3 +141,44 @@ def max_over_ranks(value: float, device=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+# ------------------------------------------------------------------------------
+# Flat-buffer collectives used by data parallelism.  NCCL runs them natively;
+# Gloo (the CPU test backend) has no AVG op, no reduce-scatter and no
+# all-gather into one tensor, so they are emulated there.
+def _nccl(group) -> bool:
+    return dist.get_backend(group) == "nccl"
+
+
+def all_reduce_avg_(t: torch.Tensor, group=None) -> torch.Tensor:
+    if _nccl(group):
+        dist.all_reduce(t, op=dist.ReduceOp.AVG, group=group)
+    else:
+        dist.all_reduce(t, group=group)
+        t.div_(dist.get_world_size(group))
+    return t
+
+
+def reduce_scatter_avg_(out: torch.Tensor, inp: torch.Tensor, group=None) -> torch.Tensor:
+    """out = mean over ranks of inp's chunk for this rank (out may alias inp)."""
+    if _nccl(group):
+        dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.AVG, group=group)
+        return out
+    ws, r = dist.get_world_size(group), dist.get_rank(group)
+    tmp = inp.clone()
+    dist.all_reduce(tmp, group=group)
+    n = out.numel()
+    out.copy_(tmp[r * n:(r + 1) * n].view_as(out) / ws)
+    return out
+
+
+def all_gather_flat_(out: torch.Tensor, inp: torch.Tensor, group=None) -> torch.Tensor:
+    """out = concatenation over ranks of inp."""
+    if _nccl(group):
+        dist.all_gather_into_tensor(out, inp, group=group)
+        return out
+    parts = [torch.empty_like(inp) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, inp.contiguous(), group=group)
+    out.copy_(torch.cat(parts).view_as(out))
+    return out

@@ -26,7 +26,8 @@ import torch
 import torch.distributed as dist
 
 from ..runtime.flat_params import ALIGN, FlatParamStore
-from .comm import get_rank, get_world_size, is_dist
+from .comm import (all_gather_flat_, all_reduce_avg_, get_rank, get_world_size, is_dist,
+                   reduce_scatter_avg_)
 
 
 def shard_bounds(numel: int, world: int, rank: int) -> Tuple[int, int]:
@@ -92,8 +93,7 @@ class DataParallel:
         if self.mode == "replicate":
             for b, e in self._dense_ranges(g.numel()):
                 for s in range(b, e, self.bucket_elems):
-                    dist.all_reduce(g[s:min(e, s + self.bucket_elems)], op=dist.ReduceOp.AVG,
-                                    group=self.group)
+                    all_reduce_avg_(g[s:min(e, s + self.bucket_elems)], self.group)
             if self.expert_span is not None:
                 xb, xe = self.expert_span
                 if self.expert_group is not None and get_world_size(self.expert_group) > 1:
@@ -102,7 +102,7 @@ class DataParallel:
             return
         gp = self._padded(g, "_grad_pad")
         out = gp[self.rank * self.per:(self.rank + 1) * self.per]
-        dist.reduce_scatter_tensor(out, gp, op=dist.ReduceOp.AVG, group=self.group)
+        reduce_scatter_avg_(out, gp, self.group)
         if gp.data_ptr() != g.data_ptr():
             b, e = self.shard
             g[b:e].copy_(gp[b:e])
@@ -133,7 +133,7 @@ class DataParallel:
         if bp.data_ptr() != buf.data_ptr():
             b, e = self.shard
             mine[: e - b].copy_(buf[b:e])
-        dist.all_gather_into_tensor(bp, mine.clone(), group=self.group)
+        all_gather_flat_(bp, mine.clone(), self.group)
         if bp.data_ptr() != buf.data_ptr():
             buf.copy_(bp[: buf.numel()])
 
@@ -144,7 +144,7 @@ class DataParallel:
         m = self.store.master
         mp = self._padded(m, "_master_pad")
         mine = mp[self.rank * self.per:(self.rank + 1) * self.per].clone()
-        dist.all_gather_into_tensor(mp, mine, group=self.group)
+        all_gather_flat_(mp, mine, self.group)
         if mp.data_ptr() != m.data_ptr():
             m.copy_(mp[: m.numel()])
 

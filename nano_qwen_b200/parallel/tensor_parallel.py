@@ -232,8 +232,9 @@ def _mark_replicated(lm: nn.Module, sp: bool) -> None:
     """Tag every replicated parameter with how its gradient combines over TP.
 
     ``sum``: each rank holds a partial gradient -- q/k-norm weights (local
-    heads only), routers (their gradient is scaled by 1/tp in the MoE layer,
-    whose tokens are the same on every rank), and under sequence parallelism
+    heads only), routers (the combine weights see only the rank's partial
+    expert outputs, and the aux loss, identical on every rank, is
+    back-propagated at 1/tp by the MoE layer), and under sequence parallelism
     everything that runs on the rank's sequence slice (norms, lm_head, the
     embedding, which is looked up for the local slice only).  ``none``: the
     gradient is already identical on every rank (without sequence parallelism

@@ -1,0 +1,249 @@
+"""Worker functions for the multi-rank CPU tests (Gloo, spawned processes).
+
+Every worker builds the same tiny model from the same seed, computes a
+single-process oracle locally (the full model on the full batch), runs the
+parallel variant and asserts agreement; an assertion error in any rank fails
+the spawning test.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+
+
+def init(rank: int, world: int, port: int) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["RANK"] = str(rank)
+    os.environ["WORLD_SIZE"] = str(world)
+    os.environ["LOCAL_RANK"] = str(rank)
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+
+
+def tiny_cfg(moe: bool = False, **kw):
+    from nano_qwen_b200.config import ModelConfig
+    base = dict(hidden_size=32, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                head_dim=8, intermediate_size=64, vocab_size=97, max_position_embeddings=64,
+                tie_word_embeddings=False, rope_theta=1e4)
+    if moe:
+        base.update(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=16)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+def build(cfg, seed: int = 0):
+    from nano_qwen_b200.models import Qwen3Model
+    torch.manual_seed(seed)
+    m = Qwen3Model(cfg)
+    with torch.no_grad():  # larger than the default init so the test sees real gradients
+        for n, p in m.named_parameters():
+            if p.ndim >= 2:
+                p.normal_(0.0, 0.2)
+    return m
+
+
+def batch(cfg, B: int, S: int, seed: int = 1):
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g)
+    return ids
+
+
+def close(a, b, tol=2e-4, what=""):
+    a, b = a.detach().float(), b.detach().float()
+    err = ((a - b).norm() / (b.norm() + 1e-8)).item()
+    assert err < tol, f"{what}: rel err {err:.3e}"
+
+
+def _full_grads(cfg, ids, moe_scale=False):
+    ref = build(cfg)
+    out = ref(ids, labels=ids)
+    out["loss"].backward()
+    return ref, out["loss"].detach(), {n: p.grad.clone() for n, p in ref.named_parameters()}
+
+
+# ------------------------------------------------------------------ TP (+SP)
+def tp_worker(rank, world, port, sp, moe):
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.tensor_parallel import apply_tensor_parallel, sync_replicated_grads
+    cfg = tiny_cfg(moe)
+    ids = batch(cfg, 2, 16)
+    ref, ref_loss, ref_g = _full_grads(cfg, ids)
+    m = build(cfg)
+    grp = dist.new_group(list(range(world)))
+    apply_tensor_parallel(m, grp, sequence_parallel=sp)
+    out = m(ids, labels=ids)
+    out["loss"].backward()
+    sync_replicated_grads(m, grp)
+    close(out["loss"], ref_loss, 1e-5, "loss")
+    for n, p in m.named_parameters():
+        g = ref_g[n]
+        if getattr(p, "_tp_sharded", False):
+            if p.shape[0] != g.shape[0]:  # row shard (column-parallel)
+                k = p.shape[0]
+                g = g[rank * k:(rank + 1) * k]
+            else:                         # column shard (row-parallel)
+                k = p.shape[1]
+                g = g[:, rank * k:(rank + 1) * k]
+        close(p.grad, g, 2e-4, n)
+    dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ DP
+def dp_worker(rank, world, port, mode):
+    init(rank, world, port)
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg()
+    ids = batch(cfg, 2 * world, 16)
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"))
+    full = [{"input_ids": ids[i:i + 2], "labels": ids[i:i + 2]} for i in range(0, 2 * world, 2)]
+    for _ in range(2):
+        r_out = ref.train_step(full)
+    eng = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_mode=mode)
+    mine = [{"input_ids": ids[2 * rank:2 * rank + 2], "labels": ids[2 * rank:2 * rank + 2]}]
+    for _ in range(2):
+        o = eng.train_step(mine)
+    eng.state_for_save()
+    close(o["grad_norm"], r_out["grad_norm"], 1e-4, "grad norm")
+    for (n, p), (_, q) in zip(eng.model.named_parameters(), ref.model.named_parameters()):
+        close(p, q, 1e-5, n)
+    dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ EP
+def ep_worker(rank, world, port):
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.data_parallel import DataParallel
+    from nano_qwen_b200.parallel.expert_parallel import apply_expert_parallel
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    cfg = tiny_cfg(moe=True)
+    ids = batch(cfg, 2 * world, 16)
+    # oracle: mean of the per-rank losses = loss over all micro-batches
+    ref = build(cfg)
+    ref_losses = []
+    for r in range(world):
+        o = ref(ids[2 * r:2 * r + 2], labels=ids[2 * r:2 * r + 2])
+        (o["loss"] / world).backward()
+        ref_losses.append(o["loss"].detach())
+    ref_g = {n: p.grad.clone() for n, p in ref.named_parameters()}
+    m = build(cfg)
+    grp = dist.new_group(list(range(world)))
+    apply_expert_parallel(m, grp)
+    store = attach_param_store(m, torch.float32, torch.device("cpu"))
+    dp = DataParallel(store, mode="replicate", group=grp, expert_group=None)
+    out = m(ids[2 * rank:2 * rank + 2], labels=ids[2 * rank:2 * rank + 2])
+    out["loss"].backward()
+    close(out["loss"], ref_losses[rank], 1e-5, "loss")
+    dp.sync_grads()
+    e_loc = cfg.num_experts // world
+    for n, p in m.named_parameters():
+        rn = n
+        if ".experts." in n:
+            pre, rest = n.split(".experts.", 1)
+            e, tail = rest.split(".", 1)
+            rn = f"{pre}.experts.{int(e) + rank * e_loc}.{tail}"
+        close(p.grad, ref_g[rn], 2e-4, n)
+    dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ CP
+def cp_worker(rank, world, port, moe):
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.context_parallel import apply_context_parallel
+    from nano_qwen_b200.parallel.data_parallel import DataParallel
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    # aux-loss statistics are per rank under CP, so the exact comparison runs with coef 0
+    cfg = tiny_cfg(moe, router_aux_loss_coef=0.0)
+    ids = batch(cfg, 2, 8 * world)
+    ref, ref_loss, ref_g = _full_grads(cfg, ids)
+    m = build(cfg)
+    grp = dist.new_group(list(range(world)))
+    apply_context_parallel(m, grp)
+    store = attach_param_store(m, torch.float32, torch.device("cpu"))
+    dp = DataParallel(store, mode="replicate", group=grp)
+    out = m(ids, labels=ids)
+    out["loss"].backward()
+    dp.sync_grads()
+    close(out["loss"], ref_loss, 1e-5, "loss")
+    for n, p in m.named_parameters():
+        close(p.grad, ref_g[n], 2e-4, n)
+    logits = m(ids)["logits"]
+    close(logits, ref(ids)["logits"], 1e-5, "logits")
+    dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ PP
+def pp_worker(rank, world, port, tied, micro):
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.pipeline_parallel import apply_pipeline_parallel
+    cfg = tiny_cfg(tie_word_embeddings=tied, num_hidden_layers=4)
+    ids = batch(cfg, 4, 16)
+    ref = build(cfg)
+    loss_ref = 0.0
+    for c in ids.chunk(micro):
+        o = ref(c, labels=c)
+        (o["loss"] / micro).backward()
+        loss_ref += o["loss"].item() / micro
+    ref_g = {n: p.grad.clone() for n, p in ref.named_parameters()}
+    m = build(cfg)
+    grp = dist.new_group(list(range(world)))
+    pm = apply_pipeline_parallel(m, grp, list(range(world)), n_microbatches=micro)
+    loss, _ = pm.pipeline_forward_backward([{"input_ids": ids, "labels": ids}])
+    assert abs(loss.item() - loss_ref) < 1e-5 * max(1.0, abs(loss_ref)), (loss.item(), loss_ref)
+    off = pm.stage_layers[rank][0]
+    for n, p in pm.model.named_parameters():
+        rn = n
+        if n.startswith("layers."):
+            i, tail = n[len("layers."):].split(".", 1)
+            rn = f"layers.{int(i) + off}.{tail}"
+        if tied and rn == "lm_head.weight":
+            rn = "embed.embed_tokens.weight"
+        close(p.grad, ref_g[rn], 2e-4, n)
+    dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ manager
+def manager_worker(rank, world, port, tp, cp, pp, ep):
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+    pm = ParallelismManager(ParallelConfig(tp_size=tp, cp_size=cp, pp_size=pp, ep_size=ep))
+    c = pm.coords
+    assert pm.ranks["tp"] == [r for r in range(world) if r // tp == rank // tp]
+    for axis in ("tp", "cp", "dp", "pp"):
+        assert rank in pm.ranks[axis]
+    assert len(pm.ranks["dp"]) == pm.config.dp_size
+    assert len(pm.ranks["ep"]) == ep
+    if ep > 1:
+        assert len(pm.ranks["edp"]) == pm.config.dp_size // ep
+    assert c["tp"] == rank % tp
+    dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ failure detection
+def heartbeat_worker(rank, world, port, dead_rank):
+    init(rank, world, port)
+    from nano_qwen_b200.utils.fault import HeartbeatMonitor, PeerFailure
+    store = dist.distributed_c10d._get_default_store()
+    mon = HeartbeatMonitor(store, rank, world, interval_s=0.1, timeout_s=1.0)
+    mon.beat()
+    if rank == dead_rank:
+        return  # leaves between steps without further heartbeats (no collective in flight)
+    import time
+    t0 = time.time()
+    failed = None
+    while time.time() - t0 < 10.0:
+        mon.beat()
+        try:
+            mon.check()
+        except PeerFailure as e:
+            failed = e
+            break
+        time.sleep(0.1)
+    assert failed is not None and dead_rank in failed.ranks, failed

@@ -1,0 +1,54 @@
+"""Multi-rank CPU tests (Gloo): every parallel axis against the
+single-process oracle; the workers live in ``dist_workers``."""
+
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+import dist_workers as W
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(fn, world, *args):
+    mp.spawn(fn, args=(world, _port()) + args, nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("sp", [True, False])
+@pytest.mark.parametrize("moe", [False, True])
+def test_tensor_parallel_matches_single(sp, moe):
+    _run(W.tp_worker, 2, sp, moe)
+
+
+@pytest.mark.parametrize("mode", ["replicate", "shard"])
+def test_data_parallel_matches_accumulation(mode):
+    _run(W.dp_worker, 2, mode)
+
+
+def test_expert_parallel_matches_single():
+    _run(W.ep_worker, 2)
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_context_parallel_matches_single(moe):
+    _run(W.cp_worker, 2, moe)
+
+
+@pytest.mark.parametrize("tied,micro", [(False, 2), (True, 4)])
+def test_pipeline_parallel_matches_accumulation(tied, micro):
+    _run(W.pp_worker, 2, tied, micro)
+
+
+def test_manager_grid_groups():
+    _run(W.manager_worker, 4, 2, 1, 1, 2)
+
+
+def test_heartbeat_detects_silent_rank():
+    _run(W.heartbeat_worker, 3, 1)
