@@ -187,3 +187,108 @@ torch::Tensor decode_attn(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, t
 }
 
 }  // namespace nq
+
+
+// ----------------------------------------------------------------------------
+// Allocation-free entry point (declared, with its contract, in
+// decode_noalloc.h).  Same kernels and split choice as decode_attn above; the
+// split-K partials go to a fixed file-scope device array instead of buffers
+// from PyTorch's allocator.
+#include <mutex>
+#include <cstdio>
+#include "decode_noalloc.h"
+
+namespace nq {
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = NQ_DECODE_NOALLOC_SCRATCH_BYTES / sizeof(float);
+// Host code sees this name only as a symbol handle; its device address comes
+// from cudaGetSymbolAddress below.
+static __device__ __align__(256) float g_decode_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+int noalloc_fail(char* err, int err_len, int code, const char* msg) {
+  if (err != nullptr && err_len > 0) std::snprintf(err, static_cast<size_t>(err_len), "%s", msg);
+  return code;
+}
+
+}  // namespace
+}  // namespace nq
+
+extern "C" int nq_decode_attn_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                      const int* cache_len, const int* q_start, void* out, int B,
+                                      int Sq, int Hq, int Hk, int D, int Smax, float scale,
+                                      cudaStream_t stream, char* err, int err_len) {
+  using namespace nq;
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || cache_len == nullptr ||
+      q_start == nullptr || out == nullptr)
+    return noalloc_fail(err, err_len, NQ_NOALLOC_BAD_ARG, "nq_decode_attn_noalloc: null pointer");
+  if (B <= 0 || Sq <= 0 || Hq <= 0 || Hk <= 0 || Smax <= 0 || Hq % Hk != 0)
+    return noalloc_fail(err, err_len, NQ_NOALLOC_BAD_ARG,
+                        "nq_decode_attn_noalloc: bad shape (B, Sq, Hq, Hk, Smax > 0; Hq % Hk == 0)");
+  if (D != 64 && D != 128)
+    return noalloc_fail(err, err_len, NQ_NOALLOC_BAD_ARG, "nq_decode_attn_noalloc: head_dim must be 64 or 128");
+  if ((Hq / Hk) * Sq > kDecMaxRows)
+    return noalloc_fail(err, err_len, NQ_NOALLOC_BAD_ARG,
+                        "nq_decode_attn_noalloc: (Hq/Hk)*Sq must be <= 32");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+    return noalloc_fail(err, err_len, NQ_NOALLOC_CUDA_ERROR, "nq_decode_attn_noalloc: cudaGetDevice failed");
+  const int want = std::max(1, (2 * num_sms() + B * Hk - 1) / (B * Hk));
+  const int splits = std::max(1, std::min(want, (Smax + 255) / 256));
+  const size_t rows = static_cast<size_t>(B) * Hq * Sq;
+  const size_t need = rows * splits * (static_cast<size_t>(D) + 2);
+  if (need > kNoAllocScratchFloats) {
+    char msg[256];
+    std::snprintf(msg, sizeof(msg),
+                  "nq_decode_attn_noalloc: needs %zu bytes of scratch, the library's fixed maximum is %zu bytes "
+                  "(reduce batch, heads, query rows or cache length)",
+                  need * sizeof(float), static_cast<size_t>(NQ_DECODE_NOALLOC_SCRATCH_BYTES));
+    return noalloc_fail(err, err_len, NQ_NOALLOC_TOO_LARGE, msg);
+  }
+  float* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      const cudaError_t rc = cudaGetSymbolAddress(&p, g_decode_scratch);
+      if (rc != cudaSuccess || p == nullptr) {
+        char msg[256];
+        std::snprintf(msg, sizeof(msg), "nq_decode_attn_noalloc: cudaGetSymbolAddress failed: %s",
+                      cudaGetErrorString(rc));
+        return noalloc_fail(err, err_len, NQ_NOALLOC_CUDA_ERROR, msg);
+      }
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    base = g_noalloc_ptr[dev];
+  }
+  float* po = base;
+  float* pm = po + rows * splits * D;
+  float* pl = pm + rows * splits;
+  const float sl2 = scale * 1.4426950408889634f;
+  const auto* qb = static_cast<const __nv_bfloat16*>(q);
+  const auto* kb = static_cast<const __nv_bfloat16*>(k_cache);
+  const auto* vb = static_cast<const __nv_bfloat16*>(v_cache);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+  if (D == 128) {
+    decode_partial_kernel<128><<<B * Hk * splits, kDecThreads, 0, stream>>>(
+        qb, kb, vb, cache_len, q_start, po, pm, pl, Sq, Hq, Hk, Smax, splits, sl2);
+    decode_combine_kernel<128><<<static_cast<int>(rows), 128, 0, stream>>>(po, pm, pl, ob, static_cast<int>(rows),
+                                                                        splits, Sq, Hq);
+  } else {
+    decode_partial_kernel<64><<<B * Hk * splits, kDecThreads, 0, stream>>>(
+        qb, kb, vb, cache_len, q_start, po, pm, pl, Sq, Hq, Hk, Smax, splits, sl2);
+    decode_combine_kernel<64><<<static_cast<int>(rows), 64, 0, stream>>>(po, pm, pl, ob, static_cast<int>(rows),
+                                                                      splits, Sq, Hq);
+  }
+  const cudaError_t rc = cudaGetLastError();
+  if (rc != cudaSuccess) {
+    char msg[256];
+    std::snprintf(msg, sizeof(msg), "nq_decode_attn_noalloc: launch failed: %s", cudaGetErrorString(rc));
+    return noalloc_fail(err, err_len, NQ_NOALLOC_CUDA_ERROR, msg);
+  }
+  return NQ_NOALLOC_OK;
+}
