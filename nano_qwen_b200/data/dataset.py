@@ -50,7 +50,7 @@ class PackedTextDataset(Dataset):
             try:
                 from ..runtime.native import TokenWindowReader
                 self._native = TokenWindowReader([str(f) for f in files],
-                                                 np.dtype(dtype).itemsize)
+                                                 np.dtype(dtype).itemsize, eos_id)
             except Exception:
                 self._native = None
 

@@ -149,7 +149,11 @@ class TextGenerator:
         self.model = model
         self.tokenizer = tokenizer
         self.device = device
-        self.max_len = max_len
+        # never past the RoPE table (positions >= max_position_embeddings have no angles)
+        cfg = getattr(model, "config", None)
+        mp = getattr(getattr(model, "language_model", model), "config", cfg)
+        limit = getattr(mp, "max_position_embeddings", None)
+        self.max_len = min(max_len, limit) if limit else max_len
         self.use_graph = use_graph
         self.model.eval()
 
@@ -222,6 +226,9 @@ class TextGenerator:
         mask [B, T] of tokens before and including the first EOS).
         """
         B, P = prompt_ids.shape
+        if P >= self.max_len:
+            raise ValueError(f"prompt length {P} leaves no room below the {self.max_len}-position limit")
+        max_new_tokens = min(max_new_tokens, self.max_len - P)
         st = DecodeState(self.model, B, min(self.max_len, P + max_new_tokens + 8), self.device,
                          self._dtype())
         logits = prefill(self.model, st, prompt_ids.to(self.device))

@@ -53,6 +53,21 @@ def compute_mfu(model_params: int, tokens_per_sec: float, num_gpus: int,
     return 6 * model_params * tokens_per_sec / peak if peak > 0 else 0.0
 
 
+def build_parallel(training_config: dict, world_size: int):
+    """A ``ParallelismManager`` when the ``distributed`` section asks for any
+    model-parallel axis (tp/pp/ep/cp > 1); plain data parallelism otherwise."""
+    d = training_config.get("distributed", {}) or {}
+    sizes = {k: int(d.get(k, 1) or 1) for k in ("tp_size", "pp_size", "ep_size", "cp_size")}
+    if world_size <= 1 or all(v == 1 for v in sizes.values()):
+        return None
+    from ..parallel.manager import ParallelConfig, ParallelismManager
+    pc = ParallelConfig(dp_size=int(d.get("dp_size", -1) or -1), **sizes,
+                        fsdp_enabled=bool(d.get("fsdp_enabled", True)),
+                        sequence_parallel=bool(d.get("sequence_parallel", True)),
+                        pp_microbatches=int(d.get("pp_microbatches", 4)))
+    return ParallelismManager(pc)
+
+
 class PreTrainer:
     def __init__(self, model_config: ModelConfig, training_config: dict, stage: int = 1):
         self.model_config = model_config
@@ -69,7 +84,13 @@ class PreTrainer:
         if is_main_process():
             c = model.count_parameters()
             print(f"Model parameters: {c['total']:,} total, {c['trainable']:,} trainable")
-        self.engine = TrainEngine(model, training_config, self.device)
+        self.parallel = build_parallel(training_config, self.world_size)
+        self.dp_rank, self.dp_size = self.rank, self.world_size
+        if self.parallel is not None:
+            model = self.parallel.apply_parallelism(model.to(self.device))
+            self.dp_rank = self.parallel.coords["dp"]
+            self.dp_size = self.parallel.config.dp_size
+        self.engine = TrainEngine(model, training_config, self.device, parallel=self.parallel)
         self.model = self.engine.model
         self.optimizer = self.engine.optimizer
         self.scheduler = self.engine.scheduler
@@ -103,7 +124,7 @@ class PreTrainer:
                     b = next(it)
                 mbs.append({k: v.to(self.device, non_blocking=True) for k, v in b.items()})
             seq_len = mbs[0]["input_ids"].shape[1]
-            ntok = sum(m["input_ids"].numel() for m in mbs) * self.world_size
+            ntok = sum(m["input_ids"].numel() for m in mbs) * self.dp_size
             if cuda:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
@@ -151,7 +172,8 @@ def run_pretraining(model_config_path: str, training_config_path: str,
     dataset = PackedTextDataset(data_dir=data_cfg.get("train_data", "data/train"),
                                 max_seq_len=batch_cfg.get("max_seq_len", 4096),
                                 vocab_size=model_config.vocab_size)
-    sampler = DistributedSampler(dataset, num_replicas=trainer.world_size, rank=trainer.rank)
+    # one data shard per data-parallel rank (TP/CP/PP ranks of a replica read the same batch)
+    sampler = DistributedSampler(dataset, num_replicas=trainer.dp_size, rank=trainer.dp_rank)
     loader = DataLoader(dataset, batch_size=batch_cfg.get("micro_batch_size", 4), sampler=sampler,
                         collate_fn=TextCollator(),
                         num_workers=data_cfg.get("num_workers", 4),

@@ -1,4 +1,5 @@
-"""Builds the in-tree sm_100a extension ``nano_qwen_b200._C``.
+"""Builds the in-tree extensions: ``nano_qwen_b200._C`` (sm_100a kernels) and
+``nano_qwen_b200._runtime`` (host-side C++ runtime).
 
     python setup.py build_ext --inplace
 
@@ -10,7 +11,7 @@ import glob
 import os
 
 from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 SOURCES = sorted(glob.glob(os.path.join("csrc", "*.cu"))) + [os.path.join("csrc", "bindings.cpp")]
@@ -41,7 +42,13 @@ setup(
             name="nano_qwen_b200._C",
             sources=SOURCES,
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
+        ),
+        # host-side runtime (no CUDA): native data-path helpers
+        CppExtension(
+            name="nano_qwen_b200._runtime",
+            sources=[os.path.join("csrc", "runtime", "token_reader.cpp")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"]},
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -1,0 +1,203 @@
+"""CPU tests of the model, config, optimizer, scheduler and checkpointing
+against the reference implementation (imported read-only from
+``baseline/_ref``) and against plain PyTorch."""
+
+import math
+import os
+import sys
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+HAS_REF = os.path.isdir(os.path.join(REF, "model"))
+
+
+def _ref_import():
+    if REF not in sys.path:
+        sys.path.append(REF)
+    from model.config import ModelConfig as RC
+    from model.transformer import Qwen3Model as RM
+    return RC, RM
+
+
+TINY = dict(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+            head_dim=16, intermediate_size=128, vocab_size=256, max_position_embeddings=128,
+            tie_word_embeddings=True)
+TINY_MOE = dict(TINY, num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32,
+                tie_word_embeddings=False)
+
+
+# ------------------------------------------------------------------ config
+def test_config_defaults_and_yaml():
+    from nano_qwen_b200.config import PRESETS, ModelConfig
+    c = ModelConfig()
+    assert c.head_dim == c.hidden_size // c.num_attention_heads
+    for name in ("debug", "small", "medium", "large"):
+        y = ModelConfig.from_yaml(os.path.join(ROOT, "configs", "model", f"{name}.yaml"))
+        assert y.hidden_size > 0 and y.num_hidden_layers > 0
+    assert "debug" in PRESETS
+    m = ModelConfig(**TINY_MOE)
+    assert m.layer_is_moe(0) and m.active_params_per_token() < m.total_params_estimate()
+
+
+@pytest.mark.skipif(not HAS_REF, reason="reference copy not present")
+@pytest.mark.parametrize("cfg", [TINY, TINY_MOE])
+def test_model_matches_reference(cfg):
+    RC, RM = _ref_import()
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    torch.manual_seed(0)
+    ref = RM(RC(**cfg))
+    ours = Qwen3Model(ModelConfig(**cfg))
+    ours.load_state_dict(ref.state_dict())
+    ids = torch.randint(0, cfg["vocab_size"], (2, 24))
+    a = ref(input_ids=ids, labels=ids)
+    b = ours(ids, labels=ids)
+    assert torch.allclose(a["loss"], b["loss"], atol=1e-5, rtol=1e-5)
+    a["loss"].backward()
+    b["loss"].backward()
+    rp = dict(ref.named_parameters())
+    for n, p in ours.named_parameters():
+        assert torch.allclose(p.grad, rp[n].grad, atol=1e-5, rtol=1e-4), n
+    la = ref(input_ids=ids)["logits"]
+    lb = ours(ids)["logits"]
+    assert torch.allclose(la, lb, atol=1e-5, rtol=1e-5)
+
+
+def test_kv_cache_decode_matches_full_forward():
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.models.kv_cache import KVCache
+    torch.manual_seed(0)
+    cfg = ModelConfig(**TINY)
+    m = Qwen3Model(cfg).eval()
+    ids = torch.randint(0, 256, (2, 12))
+    with torch.no_grad():
+        full = m(ids)["logits"]
+        caches = [KVCache() for _ in range(cfg.num_hidden_layers)]
+        a = m(ids[:, :8], kv_caches=caches)["logits"]
+        steps = [a]
+        for t in range(8, 12):
+            steps.append(m(ids[:, t:t + 1], kv_caches=caches)["logits"])
+    inc = torch.cat(steps, 1)
+    assert torch.allclose(inc, full, atol=1e-4, rtol=1e-4)
+
+
+def test_yarn_rope_tables():
+    from nano_qwen_b200.models.rope import rope_tables
+    cos, sin = rope_tables(64, 128, 1e6, {"type": "yarn", "factor": 4.0,
+                                         "original_max_position_embeddings": 32})
+    assert cos.shape == (128, 32) and torch.isfinite(cos).all() and torch.isfinite(sin).all()
+    c0, _ = rope_tables(64, 128, 1e6, None)
+    assert not torch.allclose(cos, c0)
+
+
+# ------------------------------------------------------------------ optimizer
+def test_fused_adamw_cpu_matches_torch():
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.optimizer import attach_param_store, build_optimizer
+    torch.manual_seed(0)
+    cfg = ModelConfig(**TINY)
+    a = Qwen3Model(cfg)
+    b = Qwen3Model(cfg)
+    b.load_state_dict(a.state_dict())
+    store = attach_param_store(a, torch.float32, torch.device("cpu"))
+    opt_a = build_optimizer(a, lr=1e-2, weight_decay=0.1, fused=True, store=store)
+    decay = [p for n, p in b.named_parameters()
+             if not (p.ndim <= 1 or "norm" in n or "bias" in n or "embed" in n)]
+    nodecay = [p for n, p in b.named_parameters()
+               if (p.ndim <= 1 or "norm" in n or "bias" in n or "embed" in n)]
+    opt_b = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1},
+                               {"params": nodecay, "weight_decay": 0.0}],
+                              lr=1e-2, betas=(0.9, 0.95), eps=1e-8)
+    ids = torch.randint(0, 256, (2, 16))
+    for _ in range(3):
+        store.zero_grad()
+        a(ids, labels=ids)["loss"].backward()
+        opt_a.clip_grad_norm_(0.0)
+        opt_a.step()
+        opt_b.zero_grad()
+        b(ids, labels=ids)["loss"].backward()
+        opt_b.step()
+    bp = dict(b.named_parameters())
+    for n, p in a.named_parameters():
+        assert torch.allclose(p, bp[n], atol=1e-5, rtol=1e-4), n
+
+
+def test_grad_clip_norm():
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.optimizer import attach_param_store, build_optimizer
+    torch.manual_seed(0)
+    m = Qwen3Model(ModelConfig(**TINY))
+    store = attach_param_store(m, torch.float32, torch.device("cpu"))
+    opt = build_optimizer(m, lr=1e-3, fused=True, store=store)
+    ids = torch.randint(0, 256, (2, 16))
+    m(ids, labels=ids)["loss"].backward()
+    ref = torch.sqrt(sum((p.grad.double() ** 2).sum() for p in m.parameters())).item()
+    n = opt.clip_grad_norm_(1e-3)
+    assert abs(float(n) - ref) < 1e-4 * ref
+    assert abs(float(opt.clip_scale) - 1e-3 / (ref + 1e-6)) < 1e-6
+
+
+@pytest.mark.skipif(not HAS_REF, reason="reference copy not present")
+@pytest.mark.parametrize("kind", ["cosine", "wsd"])
+def test_scheduler_matches_reference(kind):
+    if REF not in sys.path:
+        sys.path.append(REF)
+    from training.scheduler import build_scheduler as ref_build
+    from nano_qwen_b200.training.scheduler import build_scheduler
+    p1 = [torch.nn.Parameter(torch.zeros(1))]
+    p2 = [torch.nn.Parameter(torch.zeros(1))]
+    o1 = torch.optim.SGD(p1, lr=1.0)
+    o2 = torch.optim.SGD(p2, lr=1.0)
+    kw = dict(warmup_steps=10, total_steps=100)
+    if kind == "wsd":
+        kw["stable_steps"] = 60
+    s1 = ref_build(o1, scheduler_type=kind, **kw)
+    s2 = build_scheduler(o2, scheduler_type=kind, **kw)
+    for _ in range(100):
+        assert math.isclose(s1.get_last_lr()[0], s2.get_last_lr()[0], rel_tol=1e-6, abs_tol=1e-9)
+        o1.step(); o2.step(); s1.step(); s2.step()
+
+
+# ------------------------------------------------------------------ checkpoint
+def test_checkpoint_roundtrip_plain_and_dcp(tmp_path):
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    torch.manual_seed(0)
+    cfg = ModelConfig(**TINY)
+    tc = {"optimizer": {"lr": 1e-2}, "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    eng = TrainEngine(Qwen3Model(cfg), tc, torch.device("cpu"))
+    ids = torch.randint(0, 256, (2, 16))
+    eng.train_step([{"input_ids": ids, "labels": ids}])
+    mgr = CheckpointManager(save_dir=str(tmp_path), save_interval=1, async_save=False)
+    model, opt, sch = eng.state_for_save()
+    mgr.save(1, model, opt, sch, extra_state={"step": 1})
+    path = mgr.latest()
+    assert path is not None and os.path.exists(os.path.join(path, "meta.json"))
+    eng2 = TrainEngine(Qwen3Model(cfg), tc, torch.device("cpu"))
+    extra = mgr.load(eng2.model, eng2.optimizer, eng2.scheduler, path)
+    assert int(extra.get("step", 0)) == 1
+    for (n, p), (_, q) in zip(eng.model.named_parameters(), eng2.model.named_parameters()):
+        assert torch.equal(p, q), n
+    # the next step is identical after the reload
+    o1 = eng.train_step([{"input_ids": ids, "labels": ids}])
+    o2 = eng2.train_step([{"input_ids": ids, "labels": ids}])
+    assert torch.allclose(o1["loss"], o2["loss"])
+    for (n, p), (_, q) in zip(eng.model.named_parameters(), eng2.model.named_parameters()):
+        assert torch.allclose(p, q, atol=1e-7), n
+    out = str(tmp_path / "checkpoint.pt")
+    mgr.export_plain(out, eng.model, step=2)
+    from nano_qwen_b200.cli import load_model_for_eval
+    import yaml
+    yp = tmp_path / "m.yaml"
+    yp.write_text(yaml.safe_dump(TINY))
+    m3 = load_model_for_eval(str(yp), out)
+    for (n, p), (_, q) in zip(eng.model.named_parameters(), m3.named_parameters()):
+        assert torch.equal(p.detach(), q.detach()), n
