@@ -38,6 +38,10 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
+DP_LABEL = {"p2p": "ZeRO-2, fused peer-memory reduce-scatter + sharded AdamW + all-gather kernels",
+            "shard": "ZeRO-2 over NCCL reduce-scatter / all-gather",
+            "replicate": "NCCL all-reduce"}
+
 BASELINE_METRIC = "train tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; MFU"
 
 CONFIGS = {
@@ -54,6 +58,19 @@ CONFIGS = {
                        max_position_embeddings=2048, rope_theta=1e6, qk_norm=True,
                        tie_word_embeddings=True, num_experts=64, num_experts_per_tok=8,
                        moe_intermediate_size=256, router_aux_loss_coef=0.001), 8, 2048, "dp"),
+    # BASELINE config 2 with expert parallelism over all ranks (per-GPU batch 8 x 2048)
+    "debug-moe-ep": (dict(hidden_size=512, num_hidden_layers=8, num_attention_heads=8,
+                          num_key_value_heads=2, head_dim=64, intermediate_size=1408,
+                          vocab_size=32000, max_position_embeddings=2048, rope_theta=1e6,
+                          qk_norm=True, tie_word_embeddings=True, num_experts=64,
+                          num_experts_per_tok=8, moe_intermediate_size=256,
+                          router_aux_loss_coef=0.001), 8, 2048, "ep"),
+    # Qwen3-8B shape, tensor + sequence parallel over all ranks,
+    # global batch 8 x 8192 (the same tokens on every rank: strong scaling)
+    "qwen3-8b-tp": (dict(hidden_size=4096, num_hidden_layers=36, num_attention_heads=32,
+                         num_key_value_heads=8, head_dim=128, intermediate_size=12288,
+                         vocab_size=151936, max_position_embeddings=8192, rope_theta=1e6,
+                         qk_norm=True, tie_word_embeddings=False), 8, 8192, "tp"),
 }
 
 
@@ -66,6 +83,8 @@ def parse():
     p.add_argument("--config", default="qwen3-1.7b", choices=sorted(CONFIGS))
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate"],
+                   help="ours, N>1: peer-memory fused ZeRO step (p2p) or NCCL ZeRO-2 / all-reduce")
     return p.parse_args()
 
 
@@ -243,9 +262,17 @@ def run_ours(args, world, rank, local):
     tcfg = {"optimizer": {"lr": 3e-4, "weight_decay": 0.1, "grad_clip": 1.0},
             "scheduler": {"type": "cosine", "warmup_steps": 100, "total_steps": 100000},
             "distributed": {"fsdp_enabled": True}}
-    eng = TrainEngine(model, tcfg, dev)
+    pm = None
+    if par in ("tp", "ep") and world > 1:
+        from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+        pm = ParallelismManager(ParallelConfig(tp_size=world if par == "tp" else 1,
+                                               ep_size=world if par == "ep" else 1))
+        model = pm.apply_parallelism(model)
+    eng = TrainEngine(model, tcfg, dev, dp_mode=args.dp_mode if world > 1 else None, parallel=pm)
     del model
-    inputs = synthetic_batches(4, B, S, cfg.vocab_size, dev, seed=1234 + rank)
+    # tensor parallelism: every rank sees the same global batch
+    seed_rank = 0 if par == "tp" else rank
+    inputs = synthetic_batches(4, B, S, cfg.vocab_size, dev, seed=1234 + seed_rank)
 
     def step(ids):
         eng.train_step([{"input_ids": ids, "labels": ids}])
@@ -257,7 +284,13 @@ def run_ours(args, world, rank, local):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e_ours(eng, args, B, S, cfg.vocab_size, dev, rank)
-    return ms, clocks, {"kernel_error_flag": err, "gpu_launches_per_step": launches}, e2e
+    mode = None
+    if eng.dp is not None:
+        mode = "p2p" if hasattr(eng.dp, "fused_step") else eng.dp.mode
+    if par == "tp" and world > 1:
+        mode = "tp-fused" if getattr(eng.model, "tp_fused", False) else "tp-nccl"
+    return ms, clocks, {"kernel_error_flag": err, "gpu_launches_per_step": launches,
+                        "dp_mode": mode}, e2e
 
 
 def count_launches(step_fn, ids):
@@ -317,6 +350,10 @@ def run_reference(args, world, rank, local):
     from training.scheduler import build_scheduler
 
     mk, B, S, par = CONFIGS[args.config]
+    if par == "tp":
+        # substituted baseline (the reference's TP path does not run): FSDP2 over the
+        # same global batch, i.e. B / N sequences per rank
+        B = max(1, B // world)
     rk = dict(mk)
     torch.manual_seed(0)
     model = RM(RC(**rk))
@@ -367,6 +404,19 @@ def run_reference(args, world, rank, local):
     return ms, clocks, {}, e2e
 
 
+def parallel_label(par, world, impl, mode):
+    if world == 1:
+        return "dp1"
+    if impl == "reference":
+        return f"dp{world} (FSDP2{', substituted for the reference TP/EP paths, which do not run' if par != 'dp' else ''})"
+    if par == "tp":
+        return f"tp{world}+sp (" + ("all-gather / reduce-scatter fused into the norm and GEMM kernels over peer memory"
+                                    if mode == "tp-fused" else "NCCL collectives") + ")"
+    if par == "ep":
+        return f"ep{world} x dp{world} (NCCL all-to-all dispatch/combine)"
+    return f"dp{world} ({DP_LABEL.get(mode, '')})"
+
+
 # --------------------------------------------------------------------- main
 def main():
     args = parse()
@@ -386,7 +436,7 @@ def main():
         if rank == 0:
             print(json.dumps({"impl": args.impl, "unavailable": str(e)}))
         return 0
-    tokens_per_step = B * S * world
+    tokens_per_step = B * S * (1 if par == "tp" else world)
     value = tokens_per_step / (ms / 1e3)
     fpt = flops_per_token(mk, S)
     mfu = value * fpt / (measured_peak() * world)
@@ -399,15 +449,14 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if par == "tp" else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic uniform-random token ids, random-init weights",
         "config": {"model": f"{args.config} (Qwen3-1.7B shape: L28 h2048 16Q/8KV hd128 I6144 V151936 tied)"
                    if args.config == "qwen3-1.7b" else args.config,
-                   "global_batch": B * world, "seq_len": S,
-                   "parallelism": f"dp{world}" + (" (ZeRO-2 sharded AdamW)" if args.impl == "ours" and world > 1
-                                                  else (" (FSDP2)" if world > 1 else "")),
+                   "global_batch": B * (1 if par == "tp" else world), "seq_len": S,
+                   "parallelism": parallel_label(par, world, args.impl, extra.get("dp_mode")),
                    "l2": "no flush: per-step working set (weights + activations) >> 126 MB L2"},
         "mfu": round(mfu, 4),
         "flops_per_token": fpt,

@@ -124,8 +124,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int S = args.S;
   constexpr int CTA_M = ABM * kTilesPerCta;
   const int n_mblk = (S + CTA_M - 1) / CTA_M;
-  const int mb = n_mblk - 1 - (blockIdx.x % n_mblk);  // heaviest first
-  const int bh = blockIdx.x / n_mblk;
+  // Heaviness-major order: the first wave holds the longest causal tiles of
+  // every (batch, head), the lightest run last (longest-processing-time-first
+  // scheduling by the hardware block scheduler); adjacent blocks are adjacent
+  // heads, which share K/V under GQA.
+  const int n_bh = gridDim.x / n_mblk;
+  const int mb = n_mblk - 1 - static_cast<int>(blockIdx.x) / n_bh;
+  const int bh = static_cast<int>(blockIdx.x) % n_bh;
   const int b = bh / args.Hq;
   const int h = bh - b * args.Hq;
   const int hk = h / (args.Hq / args.Hk);

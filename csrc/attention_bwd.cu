@@ -120,8 +120,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   int* err = args.err;
   const int S = args.S;
   const int n_kblk = (S + BKN - 1) / BKN;
-  const int nb = blockIdx.x % n_kblk;  // causal: low key blocks carry the most work, start them first
-  const int bk = blockIdx.x / n_kblk;
+  // Heaviness-major order: under causality low key blocks carry the most
+  // work; all (batch, kv-head) pairs of the heaviest key block go first.
+  const int n_bk = gridDim.x / n_kblk;
+  const int nb = static_cast<int>(blockIdx.x) / n_bk;
+  const int bk = static_cast<int>(blockIdx.x) % n_bk;
   const int b = bk / args.Hk;
   const int hk = bk - b * args.Hk;
   const int G = args.Hq / args.Hk;

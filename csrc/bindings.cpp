@@ -64,6 +64,25 @@ torch::Tensor moe_gather(torch::Tensor, torch::Tensor);
 torch::Tensor moe_combine(torch::Tensor, torch::Tensor, torch::Tensor);
 std::vector<torch::Tensor> moe_combine_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor);
 torch::Tensor moe_scatter_add(torch::Tensor, torch::Tensor, int64_t);
+// tensor-parallel fused communication (gemm.cu, tp_comm.cu)
+torch::Tensor gemm_ag(torch::Tensor, torch::Tensor, bool, int64_t, int64_t, int64_t);
+int64_t gemm_rs(torch::Tensor, torch::Tensor, bool, std::vector<int64_t>, int64_t, torch::Tensor, int64_t,
+                std::vector<int64_t>, int64_t, int64_t);
+int64_t tp_norm_fwd(torch::Tensor, c10::optional<torch::Tensor>, c10::optional<torch::Tensor>, torch::Tensor,
+                    torch::Tensor, torch::Tensor, torch::Tensor, double, std::vector<int64_t>, torch::Tensor,
+                    std::vector<int64_t>, int64_t, int64_t, int64_t, int64_t, int64_t, torch::Tensor, int64_t);
+int64_t tp_norm_bwd(c10::optional<torch::Tensor>, c10::optional<torch::Tensor>, c10::optional<torch::Tensor>,
+                    torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+                    c10::optional<torch::Tensor>, std::vector<int64_t>, torch::Tensor, std::vector<int64_t>,
+                    int64_t, int64_t, int64_t, int64_t, int64_t, torch::Tensor, int64_t);
+// zero_comm.cu
+void zero_rs(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t, int64_t,
+             torch::Tensor, int64_t, int64_t);
+void zero_clip(torch::Tensor, double, torch::Tensor, torch::Tensor);
+void zero_adamw_ag(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor,
+                   torch::Tensor, torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, double, double,
+                   double, double, double, double, double, double);
+void zero_publish(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t);
 }  // namespace nq
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -112,4 +131,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &nq::moe_combine);
   m.def("moe_combine_bwd", &nq::moe_combine_bwd);
   m.def("moe_scatter_add", &nq::moe_scatter_add);
+  m.def("gemm_ag", &nq::gemm_ag, "GEMM whose A rows arrive from peers (waits on all-gather flags)");
+  m.def("gemm_rs", &nq::gemm_rs, "GEMM whose row tiles are stored into their owners' partial buffers");
+  m.def("tp_norm_fwd", &nq::tp_norm_fwd, "residual + sum of TP partials + RMSNorm, all-gathered to peers");
+  m.def("tp_norm_bwd", &nq::tp_norm_bwd, "RMSNorm backward with TP partial inputs and all-gathered output");
+  m.def("zero_rs", &nq::zero_rs, "peer-memory reduce-scatter of the mean gradient + squared norm");
+  m.def("zero_clip", &nq::zero_clip);
+  m.def("zero_adamw_ag", &nq::zero_adamw_ag, "sharded AdamW fused with the bf16 all-gather by P2P stores");
+  m.def("zero_publish", &nq::zero_publish);
 }

@@ -193,7 +193,17 @@ void axpy_(torch::Tensor y, torch::Tensor x, torch::Tensor a) {
 }
 
 // --------------------------------------------------------------- embedding
-__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ w,
+__device__ __forceinline__ float4 load4f(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 load4f(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// Row gather into the fp32 residual stream from an fp32 or bf16 table.
+template <typename TW>
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const TW* __restrict__ w,
                                      float* __restrict__ out, int64_t T, int H, int64_t V, int* err) {
   const int H4 = H / 4;
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < T * H4; v += (int64_t)gridDim.x * blockDim.x) {
@@ -201,7 +211,7 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const floa
     const int c = static_cast<int>(v - t * H4);
     int64_t id = ids[t];
     if (id < 0 || id >= V) { atomicCAS(err, 0, kErrBadArg); id = 0; }
-    reinterpret_cast<float4*>(out)[v] = reinterpret_cast<const float4*>(w + id * H)[c];
+    reinterpret_cast<float4*>(out)[v] = load4f(w + id * H + c * 4);
   }
 }
 
@@ -218,15 +228,23 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const floa
 }
 
 torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w) {
-  TORCH_CHECK(w.scalar_type() == torch::kFloat32 && w.is_contiguous() && w.size(1) % 4 == 0, "embedding weight fp32 [V,H%4]");
+  const bool bf = w.scalar_type() == torch::kBFloat16;
+  TORCH_CHECK((bf || w.scalar_type() == torch::kFloat32) && w.is_contiguous() && w.size(1) % 4 == 0,
+              "embedding weight fp32 or bf16 [V,H%4]");
   auto idc = ids.to(torch::kInt64).contiguous();
   const int64_t T = idc.numel();
   const int H = w.size(1);
   c10::cuda::CUDAGuard g(w.device());
-  auto out = torch::empty({T, H}, w.options());
+  auto out = torch::empty({T, H}, w.options().dtype(torch::kFloat32));
   if (T == 0) return out;
-  embedding_fwd_kernel<<<ew_grid(T * H / 4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      idc.data_ptr<int64_t>(), w.data_ptr<float>(), out.data_ptr<float>(), T, H, w.size(0), error_flag_ptr());
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (bf)
+    embedding_fwd_kernel<__nv_bfloat16><<<ew_grid(T * H / 4), 256, 0, st>>>(
+        idc.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), out.data_ptr<float>(),
+        T, H, w.size(0), error_flag_ptr());
+  else
+    embedding_fwd_kernel<float><<<ew_grid(T * H / 4), 256, 0, st>>>(
+        idc.data_ptr<int64_t>(), w.data_ptr<float>(), out.data_ptr<float>(), T, H, w.size(0), error_flag_ptr());
   NQ_CHECK_CUDA(cudaGetLastError());
   return out;
 }

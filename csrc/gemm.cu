@@ -13,7 +13,7 @@
 // -> global) so the epilogue of tile i overlaps the main loop of tile i+1.  One
 // CTA per SM walks the tile list with a grid stride; tiles are rasterised in
 // bands of 8 M-tiles for L2 reuse of B.
-#include "sm100.cuh"
+#include "peer.cuh"
 #include "tmap.h"
 
 namespace nq {
@@ -36,6 +36,22 @@ struct GemmArgs {
   int64_t c_group_stride;   // group K: elements between the groups' outputs
   int b_group_rows;         // group M: rows of B per group in the tensor map's row space
   int* err;
+  // Tensor-parallel all-gather consumer (peer.cuh protocol): before loading the
+  // first A tile of an m-tile, wait until ag_flags[row owner] reaches ag_seq.
+  const unsigned* ag_flags;  // null: no wait
+  unsigned ag_seq;
+  int tp_rows;               // rows per rank: owner = row / tp_rows
+  // Tensor-parallel reduce-scatter epilogue: a finished row tile is stored into
+  // rs_dst[owner] at the owner-local row; the last CTA publishes rs_seq into
+  // every rank's flag block at rs_flag_idx.
+  int rs;
+  int tp_world;
+  __nv_bfloat16* rs_dst[8];
+  unsigned* rs_flag_dst[8];
+  int rs_flag_idx;
+  unsigned rs_seq;
+  unsigned* rs_counter;
+  unsigned rs_target;
 };
 
 template <int BN, int STAGES>
@@ -153,10 +169,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int waited_owner = -1;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         int m0, n0, g, kb, ke;
         decode(t, m0, n0, g, kb, ke);
         const int b_row_off = (args.group_mode == kGroupM) ? g * args.b_group_rows : 0;
+        if (args.ag_flags != nullptr) {
+          const int owner = m0 / args.tp_rows;
+          if (owner != waited_owner) {
+            if (!wait_flag(args.ag_flags + owner, args.ag_seq, err)) { ok = false; break; }
+            // peers wrote these rows with generic stores; TMA reads via the async proxy
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            waited_owner = owner;
+          }
+        }
         for (int k0 = kb; k0 < ke; k0 += GBK) {
           if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTimeoutProducer)) { ok = false; break; }
           uint8_t* sA = smem + stage * L::kStageBytes;
@@ -252,7 +278,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!row_ok || col >= args.N) continue;
           const int ncols = min(32, args.N - col);
           if (EPI == kEpiBF16) {
-            __nv_bfloat16* Cp = reinterpret_cast<__nv_bfloat16*>(args.C) + static_cast<int64_t>(row) * args.ldc + col;
+            __nv_bfloat16* Cp;
+            if (args.rs) {
+              const int owner = row / args.tp_rows;
+              Cp = args.rs_dst[owner] + static_cast<int64_t>(row - owner * args.tp_rows) * args.ldc + col;
+            } else {
+              Cp = reinterpret_cast<__nv_bfloat16*>(args.C) + static_cast<int64_t>(row) * args.ldc + col;
+            }
             if (ncols == 32 && (reinterpret_cast<uintptr_t>(Cp) & 15) == 0) {
               uint4* dst = reinterpret_cast<uint4*>(Cp);
 #pragma unroll
@@ -299,6 +331,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (args.rs)
+    grid_done_signal(args.rs_counter, args.rs_target, args.rs_flag_dst, args.rs_flag_idx,
+                     args.tp_world, args.rs_seq);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -395,6 +430,81 @@ void gemm_tn_acc(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
   auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
   launch_gemm<kBN, kStages, true, true, kEpiAccF32>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
                                                     at::cuda::getCurrentCUDAStream());
+}
+
+// ------------------------------------------------------ tensor-parallel GEMMs
+// A [M, K] is a full-sequence buffer whose rows [r*tp_rows, (r+1)*tp_rows) are
+// written by rank r; B [N, K] (nt) or [K, N] (nn).  The producer waits for
+// ag_flags[r] >= ag_seq before loading rows of rank r.
+torch::Tensor gemm_ag(torch::Tensor A, torch::Tensor B, bool nn, int64_t ag_flags, int64_t ag_seq,
+                      int64_t tp_rows) {
+  check_bf16(A, "A"); check_bf16(B, "B");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous(), "gemm_ag: contiguous operands");
+  const int M = A.size(0), K = A.size(1);
+  const int N = nn ? B.size(1) : B.size(0);
+  TORCH_CHECK((nn ? B.size(0) : B.size(1)) == K, "gemm_ag: shape mismatch");
+  TORCH_CHECK(tp_rows > 0 && tp_rows % GBM == 0 && M % tp_rows == 0, "gemm_ag: rows per rank must be a multiple of 128");
+  auto C = torch::empty({M, N}, A.options());
+  if (M == 0 || N == 0) return C;
+  c10::cuda::CUDAGuard g(A.device());
+  auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, K, 64, GBM);
+  auto a = base_args(M, N, K, C.data_ptr(), N);
+  a.ag_flags = reinterpret_cast<const unsigned*>(ag_flags);
+  a.ag_seq = static_cast<unsigned>(ag_seq);
+  a.tp_rows = static_cast<int>(tp_rows);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (nn) {
+    auto tb = make_tmap_2d_bf16(B.data_ptr(), K, N, N, 64, 64);
+    launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN), st);
+  } else {
+    auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, K, 64, kBN);
+    launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN), st);
+  }
+  return C;
+}
+
+// C = A @ B^T (nt) or A @ B (nn), [M, N] with M the full sequence; row tile of
+// owner r goes to rs_dst[r] (that rank's partial plane for this source).
+// Returns the grid size (the caller's block counter advances by it).
+int64_t gemm_rs(torch::Tensor A, torch::Tensor B, bool nn, std::vector<int64_t> rs_dst, int64_t tp_rows,
+                torch::Tensor counter, int64_t counter_before, std::vector<int64_t> flag_dst,
+                int64_t flag_idx, int64_t seq) {
+  check_bf16(A, "A"); check_bf16(B, "B");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous(), "gemm_rs: contiguous operands");
+  const int M = A.size(0), K = A.size(1);
+  const int N = nn ? B.size(1) : B.size(0);
+  TORCH_CHECK((nn ? B.size(0) : B.size(1)) == K, "gemm_rs: shape mismatch");
+  const int world = static_cast<int>(rs_dst.size());
+  TORCH_CHECK(world >= 1 && world <= 8 && flag_dst.size() == rs_dst.size(), "gemm_rs: 1..8 ranks");
+  TORCH_CHECK(tp_rows > 0 && tp_rows % GBM == 0 && M == tp_rows * world, "gemm_rs: M = tp_rows * world, tp_rows % 128 == 0");
+  TORCH_CHECK(N % 32 == 0, "gemm_rs: N must be a multiple of 32");
+  c10::cuda::CUDAGuard g(A.device());
+  auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, K, 64, GBM);
+  auto a = base_args(M, N, K, nullptr, N);
+  a.rs = 1;
+  a.tp_world = world;
+  a.tp_rows = static_cast<int>(tp_rows);
+  for (int r = 0; r < world; ++r) {
+    a.rs_dst[r] = reinterpret_cast<__nv_bfloat16*>(rs_dst[r]);
+    a.rs_flag_dst[r] = reinterpret_cast<unsigned*>(flag_dst[r]);
+    TORCH_CHECK(rs_dst[r] % 16 == 0, "gemm_rs: 16-byte aligned destinations");
+  }
+  a.rs_flag_idx = static_cast<int>(flag_idx);
+  a.rs_seq = static_cast<unsigned>(seq);
+  a.rs_counter = reinterpret_cast<unsigned*>(counter.data_ptr());
+  const int tiles = cdiv(M, GBM) * cdiv(N, kBN);
+  const int grid = std::min(num_sms(), std::max(1, tiles));
+  a.rs_target = static_cast<unsigned>(counter_before + grid);
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (K == 0) TORCH_CHECK(false, "gemm_rs: K must be positive");
+  if (nn) {
+    auto tb = make_tmap_2d_bf16(B.data_ptr(), K, N, N, 64, 64);
+    launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, tiles, st);
+  } else {
+    auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, K, 64, kBN);
+    launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, tiles, st);
+  }
+  return grid;
 }
 
 // ------------------------------------------------------------- grouped GEMMs

@@ -41,6 +41,20 @@ class TokenEmbedding(nn.Module):
         return ops.embedding(input_ids, self.embed_tokens.weight)
 
 
+class _GradReady(torch.autograd.Function):
+    """Identity whose backward calls ``hook()`` before passing the gradient on."""
+
+    @staticmethod
+    def forward(ctx, x, hook):
+        ctx.hook = hook
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        ctx.hook()
+        return g, None
+
+
 class TransformerBlock(nn.Module):
     def __init__(self, config: ModelConfig, layer_idx: int = 0):
         super().__init__()
@@ -51,11 +65,17 @@ class TransformerBlock(nn.Module):
         self.post_attention_layernorm = RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
         self._use_moe = config.layer_is_moe(layer_idx)
         self.feed_forward = MoELayer(config) if self._use_moe else build_ffn(config)
+        # set by data parallelism to overlap gradient reduction with the backward
+        self.grad_ready_hook = None
 
     def forward_fused(self, resid: torch.Tensor, delta: Optional[torch.Tensor],
                       position_ids=None, attention_mask=None, kv_cache=None, rope=None):
         """(resid, pending delta) -> (resid, new delta, aux).  resid is fp32."""
         eps = self.config.rms_norm_eps
+        if self.grad_ready_hook is not None and resid.requires_grad:
+            # the gradient of the block input is produced after every weight
+            # gradient of the block: the hook may start reducing them
+            resid = _GradReady.apply(resid, self.grad_ready_hook)
         resid, x = ops.add_rms_norm(resid, delta, self.input_layernorm.weight, eps)
         a = self.attention(x, position_ids, attention_mask, kv_cache, rope)
         resid, x = ops.add_rms_norm(resid, a, self.post_attention_layernorm.weight, eps)
@@ -154,6 +174,9 @@ class Qwen3Model(nn.Module):
         if getattr(self, "cp_group", None) is not None and kv_caches is None:
             return self._forward_cp(input_ids, position_ids, labels, return_logits,
                                     logits_to_keep, inputs_embeds)
+        if getattr(self, "tp_fused", False) and kv_caches is None and inputs_embeds is None \
+                and position_ids is None and attention_mask is None and input_ids.is_cuda:
+            return self._forward_tp_fused(input_ids, labels, return_logits, logits_to_keep)
         x, aux_total, n_moe = self.hidden(input_ids, position_ids, attention_mask, kv_caches,
                                           inputs_embeds)
         dtype = x.dtype
@@ -180,6 +203,49 @@ class Qwen3Model(nn.Module):
         if n_moe > 0:
             aux_out = aux_total
         return {"logits": logits, "loss": loss, "aux_loss": aux_out, "hidden_states": x}
+
+    def _forward_tp_fused(self, input_ids, labels, return_logits, logits_to_keep):
+        """Tensor + sequence parallel forward with the all-gathers fused into
+        the norms and the reduce-scatters into the row-parallel GEMMs
+        (``parallel.tp_fused``); this rank holds tokens [r*R, (r+1)*R) of the
+        flattened batch."""
+        import torch.distributed as dist
+
+        from ..parallel import tp_fused
+        from ..parallel.tensor_parallel import _AllReduce, all_gather_dim
+        grp = self.tp_group
+        W, r = dist.get_world_size(grp), dist.get_rank(grp)
+        B, S = input_ids.shape
+        T = B * S
+        if T % W:
+            raise ValueError("batch tokens must divide by tp_size")
+        R = T // W
+        comm = getattr(self, "_tp_comm", None)
+        if comm is None or comm.R != R:
+            comm = self._tp_comm = tp_fused.TPComm(grp, R, self.config.hidden_size, input_ids.device)
+        resid = self.embed(input_ids.reshape(-1)[r * R:(r + 1) * R])
+        dummy = None
+        for i, layer in enumerate(self.layers):
+            resid, dummy = tp_fused.block_forward(layer, resid, dummy, comm, i, B, S)
+        x = tp_fused.final_norm(resid, dummy, self.norm.weight, comm, self.config.rms_norm_eps)
+        dtype = x.dtype
+        if return_logits is None:
+            return_logits = labels is None
+        logits = None
+        if return_logits:
+            xf = all_gather_dim(x, 0, grp).view(B, S, -1)
+            xs = xf[:, -logits_to_keep:] if logits_to_keep else xf
+            logits = ops.linear(xs, self.lm_head_ref(dtype))
+        loss = None
+        if labels is not None:
+            t = shift_targets(labels).reshape(-1)[r * R:(r + 1) * R].contiguous()
+            n_local = (t != -100).sum().float()
+            n_global = n_local.clone()
+            dist.all_reduce(n_global, group=grp)
+            part = ops.linear_cross_entropy(x, self.lm_head_ref(dtype), t) * \
+                (n_local / n_global.clamp(min=1))
+            loss = _AllReduce.apply(part, grp)
+        return {"logits": logits, "loss": loss, "aux_loss": None, "hidden_states": x}
 
     def _forward_cp(self, input_ids, position_ids, labels, return_logits, logits_to_keep,
                     inputs_embeds):

@@ -136,6 +136,28 @@ class DataParallel:
         all_gather_flat_(bp, mine.clone(), self.group)
         if bp.data_ptr() != buf.data_ptr():
             buf.copy_(bp[: buf.numel()])
+        if st.compute is not None:
+            self.sync_fp32_span()
+
+    @torch.no_grad()
+    def sync_fp32_span(self) -> None:
+        """Make the master's fp32-read span (norm weights, biases) complete on
+        every rank after a sharded update: each rank contributes its shard's
+        part, summed with one small all-reduce."""
+        lo, hi = getattr(self.store, "fp32_span", (0, 0))
+        if self.world == 1 or self.mode != "shard" or hi <= lo:
+            return
+        m = self.store.master
+        buf = getattr(self, "_span_buf", None)
+        if buf is None or buf.numel() != hi - lo:
+            buf = self._span_buf = torch.zeros(hi - lo, dtype=torch.float32, device=m.device)
+        buf.zero_()
+        b, e = self.shard
+        ib, ie = max(lo, b), min(hi, e)
+        if ie > ib:
+            buf[ib - lo:ie - lo].copy_(m[ib:ie])
+        dist.all_reduce(buf, group=self.group)
+        m[lo:hi].copy_(buf)
 
     @torch.no_grad()
     def gather_master(self) -> None:

@@ -1,0 +1,210 @@
+"""Data parallelism whose optimizer step moves its bulk traffic with this
+library's own kernels over NVLink peer memory (``csrc/zero_comm.cu``).
+
+The flat store's gradient buffer (fp32) and compute copy (bf16) are allocated
+in symmetric memory (``torch.distributed._symmetric_memory``: every rank's
+buffer is mapped into every peer's address space; only the pointer exchange
+comes from PyTorch).  One step is:
+
+1. ``zero_rs``: signal/wait on peer flags, then each rank reads its shard of
+   every peer's gradient with P2P loads, writes the mean and accumulates the
+   squared norm (reduce-scatter fused with the 1/world scale and the norm);
+2. a 4-byte all-reduce of the squared norm (NCCL) and the clip factor;
+3. ``zero_adamw_ag``: sharded AdamW whose bf16 result is stored straight into
+   every peer's compute copy (all-gather fused into the optimizer);
+4. ``zero_publish``: flag barrier so the next forward reads complete weights.
+
+The fp32 master weights and Adam moments stay sharded by use (each rank only
+updates its slice).  Same interface as ``DataParallel``; the engine calls
+``fused_step`` instead of sync + clip + step + gather.  Requires 1, 2, 4 or 8
+ranks on one NVSwitch domain.
+"""
+
+from __future__ import annotations
+
+import importlib
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import ext
+from ..runtime.flat_params import ALIGN, FlatParamStore
+from .comm import get_rank, get_world_size
+from .data_parallel import DataParallel, shard_bounds
+
+
+def symmetric_available(group=None) -> bool:
+    if not (torch.cuda.is_available() and dist.is_initialized()):
+        return False
+    if dist.get_backend(group) != "nccl" or get_world_size(group) not in (2, 4, 8):
+        return False
+    try:
+        importlib.import_module("torch.distributed._symmetric_memory")
+        return True
+    except Exception:
+        return False
+
+
+class SymmetricAllocator:
+    """``alloc(numel, dtype, device)`` for ``FlatParamStore``: zero-filled
+    tensors in symmetric memory."""
+
+    def __init__(self, group=None):
+        symm = importlib.import_module("torch.distributed._symmetric_memory")
+        self.symm = symm
+        self.group = group or dist.group.WORLD
+        self.group_name = self.group.group_name
+        enable = getattr(symm, "enable_symm_mem_for_group", None)
+        if enable is not None:
+            try:
+                enable(self.group_name)
+            except Exception:
+                pass
+        self.tensors: List[torch.Tensor] = []
+
+    def __call__(self, numel: int, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+        t = self.symm.empty(numel, dtype=dtype, device=device)
+        t.zero_()
+        self.tensors.append(t)
+        return t
+
+    def peer_ptrs(self, t: torch.Tensor) -> List[int]:
+        h = self.symm.rendezvous(t, self.group_name)
+        self.handles = getattr(self, "handles", []) + [h]  # keep the mappings alive
+        return [int(p) for p in h.buffer_ptrs]
+
+
+class PeerDataParallel(DataParallel):
+    def __init__(self, store: FlatParamStore, allocator: SymmetricAllocator, group=None,
+                 rs_ctas: int = 0):
+        super().__init__(store, mode="shard", group=group)
+        if self.expert_span is not None:
+            raise ValueError("peer-memory data parallelism does not handle expert spans")
+        self.alloc = allocator
+        dev = store.master.device
+        self.flags = allocator(2 * 8, torch.int32, dev)
+        torch.cuda.synchronize()
+        self.p_grad = allocator.peer_ptrs(store.grad)
+        self.p_comp = allocator.peer_ptrs(store.compute)
+        self.p_flags = allocator.peer_ptrs(self.flags)
+        dist.barrier(group=group)
+        self.epoch = 0
+        self.rs_ctas = rs_ctas
+        self.sq = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.norm = torch.zeros((), dtype=torch.float32, device=dev)
+        self.clip = torch.ones((), dtype=torch.float32, device=dev)
+
+    # ------------------------------------------------------------ overlap
+    def attach_overlap(self, model, ctas: int = 16) -> None:
+        """Reduce each transformer block's gradient span on a side stream as
+        soon as the block's backward is done (last micro-batch only), with a
+        small grid that shares the SMs with the backward kernels."""
+        from ..models.transformer import TransformerBlock
+        st = self.store
+        spans = []
+        for blk in model.modules():
+            if not isinstance(blk, TransformerBlock):
+                continue
+            ps = [p for p in blk.parameters() if id(p) in st.offsets
+                  and st.offsets[id(p)] < st.decay_end]
+            if not ps:
+                continue
+            lo = min(st.offsets[id(p)] for p in ps)
+            hi = max(st.offsets[id(p)] + p.numel() for p in ps)
+            mine = {id(p) for p in ps}
+            others = [q for q in st.params if id(q) not in mine and lo <= st.offsets[id(q)] < hi]
+            if others:
+                continue  # not contiguous: reduced with the remainder at the end
+            lo = lo // ALIGN * ALIGN
+            hi = (hi + ALIGN - 1) // ALIGN * ALIGN
+            spans.append((lo, hi))
+            blk.grad_ready_hook = self._make_hook(len(spans) - 1)
+        self.spans = spans
+        self.overlap_ctas = ctas
+        self.comm_stream = torch.cuda.Stream(device=st.master.device)
+        self.final_micro = False
+        cover = sorted(spans)
+        rest, pos = [], 0
+        for lo, hi in cover:
+            if lo > pos:
+                rest.append((pos, lo))
+            pos = max(pos, hi)
+        if pos < st.numel:
+            rest.append((pos, st.numel))
+        self.rest = rest
+
+    def _make_hook(self, k: int):
+        def hook():
+            if not self.final_micro or k in self._issued:
+                return
+            self._issued.add(k)
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream())
+            self.comm_stream.wait_event(ev)
+            with torch.cuda.stream(self.comm_stream):
+                self._rs(*self.spans[k], self.overlap_ctas)
+        return hook
+
+    def begin_step(self, final_micro: bool) -> None:
+        """Called by the engine before each micro-batch's backward."""
+        if getattr(self, "spans", None) is None:
+            return
+        if final_micro and not self.final_micro:
+            self._issued = set()
+            self.sq.zero_()
+            self._calls = 0
+        self.final_micro = final_micro
+
+    def _rs(self, lo: int, hi: int, ctas: int) -> None:
+        b, e = self.shard
+        lo, hi = max(lo, b), min(hi, e)
+        if hi < lo:
+            hi = lo
+        self._calls += 1
+        ext().zero_rs(self.p_grad, self.p_comp, self.p_flags, self.rank, lo, hi, self.sq,
+                      self.epoch + self._calls, ctas)
+
+    def sync_grads(self) -> None:
+        """Reduce-scatter whatever the overlapped block reductions did not
+        cover (everything, without ``attach_overlap``)."""
+        if getattr(self, "spans", None) is None:
+            self._calls = 0
+            self.sq.zero_()
+            self._rs(0, self.store.numel, self.rs_ctas)
+        else:
+            torch.cuda.current_stream().wait_stream(self.comm_stream)
+            if not self.final_micro:  # no backward ran with the hooks armed
+                self._issued, self._calls = set(), 0
+                self.sq.zero_()
+            missing = [self.spans[k] for k in range(len(self.spans)) if k not in self._issued]
+            for lo, hi in missing + self.rest:
+                self._rs(lo, hi, self.rs_ctas)
+            self.final_micro = False
+        self.epoch += self._calls
+
+    @torch.no_grad()
+    def fused_step(self, optimizer, max_norm: float, extra_sq=None) -> torch.Tensor:
+        """Reduce-scatter + norm, clip, sharded AdamW + all-gather, publish.
+        Returns the global gradient norm (device tensor)."""
+        E = ext()
+        b, e = self.shard
+        self.sync_grads()
+        sq = self.sq
+        if extra_sq is not None:
+            sq = extra_sq(sq)
+        dist.all_reduce(sq, group=self.group)
+        E.zero_clip(sq, float(max_norm or 0.0), self.clip, self.norm)
+        optimizer.clip_scale = self.clip
+        optimizer.last_grad_norm = self.norm
+        lr_d, lr_n, b1, b2, eps, wd, bc1, bc2 = optimizer.advance()
+        E.zero_adamw_ag(self.p_grad, self.p_comp, self.p_flags, self.rank, self.store.master,
+                        optimizer.exp_avg, optimizer.exp_avg_sq, self.clip, b, e,
+                        self.store.decay_end, lr_d, lr_n, b1, b2, eps, wd, bc1, bc2)
+        E.zero_publish(self.p_grad, self.p_comp, self.p_flags, self.rank, self.epoch)
+        self.sync_fp32_span()
+        return self.norm
+
+    def gather_params(self) -> None:
+        """The fused step already wrote every peer's compute copy."""
+        return

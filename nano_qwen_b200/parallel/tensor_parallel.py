@@ -192,8 +192,14 @@ def _shard_cols(lin, rank: int, ws: int, group, sp: bool):
     lin.tp_mode, lin.tp_group, lin.tp_sp = "row", group, sp
 
 
-def apply_tensor_parallel(model: nn.Module, tp_group, sequence_parallel: bool = True) -> nn.Module:
-    """Shard every transformer block of a Qwen3Model (or the LM of a VL model)."""
+def apply_tensor_parallel(model: nn.Module, tp_group, sequence_parallel: bool = True,
+                          fused: Optional[bool] = None) -> nn.Module:
+    """Shard every transformer block of a Qwen3Model (or the LM of a VL model).
+
+    ``fused`` (default: when usable) runs dense models on CUDA through
+    ``parallel.tp_fused``: the sequence-parallel all-gathers and
+    reduce-scatters happen inside the norm and GEMM kernels over NVLink peer
+    memory instead of as NCCL collectives."""
     if hasattr(tp_group, "get_group"):  # a DeviceMesh, as in the reference's API
         tp_group = tp_group.get_group()
     ws = dist.get_world_size(tp_group)
@@ -225,6 +231,11 @@ def apply_tensor_parallel(model: nn.Module, tp_group, sequence_parallel: bool = 
     lm.tp_group = tp_group
     lm.sp_group = tp_group if sequence_parallel else None
     _mark_replicated(model, sequence_parallel)
+    if fused is None:
+        from .peer_dp import symmetric_available
+        from .tp_fused import usable
+        fused = sequence_parallel and usable(model) and symmetric_available(tp_group)
+    lm.tp_fused = bool(fused) and sequence_parallel
     return model
 
 

@@ -57,13 +57,21 @@ def default_groups(model: nn.Module) -> List[List[Tuple[str, nn.Parameter]]]:
         if id(p) not in claimed:
             groups.append([(n, p)])
             claimed.add(id(p))
+    # module order: each transformer block's weights end up contiguous, so a
+    # block's gradients form one span that can be reduced as soon as the
+    # block's backward is done
+    order = {id(p): i for i, (_, p) in enumerate(model.named_parameters())}
+    groups.sort(key=lambda g: order.get(id(g[0][1]), 0))
     return groups
 
 
 class FlatParamStore:
     def __init__(self, model: nn.Module, compute_dtype: torch.dtype = torch.bfloat16,
                  device: Optional[torch.device] = None, trainable_only: bool = True,
-                 pad_multiple: int = ALIGN):
+                 pad_multiple: int = ALIGN, alloc=None):
+        """``alloc(numel, dtype, device)`` (optional) allocates the gradient and
+        compute-copy buffers, e.g. in peer-mapped symmetric memory for the
+        peer-memory data-parallel step; it must return zero-filled tensors."""
         self.model = model
         self.compute_dtype = compute_dtype
         groups = default_groups(model)
@@ -112,10 +120,22 @@ class FlatParamStore:
         pad = max(ALIGN, int(pad_multiple))
         self.numel = (off + pad - 1) // pad * pad
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=dev)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=dev)
-        self.compute = (torch.zeros(self.numel, dtype=compute_dtype, device=dev)
-                        if compute_dtype != torch.float32 else None)
+        mk = alloc or (lambda n, dt, d: torch.zeros(n, dtype=dt, device=d))
+        self.grad = mk(self.numel, torch.float32, dev)
+        self.compute = mk(self.numel, compute_dtype, dev) if compute_dtype != torch.float32 else None
         self.offsets = offsets
+        # Parameters that kernels read in fp32 from the master copy (norm
+        # weights, biases: every 1-D parameter).  After a sharded optimizer step
+        # this span of the master is re-synchronised across data-parallel ranks.
+        one_d = [p for p in self.params if p.ndim <= 1]
+        if one_d:
+            lo = min(offsets[id(p)] for p in one_d)
+            hi = max(offsets[id(p)] + p.numel() for p in one_d)
+            if any(p.ndim > 1 and lo <= offsets[id(p)] < hi for p in self.params):
+                lo, hi = self.decay_end, off
+            self.fp32_span = (lo // ALIGN * ALIGN, min(self.numel, (hi + ALIGN - 1) // ALIGN * ALIGN))
+        else:
+            self.fp32_span = (0, 0)
         with torch.no_grad():
             for p in self.params:
                 o = offsets[id(p)]

@@ -44,9 +44,24 @@ class TrainEngine:
         dist_cfg = training_config.get("distributed", {}) or {}
         if dp_mode is None:
             dp_mode = "shard" if dist_cfg.get("fsdp_enabled", True) else "replicate"
-        self.store = attach_param_store(self.model, pad_multiple=ALIGN * max(1, world))
-        self.dp = (DataParallel(self.store, mode=dp_mode, group=dp_group, expert_group=expert_group)
-                   if world > 1 else None)
+        alloc = None
+        if dp_mode == "p2p" and parallel is not None:
+            dp_mode = "shard"
+        if dp_mode == "p2p":
+            from ..parallel.peer_dp import SymmetricAllocator, symmetric_available
+            if symmetric_available(dp_group) and expert_group is None:
+                alloc = SymmetricAllocator(dp_group)
+            else:
+                dp_mode = "shard"
+        self.store = attach_param_store(self.model, pad_multiple=ALIGN * max(1, world), alloc=alloc)
+        if world > 1 and alloc is not None:
+            from ..parallel.peer_dp import PeerDataParallel
+            self.dp = PeerDataParallel(self.store, alloc, group=dp_group)
+            if dist_cfg.get("overlap_grad_reduce", True):
+                self.dp.attach_overlap(self.model)
+        else:
+            self.dp = (DataParallel(self.store, mode=dp_mode, group=dp_group,
+                                    expert_group=expert_group) if world > 1 else None)
         if self.dp is not None:
             self.dp.broadcast_params(0)
         self._dups = self._duplicated_params()
@@ -82,7 +97,9 @@ class TrainEngine:
         if hasattr(self.model, "pipeline_forward_backward") and loss_fn is None:
             loss_sum, aux_sum = self.model.pipeline_forward_backward(micro_batches)
         else:
-            for mb in micro_batches:
+            for i, mb in enumerate(micro_batches):
+                if hasattr(self.dp, "begin_step"):
+                    self.dp.begin_step(i == n - 1)
                 if loss_fn is not None:
                     loss = loss_fn(self.model, mb) / n
                     loss.backward()
@@ -95,6 +112,10 @@ class TrainEngine:
         if self.tp_group is not None:
             from ..parallel.tensor_parallel import sync_replicated_grads
             sync_replicated_grads(self.model, self.tp_group)
+        if hasattr(self.dp, "fused_step"):
+            gnorm = self.dp.fused_step(self.optimizer, self.grad_clip)
+            self.scheduler.step()
+            return {"loss": loss_sum, "grad_norm": gnorm, "aux_loss": aux_sum}
         if self.dp is not None:
             self.dp.sync_grads()
         gnorm = self.optimizer.clip_grad_norm_(self.grad_clip, self._norm_sq_reduce)

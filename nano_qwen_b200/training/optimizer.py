@@ -79,24 +79,26 @@ class FusedAdamW(torch.optim.Optimizer):
         return norm
 
     # --------------------------------------------------------------- step
-    @torch.no_grad()
-    def step(self, closure=None):
-        loss = closure() if closure is not None else None
+    def advance(self):
+        """Count one step and return this step's hyper-parameters
+        (lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2)."""
         self.step_count += 1
         t = self.step_count
-        st = self.store
-        b, e = self.shard
         g0 = self.param_groups[0]
         beta1, beta2 = g0["betas"]
-        eps = g0["eps"]
-        lr_decay = g0["lr"]
-        wd = g0["weight_decay"] if st.decay_end > 0 else 0.0
-        lr_nodecay = self.param_groups[-1]["lr"]
-        bc1 = 1.0 - beta1 ** t
-        bc2 = 1.0 - beta2 ** t
+        wd = g0["weight_decay"] if self.store.decay_end > 0 else 0.0
         for grp in self.param_groups:
             for p in grp["params"]:
                 self.state[p]["step"].fill_(t)
+        return (g0["lr"], self.param_groups[-1]["lr"], beta1, beta2, g0["eps"], wd,
+                1.0 - beta1 ** t, 1.0 - beta2 ** t)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = closure() if closure is not None else None
+        st = self.store
+        b, e = self.shard
+        lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2 = self.advance()
         if st.master.is_cuda:
             comp = st.compute if st.compute is not None else torch.empty(0, device=st.master.device)
             ext().adamw_flat(st.master, st.grad, self.exp_avg, self.exp_avg_sq, comp,
@@ -176,12 +178,12 @@ def build_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.
 
 def attach_param_store(model: nn.Module, compute_dtype: Optional[torch.dtype] = None,
                        device: Optional[torch.device] = None,
-                       pad_multiple: int = 64) -> FlatParamStore:
+                       pad_multiple: int = 64, alloc=None) -> FlatParamStore:
     """Re-home a model's trainable parameters into a FlatParamStore."""
     dev = device or next(model.parameters()).device
     if compute_dtype is None:
         compute_dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
     store = FlatParamStore(model, compute_dtype=compute_dtype, device=dev,
-                           pad_multiple=pad_multiple)
+                           pad_multiple=pad_multiple, alloc=alloc)
     model.param_store = store
     return store

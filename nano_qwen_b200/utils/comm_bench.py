@@ -1,0 +1,127 @@
+"""Roofline benchmark of the peer-memory data-parallel kernels against NCCL.
+
+    torchrun --nproc-per-node N -m nano_qwen_b200.utils.comm_bench [--numel 1.7e9]
+
+For a flat fp32 gradient of ``numel`` elements (default: the Qwen3-1.7B
+store) it times, with CUDA events and the max over ranks:
+
+* ``zero_rs`` (P2P reduce-scatter of the mean + squared norm) vs NCCL
+  ``reduce_scatter_tensor`` (AVG) + a sum-of-squares kernel;
+* ``zero_adamw_ag`` (sharded AdamW + bf16 all-gather by P2P stores) vs the
+  AdamW kernel + NCCL ``all_gather_into_tensor``.
+
+Roofline: the slower of (bytes that must cross NVLink into each GPU ÷ the
+measured peer copy bandwidth, 770 GB/s per direction on this pool's B200s) and
+(HBM bytes ÷ the measured copy bandwidth).  NVLink bytes: (N-1)/N x numel x 4
+for the reduce-scatter, (N-1)/N x numel x 2 for the all-gather; the AdamW half
+also moves 30 bytes per shard element through HBM.  Prints one JSON line per
+path.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+LINK_GBS = 770.0
+
+
+def _timed(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / iters / 1e3], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--numel", type=float, default=1.72e9)
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args(argv)
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    world, rank = dist.get_world_size(), dist.get_rank()
+    from ..ops._ext import ext
+    from ..parallel.data_parallel import shard_bounds
+    from ..parallel.peer_dp import SymmetricAllocator
+    E = ext()
+    n = int(a.numel) // (64 * world) * (64 * world)
+    alloc = SymmetricAllocator()
+    dev = torch.device("cuda", local)
+    grad = alloc(n, torch.float32, dev)
+    comp = alloc(n, torch.bfloat16, dev)
+    flags = alloc(16, torch.int32, dev)
+    grad.normal_()
+    torch.cuda.synchronize()
+    pg, pc, pf = alloc.peer_ptrs(grad), alloc.peer_ptrs(comp), alloc.peer_ptrs(flags)
+    b, e = shard_bounds(n, world, rank)
+    sq = torch.zeros(1, device=dev)
+    epoch = [0]
+
+    def rs():
+        epoch[0] += 1
+        E.zero_rs(pg, pc, pf, rank, b, e, sq, epoch[0], 0)
+
+    master = torch.randn(n, device=dev)
+    m = torch.zeros(n, device=dev)
+    v = torch.zeros(n, device=dev)
+    clip = torch.ones((), device=dev)
+
+    def ag():
+        E.zero_adamw_ag(pg, pc, pf, rank, master, m, v, clip, b, e, e, 1e-4, 1e-4, 0.9, 0.95,
+                        1e-8, 0.1, 0.1, 0.05)
+        epoch[0] += 1
+        E.zero_publish(pg, pc, pf, rank, epoch[0])
+
+    plain = torch.randn(n, device=dev)
+    out = torch.empty(n // world, device=dev)
+    comp_plain = torch.empty(n, dtype=torch.bfloat16, device=dev)
+
+    def nccl_rs():
+        dist.reduce_scatter_tensor(out, plain, op=dist.ReduceOp.AVG)
+        E.sum_squares(out)
+
+    def nccl_ag():
+        E.adamw_flat(master, plain, m, v, comp_plain, clip, b, e, e, 1e-4, 1e-4, 0.9, 0.95, 1e-8,
+                     0.1, 0.1, 0.05)
+        dist.all_gather_into_tensor(comp_plain, comp_plain[b:e].clone())
+
+    from .flops import measured_peaks
+    hbm = measured_peaks()["hbm_gbs"]
+    shard = n / world
+    # (NVLink bytes into each GPU, HBM bytes on each GPU)
+    rs_bytes = ((world - 1) / world * n * 4, n * 4 + shard * 4)
+    ag_bytes = ((world - 1) / world * n * 2, shard * 30 + (world - 1) / world * n * 2)
+    rows = [("zero_rs (P2P reduce-scatter + norm)", rs, rs_bytes),
+            ("nccl reduce_scatter + sum_squares", nccl_rs, rs_bytes),
+            ("zero_adamw_ag (AdamW + P2P all-gather)", ag, ag_bytes),
+            ("adamw + nccl all_gather", nccl_ag, ag_bytes)]
+    for name, fn, (link, mem) in rows:
+        t = _timed(fn, a.iters)
+        if rank == 0:
+            t_roof = max(link / (LINK_GBS * 1e9), mem / (hbm * 1e9))
+            print(json.dumps({"path": name, "n_gpus": world, "numel": n, "ms": round(t * 1e3, 3),
+                              "nvlink_gb_s_per_gpu": round(link / t / 1e9, 1),
+                              "roofline_ms": round(t_roof * 1e3, 3),
+                              "frac_of_roofline": round(t_roof / t, 3)}), flush=True)
+    assert E.error_flag_read() == 0, "kernel error word set"
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -6,7 +6,7 @@ import socket
 import pytest
 import torch.multiprocessing as mp
 
-import dist_workers as W
+import dist_workers as W  # noqa: E402
 
 
 def _port() -> int:
