@@ -75,6 +75,21 @@ int64_t tp_norm_bwd(c10::optional<torch::Tensor>, c10::optional<torch::Tensor>, 
                     torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
                     c10::optional<torch::Tensor>, std::vector<int64_t>, torch::Tensor, std::vector<int64_t>,
                     int64_t, int64_t, int64_t, int64_t, int64_t, torch::Tensor, int64_t);
+// ep_comm.cu
+void ep_layout(std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor, int64_t, int64_t, int64_t,
+               torch::Tensor, torch::Tensor, torch::Tensor, int64_t);
+int64_t ep_dispatch(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor,
+                    torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+                    torch::Tensor, int64_t, int64_t, int64_t, torch::Tensor, int64_t);
+void ep_wait(std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t, int64_t);
+void ep_signal(std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t, int64_t);
+void ep_combine(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor,
+                torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, int64_t, int64_t);
+int64_t ep_combine_bwd(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor,
+                       torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, int64_t, int64_t,
+                       torch::Tensor, int64_t);
+void ep_dispatch_bwd(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor,
+                     torch::Tensor, torch::Tensor, int64_t, int64_t);
 // zero_comm.cu
 void zero_rs(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t, int64_t,
              torch::Tensor, int64_t, int64_t);
@@ -135,6 +150,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &nq::gemm_rs, "GEMM whose row tiles are stored into their owners' partial buffers");
   m.def("tp_norm_fwd", &nq::tp_norm_fwd, "residual + sum of TP partials + RMSNorm, all-gathered to peers");
   m.def("tp_norm_bwd", &nq::tp_norm_bwd, "RMSNorm backward with TP partial inputs and all-gathered output");
+  m.def("ep_layout", &nq::ep_layout, "exchange per-expert counts and compute the dispatch layout");
+  m.def("ep_dispatch", &nq::ep_dispatch, "store token rows into the expert owners' receive buffers (P2P)");
+  m.def("ep_wait", &nq::ep_wait);
+  m.def("ep_signal", &nq::ep_signal);
+  m.def("ep_combine", &nq::ep_combine, "pull expert outputs (P2P) and form the weighted top-k sum");
+  m.def("ep_combine_bwd", &nq::ep_combine_bwd);
+  m.def("ep_dispatch_bwd", &nq::ep_dispatch_bwd);
   m.def("zero_rs", &nq::zero_rs, "peer-memory reduce-scatter of the mean gradient + squared norm");
   m.def("zero_clip", &nq::zero_clip);
   m.def("zero_adamw_ag", &nq::zero_adamw_ag, "sharded AdamW fused with the bf16 all-gather by P2P stores");

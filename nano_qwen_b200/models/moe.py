@@ -113,7 +113,7 @@ class MoELayer(nn.Module):
             from ..parallel.tensor_parallel import scale_grad
             aux = scale_grad(aux, self.router.grad_scale)
         if self.ep is not None:
-            out = self.ep(self, x, weights, idx)
+            out = self.ep(self, x, weights, idx, counts)
         else:
             w_gu, w_d = self.expert_weight_refs(x.dtype)
             out = ops.moe_ffn(x, weights, idx, w_gu, w_d, self.num_experts, self.inter,

@@ -66,15 +66,38 @@ class _AllToAll(torch.autograd.Function):
 
 
 class ExpertParallel:
-    def __init__(self, group, num_experts: int):
+    """``fused``: use the peer-memory dispatch/combine kernels
+    (``parallel.ep_fused``) instead of NCCL all-to-alls.  ``shared`` holds the
+    communication buffers common to every MoE layer of the model."""
+
+    def __init__(self, group, num_experts: int, fused: bool = False, shared=None, layer: int = 0):
         self.group = group
         self.ep = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         assert num_experts % self.ep == 0, "num_experts must divide by ep_size"
         self.e_local = num_experts // self.ep
         self.e0 = self.rank * self.e_local
+        self.num_experts = num_experts
+        self.fused = fused
+        self.shared = shared if shared is not None else {}
+        self.layer = layer
 
-    def __call__(self, moe, x: torch.Tensor, weights: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    def __call__(self, moe, x: torch.Tensor, weights: torch.Tensor, idx: torch.Tensor,
+                 counts=None) -> torch.Tensor:
+        if self.fused and x.is_cuda:
+            from .ep_fused import EPComm, ep_moe
+            N, H = x.shape
+            key = (N, H, idx.shape[1])
+            comm = self.shared.get(key)
+            if comm is None:
+                comm = self.shared[key] = EPComm(self.group, self.num_experts, H, N, idx.shape[1],
+                                                 x.device)
+            if counts is None:
+                counts = torch.bincount(idx.reshape(-1).long(), minlength=self.num_experts).float()
+            return ep_moe(moe, x, weights, idx, counts, comm, self.layer)
+        return self._nccl(moe, x, weights, idx)
+
+    def _nccl(self, moe, x: torch.Tensor, weights: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
         N, H = x.shape
         k = idx.shape[1]
         flat = idx.reshape(-1).long()
@@ -107,14 +130,24 @@ class ExpertParallel:
         return (y_slot.view(N, k, H).float() * weights.unsqueeze(-1)).sum(1).to(x.dtype)
 
 
-def apply_expert_parallel(model: nn.Module, ep_group) -> nn.Module:
-    """Keep only this rank's experts in every MoE layer and route through EP."""
+def apply_expert_parallel(model: nn.Module, ep_group, fused=None) -> nn.Module:
+    """Keep only this rank's experts in every MoE layer and route through EP.
+
+    ``fused`` (default: on CUDA with symmetric memory and 2, 4 or 8 ranks)
+    selects the peer-memory dispatch/combine kernels."""
     from ..models.moe import MoELayer
     ws = dist.get_world_size(ep_group)
     r = dist.get_rank(ep_group)
+    if fused is None:
+        from .peer_dp import symmetric_available
+        fused = symmetric_available(ep_group)
+    shared: dict = {}
+    n_layer = 0
     for m in model.modules():
         if isinstance(m, MoELayer):
-            ep = ExpertParallel(ep_group, m.num_experts)
+            ep = ExpertParallel(ep_group, m.num_experts, fused=bool(fused), shared=shared,
+                                layer=n_layer)
+            n_layer += 1
             keep = list(range(r * ep.e_local, (r + 1) * ep.e_local))
             m.experts = nn.ModuleList([m.experts[i] for i in keep])
             m.expert_offset = keep[0]

@@ -11,6 +11,8 @@ Additions over the reference: the full CPU/CUDA RNG state and sampler state are
 saved and restored (the reference saves 8 bytes of CPU RNG and never restores
 them), ``async_save`` really runs DCP's ``async_save`` and the plain path keeps
 ``step`` on resume (reference: training/checkpoint.py:174 loses it).
+Model-parallel runs (tensor / expert / pipeline shards) write one
+``shard_{rank:05d}.pt`` per rank in the same step directory.
 """
 
 from __future__ import annotations
@@ -23,7 +25,7 @@ from typing import Any, Dict, Optional
 import torch
 import torch.nn as nn
 
-from ..parallel.comm import barrier, get_rank, is_main_process
+from ..parallel.comm import barrier, get_rank, get_world_size, is_main_process
 
 try:
     import torch.distributed.checkpoint as dcp
@@ -52,6 +54,15 @@ def _set_rng_state(st: Dict[str, Any]) -> None:
             torch.cuda.set_rng_state_all(states)
 
 
+def model_parallel(model: nn.Module) -> bool:
+    """True when the parameters on this rank are shards (TP / EP) or a
+    pipeline stage, so a replicated checkpoint format does not apply."""
+    if hasattr(model, "pipeline_forward_backward"):
+        return True
+    return any(getattr(p, "_tp_sharded", False) or getattr(p, "_ep_local", False)
+               for p in model.parameters())
+
+
 class CheckpointManager:
     def __init__(self, save_dir: str = "checkpoints", save_interval: int = 1000,
                  max_checkpoints: int = 5, async_save: bool = True, use_dcp: bool = True):
@@ -72,7 +83,9 @@ class CheckpointManager:
              extra_state: Optional[Dict[str, Any]] = None, sampler=None) -> Path:
         d = self.save_dir / f"step_{step:08d}"
         self.wait()
-        if self.use_dcp:
+        if model_parallel(model):
+            self._save_sharded(d, model, optimizer)
+        elif self.use_dcp:
             self._save_dcp(d, model, optimizer)
         else:
             self._save_plain(d, model, optimizer, scheduler, extra_state, step)
@@ -90,6 +103,19 @@ class CheckpointManager:
             self._cleanup()
         barrier()
         return d
+
+    def _save_sharded(self, d: Path, model, optimizer):
+        """Model-parallel runs (tensor / expert / pipeline): every rank writes
+        its own shard file with the local parameter names; loading expects the
+        same parallel layout (same world size and axis sizes)."""
+        d.mkdir(parents=True, exist_ok=True)
+        state = {"model": {k: v.detach().cpu() for k, v in model.state_dict().items()}}
+        if optimizer is not None:
+            state["optimizer"] = optimizer.state_dict()
+        torch.save(state, d / f"shard_{get_rank():05d}.pt")
+        if is_main_process():
+            with open(d / "sharded.json", "w") as f:
+                json.dump({"world_size": get_world_size()}, f)
 
     def _save_dcp(self, d: Path, model, optimizer):
         sd = {"model": get_model_state_dict(model)}
@@ -132,7 +158,14 @@ class CheckpointManager:
             if checkpoint_dir is None:
                 return {}
         d = Path(checkpoint_dir)
-        if (d / "checkpoint.pt").exists() and not (d / ".metadata").exists():
+        shard = d / f"shard_{get_rank():05d}.pt"
+        if shard.exists():
+            st = torch.load(shard, map_location="cpu", weights_only=False)
+            model.load_state_dict(st["model"])
+            if optimizer is not None and "optimizer" in st:
+                optimizer.load_state_dict(st["optimizer"])
+            out = {}
+        elif (d / "checkpoint.pt").exists() and not (d / ".metadata").exists():
             out = self._load_plain(d, model, optimizer, scheduler)
         else:
             sd = {"model": get_model_state_dict(model)}

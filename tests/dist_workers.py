@@ -247,3 +247,34 @@ def heartbeat_worker(rank, world, port, dead_rank):
             break
         time.sleep(0.1)
     assert failed is not None and dead_rank in failed.ranks, failed
+
+
+# ------------------------------------------------------------------ checkpoint (model parallel)
+def tp_checkpoint_worker(rank, world, port, tmp):
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.tensor_parallel import apply_tensor_parallel
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg()
+    ids = batch(cfg, 2, 16)
+    grp = dist.new_group(list(range(world)))
+    tcfg = {"optimizer": {"lr": 1e-2}, "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+
+    singles = [dist.new_group([r]) for r in range(world)]
+    e1 = TrainEngine(apply_tensor_parallel(build(cfg), grp, sequence_parallel=True), tcfg,
+                     torch.device("cpu"), dp_group=singles[rank])
+    e1.tp_group = grp
+    e1.train_step([{"input_ids": ids, "labels": ids}])
+    mgr = CheckpointManager(save_dir=tmp, save_interval=1, async_save=False)
+    m, o, s = e1.state_for_save()
+    path = mgr.save(1, m, o, s, extra_state={"step": 1})
+    e2 = TrainEngine(apply_tensor_parallel(build(cfg, seed=5), grp, sequence_parallel=True), tcfg,
+                     torch.device("cpu"), dp_group=singles[rank])
+    e2.tp_group = grp
+    mgr.load(e2.model, e2.optimizer, e2.scheduler, str(path))
+    for (n, p), q in zip(e1.model.named_parameters(), e2.model.parameters()):
+        assert torch.equal(p, q), n
+    a = e1.train_step([{"input_ids": ids, "labels": ids}])
+    b = e2.train_step([{"input_ids": ids, "labels": ids}])
+    assert torch.allclose(a["loss"], b["loss"])
+    dist.destroy_process_group()

@@ -143,3 +143,64 @@ def tp_fused_worker(rank, world, port):
         assert e1 < 0.05 and e2 < 0.05, (n, e1, e2, worst)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def ep_fused_worker(rank, world, port):
+    """Fused expert parallelism (peer-memory dispatch/combine kernels) against
+    the single-GPU MoE layer: loss on this rank's tokens, dense gradients, and
+    expert gradients summed over the ranks' tokens."""
+    init(rank, world, port)
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.parallel.expert_parallel import apply_expert_parallel
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=64, intermediate_size=512, vocab_size=4096,
+                      max_position_embeddings=512, tie_word_embeddings=True, num_experts=8,
+                      num_experts_per_tok=2, moe_intermediate_size=128)
+    grp = dist.new_group(list(range(world)))
+    g = torch.Generator().manual_seed(11 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (2, 256), generator=g).cuda()
+
+    def build(ep, fused):
+        torch.manual_seed(0)
+        m = Qwen3Model(cfg).cuda()
+        with torch.no_grad():
+            for n, p in m.named_parameters():
+                if p.ndim >= 2:
+                    p.normal_(0.0, 0.05)
+        if ep:
+            apply_expert_parallel(m, grp, fused=fused)
+        attach_param_store(m)
+        return m
+
+    ref = build(False, False)
+    out = ref(ids, labels=ids)
+    out["loss"].backward()
+    l_ref = float(out["loss"])
+    ref_g = {n: p.grad.float().clone() for n, p in ref.named_parameters()}
+    for n in ref_g:
+        if ".experts." in n:
+            dist.all_reduce(ref_g[n], group=grp)  # owner's expert grad covers every rank's tokens
+    results = {}
+    for fused in (True, False):
+        m = build(True, fused)
+        o = m(ids, labels=ids)
+        o["loss"].backward()
+        torch.cuda.synchronize()
+        results[fused] = (float(o["loss"]), {n: p.grad.float() for n, p in m.named_parameters()})
+    assert ext().error_flag_read() == 0, "kernel error word set"
+    e_loc = cfg.num_experts // world
+    for fused, (loss, grads) in results.items():
+        assert abs(loss - l_ref) < 2e-3 * l_ref, (fused, loss, l_ref)
+        for n, gr in grads.items():
+            rn = n
+            if ".experts." in n:
+                pre, rest = n.split(".experts.", 1)
+                e, tail = rest.split(".", 1)
+                rn = f"{pre}.experts.{int(e) + rank * e_loc}.{tail}"
+            err = ((gr - ref_g[rn]).norm() / (ref_g[rn].norm() + 1e-12)).item()
+            assert err < 2e-2, (fused, n, err)
+    dist.barrier()
+    dist.destroy_process_group()

@@ -31,3 +31,9 @@ def test_peer_memory_zero_step_matches_single_process():
 def test_fused_tensor_parallel_matches_single_gpu():
     import multi_gpu_workers as W
     mp.spawn(W.tp_fused_worker, args=(2, _port()), nprocs=2, join=True)
+
+
+@needs2
+def test_fused_expert_parallel_matches_single_gpu():
+    import multi_gpu_workers as W
+    mp.spawn(W.ep_fused_worker, args=(2, _port()), nprocs=2, join=True)

@@ -52,3 +52,7 @@ def test_manager_grid_groups():
 
 def test_heartbeat_detects_silent_rank():
     _run(W.heartbeat_worker, 3, 1)
+
+
+def test_tensor_parallel_checkpoint_roundtrip(tmp_path):
+    _run(W.tp_checkpoint_worker, 2, str(tmp_path))
