@@ -65,6 +65,14 @@ CONFIGS = {
                           qk_norm=True, tie_word_embeddings=True, num_experts=64,
                           num_experts_per_tok=8, moe_intermediate_size=256,
                           router_aux_loss_coef=0.001), 8, 2048, "ep"),
+    # Qwen3-235B-A22B layer shape truncated to 12 layers, expert
+    # parallelism over all ranks (per-GPU batch 2 x 4096)
+    "qwen3-235b-l12-ep": (dict(hidden_size=4096, num_hidden_layers=12, num_attention_heads=64,
+                               num_key_value_heads=4, head_dim=128, intermediate_size=12288,
+                               vocab_size=151936, max_position_embeddings=4096, rope_theta=1e6,
+                               qk_norm=True, tie_word_embeddings=False, num_experts=128,
+                               num_experts_per_tok=8, moe_intermediate_size=1536,
+                               router_aux_loss_coef=0.001), 2, 4096, "ep"),
     # Qwen3-8B shape, tensor + sequence parallel over all ranks,
     # global batch 8 x 8192 (the same tokens on every rank: strong scaling)
     "qwen3-8b-tp": (dict(hidden_size=4096, num_hidden_layers=36, num_attention_heads=32,
@@ -289,6 +297,9 @@ def run_ours(args, world, rank, local):
         mode = "p2p" if hasattr(eng.dp, "fused_step") else eng.dp.mode
     if par == "tp" and world > 1:
         mode = "tp-fused" if getattr(eng.model, "tp_fused", False) else "tp-nccl"
+    if par == "ep" and world > 1:
+        eps = [m.ep for m in eng.model.modules() if getattr(m, "ep", None) is not None]
+        mode = "ep-fused" if eps and all(e.fused for e in eps) else "ep-nccl"
     return ms, clocks, {"kernel_error_flag": err, "gpu_launches_per_step": launches,
                         "dp_mode": mode}, e2e
 
@@ -413,7 +424,8 @@ def parallel_label(par, world, impl, mode):
         return f"tp{world}+sp (" + ("all-gather / reduce-scatter fused into the norm and GEMM kernels over peer memory"
                                     if mode == "tp-fused" else "NCCL collectives") + ")"
     if par == "ep":
-        return f"ep{world} x dp{world} (NCCL all-to-all dispatch/combine)"
+        return f"ep{world} x dp{world} (" + ("dispatch/combine kernels over peer memory" if mode == "ep-fused"
+                                             else "NCCL all-to-all dispatch/combine") + ")"
     return f"dp{world} ({DP_LABEL.get(mode, '')})"
 
 

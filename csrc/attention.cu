@@ -301,9 +301,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 32; i += 2) {
           const float x0 = fmaf(__uint_as_float(u[c][i]), sl2, -m_new);
           const float x1 = fmaf(__uint_as_float(u[c][i + 1]), sl2, -m_new);
-          // MODE 1: one exponential in four runs on the FMA pipe (exp2_poly).
+          // MODE 1 / 2: one exponential in four / eight runs on the FMA pipe (exp2_poly).
           const float p0 = dead ? 0.f : ex2_approx(x0);
-          const float p1 = dead ? 0.f : ((MODE == 1 && (i & 2)) ? exp2_poly(x1) : ex2_approx(x1));
+          const bool poly = (MODE == 1 && (i & 2)) || (MODE == 2 && (i & 6) == 6);
+          const float p1 = dead ? 0.f : (poly ? exp2_poly(x1) : ex2_approx(x1));
           sum4[(i >> 1) & 3] += p0 + p1;
           pk[i >> 1] = pack_bf16(p0, p1);
         }
@@ -435,6 +436,7 @@ std::vector<torch::Tensor> attn_fwd_timeline(torch::Tensor qk, torch::Tensor qkv
   auto ts = torch::zeros({8192}, qk.options().dtype(torch::kInt64));
   auto* p = reinterpret_cast<unsigned long long*>(ts.data_ptr<int64_t>());
   if (mode == 1) launch_attn_fwd<128, 1>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
+  else if (mode == 2) launch_attn_fwd<128, 2>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
   else launch_attn_fwd<128, 0>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
   return {o, lse, ts};
 }

@@ -268,6 +268,7 @@ __global__ void plan_assign_kernel(const int* __restrict__ idx, int64_t n, int E
 
 std::vector<torch::Tensor> moe_plan(torch::Tensor idx, int64_t E, int64_t cap, int64_t pad) {
   TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.is_contiguous() && E <= kMaxE, "moe_plan: idx int32");
+  TORCH_CHECK(pad >= 1, "moe_plan: pad (segment alignment) must be >= 1");
   const int N = idx.size(0), K = idx.size(1);
   const int64_t n = static_cast<int64_t>(N) * K;
   const int64_t rows_cap = n + E * pad;

@@ -110,7 +110,7 @@ class _EPMoE(torch.autograd.Function):
         s0 = comm.next(CH_COUNTS)
         E.ep_layout(comm.p_flags, comm.p_counts, comm.rank, counts.float().contiguous(), comm.E, El, s0,
                     dest_base, seg_off, seg_used, comm.cap)
-        slot_of, loc_off, _ = E.moe_plan(idx, comm.E, -1, 0)
+        slot_of, loc_off, _ = E.moe_plan(idx, comm.E, -1, 1)  # pad 1: unpadded order
         recv, recv_ptrs = comm.recv_buf(layer)
         dest_row = torch.empty(N, K, dtype=torch.int32, device=dev)
         s1 = comm.next(CH_DISPATCH)
