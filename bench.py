@@ -73,6 +73,12 @@ CONFIGS = {
                                qk_norm=True, tie_word_embeddings=False, num_experts=128,
                                num_experts_per_tok=8, moe_intermediate_size=1536,
                                router_aux_loss_coef=0.001), 2, 4096, "ep"),
+    # Qwen3-1.7B shape under tensor + sequence parallelism (global batch 4 x 4096): a
+    # smaller tp configuration for comparing the fused and NCCL paths
+    "qwen3-1.7b-tp": (dict(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16,
+                           num_key_value_heads=8, head_dim=128, intermediate_size=6144,
+                           vocab_size=151936, max_position_embeddings=4096, rope_theta=1e6,
+                           qk_norm=True, tie_word_embeddings=True), 4, 4096, "tp"),
     # Qwen3-8B shape, tensor + sequence parallel over all ranks,
     # global batch 8 x 8192 (the same tokens on every rank: strong scaling)
     "qwen3-8b-tp": (dict(hidden_size=4096, num_hidden_layers=36, num_attention_heads=32,
@@ -91,6 +97,8 @@ def parse():
     p.add_argument("--config", default="qwen3-1.7b", choices=sorted(CONFIGS))
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                   help="ours, tp/ep configs: peer-memory fused kernels or NCCL collectives")
     p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate"],
                    help="ours, N>1: peer-memory fused ZeRO step (p2p) or NCCL ZeRO-2 / all-reduce")
     return p.parse_args()
@@ -273,8 +281,10 @@ def run_ours(args, world, rank, local):
     pm = None
     if par in ("tp", "ep") and world > 1:
         from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+        fused = None if args.comm == "fused" else False
         pm = ParallelismManager(ParallelConfig(tp_size=world if par == "tp" else 1,
-                                               ep_size=world if par == "ep" else 1))
+                                               ep_size=world if par == "ep" else 1,
+                                               tp_fused=fused, ep_fused=fused))
         model = pm.apply_parallelism(model)
     eng = TrainEngine(model, tcfg, dev, dp_mode=args.dp_mode if world > 1 else None, parallel=pm)
     del model

@@ -51,6 +51,12 @@ struct AttnArgs {
   float* lse;        // [B, Hq, S]
   int* err;
   unsigned long long* dbg;  // optional per-event timestamps of CTA 0 (profiling aid)
+  int head_major;           // 1: blocks of one head adjacent (profiling comparison)
+  // Keys/values: rows per batch (Sk), head index of K and V in their tensor
+  // maps.  Queries: key-space position of query row i is i + off0 for
+  // i < split, else i + off1 (context parallelism: a rank's two zigzag chunks
+  // against the gathered keys).  Self-attention: Sk = S, offsets 0.
+  int Sk, k_head, v_head, off0, off1, split;
 };
 
 #define NQ_TS(slot)                                                         \
@@ -98,7 +104,7 @@ __device__ __forceinline__ float exp2_poly(float x) {
 template <int D, int MODE>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmV,
-                    const AttnArgs args) {
+                    const __grid_constant__ CUtensorMap tmK, const AttnArgs args) {
   using L = AttnFwdSmem<D>;
   constexpr int KCH = D / 64;  // 64-wide d chunks
   extern __shared__ uint8_t smem_raw[];
@@ -129,15 +135,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // scheduling by the hardware block scheduler); adjacent blocks are adjacent
   // heads, which share K/V under GQA.
   const int n_bh = gridDim.x / n_mblk;
-  const int mb = n_mblk - 1 - static_cast<int>(blockIdx.x) / n_bh;
-  const int bh = static_cast<int>(blockIdx.x) % n_bh;
+  const int mb = args.head_major ? n_mblk - 1 - static_cast<int>(blockIdx.x) % n_mblk
+                                 : n_mblk - 1 - static_cast<int>(blockIdx.x) / n_bh;
+  const int bh = args.head_major ? static_cast<int>(blockIdx.x) / n_mblk
+                                 : static_cast<int>(blockIdx.x) % n_bh;
   const int b = bh / args.Hq;
   const int h = bh - b * args.Hq;
   const int hk = h / (args.Hq / args.Hk);
   const int q0 = mb * CTA_M;
   const int tok0 = b * S;
-  const int n_kblk = args.causal ? min((q0 + CTA_M + ABN - 1) / ABN, (S + ABN - 1) / ABN)
-                                 : (S + ABN - 1) / ABN;
+  const int Sk = args.Sk;
+  const int ktok0 = b * Sk;
+  const int qoff = (q0 < args.split) ? args.off0 : args.off1;  // CTA rows share one chunk
+  const int n_kblk = args.causal ? min((q0 + qoff + CTA_M + ABN - 1) / ABN, (Sk + ABN - 1) / ABN)
+                                 : (Sk + ABN - 1) / ABN;
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
@@ -153,6 +164,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmQK);
     tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmK);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -180,11 +192,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive_expect_tx(&k_full[st], L::kKVBytes);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-          tma_load_3d(sK + st * L::kKVBytes + c * ABN * 128, &tmQK, &k_full[st], c * 64, args.Hq + hk, tok0 + j * ABN);
+          tma_load_3d(sK + st * L::kKVBytes + c * ABN * 128, &tmK, &k_full[st], c * 64, args.k_head + hk, ktok0 + j * ABN);
         mbar_arrive_expect_tx(&v_full[st], L::kKVBytes);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-          tma_load_3d(sV + st * L::kKVBytes + c * ABN * 128, &tmV, &v_full[st], c * 64, args.Hq + args.Hk + hk, tok0 + j * ABN);
+          tma_load_3d(sV + st * L::kKVBytes + c * ABN * 128, &tmV, &v_full[st], c * 64, args.v_head + hk, ktok0 + j * ABN);
       }
     }
   } else if (warp == 1) {
@@ -267,7 +279,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_wait_ld();
       if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 0);
       const int k0 = j * ABN;
-      const bool need_mask = (args.causal && k0 + ABN - 1 > q0 + t * ABM) || (k0 + ABN > S);
+      const bool need_mask = (args.causal && k0 + ABN - 1 > q0 + qoff + t * ABM) || (k0 + ABN > Sk);
       // Raw scores stay in registers; the scale (> 0) is applied to the max and
       // folded into the exponent's FFMA.
       if (need_mask) {
@@ -276,7 +288,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int kj = k0 + c * 32 + i;
-            if (kj >= S || (args.causal && kj > qi)) u[c][i] = 0xff800000u;  // -inf
+            if (kj >= Sk || (args.causal && kj > qi + qoff)) u[c][i] = 0xff800000u;  // -inf
           }
       }
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -381,15 +393,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // --------------------------------------------------------------------- host
+// Key/value source for context parallelism: kv [B*Sk, 2*Hk*D] (k | v per row)
+// and the query offsets (see AttnArgs).
+struct AttnKV {
+  const torch::Tensor* kv = nullptr;
+  int Sk = 0, off0 = 0, off1 = 0, split = 0;
+};
+
 template <int D, int MODE = 0>
 static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, torch::Tensor& o,
                             torch::Tensor& lse, int B, int S, int Hq, int Hk, bool causal, float scale,
-                            unsigned long long* dbg = nullptr) {
+                            unsigned long long* dbg = nullptr, int head_major = 0,
+                            const AttnKV& cp = AttnKV()) {
   using L = AttnFwdSmem<D>;
   const int64_t T = static_cast<int64_t>(B) * S;
   auto tq = make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, ABM);
-  auto tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, ABN);
+  CUtensorMap tv, tk;
   AttnArgs a;
+  if (cp.kv != nullptr) {
+    const int64_t Tk = static_cast<int64_t>(B) * cp.Sk;
+    tk = make_tmap_3d_bf16(cp.kv->data_ptr(), D, 2 * Hk, Tk, D, (int64_t)(2 * Hk) * D, 64, 1, ABN);
+    tv = tk;
+    a.Sk = cp.Sk; a.k_head = 0; a.v_head = Hk;
+    a.off0 = cp.off0; a.off1 = cp.off1; a.split = cp.split;
+  } else {
+    tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, ABN);
+    tk = tq;
+    a.Sk = S; a.k_head = Hq; a.v_head = Hq + Hk;
+    a.off0 = 0; a.off1 = 0; a.split = S;
+  }
   a.B = B; a.S = S; a.Hq = Hq; a.Hk = Hk;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.causal = causal ? 1 : 0;
@@ -397,6 +429,7 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
   a.lse = lse.data_ptr<float>();
   a.err = error_flag_ptr();
   a.dbg = dbg;
+  a.head_major = head_major;
   auto kern = attn_fwd_kernel<D, MODE>;
   static bool attr = false;
   if (!attr) {
@@ -404,7 +437,7 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
     attr = true;
   }
   const int grid = B * Hq * ((S + ABM * kTilesPerCta - 1) / (ABM * kTilesPerCta));
-  kern<<<grid, kAttnThreads, L::kBytes, at::cuda::getCurrentCUDAStream()>>>(tq, tv, a);
+  kern<<<grid, kAttnThreads, L::kBytes, at::cuda::getCurrentCUDAStream()>>>(tq, tv, tk, a);
   NQ_CHECK_CUDA(cudaGetLastError());
 }
 
@@ -424,6 +457,33 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qk, torch::Tensor qkv, int64_t
   return {o, lse};
 }
 
+// Context-parallel forward: queries of this rank (qk [B*S, (Hq+Hk)*D], two
+// chunks of rows [0, split) and [split, S) at key positions +off0 / +off1)
+// against gathered keys/values kv [B*Sk, 2*Hk*D]; causal by position.
+std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor qk, torch::Tensor kv, int64_t B, int64_t S, int64_t Sk,
+                                       int64_t Hq, int64_t Hk, int64_t D, int64_t off0, int64_t off1,
+                                       int64_t split, double scale) {
+  check_bf16(qk, "qk"); check_bf16(kv, "kv");
+  TORCH_CHECK(qk.is_contiguous() && kv.is_contiguous(), "attn_fwd_cp: contiguous inputs");
+  TORCH_CHECK(qk.size(1) == (Hq + Hk) * D && kv.size(1) == 2 * Hk * D && kv.size(0) == B * Sk,
+              "attn_fwd_cp: shapes");
+  TORCH_CHECK(split % (ABM * kTilesPerCta) == 0 && S % (ABM * kTilesPerCta) == 0,
+              "attn_fwd_cp: chunk lengths must be multiples of 256");
+  TORCH_CHECK(off0 >= 0 && off1 >= 0 && off0 + split <= Sk && off1 + S - split <= Sk, "attn_fwd_cp: offsets");
+  c10::cuda::CUDAGuard g(qk.device());
+  auto o = torch::empty({B * S, Hq * D}, qk.options());
+  auto lse = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
+  if (B * S == 0) return {o, lse};
+  AttnKV cp;
+  cp.kv = &kv; cp.Sk = static_cast<int>(Sk); cp.off0 = static_cast<int>(off0);
+  cp.off1 = static_cast<int>(off1 - split);  // row i >= split sits at off1 + (i - split)
+  cp.split = static_cast<int>(split);
+  if (D == 128) launch_attn_fwd<128>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, nullptr, 0, cp);
+  else if (D == 64) launch_attn_fwd<64>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, nullptr, 0, cp);
+  else TORCH_CHECK(false, "attn_fwd_cp: head_dim must be 64 or 128");
+  return {o, lse};
+}
+
 // Same as attn_fwd, plus globaltimer stamps of pipeline events of CTA 0
 // (8 slots per key block: load issue, K ready, P0 ready, P1 ready, S0 ready,
 // P0 written, S1 ready, P1 written).  Profiling aid only.
@@ -435,9 +495,11 @@ std::vector<torch::Tensor> attn_fwd_timeline(torch::Tensor qk, torch::Tensor qkv
   auto lse = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
   auto ts = torch::zeros({8192}, qk.options().dtype(torch::kInt64));
   auto* p = reinterpret_cast<unsigned long long*>(ts.data_ptr<int64_t>());
-  if (mode == 1) launch_attn_fwd<128, 1>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
-  else if (mode == 2) launch_attn_fwd<128, 2>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
-  else launch_attn_fwd<128, 0>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p);
+  // mode bit 3: head-major block order (comparison with the default order)
+  const int hm = (mode & 8) ? 1 : 0;
+  if ((mode & 7) == 1) launch_attn_fwd<128, 1>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p, hm);
+  else if ((mode & 7) == 2) launch_attn_fwd<128, 2>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p, hm);
+  else launch_attn_fwd<128, 0>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p, hm);
   return {o, lse, ts};
 }
 

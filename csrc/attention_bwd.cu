@@ -58,6 +58,13 @@ struct AttnBwdArgs {
   __nv_bfloat16* dqkv;  // [T, (Hq+2Hk)*D]: dv written into the v slot
   int* err;
   unsigned long long* dbg;  // optional event timestamps of CTA 0 (profiling aid)
+  // Context parallelism (see AttnArgs in attention.cu): keys/values come from
+  // a gathered [B*Sk, 2*Hk*D] buffer (heads k_head / v_head of the tmK map);
+  // query row i sits at key position i + off0 (i < split) or i + off1; dK and
+  // dV of the gathered keys are written in fp32 to dkv_cp [B*Sk, 2*Hk*D].
+  // Self-attention: Sk = S, offsets 0, dkv_cp null.
+  int Sk, k_head, v_head, off0, off1, split;
+  float* dkv_cp;
 };
 
 #define NQ_BTS(slot)                                                              \
@@ -89,7 +96,7 @@ template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmV,
                     const __grid_constant__ CUtensorMap tmDO, const __grid_constant__ CUtensorMap tmDQ,
-                    const AttnBwdArgs args) {
+                    const __grid_constant__ CUtensorMap tmK, const AttnBwdArgs args) {
   using L = AttnBwdSmem<D>;
   constexpr int KCH = D / 64;
   extern __shared__ uint8_t smem_raw[];
@@ -119,20 +126,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int lane = threadIdx.x & 31;
   int* err = args.err;
   const int S = args.S;
-  const int n_kblk = (S + BKN - 1) / BKN;
-  // Heaviness-major order: under causality low key blocks carry the most
-  // work; all (batch, kv-head) pairs of the heaviest key block go first.
-  const int n_bk = gridDim.x / n_kblk;
-  const int nb = static_cast<int>(blockIdx.x) / n_bk;
-  const int bk = static_cast<int>(blockIdx.x) % n_bk;
+  const int Sk = args.Sk;
+  const int n_kblk = (Sk + BKN - 1) / BKN;
+  // Head-major order: the key blocks of one (batch, kv-head) run side by side
+  // and share its streamed Q / dO / LSE tiles in L2 (measured faster than a
+  // heaviness-major order here); within a head the heaviest (lowest) key
+  // blocks start first.
+  const int nb = static_cast<int>(blockIdx.x) % n_kblk;
+  const int bk = static_cast<int>(blockIdx.x) / n_kblk;
   const int b = bk / args.Hk;
   const int hk = bk - b * args.Hk;
   const int G = args.Hq / args.Hk;
   const int k0 = nb * BKN;
   const int tok0 = b * S;
+  const int ktok0 = b * Sk;
   const int n_mblk = (S + BQM - 1) / BQM;
-  const int mb_begin = args.causal ? (k0 / BQM) : 0;
-  const int iters_per_head = n_mblk - mb_begin;
+  // Query blocks that can see this key block, per query chunk: chunk 0 covers
+  // blocks [0, split/BQM) at offset off0, chunk 1 the rest at offset off1.
+  const int split_mb = (args.split + BQM - 1) / BQM;
+  int b0 = 0, e0 = split_mb, b1 = split_mb, e1 = n_mblk;
+  if (args.causal) {
+    // first block with a query at key position >= k0 (floor division of possibly negative values)
+    const int f0 = k0 - args.off0, f1 = k0 - args.off1;
+    b0 = max(b0, f0 >= 0 ? f0 / BQM : 0);
+    b1 = max(b1, f1 >= 0 ? f1 / BQM : 0);
+  }
+  const int n0 = max(0, e0 - b0), n1 = max(0, e1 - b1);
+  const int iters_per_head = n0 + n1;
   const int n_iter = G * iters_per_head;
 
   if (warp == 0 && lane == 0) {
@@ -155,6 +175,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmDO);
     tma_prefetch_desc(&tmDQ);
+    tma_prefetch_desc(&tmK);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -172,16 +193,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   auto iter_coords = [&](int it, int& hq, int& mb) {
     const int g = it / iters_per_head;
     hq = hk * G + g;
-    mb = mb_begin + (it - g * iters_per_head);
+    const int l = it - g * iters_per_head;
+    mb = (l < n0) ? b0 + l : b1 + (l - n0);
   };
+  auto qoff_of = [&](int q0) { return (q0 < args.split) ? args.off0 : args.off1; };
 
   if (warp == 0) {
     if (elect_one()) {
       mbar_arrive_expect_tx(kv_full, 2 * L::kTile);
 #pragma unroll
       for (int c = 0; c < KCH; ++c) {
-        tma_load_3d(sK + c * 128 * 128, &tmQK, kv_full, c * 64, args.Hq + hk, tok0 + k0);
-        tma_load_3d(sV + c * 128 * 128, &tmV, kv_full, c * 64, args.Hq + args.Hk + hk, tok0 + k0);
+        tma_load_3d(sK + c * 128 * 128, &tmK, kv_full, c * 64, args.k_head + hk, ktok0 + k0);
+        tma_load_3d(sV + c * 128 * 128, &tmV, kv_full, c * 64, args.v_head + hk, ktok0 + k0);
       }
       for (int it = 0; it < n_iter; ++it) {
         int hq, mb;
@@ -308,7 +331,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!mbar_wait(s_full, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       if (threadIdx.x == 128) NQ_BTS(8 * it + 3);
       tc_fence_after();
-      const bool need_mask = (args.causal && k0 + BKN - 1 > q0) || (q0 + BQM > S) || (k0 + BKN > S);
+      const int qoff = qoff_of(q0);
+      const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + BQM > S) || (k0 + BKN > Sk);
       uint32_t us2[2][32], ud2[2][32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -341,7 +365,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int qi = q0 + col0 + c + i;
-            const bool m = (qi >= S) || (kj >= S) || (args.causal && kj > qi);
+            const bool m = (qi >= S) || (kj >= Sk) || (args.causal && kj > qi + qoff);
             p[i] = m ? 0.f : p[i];
             ds[i] = m ? 0.f : ds[i];
           }
@@ -398,9 +422,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ------------------------------------------------------- dK / dV out
     if (ok && n_iter > 0 && mbar_wait(acc_done, 0, err, kErrTimeoutSoftmax)) {
       tc_fence_after();
-      const bool row_ok = kj < S;
-      float* dk = args.dqk + (static_cast<int64_t>(tok0 + kj) * (args.Hq + args.Hk) + args.Hq + hk) * D;
-      __nv_bfloat16* dv = args.dqkv + (static_cast<int64_t>(tok0 + kj) * (args.Hq + 2 * args.Hk) + args.Hq + args.Hk + hk) * D;
+      const bool row_ok = kj < Sk;
+      const bool cp = args.dkv_cp != nullptr;
+      float* dk = cp ? args.dkv_cp + (static_cast<int64_t>(ktok0 + kj) * (2 * args.Hk) + hk) * D
+                     : args.dqk + (static_cast<int64_t>(tok0 + kj) * (args.Hq + args.Hk) + args.Hq + hk) * D;
+      float* dv_cp = cp ? args.dkv_cp + (static_cast<int64_t>(ktok0 + kj) * (2 * args.Hk) + args.Hk + hk) * D
+                        : nullptr;
+      __nv_bfloat16* dv = cp ? nullptr
+                             : args.dqkv + (static_cast<int64_t>(tok0 + kj) * (args.Hq + 2 * args.Hk) + args.Hq + args.Hk + hk) * D;
 #pragma unroll
       for (int c = 0; c < D / 2; c += 32) {
         const int cc = (D / 2) * wg + c;
@@ -413,14 +442,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int i = 0; i < 32; i += 4)
             *reinterpret_cast<float4*>(dk + cc + i) = make_float4(__uint_as_float(uk[i]), __uint_as_float(uk[i + 1]),
                                                                 __uint_as_float(uk[i + 2]), __uint_as_float(uk[i + 3]));
+          if (cp) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 v;
-            v.x = pack_bf16(__uint_as_float(uv[q * 8 + 0]), __uint_as_float(uv[q * 8 + 1]));
-            v.y = pack_bf16(__uint_as_float(uv[q * 8 + 2]), __uint_as_float(uv[q * 8 + 3]));
-            v.z = pack_bf16(__uint_as_float(uv[q * 8 + 4]), __uint_as_float(uv[q * 8 + 5]));
-            v.w = pack_bf16(__uint_as_float(uv[q * 8 + 6]), __uint_as_float(uv[q * 8 + 7]));
-            reinterpret_cast<uint4*>(dv + cc)[q] = v;
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dv_cp + cc + i) = make_float4(__uint_as_float(uv[i]), __uint_as_float(uv[i + 1]),
+                                                                       __uint_as_float(uv[i + 2]), __uint_as_float(uv[i + 3]));
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              v.x = pack_bf16(__uint_as_float(uv[q * 8 + 0]), __uint_as_float(uv[q * 8 + 1]));
+              v.y = pack_bf16(__uint_as_float(uv[q * 8 + 2]), __uint_as_float(uv[q * 8 + 3]));
+              v.z = pack_bf16(__uint_as_float(uv[q * 8 + 4]), __uint_as_float(uv[q * 8 + 5]));
+              v.w = pack_bf16(__uint_as_float(uv[q * 8 + 6]), __uint_as_float(uv[q * 8 + 7]));
+              reinterpret_cast<uint4*>(dv + cc)[q] = v;
+            }
           }
         }
       }
@@ -464,11 +500,17 @@ __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dO, const 
   }
 }
 
+struct AttnBwdKV {           // context parallelism (see AttnBwdArgs)
+  const torch::Tensor* kv = nullptr;
+  torch::Tensor* dkv = nullptr;
+  int Sk = 0, off0 = 0, off1 = 0, split = 0;
+};
+
 template <int D>
 static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tensor& qk, const torch::Tensor& qkv,
                                      const torch::Tensor& O, const torch::Tensor& lse, torch::Tensor& dqkv,
                                      int B, int S, int Hq, int Hk, bool causal, float scale,
-                                     unsigned long long* dbg = nullptr) {
+                                     unsigned long long* dbg = nullptr, const AttnBwdKV& cp = AttnBwdKV()) {
   using L = AttnBwdSmem<D>;
   static_assert(L::kBytes <= 232448, "attention backward shared memory budget");
   const int64_t T = static_cast<int64_t>(B) * S;
@@ -484,10 +526,24 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
     NQ_CHECK_CUDA(cudaGetLastError());
   }
   auto tq = make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, 128);
-  auto tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, 128);
   auto tdo = make_tmap_3d_bf16(dO.data_ptr(), D, Hq, T, D, (int64_t)Hq * D, 64, 1, 128);
   auto tdq = make_tmap_3d_f32(dqk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 32, 1, 128);
+  CUtensorMap tv, tk;
   AttnBwdArgs a;
+  if (cp.kv != nullptr) {
+    const int64_t Tk = static_cast<int64_t>(B) * cp.Sk;
+    tk = make_tmap_3d_bf16(cp.kv->data_ptr(), D, 2 * Hk, Tk, D, (int64_t)(2 * Hk) * D, 64, 1, 128);
+    tv = tk;
+    a.Sk = cp.Sk; a.k_head = 0; a.v_head = Hk;
+    a.off0 = cp.off0; a.off1 = cp.off1; a.split = cp.split;
+    a.dkv_cp = cp.dkv->data_ptr<float>();
+  } else {
+    tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, 128);
+    tk = tq;
+    a.Sk = S; a.k_head = Hq; a.v_head = Hq + Hk;
+    a.off0 = 0; a.off1 = 0; a.split = S;
+    a.dkv_cp = nullptr;
+  }
   a.B = B; a.S = S; a.Hq = Hq; a.Hk = Hk;
   a.scale = scale;
   a.scale_log2 = scale * 1.4426950408889634f;
@@ -504,8 +560,8 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
     NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     attr = true;
   }
-  const int grid = B * Hk * ((S + BKN - 1) / BKN);
-  kern<<<grid, kBwdThreads, L::kBytes, st>>>(tq, tv, tdo, tdq, a);
+  const int grid = B * Hk * ((a.Sk + BKN - 1) / BKN);
+  kern<<<grid, kBwdThreads, L::kBytes, st>>>(tq, tv, tdo, tdq, tk, a);
   NQ_CHECK_CUDA(cudaGetLastError());
   return dqk;
 }
@@ -521,6 +577,33 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qk, torch::Tensor qkv, to
   if (D == 64) return launch_attn_bwd<64>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale);
   TORCH_CHECK(false, "attn_bwd: head_dim must be 64 or 128");
   return torch::Tensor();
+}
+
+// Context-parallel backward (see attn_fwd_cp): returns dq (and an unused dk
+// slot) fp32 [B*S, (Hq+Hk)*D] for the local queries and dkv fp32
+// [B*Sk, 2*Hk*D], this rank's partial gradient of the gathered keys/values.
+std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor dO, torch::Tensor qk, torch::Tensor kv, torch::Tensor O,
+                                       torch::Tensor lse, int64_t B, int64_t S, int64_t Sk, int64_t Hq,
+                                       int64_t Hk, int64_t D, int64_t off0, int64_t off1, int64_t split,
+                                       double scale) {
+  check_bf16(dO, "dO"); check_bf16(qk, "qk"); check_bf16(kv, "kv"); check_bf16(O, "O");
+  TORCH_CHECK(dO.is_contiguous() && O.is_contiguous() && qk.is_contiguous() && kv.is_contiguous(),
+              "attn_bwd_cp: contiguous");
+  TORCH_CHECK(kv.size(0) == B * Sk && kv.size(1) == 2 * Hk * D, "attn_bwd_cp: kv shape");
+  TORCH_CHECK(split % BQM == 0 && S % BQM == 0, "attn_bwd_cp: chunk lengths must be multiples of 128");
+  c10::cuda::CUDAGuard g(qk.device());
+  // key blocks no local query can see keep zero gradients
+  auto dkv = torch::zeros({B * Sk, 2 * Hk * D}, qk.options().dtype(torch::kFloat32));
+  AttnBwdKV cp;
+  cp.kv = &kv; cp.dkv = &dkv; cp.Sk = static_cast<int>(Sk); cp.off0 = static_cast<int>(off0);
+  cp.off1 = static_cast<int>(off1 - split);
+  cp.split = static_cast<int>(split);
+  torch::Tensor dummy_qkv = qk;  // unused V source in this mode
+  torch::Tensor dq;
+  if (D == 128) dq = launch_attn_bwd<128>(dO, qk, qk, O, lse, dummy_qkv, B, S, Hq, Hk, true, (float)scale, nullptr, cp);
+  else if (D == 64) dq = launch_attn_bwd<64>(dO, qk, qk, O, lse, dummy_qkv, B, S, Hq, Hk, true, (float)scale, nullptr, cp);
+  else TORCH_CHECK(false, "attn_bwd_cp: head_dim must be 64 or 128");
+  return {dq, dkv};
 }
 
 // attn_bwd plus globaltimer stamps of CTA 0's pipeline events (8 per

@@ -37,6 +37,11 @@ torch::Tensor attn_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tenso
                        int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
 std::vector<torch::Tensor> attn_bwd_timeline(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
                                              torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
+std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                       int64_t, int64_t, int64_t, int64_t, double);
+std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
+                                       int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                       int64_t, double);
 torch::Tensor decode_attn(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, double);
 // elementwise.cu
 int64_t error_flag_read();
@@ -122,6 +127,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &nq::attn_bwd);
   m.def("attn_fwd_timeline", &nq::attn_fwd_timeline);
   m.def("attn_bwd_timeline", &nq::attn_bwd_timeline);
+  m.def("attn_fwd_cp", &nq::attn_fwd_cp, "context-parallel attention forward (local queries, gathered keys)");
+  m.def("attn_bwd_cp", &nq::attn_bwd_cp, "context-parallel attention backward");
   m.def("decode_attn", &nq::decode_attn);
   m.def("error_flag_read", &nq::error_flag_read);
   m.def("error_flag_clear", &nq::error_flag_clear);

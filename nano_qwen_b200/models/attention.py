@@ -90,7 +90,10 @@ class Attention(nn.Module):
     def _attend_cp(self, qkv, qw, kw, cos, sin, position_ids, B, S, Hq, Hk, D, eps, group):
         """Context-parallel attention: local queries against the group's keys
         (``parallel.context_parallel.cp_attention``); positions are global."""
-        from ..parallel.context_parallel import cp_attention
+        from ..parallel.context_parallel import cp_attention, cp_attention_kernel, kernel_usable
+        if qkv.is_cuda and kernel_usable(S):
+            pos = position_ids.expand(B, S).to(torch.int64)
+            return cp_attention_kernel(qkv, qw, kw, cos, sin, pos, group, Hq, Hk, D, eps)
         q, k, v = qkv.split([Hq * D, Hk * D, Hk * D], dim=-1)
         q = q.reshape(B, S, Hq, D)
         k = k.reshape(B, S, Hk, D)

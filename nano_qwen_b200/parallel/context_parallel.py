@@ -111,6 +111,75 @@ def cp_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: torch.T
     return o.transpose(1, 2)
 
 
+class _CPAttnKernelFn(torch.autograd.Function):
+    """GPU context-parallel attention on the sm_100a kernels.
+
+    Forward: fused QK-norm + RoPE at the local tokens' global positions, k|v of
+    the local tokens gathered over the group into natural position order, then
+    ``attn_fwd_cp``: the rank's two zigzag query chunks against the gathered
+    keys, causal by position, in one launch.  Backward: ``attn_bwd_cp`` gives
+    dq for the local queries and this rank's partial dk|dv for every gathered
+    key; the partials are reduce-scattered back to the keys' owners and the
+    QK-norm/RoPE backward runs locally.
+    """
+
+    @staticmethod
+    def forward(ctx, qkv, q_w, k_w, cos, sin, pos, group, Hq, Hk, D, eps, scale):
+        from ..ops._ext import ext
+        E = ext()
+        B, S, W = qkv.shape
+        cp = dist.get_world_size(group)
+        r = dist.get_rank(group)
+        c = S // 2
+        qkv2 = qkv.reshape(B * S, W).contiguous()
+        qk, rstd = E.qknorm_rope_fwd(qkv2, q_w, k_w, cos, sin, pos.reshape(-1), B, S, Hq, Hk, D, float(eps))
+        kv_loc = torch.cat([qk[:, Hq * D:], qkv2[:, (Hq + Hk) * D:]], dim=1).view(B, S, 2 * Hk * D)
+        kv_all = all_gather_dim(kv_loc.contiguous(), 1, group)          # [B, cp*S] rank-major
+        order = torch.cat([zigzag_indices(S * cp, cp, q, qkv.device) for q in range(cp)])
+        kv_nat = torch.empty_like(kv_all)
+        kv_nat[:, order] = kv_all                                       # natural positions
+        kv_nat = kv_nat.reshape(B * S * cp, 2 * Hk * D).contiguous()
+        off0, off1 = r * c, (2 * cp - 1 - r) * c
+        o, lse = E.attn_fwd_cp(qk, kv_nat, B, S, S * cp, Hq, Hk, D, off0, off1, c, float(scale))
+        ctx.save_for_backward(qkv2, qk, rstd, kv_nat, o, lse, q_w, k_w, cos, sin, pos, order)
+        ctx.meta = (B, S, cp, Hq, Hk, D, float(scale), off0, off1, c)
+        ctx.group = group
+        return o.view(B, S, Hq * D)
+
+    @staticmethod
+    def backward(ctx, do):
+        from ..ops._ext import ext
+        from ..ops.common import grad_buffer
+        E = ext()
+        qkv2, qk, rstd, kv_nat, o, lse, q_w, k_w, cos, sin, pos, order = ctx.saved_tensors
+        B, S, cp, Hq, Hk, D, scale, off0, off1, c = ctx.meta
+        do2 = do.reshape(B * S, Hq * D).to(torch.bfloat16).contiguous()
+        dqk, dkv = E.attn_bwd_cp(do2, qk, kv_nat, o, lse, B, S, S * cp, Hq, Hk, D, off0, off1, c, scale)
+        dkv = dkv.view(B, S * cp, 2 * Hk * D)[:, order]                  # back to rank-major
+        dkv_loc = reduce_scatter_dim(dkv.contiguous(), 1, ctx.group).reshape(B * S, 2 * Hk * D)
+        dqk[:, Hq * D:] = dkv_loc[:, :Hk * D]
+        dqkv = torch.empty_like(qkv2)
+        dqkv[:, (Hq + Hk) * D:] = dkv_loc[:, Hk * D:].to(dqkv.dtype)
+        dqw = grad_buffer(q_w) if (q_w is not None and q_w.requires_grad) else None
+        dkw = grad_buffer(k_w) if (k_w is not None and k_w.requires_grad) else None
+        E.qknorm_rope_bwd(dqk, qkv2, q_w, k_w, rstd, cos, sin, pos.reshape(-1), dqkv, dqw, dkw,
+                          B, S, Hq, Hk, D)
+        return (dqkv.view(B, S, -1),) + (None,) * 11
+
+
+def cp_attention_kernel(qkv, q_w, k_w, cos, sin, pos, group, Hq, Hk, D, eps, scale=None):
+    """qkv [B, S_local, (Hq+2Hk)*D] of this rank's zigzag tokens at global
+    positions ``pos`` -> attention output [B, S_local, Hq*D] (CUDA)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    return _CPAttnKernelFn.apply(qkv, q_w, k_w, cos, sin, pos.contiguous(), group, Hq, Hk, D, eps,
+                                 scale)
+
+
+def kernel_usable(S_local: int) -> bool:
+    """The CP attention kernels tile query chunks of 256 rows."""
+    return torch.cuda.is_available() and S_local % 512 == 0
+
+
 def apply_context_parallel(model: nn.Module, cp_group, cp_ranks=None) -> nn.Module:
     """Mark a Qwen3Model (or the LM of a VL model) for context parallelism."""
     from ..models.attention import Attention

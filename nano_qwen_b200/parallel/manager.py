@@ -39,6 +39,10 @@ class ParallelConfig:
     reshard_after_forward: bool = True
     sequence_parallel: bool = True
     pp_microbatches: int = 4
+    # None: the peer-memory fused kernels when usable (CUDA, symmetric memory),
+    # False: NCCL collectives
+    tp_fused: Optional[bool] = None
+    ep_fused: Optional[bool] = None
 
 
 def grid_coords(rank: int, tp: int, cp: int, dp: int, pp: int) -> Dict[str, int]:
@@ -140,10 +144,11 @@ class ParallelismManager:
         c = self.config
         if c.tp_size > 1:
             from .tensor_parallel import apply_tensor_parallel
-            apply_tensor_parallel(model, self.groups["tp"], sequence_parallel=c.sequence_parallel)
+            apply_tensor_parallel(model, self.groups["tp"], sequence_parallel=c.sequence_parallel,
+                                  fused=c.tp_fused)
         if c.ep_size > 1:
             from .expert_parallel import apply_expert_parallel
-            apply_expert_parallel(model, self.groups["ep"])
+            apply_expert_parallel(model, self.groups["ep"], fused=c.ep_fused)
         if c.cp_size > 1:
             from .context_parallel import apply_context_parallel
             apply_context_parallel(model, self.groups["cp"], self.ranks["cp"])

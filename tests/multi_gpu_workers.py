@@ -204,3 +204,51 @@ def ep_fused_worker(rank, world, port):
             assert err < 2e-2, (fused, n, err)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def cp_kernel_worker(rank, world, port):
+    """Context parallelism on the attention kernels (2 ranks, zigzag) against
+    the single-GPU model on the full sequence: loss and gradients."""
+    init(rank, world, port)
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.parallel.context_parallel import apply_context_parallel
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    from nano_qwen_b200.config import ModelConfig
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=128, intermediate_size=512, vocab_size=4096,
+                      max_position_embeddings=2048, tie_word_embeddings=True)
+    grp = dist.new_group(list(range(world)))
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, cfg.vocab_size, (1, 2048), generator=g).cuda()
+
+    def build(cp):
+        torch.manual_seed(0)
+        m = Qwen3Model(cfg).cuda()
+        with torch.no_grad():
+            for n, p in m.named_parameters():
+                if p.ndim >= 2:
+                    p.normal_(0.0, 0.05)
+        if cp:
+            apply_context_parallel(m, grp)
+        attach_param_store(m)
+        return m
+
+    ref = build(False)
+    o = ref(ids, labels=ids)
+    o["loss"].backward()
+    cpm = build(True)
+    oc = cpm(ids, labels=ids)
+    oc["loss"].backward()
+    torch.cuda.synchronize()
+    assert ext().error_flag_read() == 0, "kernel error word set"
+    assert abs(float(oc["loss"]) - float(o["loss"])) < 1e-2 * float(o["loss"]), (float(oc["loss"]), float(o["loss"]))
+    rp = dict(ref.named_parameters())
+    for n, p in cpm.named_parameters():
+        gsum = p.grad.float().clone()
+        dist.all_reduce(gsum, group=grp)  # replicated parameters: partial sums over the sequence chunks
+        gr = rp[n].grad.float()
+        err = ((gsum - gr).norm() / (gr.norm() + 1e-12)).item()
+        assert err < 5e-2, (n, err)
+    dist.barrier()
+    dist.destroy_process_group()

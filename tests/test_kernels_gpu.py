@@ -364,3 +364,42 @@ def test_moe_ffn_matches_loop(E):
     d2 = L.WeightRef(Wd.bfloat16().float().cpu(), torch.zeros_like(Wd).cpu(), [Wd.cpu()])
     ref = _moe_ffn_cpu(x.float().cpu(), w.cpu(), idx.cpu(), g2, d2, Ex, I, None)
     assert rel_err(out.cpu(), ref) < 2e-2
+
+
+# ------------------------------------------------- context-parallel attention
+@pytest.mark.parametrize("rank", [0, 1])
+def test_attention_cp_kernels_match_reference(E, rank):
+    """attn_fwd_cp / attn_bwd_cp for one rank of a cp=2 zigzag split, against
+    fp32 attention of that rank's queries over all keys (causal by position)."""
+    torch.manual_seed(20 + rank)
+    B, S_full, Hq, Hk, D, cp = 1, 2048, 4, 2, 128, 2
+    c = S_full // (2 * cp)
+    pos = torch.cat([torch.arange(rank * c, (rank + 1) * c),
+                     torch.arange((2 * cp - 1 - rank) * c, (2 * cp - rank) * c)]).to(DEV)
+    S = pos.numel()
+    q = (torch.randn(B, S, Hq, D, device=DEV) * 0.5).bfloat16()
+    k = (torch.randn(B, S_full, Hk, D, device=DEV) * 0.5).bfloat16()
+    v = torch.randn(B, S_full, Hk, D, device=DEV).bfloat16()
+    scale = 1.0 / math.sqrt(D)
+    qk = torch.cat([q.reshape(B * S, Hq * D), torch.zeros(B * S, Hk * D, device=DEV).bfloat16()], 1).contiguous()
+    kv = torch.cat([k.reshape(B * S_full, Hk * D), v.reshape(B * S_full, Hk * D)], 1).contiguous()
+    o, lse = E.attn_fwd_cp(qk, kv, B, S, S_full, Hq, Hk, D, rank * c, (2 * cp - 1 - rank) * c, c, scale)
+    # reference
+    qf = q.float().requires_grad_(True)
+    kf = k.float().requires_grad_(True)
+    vf = v.float().requires_grad_(True)
+    g = Hq // Hk
+    s = torch.einsum("bqhd,bkhd->bhqk", qf, kf.repeat_interleave(g, 2)) * scale
+    mask = torch.arange(S_full, device=DEV)[None, :] > pos[:, None]
+    s = s.masked_fill(mask, float("-inf"))
+    p = torch.softmax(s, -1)
+    ref = torch.einsum("bhqk,bkhd->bqhd", p, vf.repeat_interleave(g, 2))
+    assert rel_err(o.view(B, S, Hq, D), ref) < 2e-2
+    do = torch.randn(B, S, Hq, D, device=DEV).bfloat16()
+    ref.backward(do.float())
+    dqk, dkv = E.attn_bwd_cp(do.reshape(B * S, Hq * D).contiguous(), qk, kv, o, lse, B, S, S_full, Hq, Hk, D,
+                             rank * c, (2 * cp - 1 - rank) * c, c, scale)
+    assert rel_err(dqk[:, :Hq * D].view(B, S, Hq, D), qf.grad) < 3e-2
+    assert rel_err(dkv[:, :Hk * D].view(B, S_full, Hk, D), kf.grad) < 3e-2
+    assert rel_err(dkv[:, Hk * D:].view(B, S_full, Hk, D), vf.grad) < 3e-2
+    assert E.error_flag_read() == 0

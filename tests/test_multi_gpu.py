@@ -37,3 +37,9 @@ def test_fused_tensor_parallel_matches_single_gpu():
 def test_fused_expert_parallel_matches_single_gpu():
     import multi_gpu_workers as W
     mp.spawn(W.ep_fused_worker, args=(2, _port()), nprocs=2, join=True)
+
+
+@needs2
+def test_context_parallel_kernels_match_single_gpu():
+    import multi_gpu_workers as W
+    mp.spawn(W.cp_kernel_worker, args=(2, _port()), nprocs=2, join=True)
