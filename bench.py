@@ -79,6 +79,12 @@ CONFIGS = {
                            num_key_value_heads=8, head_dim=128, intermediate_size=6144,
                            vocab_size=151936, max_position_embeddings=4096, rope_theta=1e6,
                            qk_norm=True, tie_word_embeddings=True), 4, 4096, "tp"),
+    # long context: Qwen3-1.7B shape, one 32768-token sequence split over the ranks by
+    # context parallelism (zigzag), strong scaling
+    "qwen3-1.7b-cp32k": (dict(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16,
+                              num_key_value_heads=8, head_dim=128, intermediate_size=6144,
+                              vocab_size=151936, max_position_embeddings=32768, rope_theta=1e6,
+                              qk_norm=True, tie_word_embeddings=True), 1, 32768, "cp"),
     # Qwen3-8B shape, tensor + sequence parallel over all ranks,
     # global batch 8 x 8192 (the same tokens on every rank: strong scaling)
     "qwen3-8b-tp": (dict(hidden_size=4096, num_hidden_layers=36, num_attention_heads=32,
@@ -279,17 +285,18 @@ def run_ours(args, world, rank, local):
             "scheduler": {"type": "cosine", "warmup_steps": 100, "total_steps": 100000},
             "distributed": {"fsdp_enabled": True}}
     pm = None
-    if par in ("tp", "ep") and world > 1:
+    if par in ("tp", "ep", "cp") and world > 1:
         from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
         fused = None if args.comm == "fused" else False
         pm = ParallelismManager(ParallelConfig(tp_size=world if par == "tp" else 1,
                                                ep_size=world if par == "ep" else 1,
+                                               cp_size=world if par == "cp" else 1,
                                                tp_fused=fused, ep_fused=fused))
         model = pm.apply_parallelism(model)
     eng = TrainEngine(model, tcfg, dev, dp_mode=args.dp_mode if world > 1 else None, parallel=pm)
     del model
     # tensor parallelism: every rank sees the same global batch
-    seed_rank = 0 if par == "tp" else rank
+    seed_rank = 0 if par in ("tp", "cp") else rank
     inputs = synthetic_batches(4, B, S, cfg.vocab_size, dev, seed=1234 + seed_rank)
 
     def step(ids):
@@ -433,6 +440,8 @@ def parallel_label(par, world, impl, mode):
     if par == "tp":
         return f"tp{world}+sp (" + ("all-gather / reduce-scatter fused into the norm and GEMM kernels over peer memory"
                                     if mode == "tp-fused" else "NCCL collectives") + ")"
+    if par == "cp":
+        return f"cp{world} (zigzag; K/V exchange by P2P stores consumed by the attention kernels)"
     if par == "ep":
         return f"ep{world} x dp{world} (" + ("dispatch/combine kernels over peer memory" if mode == "ep-fused"
                                              else "NCCL all-to-all dispatch/combine") + ")"
@@ -448,6 +457,12 @@ def main():
         print(json.dumps({"error": "launch N>1 with torch.distributed.run"}))
         return 2
     mk, B, S, par = CONFIGS[args.config]
+    if args.impl == "reference" and par == "cp" and world > 1:
+        maybe_init_pg(world, local)
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference never wires context "
+                              "parallelism (RingAttention is unused, distributed/context_parallel.py)"}))
+        return 0
     try:
         if args.impl == "reference":
             maybe_init_pg(world, local)
@@ -458,7 +473,7 @@ def main():
         if rank == 0:
             print(json.dumps({"impl": args.impl, "unavailable": str(e)}))
         return 0
-    tokens_per_step = B * S * (1 if par == "tp" else world)
+    tokens_per_step = B * S * (1 if par in ("tp", "cp") else world)
     value = tokens_per_step / (ms / 1e3)
     fpt = flops_per_token(mk, S)
     mfu = value * fpt / (measured_peak() * world)
@@ -471,13 +486,13 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "scaling": "strong" if par == "tp" else "weak",
+        "scaling": "strong" if par in ("tp", "cp") else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic uniform-random token ids, random-init weights",
         "config": {"model": f"{args.config} (Qwen3-1.7B shape: L28 h2048 16Q/8KV hd128 I6144 V151936 tied)"
                    if args.config == "qwen3-1.7b" else args.config,
-                   "global_batch": B * (1 if par == "tp" else world), "seq_len": S,
+                   "global_batch": B * (1 if par in ("tp", "cp") else world), "seq_len": S,
                    "parallelism": parallel_label(par, world, args.impl, extra.get("dp_mode")),
                    "l2": "no flush: per-step working set (weights + activations) >> 126 MB L2"},
         "mfu": round(mfu, 4),

@@ -21,7 +21,7 @@
 // TMEM: S/P tile 0 cols [0,128), tile 1 [128,256), O tile 0 [256,256+D),
 // O tile 1 [384,384+D).  Outputs bf16 O [T, Hq*D] and fp32 LSE [B, Hq, S].
 #include "common.cuh"
-#include "sm100.cuh"
+#include "peer.cuh"
 #include "tmap.h"
 
 namespace nq {
@@ -57,6 +57,12 @@ struct AttnArgs {
   // i < split, else i + off1 (context parallelism: a rank's two zigzag chunks
   // against the gathered keys).  Self-attention: Sk = S, offsets 0.
   int Sk, k_head, v_head, off0, off1, split;
+  // Peer-memory K/V gather (context parallelism): before loading the key block
+  // at position p, wait until kv_flags[owner(p)] reaches kv_seq, where
+  // owner(p) = zigzag owner of chunk p / cp_c among cp_world ranks.  null: no wait.
+  const unsigned* kv_flags;
+  unsigned kv_seq;
+  int cp_c, cp_world;
 };
 
 #define NQ_TS(slot)                                                         \
@@ -184,10 +190,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
           tma_load_3d(sQ + t * L::kQBytes + c * ABM * 128, &tmQK, q_full, c * 64, h, tok0 + q0 + t * ABM);
+      int waited = -1;
       for (int j = 0; j < n_kblk && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&kv_empty[st], ph ^ 1, err, kErrTimeoutProducer)) { ok = false; break; }
+        if (args.kv_flags != nullptr) {
+          const int chunk = (j * ABN) / args.cp_c;
+          const int owner = chunk < args.cp_world ? chunk : 2 * args.cp_world - 1 - chunk;
+          if (owner != waited) {
+            if (!wait_flag(args.kv_flags + owner, args.kv_seq, err)) { ok = false; break; }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            waited = owner;
+          }
+        }
         NQ_TS(8 * j + 0);
         mbar_arrive_expect_tx(&k_full[st], L::kKVBytes);
 #pragma unroll
@@ -398,6 +414,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 struct AttnKV {
   const torch::Tensor* kv = nullptr;
   int Sk = 0, off0 = 0, off1 = 0, split = 0;
+  const unsigned* kv_flags = nullptr;
+  unsigned kv_seq = 0;
+  int cp_c = 1, cp_world = 1;
 };
 
 template <int D, int MODE = 0>
@@ -416,7 +435,9 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
     tv = tk;
     a.Sk = cp.Sk; a.k_head = 0; a.v_head = Hk;
     a.off0 = cp.off0; a.off1 = cp.off1; a.split = cp.split;
+    a.kv_flags = cp.kv_flags; a.kv_seq = cp.kv_seq; a.cp_c = cp.cp_c; a.cp_world = cp.cp_world;
   } else {
+    a.kv_flags = nullptr; a.kv_seq = 0; a.cp_c = 1; a.cp_world = 1;
     tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, ABN);
     tk = tq;
     a.Sk = S; a.k_head = Hq; a.v_head = Hq + Hk;
@@ -462,7 +483,8 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qk, torch::Tensor qkv, int64_t
 // against gathered keys/values kv [B*Sk, 2*Hk*D]; causal by position.
 std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor qk, torch::Tensor kv, int64_t B, int64_t S, int64_t Sk,
                                        int64_t Hq, int64_t Hk, int64_t D, int64_t off0, int64_t off1,
-                                       int64_t split, double scale) {
+                                       int64_t split, double scale, int64_t kv_flags, int64_t kv_seq,
+                                       int64_t cp_world) {
   check_bf16(qk, "qk"); check_bf16(kv, "kv");
   TORCH_CHECK(qk.is_contiguous() && kv.is_contiguous(), "attn_fwd_cp: contiguous inputs");
   TORCH_CHECK(qk.size(1) == (Hq + Hk) * D && kv.size(1) == 2 * Hk * D && kv.size(0) == B * Sk,
@@ -478,6 +500,14 @@ std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor qk, torch::Tensor kv, int64
   cp.kv = &kv; cp.Sk = static_cast<int>(Sk); cp.off0 = static_cast<int>(off0);
   cp.off1 = static_cast<int>(off1 - split);  // row i >= split sits at off1 + (i - split)
   cp.split = static_cast<int>(split);
+  if (kv_flags != 0) {
+    TORCH_CHECK(cp_world >= 1 && cp_world <= 8 && Sk % (2 * cp_world) == 0 && (Sk / (2 * cp_world)) % ABN == 0,
+                "attn_fwd_cp: zigzag chunks must be multiples of the key block");
+    cp.kv_flags = reinterpret_cast<const unsigned*>(kv_flags);
+    cp.kv_seq = static_cast<unsigned>(kv_seq);
+    cp.cp_world = static_cast<int>(cp_world);
+    cp.cp_c = static_cast<int>(Sk / (2 * cp_world));
+  }
   if (D == 128) launch_attn_fwd<128>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, nullptr, 0, cp);
   else if (D == 64) launch_attn_fwd<64>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, nullptr, 0, cp);
   else TORCH_CHECK(false, "attn_fwd_cp: head_dim must be 64 or 128");

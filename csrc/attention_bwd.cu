@@ -585,7 +585,7 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qk, torch::Tensor qkv, to
 std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor dO, torch::Tensor qk, torch::Tensor kv, torch::Tensor O,
                                        torch::Tensor lse, int64_t B, int64_t S, int64_t Sk, int64_t Hq,
                                        int64_t Hk, int64_t D, int64_t off0, int64_t off1, int64_t split,
-                                       double scale) {
+                                       double scale, c10::optional<torch::Tensor> dkv_out) {
   check_bf16(dO, "dO"); check_bf16(qk, "qk"); check_bf16(kv, "kv"); check_bf16(O, "O");
   TORCH_CHECK(dO.is_contiguous() && O.is_contiguous() && qk.is_contiguous() && kv.is_contiguous(),
               "attn_bwd_cp: contiguous");
@@ -593,7 +593,15 @@ std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor dO, torch::Tensor qk, torch
   TORCH_CHECK(split % BQM == 0 && S % BQM == 0, "attn_bwd_cp: chunk lengths must be multiples of 128");
   c10::cuda::CUDAGuard g(qk.device());
   // key blocks no local query can see keep zero gradients
-  auto dkv = torch::zeros({B * Sk, 2 * Hk * D}, qk.options().dtype(torch::kFloat32));
+  torch::Tensor dkv;
+  if (dkv_out.has_value() && dkv_out->defined()) {
+    dkv = *dkv_out;
+    TORCH_CHECK(dkv.scalar_type() == torch::kFloat32 && dkv.is_contiguous() && dkv.numel() == B * Sk * 2 * Hk * D,
+                "attn_bwd_cp: dkv_out fp32 [B*Sk, 2*Hk*D]");
+    dkv.zero_();
+  } else {
+    dkv = torch::zeros({B * Sk, 2 * Hk * D}, qk.options().dtype(torch::kFloat32));
+  }
   AttnBwdKV cp;
   cp.kv = &kv; cp.dkv = &dkv; cp.Sk = static_cast<int>(Sk); cp.off0 = static_cast<int>(off0);
   cp.off1 = static_cast<int>(off1 - split);

@@ -38,10 +38,17 @@ torch::Tensor attn_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tenso
 std::vector<torch::Tensor> attn_bwd_timeline(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
                                              torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
 std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t,
-                                       int64_t, int64_t, int64_t, int64_t, double);
+                                       int64_t, int64_t, int64_t, int64_t, double, int64_t, int64_t, int64_t);
 std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
                                        int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                                       int64_t, double);
+                                       int64_t, double, c10::optional<torch::Tensor>);
+// cp_comm.cu
+int64_t cp_kv_scatter(std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor, torch::Tensor,
+                      torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, torch::Tensor,
+                      int64_t);
+void cp_signal(std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t, int64_t);
+torch::Tensor cp_dkv_gather(std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor, int64_t, int64_t,
+                            int64_t, int64_t, int64_t);
 torch::Tensor decode_attn(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, double);
 // elementwise.cu
 int64_t error_flag_read();
@@ -129,6 +136,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_timeline", &nq::attn_bwd_timeline);
   m.def("attn_fwd_cp", &nq::attn_fwd_cp, "context-parallel attention forward (local queries, gathered keys)");
   m.def("attn_bwd_cp", &nq::attn_bwd_cp, "context-parallel attention backward");
+  m.def("cp_kv_scatter", &nq::cp_kv_scatter, "store local k|v rows into every CP rank's gathered buffer (P2P)");
+  m.def("cp_signal", &nq::cp_signal);
+  m.def("cp_dkv_gather", &nq::cp_dkv_gather, "sum every CP rank's dk|dv partials of the local tokens (P2P)");
   m.def("decode_attn", &nq::decode_attn);
   m.def("error_flag_read", &nq::error_flag_read);
   m.def("error_flag_clear", &nq::error_flag_clear);

@@ -93,7 +93,8 @@ class Attention(nn.Module):
         from ..parallel.context_parallel import cp_attention, cp_attention_kernel, kernel_usable
         if qkv.is_cuda and kernel_usable(S):
             pos = position_ids.expand(B, S).to(torch.int64)
-            return cp_attention_kernel(qkv, qw, kw, cos, sin, pos, group, Hq, Hk, D, eps)
+            return cp_attention_kernel(qkv, qw, kw, cos, sin, pos, group, Hq, Hk, D, eps,
+                                       layer=self.layer_idx)
         q, k, v = qkv.split([Hq * D, Hk * D, Hk * D], dim=-1)
         q = q.reshape(B, S, Hq, D)
         k = k.reshape(B, S, Hk, D)

@@ -111,6 +111,49 @@ def cp_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pos: torch.T
     return o.transpose(1, 2)
 
 
+class CPComm:
+    """Symmetric buffers and flags of the peer-memory K/V exchange
+    (``csrc/cp_comm.cu``): one gathered k|v buffer per attention layer (kept
+    for the backward) and two ping-pong dk|dv partial buffers."""
+
+    def __init__(self, group, device):
+        from .peer_dp import SymmetricAllocator
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.alloc = SymmetricAllocator(group)
+        self.flags = self.alloc(2 * 8, torch.int32, device)
+        torch.cuda.synchronize()
+        self.p_flags = self.alloc.peer_ptrs(self.flags)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.count = 0
+        self.seq = [0, 0]
+        self.kv = {}
+        self.dkv = {}
+        dist.barrier(group=group)
+
+    def _buf(self, numel, dtype):
+        t = self.alloc(numel, dtype, self.flags.device)
+        torch.cuda.synchronize()
+        return t, self.alloc.peer_ptrs(t)
+
+    def kv_buf(self, layer, numel):
+        key = (layer, numel)
+        if key not in self.kv:  # collective: same order on every rank
+            self.kv[key] = self._buf(numel, torch.bfloat16)
+        return self.kv[key]
+
+    def dkv_buf(self, parity, numel):
+        key = (parity, numel)
+        if key not in self.dkv:
+            self.dkv[key] = self._buf(numel, torch.float32)
+        return self.dkv[key]
+
+    def next(self, ch):
+        self.seq[ch] += 1
+        return self.seq[ch]
+
+
 class _CPAttnKernelFn(torch.autograd.Function):
     """GPU context-parallel attention on the sm_100a kernels.
 
@@ -124,26 +167,40 @@ class _CPAttnKernelFn(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, qkv, q_w, k_w, cos, sin, pos, group, Hq, Hk, D, eps, scale):
+    def forward(ctx, qkv, q_w, k_w, cos, sin, pos, group, Hq, Hk, D, eps, scale, comm, layer):
         from ..ops._ext import ext
         E = ext()
         B, S, W = qkv.shape
         cp = dist.get_world_size(group)
         r = dist.get_rank(group)
         c = S // 2
+        Sk = S * cp
         qkv2 = qkv.reshape(B * S, W).contiguous()
-        qk, rstd = E.qknorm_rope_fwd(qkv2, q_w, k_w, cos, sin, pos.reshape(-1), B, S, Hq, Hk, D, float(eps))
-        kv_loc = torch.cat([qk[:, Hq * D:], qkv2[:, (Hq + Hk) * D:]], dim=1).view(B, S, 2 * Hk * D)
-        kv_all = all_gather_dim(kv_loc.contiguous(), 1, group)          # [B, cp*S] rank-major
-        order = torch.cat([zigzag_indices(S * cp, cp, q, qkv.device) for q in range(cp)])
-        kv_nat = torch.empty_like(kv_all)
-        kv_nat[:, order] = kv_all                                       # natural positions
-        kv_nat = kv_nat.reshape(B * S * cp, 2 * Hk * D).contiguous()
+        pos1 = pos.reshape(-1).contiguous()
+        qk, rstd = E.qknorm_rope_fwd(qkv2, q_w, k_w, cos, sin, pos1, B, S, Hq, Hk, D, float(eps))
+        order = torch.cat([zigzag_indices(Sk, cp, q, qkv.device) for q in range(cp)])
         off0, off1 = r * c, (2 * cp - 1 - r) * c
-        o, lse = E.attn_fwd_cp(qk, kv_nat, B, S, S * cp, Hq, Hk, D, off0, off1, c, float(scale))
-        ctx.save_for_backward(qkv2, qk, rstd, kv_nat, o, lse, q_w, k_w, cos, sin, pos, order)
+        if comm is not None:
+            # every rank stores its rows straight into every rank's gathered buffer;
+            # the attention producer waits per key block for the owner's flag
+            kvb, kv_ptrs = comm.kv_buf(layer, B * Sk * 2 * Hk * D)
+            kv_nat = kvb.view(B * Sk, 2 * Hk * D)
+            seq = comm.next(0)
+            grid = E.cp_kv_scatter(kv_ptrs, comm.p_flags, comm.rank, qk, qkv2, pos1, B, S, Sk, Hq, Hk, D,
+                                   seq, comm.counter, comm.count)
+            comm.count += int(grid)
+            o, lse = E.attn_fwd_cp(qk, kv_nat, B, S, Sk, Hq, Hk, D, off0, off1, c, float(scale),
+                                   comm.flags.data_ptr(), seq, cp)
+        else:
+            kv_loc = torch.cat([qk[:, Hq * D:], qkv2[:, (Hq + Hk) * D:]], dim=1).view(B, S, 2 * Hk * D)
+            kv_all = all_gather_dim(kv_loc.contiguous(), 1, group)      # [B, cp*S] rank-major
+            kv_nat = torch.empty_like(kv_all)
+            kv_nat[:, order] = kv_all                                   # natural positions
+            kv_nat = kv_nat.reshape(B * Sk, 2 * Hk * D).contiguous()
+            o, lse = E.attn_fwd_cp(qk, kv_nat, B, S, Sk, Hq, Hk, D, off0, off1, c, float(scale), 0, 0, cp)
+        ctx.save_for_backward(qkv2, qk, rstd, kv_nat, o, lse, q_w, k_w, cos, sin, pos1, order)
         ctx.meta = (B, S, cp, Hq, Hk, D, float(scale), off0, off1, c)
-        ctx.group = group
+        ctx.group, ctx.comm = group, comm
         return o.view(B, S, Hq * D)
 
     @staticmethod
@@ -154,25 +211,49 @@ class _CPAttnKernelFn(torch.autograd.Function):
         qkv2, qk, rstd, kv_nat, o, lse, q_w, k_w, cos, sin, pos, order = ctx.saved_tensors
         B, S, cp, Hq, Hk, D, scale, off0, off1, c = ctx.meta
         do2 = do.reshape(B * S, Hq * D).to(torch.bfloat16).contiguous()
-        dqk, dkv = E.attn_bwd_cp(do2, qk, kv_nat, o, lse, B, S, S * cp, Hq, Hk, D, off0, off1, c, scale)
-        dkv = dkv.view(B, S * cp, 2 * Hk * D)[:, order]                  # back to rank-major
-        dkv_loc = reduce_scatter_dim(dkv.contiguous(), 1, ctx.group).reshape(B * S, 2 * Hk * D)
+        comm = ctx.comm
+        Sk = S * cp
+        if comm is not None:
+            seq = comm.next(1)
+            dkb, dk_ptrs = comm.dkv_buf(seq % 2, B * Sk * 2 * Hk * D)
+            dqk, _ = E.attn_bwd_cp(do2, qk, kv_nat, o, lse, B, S, Sk, Hq, Hk, D, off0, off1, c, scale, dkb)
+            E.cp_signal(dk_ptrs, comm.p_flags, comm.rank, 1, seq)
+            dkv_loc = E.cp_dkv_gather(dk_ptrs, comm.p_flags, comm.rank, pos, B, S, Sk, 2 * Hk * D, seq)
+        else:
+            dqk, dkv = E.attn_bwd_cp(do2, qk, kv_nat, o, lse, B, S, Sk, Hq, Hk, D, off0, off1, c, scale,
+                                     None)
+            dkv = dkv.view(B, Sk, 2 * Hk * D)[:, order]                  # back to rank-major
+            dkv_loc = reduce_scatter_dim(dkv.contiguous(), 1, ctx.group).reshape(B * S, 2 * Hk * D)
         dqk[:, Hq * D:] = dkv_loc[:, :Hk * D]
         dqkv = torch.empty_like(qkv2)
         dqkv[:, (Hq + Hk) * D:] = dkv_loc[:, Hk * D:].to(dqkv.dtype)
         dqw = grad_buffer(q_w) if (q_w is not None and q_w.requires_grad) else None
         dkw = grad_buffer(k_w) if (k_w is not None and k_w.requires_grad) else None
-        E.qknorm_rope_bwd(dqk, qkv2, q_w, k_w, rstd, cos, sin, pos.reshape(-1), dqkv, dqw, dkw,
+        E.qknorm_rope_bwd(dqk, qkv2, q_w, k_w, rstd, cos, sin, pos, dqkv, dqw, dkw,
                           B, S, Hq, Hk, D)
-        return (dqkv.view(B, S, -1),) + (None,) * 11
+        return (dqkv.view(B, S, -1),) + (None,) * 13
 
 
-def cp_attention_kernel(qkv, q_w, k_w, cos, sin, pos, group, Hq, Hk, D, eps, scale=None):
+_COMMS = {}
+
+
+def cp_comm(group, device):
+    """The peer-memory exchange for ``group`` (None when symmetric memory is
+    unavailable: the NCCL all-gather path is used then)."""
+    from .peer_dp import symmetric_available
+    key = id(group)
+    if key not in _COMMS:
+        _COMMS[key] = CPComm(group, device) if symmetric_available(group) else None
+    return _COMMS[key]
+
+
+def cp_attention_kernel(qkv, q_w, k_w, cos, sin, pos, group, Hq, Hk, D, eps, scale=None, layer=0):
     """qkv [B, S_local, (Hq+2Hk)*D] of this rank's zigzag tokens at global
     positions ``pos`` -> attention output [B, S_local, Hq*D] (CUDA)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    comm = cp_comm(group, qkv.device)
     return _CPAttnKernelFn.apply(qkv, q_w, k_w, cos, sin, pos.contiguous(), group, Hq, Hk, D, eps,
-                                 scale)
+                                 scale, comm, layer)
 
 
 def kernel_usable(S_local: int) -> bool:

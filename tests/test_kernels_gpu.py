@@ -383,7 +383,7 @@ def test_attention_cp_kernels_match_reference(E, rank):
     scale = 1.0 / math.sqrt(D)
     qk = torch.cat([q.reshape(B * S, Hq * D), torch.zeros(B * S, Hk * D, device=DEV).bfloat16()], 1).contiguous()
     kv = torch.cat([k.reshape(B * S_full, Hk * D), v.reshape(B * S_full, Hk * D)], 1).contiguous()
-    o, lse = E.attn_fwd_cp(qk, kv, B, S, S_full, Hq, Hk, D, rank * c, (2 * cp - 1 - rank) * c, c, scale)
+    o, lse = E.attn_fwd_cp(qk, kv, B, S, S_full, Hq, Hk, D, rank * c, (2 * cp - 1 - rank) * c, c, scale, 0, 0, cp)
     # reference
     qf = q.float().requires_grad_(True)
     kf = k.float().requires_grad_(True)
@@ -398,7 +398,7 @@ def test_attention_cp_kernels_match_reference(E, rank):
     do = torch.randn(B, S, Hq, D, device=DEV).bfloat16()
     ref.backward(do.float())
     dqk, dkv = E.attn_bwd_cp(do.reshape(B * S, Hq * D).contiguous(), qk, kv, o, lse, B, S, S_full, Hq, Hk, D,
-                             rank * c, (2 * cp - 1 - rank) * c, c, scale)
+                             rank * c, (2 * cp - 1 - rank) * c, c, scale, None)
     assert rel_err(dqk[:, :Hq * D].view(B, S, Hq, D), qf.grad) < 3e-2
     assert rel_err(dkv[:, :Hk * D].view(B, S_full, Hk, D), kf.grad) < 3e-2
     assert rel_err(dkv[:, Hk * D:].view(B, S_full, Hk, D), vf.grad) < 3e-2
