@@ -22,6 +22,30 @@ from .optimizer import attach_param_store, build_optimizer
 from .scheduler import build_scheduler
 
 
+def set_global_batch_balance(model: nn.Module, group) -> int:
+    """Route every MoE layer's routing fractions f_i through an all-reduce over
+    the data-parallel group, so the load-balancing loss is the global-batch
+    one (E * sum_i f_i p_i with f_i counted over every rank's tokens; the
+    probabilities p_i and the gradient stay local).  The reference describes
+    this balancing but never wires it (reference: model/moe.py:201-249).
+    Returns the number of MoE layers configured."""
+    import torch.distributed as dist
+    from ..models.moe import MoELayer
+
+    def stats(counts, n):
+        t = torch.cat([counts.detach().float().reshape(-1),
+                       torch.full((1,), float(n), device=counts.device)])
+        dist.all_reduce(t, group=group)
+        return t[:-1], t[-1]
+
+    k = 0
+    for m in model.modules():
+        if isinstance(m, MoELayer):
+            m.global_stats_fn = stats
+            k += 1
+    return k
+
+
 class TrainEngine:
     """``parallel``: an optional ``ParallelismManager`` whose model has already
     been through ``apply_parallelism``; its groups then drive the gradient
@@ -65,6 +89,9 @@ class TrainEngine:
         if self.dp is not None:
             self.dp.broadcast_params(0)
         self._dups = self._duplicated_params()
+        moe_cfg = training_config.get("moe", {}) or {}
+        if world > 1 and moe_cfg.get("global_batch_balance", True):
+            set_global_batch_balance(self.model, dp_group)
         opt = training_config.get("optimizer", {}) or {}
         self.optimizer = build_optimizer(
             self.model, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),

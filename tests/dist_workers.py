@@ -278,3 +278,39 @@ def tp_checkpoint_worker(rank, world, port, tmp):
     b = e2.train_step([{"input_ids": ids, "labels": ids}])
     assert torch.allclose(a["loss"], b["loss"])
     dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ global-batch MoE balance
+def global_balance_worker(rank, world, port):
+    init(rank, world, port)
+    from nano_qwen_b200 import ops
+    from nano_qwen_b200.training.engine import set_global_batch_balance
+    cfg = tiny_cfg(moe=True)
+    ids = batch(cfg, 2 * world, 16)
+    m = build(cfg)
+    n = set_global_batch_balance(m, None)
+    assert n == cfg.num_hidden_layers
+    out = m(ids[2 * rank:2 * rank + 2], labels=ids[2 * rank:2 * rank + 2])
+    # oracle: f from every rank's routing counts, p from this rank's tokens
+    ref = build(cfg)
+    moe = ref.layers[0].feed_forward
+    h = ref.embed(ids)
+    resid, xn = ops.add_rms_norm(h, None, ref.layers[0].input_layernorm.weight, cfg.rms_norm_eps)
+    a = ref.layers[0].attention(xn)
+    resid, xn = ops.add_rms_norm(resid, a, ref.layers[0].post_attention_layernorm.weight, cfg.rms_norm_eps)
+    x = xn.reshape(2 * world, 16, -1)
+    w_all, idx_all, counts_all, ps_all = moe.router(x.reshape(-1, x.shape[-1]))
+    mine = x[2 * rank:2 * rank + 2].reshape(-1, x.shape[-1])
+    _, _, counts_loc, ps_loc = moe.router(mine)
+    N = mine.shape[0]
+    expect = ops.aux_loss_from_stats(counts_loc, ps_loc, N, moe.top_k, moe.num_experts,
+                                     counts_all, N * world)
+    # recompute layer 0's aux of the balanced model on this rank's tokens
+    h2 = m.embed(ids[2 * rank:2 * rank + 2])
+    r2, x2 = ops.add_rms_norm(h2, None, m.layers[0].input_layernorm.weight, cfg.rms_norm_eps)
+    a2 = m.layers[0].attention(x2)
+    r2, x2 = ops.add_rms_norm(r2, a2, m.layers[0].post_attention_layernorm.weight, cfg.rms_norm_eps)
+    _, aux0 = m.layers[0].feed_forward(x2)
+    assert torch.allclose(aux0, expect, rtol=1e-5, atol=1e-6), (float(aux0), float(expect))
+    assert torch.isfinite(out["loss"])
+    dist.destroy_process_group()

@@ -56,3 +56,7 @@ def test_heartbeat_detects_silent_rank():
 
 def test_tensor_parallel_checkpoint_roundtrip(tmp_path):
     _run(W.tp_checkpoint_worker, 2, str(tmp_path))
+
+
+def test_global_batch_moe_balance():
+    _run(W.global_balance_worker, 2)
