@@ -103,6 +103,8 @@ def parse():
     p.add_argument("--config", default="qwen3-1.7b", choices=sorted(CONFIGS))
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--overlap", action="store_true",
+                   help="ours, dp p2p: reduce-scatter per block during the backward instead of after it")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="ours, tp/ep configs: peer-memory fused kernels or NCCL collectives")
     p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate"],
@@ -283,7 +285,7 @@ def run_ours(args, world, rank, local):
         model = Qwen3Model(cfg)
     tcfg = {"optimizer": {"lr": 3e-4, "weight_decay": 0.1, "grad_clip": 1.0},
             "scheduler": {"type": "cosine", "warmup_steps": 100, "total_steps": 100000},
-            "distributed": {"fsdp_enabled": True}}
+            "distributed": {"fsdp_enabled": True, "overlap_grad_reduce": args.overlap}}
     pm = None
     if par in ("tp", "ep", "cp") and world > 1:
         from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager

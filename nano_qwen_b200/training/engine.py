@@ -81,7 +81,11 @@ class TrainEngine:
         if world > 1 and alloc is not None:
             from ..parallel.peer_dp import PeerDataParallel
             self.dp = PeerDataParallel(self.store, alloc, group=dp_group)
-            if dist_cfg.get("overlap_grad_reduce", True):
+            # Off by default: the per-block reduce-scatter kernels wait on every
+            # rank's block, and with 4 ranks their spinning CTAs held SMs that the
+            # persistent GEMM / attention grids needed (Qwen3-1.7B dp4: 371 ms/step
+            # overlapped vs 237 ms reduced after the backward; 1 GPU 232 ms).
+            if dist_cfg.get("overlap_grad_reduce", False):
                 self.dp.attach_overlap(self.model)
         else:
             self.dp = (DataParallel(self.store, mode=dp_mode, group=dp_group,

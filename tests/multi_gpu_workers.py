@@ -26,13 +26,14 @@ def _cfg():
                        vocab_size=4096, max_position_embeddings=512, tie_word_embeddings=True)
 
 
-def _engine(mode, group):
+def _engine(mode, group, overlap=False):
     from nano_qwen_b200.models import Qwen3Model
     from nano_qwen_b200.training.engine import TrainEngine
     torch.manual_seed(0)
     dev = torch.device("cuda", torch.cuda.current_device())
     tc = {"optimizer": {"lr": 1e-3, "grad_clip": 0.5},
-          "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+          "scheduler": {"warmup_steps": 0, "total_steps": 10},
+          "distributed": {"overlap_grad_reduce": overlap}}
     return TrainEngine(Qwen3Model(_cfg()), tc, dev, dp_mode=mode, dp_group=group)
 
 
@@ -50,26 +51,30 @@ def peer_dp_worker(rank, world, port):
     p2p = _engine("p2p", None)
     assert hasattr(p2p.dp, "fused_step"), "symmetric memory unavailable"
     nccl = _engine("shard", None)
+    ovl = _engine("p2p", None, overlap=True)  # per-block reduce-scatter during the backward
     log = []
     for _ in range(3):
         r = ref.train_step(full)
         a = p2p.train_step(mine)
         b = nccl.train_step(mine)
-        log.append([float(x[k]) for x in (r, a, b) for k in ("loss", "grad_norm")])
+        c = ovl.train_step(mine)
+        log.append([float(x[k]) for x in (r, a, b, c) for k in ("loss", "grad_norm")])
     torch.cuda.synchronize()
     assert ext().error_flag_read() == 0, "kernel error word set"
-    for x in (a, b):
+    for x in (a, b, c):
         assert abs(float(x["grad_norm"]) - float(r["grad_norm"])) < 1e-3 * float(r["grad_norm"]), \
             f"rank {rank} (loss, norm) ref/p2p/nccl per step: {log}"
     p2p.state_for_save()
+    ovl.state_for_save()
     nccl.state_for_save()
     def rel(a_, b_):
         return ((a_ - b_).norm() / (b_.norm() + 1e-12)).item()
 
-    for (n, p), q, s in zip(ref.model.named_parameters(), p2p.model.parameters(),
-                            nccl.model.parameters()):
-        # the two data-parallel paths reduce the same per-rank gradients
+    for (n, p), q, s, o in zip(ref.model.named_parameters(), p2p.model.parameters(),
+                               nccl.model.parameters(), ovl.model.parameters()):
+        # the data-parallel paths reduce the same per-rank gradients
         assert rel(q, s) < 1e-3, (n, rel(q, s))
+        assert rel(q, o) < 1e-3, (n, rel(q, o))
         # against gradient accumulation in one process the fp32 summation order
         # differs, and Adam's m/sqrt(v) amplifies that on near-zero gradients
         assert rel(q, p) < 2e-3, (n, rel(q, p))
