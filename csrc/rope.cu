@@ -62,6 +62,7 @@ __device__ __forceinline__ void ld_grad(const __nv_bfloat16* p, float (&v)[EPL])
 // Heads processed per inner step: their loads are issued together so each warp
 // keeps several independent row reads in flight.
 constexpr int kRopeUnroll = 4;
+constexpr int kRopeBwdUnroll = 2;  // the backward holds three rows per head in registers
 
 template <int D>
 __global__ void __launch_bounds__(256) qknorm_rope_fwd_kernel(
@@ -123,7 +124,7 @@ __global__ void __launch_bounds__(256) qknorm_rope_fwd_kernel(
 }
 
 template <int D, typename TG>
-__global__ void __launch_bounds__(256) qknorm_rope_bwd_kernel(
+__global__ void __launch_bounds__(256, (D <= 128 ? 3 : 1)) qknorm_rope_bwd_kernel(
     const TG* __restrict__ dqk, const __nv_bfloat16* __restrict__ qkv,
     const float* __restrict__ qw, const float* __restrict__ kw, const float* __restrict__ rstd,
     const float* __restrict__ cosT, const float* __restrict__ sinT,
@@ -152,10 +153,10 @@ __global__ void __launch_bounds__(256) qknorm_rope_bwd_kernel(
     const TG* gsrc = dqk + static_cast<int64_t>(t) * Hqk * D + e0;
     const __nv_bfloat16* xsrc = qkv + static_cast<int64_t>(t) * W + e0;
     __nv_bfloat16* dst = dqkv + static_cast<int64_t>(t) * W + e0;
-    for (int h0 = 0; h0 < Hqk; h0 += kRopeUnroll) {
-      float g[kRopeUnroll][EPL], x[kRopeUnroll][EPL], rr[kRopeUnroll];
+    for (int h0 = 0; h0 < Hqk; h0 += kRopeBwdUnroll) {
+      float g[kRopeBwdUnroll][EPL], x[kRopeBwdUnroll][EPL], rr[kRopeBwdUnroll];
 #pragma unroll
-      for (int u = 0; u < kRopeUnroll; ++u) {
+      for (int u = 0; u < kRopeBwdUnroll; ++u) {
         if (h0 + u < Hqk) {
           ld_grad<EPL>(gsrc + (h0 + u) * D, g[u]);
           if (norm) {
@@ -165,7 +166,7 @@ __global__ void __launch_bounds__(256) qknorm_rope_bwd_kernel(
         }
       }
 #pragma unroll
-      for (int u = 0; u < kRopeUnroll; ++u) {
+      for (int u = 0; u < kRopeBwdUnroll; ++u) {
         const int h = h0 + u;
         if (h >= Hqk) break;
         float dn[EPL];
@@ -289,12 +290,12 @@ void qknorm_rope_bwd(torch::Tensor dqk, torch::Tensor qkv, c10::optional<torch::
   auto st = at::cuda::getCurrentCUDAStream();
   auto dqkc = dqk.contiguous();
   if (dqkc.scalar_type() == torch::kFloat32) {
-    NQ_D_DISPATCH(D, qknorm_rope_bwd_kernel<DD, float><<<rope_grid(T, 4), 256, 0, st>>>(
+    NQ_D_DISPATCH(D, qknorm_rope_bwd_kernel<DD, float><<<rope_grid(T, 3), 256, 0, st>>>(
         dqkc.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
         opt_f32(qw), opt_f32(kw), rstd.data_ptr<float>(), cc.data_ptr<float>(), sc.data_ptr<float>(),
         pp, reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dq, dk, T, S, Hq, Hk));
   } else {
-    NQ_D_DISPATCH(D, qknorm_rope_bwd_kernel<DD, __nv_bfloat16><<<rope_grid(T, 4), 256, 0, st>>>(
+    NQ_D_DISPATCH(D, qknorm_rope_bwd_kernel<DD, __nv_bfloat16><<<rope_grid(T, 3), 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(dqkc.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),
         opt_f32(qw), opt_f32(kw), rstd.data_ptr<float>(), cc.data_ptr<float>(), sc.data_ptr<float>(),
         pp, reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dq, dk, T, S, Hq, Hk));
