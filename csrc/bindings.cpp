@@ -7,6 +7,7 @@ namespace nq {
 // gemm.cu
 torch::Tensor gemm_nt(torch::Tensor A, torch::Tensor B);
 void gemm_nt_out(torch::Tensor A, torch::Tensor B, torch::Tensor C);
+std::vector<torch::Tensor> gemm_nt_swiglu(torch::Tensor A, torch::Tensor B);
 torch::Tensor gemm_nn(torch::Tensor A, torch::Tensor B);
 void gemm_nn_out(torch::Tensor A, torch::Tensor B, torch::Tensor C);
 void gemm_tn_acc(torch::Tensor A, torch::Tensor B, torch::Tensor C);
@@ -116,6 +117,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_qwen_b200 sm_100a kernels";
   m.def("gemm_nt", &nq::gemm_nt, "C = A @ B^T (bf16, tcgen05)");
   m.def("gemm_nt_out", &nq::gemm_nt_out);
+  m.def("gemm_nt_swiglu", &nq::gemm_nt_swiglu, "gu = A @ [gate; up]^T, h = silu(g) * u (one GEMM)");
   m.def("gemm_nn", &nq::gemm_nn, "C = A @ B (bf16, tcgen05)");
   m.def("gemm_nn_out", &nq::gemm_nn_out);
   m.def("gemm_tn_acc", &nq::gemm_tn_acc, "C(fp32) += A^T @ B (tcgen05)");

@@ -24,7 +24,13 @@ constexpr int kGemmThreads = 192;
 constexpr int kMaxGroups = 256;
 
 enum GroupMode : int { kGroupNone = 0, kGroupM = 1, kGroupK = 2 };
-enum EpiMode : int { kEpiBF16 = 0, kEpiAccF32 = 1 };
+// kEpiSwiGLU: B = [gate; up] rows [2I, K]; tile n covers gate rows
+// [128n, 128n+128) and the matching up rows (two 128-row TMA boxes stacked in
+// the B stage), so one accumulator holds g and u of the same 128 intermediate
+// columns.  The epilogue stores gu = [g | u] (bf16, kept for the backward) and
+// h = silu(g) * u computed from the bf16-rounded g, u (what a separate SwiGLU
+// pass over gu would produce).
+enum EpiMode : int { kEpiBF16 = 0, kEpiAccF32 = 1, kEpiSwiGLU = 2 };
 
 struct GemmArgs {
   int M, N, K;
@@ -36,6 +42,8 @@ struct GemmArgs {
   int64_t c_group_stride;   // group K: elements between the groups' outputs
   int b_group_rows;         // group M: rows of B per group in the tensor map's row space
   int* err;
+  __nv_bfloat16* H;          // kEpiSwiGLU: h [M, N/2]
+  int64_t ldh;
   // Tensor-parallel all-gather consumer (peer.cuh protocol): before loading the
   // first A tile of an m-tile, wait until ag_flags[row owner] reaches ag_seq.
   const unsigned* ag_flags;  // null: no wait
@@ -194,7 +202,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int j = 0; j < GBM / 64; ++j) tma_load_2d(sA + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0);
           }
-          if (!B_MN) {
+          if (EPI == kEpiSwiGLU) {
+            tma_load_2d(sB, &tmB, &full[stage], k0, n0 / 2);                         // gate rows
+            tma_load_2d(sB + 128 * GBK * 2, &tmB, &full[stage], k0, args.N / 2 + n0 / 2);  // up rows
+          } else if (!B_MN) {
             tma_load_2d(sB, &tmB, &full[stage], k0, b_row_off + n0);
           } else {
 #pragma unroll
@@ -268,7 +279,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m_limit = (args.group_mode == kGroupM) ? s_off[args.num_groups] : args.M;
       const bool row_ok = row < m_limit;
       const bool has_acc = ke > kb;
-      if (has_acc) {
+      if (EPI == kEpiSwiGLU) {
+        const int I = args.N >> 1;
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t rg[32], ru[32];
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + c;
+          tmem_ld32(taddr, rg);
+          tmem_ld32(taddr + BN / 2, ru);
+          tmem_wait_ld();
+          const int jc = n0 / 2 + c;
+          if (!row_ok || jc >= I) continue;
+          __nv_bfloat16* G = reinterpret_cast<__nv_bfloat16*>(args.C) + static_cast<int64_t>(row) * args.ldc + jc;
+          __nv_bfloat16* Hp = args.H + static_cast<int64_t>(row) * args.ldh + jc;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float g[8], u[8], h[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              g[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[q * 8 + e])));
+              u[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[q * 8 + e])));
+              const float sg = 1.f / (1.f + __expf(-g[e]));
+              h[e] = g[e] * sg * u[e];
+            }
+            reinterpret_cast<uint4*>(G)[q] = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]),
+                                                        pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
+            reinterpret_cast<uint4*>(G + I)[q] = make_uint4(pack_bf16(u[0], u[1]), pack_bf16(u[2], u[3]),
+                                                            pack_bf16(u[4], u[5]), pack_bf16(u[6], u[7]));
+            reinterpret_cast<uint4*>(Hp)[q] = make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]),
+                                                         pack_bf16(h[4], h[5]), pack_bf16(h[6], h[7]));
+          }
+        }
+      } else if (has_acc) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -390,6 +432,28 @@ torch::Tensor gemm_nt(torch::Tensor A, torch::Tensor B) {
   auto C = torch::empty({A.size(0), B.size(0)}, A.options());
   gemm_nt_out(A, B, C);
   return C;
+}
+
+// gu[M, 2I] = A[M,K] @ [gate; up]^T and h[M, I] = silu(gu[:, :I]) * gu[:, I:]
+// in one GEMM (kEpiSwiGLU).  I must be a multiple of 128.
+std::vector<torch::Tensor> gemm_nt_swiglu(torch::Tensor A, torch::Tensor B) {
+  check_bf16(A, "A"); check_bf16(B, "B");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "gemm_nt_swiglu: shape mismatch");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_nt_swiglu: inner dim must be contiguous");
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(N % kBN == 0 && K > 0, "gemm_nt_swiglu: [gate; up] rows must be a multiple of 256, K > 0");
+  auto gu = torch::empty({M, N}, A.options());
+  auto h = torch::empty({M, N / 2}, A.options());
+  if (M == 0) return {gu, h};
+  c10::cuda::CUDAGuard g(A.device());
+  auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, GBM);
+  auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, 128);
+  auto a = base_args(M, N, K, gu.data_ptr(), gu.stride(0));
+  a.H = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
+  a.ldh = N / 2;
+  launch_gemm<kBN, kStages, false, false, kEpiSwiGLU>(ta, tb, a, cdiv(M, GBM) * (N / kBN),
+                                                      at::cuda::getCurrentCUDAStream());
+  return {gu, h};
 }
 
 // C[M,N] (bf16) = A[M,K] @ B[K,N]

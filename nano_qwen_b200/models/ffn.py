@@ -1,7 +1,8 @@
 """SwiGLU feed-forward network (reference: model/ffn.py:16-34).
 
 The gate and up weights are one contiguous [2I, H] fusion group: one GEMM
-produces [g | u], one kernel applies SiLU-gating, one GEMM projects down.
+produces [g | u] and, on CUDA, applies the SiLU gating in its epilogue; one
+GEMM projects down.
 """
 
 from __future__ import annotations
@@ -25,6 +26,11 @@ class SwiGLU(nn.Module):
         return [["gate_proj.weight", "up_proj.weight"]]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda and getattr(self.gate_proj, "tp_mode", None) is None and self.gate_proj.bias is None:
+            wref = ops.weight_ref([self.gate_proj.weight, self.up_proj.weight], x.dtype)
+            if ops.linear_swiglu_supported(x, wref):
+                h = ops.linear_swiglu(x, wref)
+                return fused_linear(h, [self.down_proj], x.dtype)
         gu = fused_linear(x, [self.gate_proj, self.up_proj], x.dtype)
         h = ops.swiglu_packed(gu)
         return fused_linear(h, [self.down_proj], x.dtype)

@@ -13,7 +13,7 @@ from .attention import attention_core, decode_attention, full_attention, rope_qk
 from .embedding import embedding
 from .linear import WeightRef, dense, linear, weight_ref
 from .loss import linear_cross_entropy, token_logprobs
-from .mlp import swiglu_packed
+from .mlp import linear_swiglu, linear_swiglu_supported, swiglu_packed
 from .moe import aux_loss_from_stats, moe_ffn, route
 from .norm import add_rms_norm, rms_norm
 from .vision import gelu, layer_norm, patchify
@@ -21,6 +21,6 @@ from .vision import gelu, layer_norm, patchify
 __all__ = [
     "reference", "native_available", "ext", "attention_core", "decode_attention",
     "full_attention", "rope_qk", "embedding", "WeightRef", "linear", "weight_ref",
-    "linear_cross_entropy", "token_logprobs", "swiglu_packed", "aux_loss_from_stats",
+    "linear_cross_entropy", "token_logprobs", "swiglu_packed", "linear_swiglu", "linear_swiglu_supported", "aux_loss_from_stats",
     "moe_ffn", "route", "add_rms_norm", "rms_norm", "gelu", "layer_norm", "patchify",
 ]

@@ -104,29 +104,33 @@ class _LinearFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         (x2,) = ctx.saved_tensors
-        wref: WeightRef = ctx.wref
-        w = wref.compute
-        dy2 = dy.reshape(-1, dy.shape[-1])
-        if not dy2.is_contiguous():
-            dy2 = dy2.contiguous()
-        dx = None
-        if dy.is_cuda:
-            E = ext()
-            if ctx.needs_input_grad[0]:
-                dx = E.gemm_nn(dy2, w).view(ctx.in_shape)
-            if wref.requires_grad:
-                if wref.grad is not None:
-                    E.gemm_tn_acc(dy2, x2, wref.grad)
-                else:
-                    dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
-                    E.gemm_tn_acc(dy2, x2, dw)
-                    wref.accumulate(dw)
-        else:
-            if ctx.needs_input_grad[0]:
-                dx = (dy2 @ w).view(ctx.in_shape)
-            if wref.requires_grad:
-                wref.accumulate(dy2.t().to(torch.float32) @ x2.to(torch.float32))
-        return (dx, None) + (None,) * len(wref.anchors)
+        dx = linear_backward(dy.reshape(-1, dy.shape[-1]), x2, ctx.wref, ctx.needs_input_grad[0], ctx.in_shape)
+        return (dx, None) + (None,) * len(ctx.wref.anchors)
+
+
+def linear_backward(dy2: torch.Tensor, x2: torch.Tensor, wref: WeightRef, need_dx: bool, in_shape):
+    """dx = dy W (if ``need_dx``) and W.grad += dy^T x for y = x W^T."""
+    w = wref.compute
+    if not dy2.is_contiguous():
+        dy2 = dy2.contiguous()
+    dx = None
+    if dy2.is_cuda:
+        E = ext()
+        if need_dx:
+            dx = E.gemm_nn(dy2, w).view(in_shape)
+        if wref.requires_grad:
+            if wref.grad is not None:
+                E.gemm_tn_acc(dy2, x2, wref.grad)
+            else:
+                dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+                E.gemm_tn_acc(dy2, x2, dw)
+                wref.accumulate(dw)
+    else:
+        if need_dx:
+            dx = (dy2 @ w).view(in_shape)
+        if wref.requires_grad:
+            wref.accumulate(dy2.t().to(torch.float32) @ x2.to(torch.float32))
+    return dx
 
 
 class _DenseFn(torch.autograd.Function):

@@ -49,6 +49,12 @@ def cases(T: int, H: int, Hq: int, Hk: int, D: int, I: int, B: int, S: int) -> D
         return (lambda: E.gemm_nt(a, w)), 2.0 * T * H * 2 * I, None
     out["gemm_nt"] = gemm_nt
 
+    def gemm_nt_swiglu():
+        x = torch.randn(T, H, device=dev).bfloat16()
+        w = (torch.randn(2 * I, H, device=dev) / math.sqrt(H)).bfloat16()
+        return (lambda: E.gemm_nt_swiglu(x, w)), 2.0 * T * H * 2 * I, None
+    out["gemm_nt_swiglu"] = gemm_nt_swiglu
+
     def gemm_nn():
         dy = torch.randn(T, 2 * I, device=dev).bfloat16()
         w = torch.randn(2 * I, H, device=dev).bfloat16()

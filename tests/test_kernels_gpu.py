@@ -38,6 +38,22 @@ def test_gemm_nt(E, M, N, K):
     assert rel_err(C, ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,I,K", [(128, 128, 64), (200, 256, 72), (1000, 384, 1032), (4096, 6144, 2048)])
+def test_gemm_nt_swiglu(E, M, I, K):
+    """GEMM with the SwiGLU epilogue: gu equals the plain GEMM bit for bit and
+    h equals the separate SwiGLU kernel on that gu, and both match fp32."""
+    torch.manual_seed(3)
+    A = (torch.randn(M, K, device=DEV) * 0.5).bfloat16()
+    W = (torch.randn(2 * I, K, device=DEV) / math.sqrt(K)).bfloat16()
+    gu, h = E.gemm_nt_swiglu(A, W)
+    assert torch.equal(gu, E.gemm_nt(A, W))
+    assert torch.equal(h, E.swiglu_fwd(gu))
+    ref = A.float() @ W.float().t()
+    assert rel_err(gu, ref) < 1e-2
+    g, u = ref.chunk(2, -1)
+    assert rel_err(h, torch.nn.functional.silu(g) * u) < 1e-2
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (200, 136, 72), (1000, 520, 1032)])
 def test_gemm_nn(E, M, N, K):
     torch.manual_seed(1)
