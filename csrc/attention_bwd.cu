@@ -23,6 +23,12 @@
 // prefetches the next iteration's lse / delta.  The fp32 dq buffer is zeroed by
 // the pre-pass kernel, which also computes delta = rowsum(dO * O).
 // Outputs: dq|dk fp32 [T, (Hq+Hk)*D]; dv bf16 written into the v slot of dqkv.
+//
+// That serial schedule is kept for head_dim 64.  head_dim 128 runs
+// attn_bwd_pp_kernel (below): 64-query iterations alternate between the two
+// warpgroups, each with its own S^T / dP^T region in TMEM, so the tensor pipe
+// works on one warpgroup's iteration while the other computes P^T / dS^T
+// (4 x 4096 tokens, 16/8 heads: 1159 -> 1067 us on B200).
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -317,7 +323,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int wg = (warp - 4) >> 2;     // column half
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane: key row (P/dS phase) or query row (dQ phase)
-    const int tid = (warp - 4) * 32 + lane - wg * 128;  // 0..127 within the WG
     const int col0 = wg * 64;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int kj = k0 + r;              // this thread's key position
@@ -471,6 +476,423 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// head_dim 128: ping-pong schedule over 64-query iterations.
+//
+// The serial schedule above leaves the tensor pipe idle while the compute
+// warpgroups turn S^T / dP^T into P^T / dS^T (about 60% of an iteration on
+// B200).  Here warpgroup w owns iterations it with it % 2 == w and its own
+// TMEM region: S^T[w] (128 keys x 64 queries) and dP^T[w] (then dQ^T[w] =
+// K^T dS^T, 128 head dims x 64 queries) in columns [128w, 128w + 128); dK and
+// dV keep columns [256, 512).  The MMA warp issues S^T/dP^T of iteration it+1
+// before it waits for iteration it's P^T/dS^T, so one warpgroup's exp / dS
+// work runs while the tensor pipe serves the other.  Q/dO stream through a
+// 4-deep ring of 64-row tiles; dQ^T is staged (fp32, 128B-swizzled, query
+// rows) in the iteration's Q/dO stage and added into the fp32 dq buffer with
+// TMA bulk reductions by warp 2.  Warp 3 prefetches lse / delta per warpgroup.
+constexpr int PBQ = 64;    // queries per iteration
+constexpr int PNS = 4;     // Q/dO ring depth
+
+struct AttnBwdPPSmem {
+  static constexpr int kKV = 128 * 128 * 2;    // K or V tile: 2 regions of 128 rows x 128 B
+  static constexpr int kQT = PBQ * 128 * 2;    // Q or dO tile: 2 regions of 64 rows x 128 B
+  static constexpr int kDS = 128 * PBQ * 2;    // dS^T tile: 128 key rows x 128 B
+  static constexpr int kKOff = 0;
+  static constexpr int kVOff = kKOff + kKV;
+  static constexpr int kStageOff = kVOff + kKV;             // [PNS] x (Q | dO)
+  static constexpr int kDSOff = kStageOff + PNS * 2 * kQT;  // [2]
+  static constexpr int kLseOff = kDSOff + 2 * kDS;          // [2] x (64 lse + 64 delta)
+  static constexpr int kBarOff = kLseOff + 2 * 2 * PBQ * 4;
+  static constexpr int kBytes = kBarOff + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmV,
+                       const __grid_constant__ CUtensorMap tmDO, const __grid_constant__ CUtensorMap tmDQ,
+                       const __grid_constant__ CUtensorMap tmK, const AttnBwdArgs args) {
+  using L = AttnBwdPPSmem;
+  constexpr int D = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + L::kKOff;
+  uint8_t* sV = smem + L::kVOff;
+  auto sQ = [&](int s) { return smem + L::kStageOff + s * 2 * L::kQT; };
+  auto sDO = [&](int s) { return smem + L::kStageOff + s * 2 * L::kQT + L::kQT; };
+  auto sDS = [&](int w) { return smem + L::kDSOff + w * L::kDS; };
+  auto sLse = [&](int w) { return reinterpret_cast<float*>(smem + L::kLseOff) + w * 2 * PBQ; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;    // [PNS]
+  uint64_t* qdo_empty = bars + 5;   // [PNS] this iteration's MMAs are done with Q/dO
+  uint64_t* qdo_rel = bars + 9;     // [PNS] the bulk reduce has read the staged dQ
+  uint64_t* staged = bars + 13;     // [PNS] dQ staged in the stage (4 warps)
+  uint64_t* s_full = bars + 17;     // [2] S^T[w], dP^T[w] in TMEM
+  uint64_t* pds_ready = bars + 19;  // [2] P^T[w] in TMEM, dS^T[w] in SMEM (4 warps)
+  uint64_t* dq_full = bars + 21;    // [2] dQ^T[w] in TMEM
+  uint64_t* dq_free = bars + 23;    // [2] dQ^T[w] drained (4 warps)
+  uint64_t* lse_rdy = bars + 25;    // [2]
+  uint64_t* acc_done = bars + 27;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* err = args.err;
+  const int S = args.S;
+  const int Sk = args.Sk;
+  const int n_kblk = (Sk + BKN - 1) / BKN;
+  const int nb = static_cast<int>(blockIdx.x) % n_kblk;
+  const int bk = static_cast<int>(blockIdx.x) / n_kblk;
+  const int b = bk / args.Hk;
+  const int hk = bk - b * args.Hk;
+  const int G = args.Hq / args.Hk;
+  const int k0 = nb * BKN;
+  const int tok0 = b * S;
+  const int ktok0 = b * Sk;
+  const int n_mblk = (S + PBQ - 1) / PBQ;
+  const int split_mb = (args.split + PBQ - 1) / PBQ;
+  int b0 = 0, e0 = split_mb, b1 = split_mb, e1 = n_mblk;
+  if (args.causal) {
+    const int f0 = k0 - args.off0, f1 = k0 - args.off1;
+    b0 = max(b0, f0 >= 0 ? f0 / PBQ : 0);
+    b1 = max(b1, f1 >= 0 ? f1 / PBQ : 0);
+  }
+  const int n0 = max(0, e0 - b0), n1 = max(0, e1 - b1);
+  const int iters_per_head = n0 + n1;
+  const int n_iter = G * iters_per_head;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < PNS; ++s) {
+      mbar_init(&qdo_full[s], 1);
+      mbar_init(&qdo_empty[s], 1);
+      mbar_init(&qdo_rel[s], 1);
+      mbar_init(&staged[s], 4);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&s_full[w], 1);
+      mbar_init(&pds_ready[w], 4);
+      mbar_init(&dq_full[w], 1);
+      mbar_init(&dq_free[w], 4);
+      mbar_init(&lse_rdy[w], 1);
+    }
+    mbar_init(acc_done, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
+    tma_prefetch_desc(&tmK);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDK = tmem + 256;
+  const uint32_t tDV = tmem + 384;
+
+  auto iter_coords = [&](int it, int& hq, int& mb) {
+    const int g = it / iters_per_head;
+    hq = hk * G + g;
+    const int l = it - g * iters_per_head;
+    mb = (l < n0) ? b0 + l : b1 + (l - n0);
+  };
+  auto qoff_of = [&](int q0) { return (q0 < args.split) ? args.off0 : args.off1; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * L::kKV);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tma_load_3d(sK + c * 128 * 128, &tmK, kv_full, c * 64, args.k_head + hk, ktok0 + k0);
+        tma_load_3d(sV + c * 128 * 128, &tmV, kv_full, c * 64, args.v_head + hk, ktok0 + k0);
+      }
+      for (int it = 0; it < n_iter; ++it) {
+        int hq, mb;
+        iter_coords(it, hq, mb);
+        const int s = it % PNS;
+        const uint32_t u = static_cast<uint32_t>(it / PNS) & 1;
+        if (!mbar_wait(&qdo_empty[s], u ^ 1, err, kErrTimeoutProducer)) break;
+        if (!mbar_wait(&qdo_rel[s], u ^ 1, err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&qdo_full[s], 2 * L::kQT);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(sQ(s) + c * PBQ * 128, &tmQ, &qdo_full[s], c * 64, hq, tok0 + mb * PBQ);
+          tma_load_3d(sDO(s) + c * PBQ * 128, &tmDO, &qdo_full[s], c * 64, hq, tok0 + mb * PBQ);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t id_s = idesc_bf16(BKN, PBQ, false, false);  // K Q^T, V dO^T (keys x queries)
+      constexpr uint32_t id_kv = idesc_bf16(BKN, D, false, true);    // P^T dO, dS^T Q (keys x head dims)
+      constexpr uint32_t id_q = idesc_bf16(D, PBQ, true, true);      // K^T dS^T (head dims x queries)
+      bool ok = mbar_wait(kv_full, 0, err, kErrTimeoutMma);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      // S^T[w] = K Q^T and dP^T[w] = V dO^T of iteration j (w = j % 2)
+      auto issue_sdp = [&](int j) -> bool {
+        const int w = j & 1, s = j % PNS;
+        if (!mbar_wait(&qdo_full[s], static_cast<uint32_t>(j / PNS) & 1, err, kErrTimeoutMma)) return false;
+        // dP^T[w] is where dQ^T of iteration j-2 waits to be drained
+        if (!mbar_wait(&dq_free[w], static_cast<uint32_t>((j >> 1) & 1) ^ 1, err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        NQ_BTS(8 * j + 0);
+        const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s));
+        const uint32_t tS = tmem + 128 * w, tP = tS + 64;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t oa = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          const uint32_t ob = (kk >> 2) * (PBQ * 128) + (kk & 3) * 32;
+          umma_bf16(tS, sdesc_sw128(aK + oa, 16, 1024), sdesc_sw128(aQ + ob, 16, 1024), id_s, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t oa = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          const uint32_t ob = (kk >> 2) * (PBQ * 128) + (kk & 3) * 32;
+          umma_bf16(tP, sdesc_sw128(aV + oa, 16, 1024), sdesc_sw128(aDO + ob, 16, 1024), id_s, kk > 0);
+        }
+        umma_commit(&s_full[w]);
+        NQ_BTS(8 * j + 1);
+        return true;
+      };
+      if (ok && n_iter > 0) ok = issue_sdp(0);
+      for (int it = 0; it < n_iter && ok; ++it) {
+        const int w = it & 1, s = it % PNS;
+        if (it + 1 < n_iter && !issue_sdp(it + 1)) { ok = false; break; }
+        if (!mbar_wait(&pds_ready[w], static_cast<uint32_t>(it >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        NQ_BTS(8 * it + 2);
+        const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s)), aDS = smem_u32(sDS(w));
+        const uint32_t tS = tmem + 128 * w, tP = tS + 64;
+#pragma unroll
+        for (int kk = 0; kk < PBQ / 16; ++kk) {
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          // dV += P^T dO : A = P^T from TMEM (K = queries), B = dO MN-major
+          umma_bf16_ts(tDV, tS + kk * 8, sdesc_sw128(aDO + kk * 2048, PBQ * 128, 1024), id_kv, acc);
+          // dK += dS^T Q : A = dS^T smem K-major, B = Q MN-major
+          umma_bf16(tDK, sdesc_sw128(aDS + kk * 32, 16, 1024), sdesc_sw128(aQ + kk * 2048, PBQ * 128, 1024),
+                    id_kv, acc);
+        }
+        // dQ^T = K^T dS^T (M = head dims, N = queries, K = keys): A = K read
+        // MN-major, B = dS^T read MN-major; lands over the consumed dP^T[w]
+#pragma unroll
+        for (int kk = 0; kk < BKN / 16; ++kk) {
+          umma_bf16(tP, sdesc_sw128(aK + kk * 2048, 128 * 128, 1024), sdesc_sw128(aDS + kk * 2048, L::kDS, 1024),
+                    id_q, kk > 0);
+        }
+        umma_commit(&dq_full[w]);
+        umma_commit(&qdo_empty[s]);
+      }
+      if (ok) umma_commit(acc_done);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------ dQ bulk-reduce issuer
+    if (elect_one()) {
+      for (int it = 0; it < n_iter; ++it) {
+        int hq, mb;
+        iter_coords(it, hq, mb);
+        const int s = it % PNS;
+        if (!mbar_wait(&staged[s], static_cast<uint32_t>(it / PNS) & 1, err, kErrTimeoutDrain)) break;
+#pragma unroll
+        for (int bx = 0; bx < D / 32; ++bx)
+          tma_reduce_add_3d(&tmDQ, (bx < 2 ? sQ(s) : sDO(s)) + (bx & 1) * (PBQ * 128), 32 * bx, hq, tok0 + mb * PBQ);
+        bulk_commit();
+        bulk_wait_read_all();
+        mbar_arrive(&qdo_rel[s]);
+      }
+      bulk_wait_all();
+    }
+  } else if (warp == 3) {
+    // ------------------------------------- lse / delta prefetch (per iteration)
+    for (int it = 0; it < n_iter; ++it) {
+      int hq, mb;
+      iter_coords(it, hq, mb);
+      const int w = it & 1;
+      // warpgroup w read these values for iteration it-2 before publishing P/dS
+      if (it >= 2 && !mbar_wait(&pds_ready[w], static_cast<uint32_t>((it - 2) >> 1) & 1, err, kErrTimeoutDrain)) break;
+      const int q0 = mb * PBQ;
+      float* lse = sLse(w);
+#pragma unroll
+      for (int e = 0; e < PBQ / 32; ++e) {
+        const int ql = e * 32 + lane;
+        const int q = q0 + ql;
+        const int64_t idx = (static_cast<int64_t>(b) * args.Hq + hq) * S + q;
+        lse[ql] = (q < S) ? args.lse[idx] * 1.4426950408889634f : INFINITY;
+        lse[PBQ + ql] = (q < S) ? args.delta[idx] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&lse_rdy[w]);
+    }
+  } else {
+    // ------------------------------------------------------- compute WGs
+    const int w = (warp - 4) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // TMEM lane: key row (P/dS) or head dim (dQ^T)
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + 128 * w + lane_base, tP = tS + 64;
+    const int kj = k0 + r;
+    const float* lse = sLse(w);
+    const float* dlt = lse + PBQ;
+    uint8_t* ds_tile = sDS(w);
+    bool ok = true;
+    for (int it = w; it < n_iter; it += 2) {
+      int hq, mb;
+      iter_coords(it, hq, mb);
+      const uint32_t ph = static_cast<uint32_t>(it >> 1) & 1;
+      const int s = it % PNS;
+      const int q0 = mb * PBQ;
+      if (!mbar_wait(&lse_rdy[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      if (!mbar_wait(&s_full[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 3);
+      const int qoff = qoff_of(q0);
+      const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + PBQ > S) || (k0 + BKN > Sk);
+      uint32_t us2[2][32], ud2[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld32(tS + 32 * c, us2[c]);
+        tmem_ld32(tP + 32 * c, ud2[c]);
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t* us = us2[c];
+        const uint32_t* ud = ud2[c];
+        float p[32], ds[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(lse + 32 * c + i);
+          const float4 d4 = *reinterpret_cast<const float4*>(dlt + 32 * c + i);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+          const float dl[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float pv = bwd_ex2(fmaf(__uint_as_float(us[i + e]), args.scale_log2, -lv[e]));
+            p[i + e] = pv;
+            ds[i + e] = pv * (__uint_as_float(ud[i + e]) - dl[e]) * args.scale;
+          }
+        }
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int qi = q0 + 32 * c + i;
+            const bool m = (qi >= S) || (kj >= Sk) || (args.causal && kj > qi + qoff);
+            p[i] = m ? 0.f : p[i];
+            ds[i] = m ? 0.f : ds[i];
+          }
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16(p[2 * i], p[2 * i + 1]);
+        // P^T as packed bf16 over S^T[w]: query column q lands in TMEM column q / 2
+        // (this thread's own lane, already loaded, so no cross-thread hazard).
+        tmem_st16(tS + 16 * c, pk);
+        // dS^T row r, query columns [32c, 32c + 32): 128B-swizzled K-major tile
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          const int unit = (32 * c + i) >> 3;
+          uint4 v;
+          v.x = pack_bf16(ds[i + 0], ds[i + 1]);
+          v.y = pack_bf16(ds[i + 2], ds[i + 3]);
+          v.z = pack_bf16(ds[i + 4], ds[i + 5]);
+          v.w = pack_bf16(ds[i + 6], ds[i + 7]);
+          *reinterpret_cast<uint4*>(ds_tile + r * 128 + ((unit ^ (r & 7)) << 4)) = v;
+        }
+      }
+      tmem_wait_st();
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 4);
+      if (lane == 0) mbar_arrive(&pds_ready[w]);
+      // dQ^T drain: thread = head dim r, 64 query columns -> fp32 staging in the
+      // Q/dO stage of this iteration (all of its MMAs are done) as four
+      // 64-row x 32-column 128B-swizzled boxes; the lanes of a warp write one
+      // 128-byte row per store.
+      if (!mbar_wait(&dq_full[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 5);
+      {
+        uint32_t u[2][32];
+        tmem_ld32(tP, u[0]);
+        tmem_ld32(tP + 32, u[1]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_free[w]);
+        uint8_t* box = (quarter < 2 ? sQ(s) : sDO(s)) + (quarter & 1) * (PBQ * 128);
+        const int chunk = lane >> 2, sub = (lane & 3) * 4;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int q = 32 * c + i;
+            *reinterpret_cast<uint32_t*>(box + q * 128 + ((chunk ^ (q & 7)) << 4) + sub) = u[c][i];
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&staged[s]);
+      }
+      if (threadIdx.x == 128) NQ_BTS(8 * it + 6);
+    }
+    // ------------------------------------------------------- dK / dV out
+    if (ok && n_iter > 0 && mbar_wait(acc_done, 0, err, kErrTimeoutSoftmax)) {
+      tc_fence_after();
+      const bool row_ok = kj < Sk;
+      const bool cp = args.dkv_cp != nullptr;
+      float* dk = cp ? args.dkv_cp + (static_cast<int64_t>(ktok0 + kj) * (2 * args.Hk) + hk) * D
+                     : args.dqk + (static_cast<int64_t>(tok0 + kj) * (args.Hq + args.Hk) + args.Hq + hk) * D;
+      float* dv_cp = cp ? args.dkv_cp + (static_cast<int64_t>(ktok0 + kj) * (2 * args.Hk) + args.Hk + hk) * D
+                        : nullptr;
+      __nv_bfloat16* dv = cp ? nullptr
+                             : args.dqkv + (static_cast<int64_t>(tok0 + kj) * (args.Hq + 2 * args.Hk) + args.Hq + args.Hk + hk) * D;
+#pragma unroll
+      for (int c = 0; c < D / 2; c += 32) {
+        const int cc = (D / 2) * w + c;
+        uint32_t uk[32], uv[32];
+        tmem_ld32(tDK + lane_base + cc, uk);
+        tmem_ld32(tDV + lane_base + cc, uv);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dk + cc + i) = make_float4(__uint_as_float(uk[i]), __uint_as_float(uk[i + 1]),
+                                                                __uint_as_float(uk[i + 2]), __uint_as_float(uk[i + 3]));
+          if (cp) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dv_cp + cc + i) = make_float4(__uint_as_float(uv[i]), __uint_as_float(uv[i + 1]),
+                                                                       __uint_as_float(uv[i + 2]), __uint_as_float(uv[i + 3]));
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              v.x = pack_bf16(__uint_as_float(uv[q * 8 + 0]), __uint_as_float(uv[q * 8 + 1]));
+              v.y = pack_bf16(__uint_as_float(uv[q * 8 + 2]), __uint_as_float(uv[q * 8 + 3]));
+              v.z = pack_bf16(__uint_as_float(uv[q * 8 + 4]), __uint_as_float(uv[q * 8 + 5]));
+              v.w = pack_bf16(__uint_as_float(uv[q * 8 + 6]), __uint_as_float(uv[q * 8 + 7]));
+              reinterpret_cast<uint4*>(dv + cc)[q] = v;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // delta[b,h,q] = sum_d dO * O ; also zeroes the dq part of dqk.
 template <int D>
 __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dO, const __nv_bfloat16* __restrict__ O,
@@ -512,7 +934,7 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
                                      int B, int S, int Hq, int Hk, bool causal, float scale,
                                      unsigned long long* dbg = nullptr, const AttnBwdKV& cp = AttnBwdKV()) {
   using L = AttnBwdSmem<D>;
-  static_assert(L::kBytes <= 232448, "attention backward shared memory budget");
+  static_assert(L::kBytes <= 232448 && AttnBwdPPSmem::kBytes <= 232448, "attention backward shared memory budget");
   const int64_t T = static_cast<int64_t>(B) * S;
   auto dqk = torch::empty({T, (int64_t)(Hq + Hk) * D}, qk.options().dtype(torch::kFloat32));
   auto delta = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
@@ -525,9 +947,12 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
         delta.data_ptr<float>(), dqk.data_ptr<float>(), B, S, Hq, Hk);
     NQ_CHECK_CUDA(cudaGetLastError());
   }
-  auto tq = make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, 128);
-  auto tdo = make_tmap_3d_bf16(dO.data_ptr(), D, Hq, T, D, (int64_t)Hq * D, 64, 1, 128);
-  auto tdq = make_tmap_3d_f32(dqk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 32, 1, 128);
+  // head_dim 128 runs the ping-pong kernel on 64-query tiles
+  constexpr bool kPP = (D == 128);
+  const int qrows = kPP ? PBQ : 128;
+  auto tq = make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, qrows);
+  auto tdo = make_tmap_3d_bf16(dO.data_ptr(), D, Hq, T, D, (int64_t)Hq * D, 64, 1, qrows);
+  auto tdq = make_tmap_3d_f32(dqk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 32, 1, qrows);
   CUtensorMap tv, tk;
   AttnBwdArgs a;
   if (cp.kv != nullptr) {
@@ -539,7 +964,7 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
     a.dkv_cp = cp.dkv->data_ptr<float>();
   } else {
     tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, 128);
-    tk = tq;
+    tk = kPP ? make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, 128) : tq;
     a.Sk = S; a.k_head = Hq; a.v_head = Hq + Hk;
     a.off0 = 0; a.off1 = 0; a.split = S;
     a.dkv_cp = nullptr;
@@ -554,14 +979,19 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.err = error_flag_ptr();
   a.dbg = dbg;
-  auto kern = attn_bwd_kernel<D>;
+  auto kern = attn_bwd_pp_kernel;
+  int bytes = AttnBwdPPSmem::kBytes;
+  if constexpr (!kPP) {
+    kern = attn_bwd_kernel<D>;
+    bytes = L::kBytes;
+  }
   static bool attr = false;
   if (!attr) {
-    NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
     attr = true;
   }
   const int grid = B * Hk * ((a.Sk + BKN - 1) / BKN);
-  kern<<<grid, kBwdThreads, L::kBytes, st>>>(tq, tv, tdo, tdq, tk, a);
+  kern<<<grid, kBwdThreads, bytes, st>>>(tq, tv, tdo, tdq, tk, a);
   NQ_CHECK_CUDA(cudaGetLastError());
   return dqk;
 }

@@ -220,7 +220,8 @@ def test_qknorm_rope(E):
 
 @pytest.mark.parametrize("B,S,Hq,Hk,D,causal", [(1, 128, 2, 1, 128, True), (2, 256, 4, 2, 128, True),
                                                 (1, 200, 2, 2, 128, True), (2, 384, 8, 2, 64, False),
-                                                (1, 1024, 2, 1, 128, True)])
+                                                (1, 1024, 2, 1, 128, True), (1, 192, 1, 1, 128, True),
+                                                (2, 384, 4, 2, 128, False)])
 def test_attention_fwd_bwd(E, B, S, Hq, Hk, D, causal):
     from nano_qwen_b200.ops import reference as R
     torch.manual_seed(7)
