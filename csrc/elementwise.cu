@@ -46,7 +46,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfl
     load8(gu + t * 2 * I + I + c, u);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float s = 1.f / (1.f + __expf(-g[i]));
+      const float s = sigmoid_fast(g[i]);
       o[i] = g[i] * s * u[i];
     }
     store8(h + e, o);
@@ -67,7 +67,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, const __
     load8(dh + e, d);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float s = 1.f / (1.f + __expf(-g[i]));
+      const float s = sigmoid_fast(g[i]);
       dg[i] = d[i] * u[i] * s * (1.f + g[i] * (1.f - s));
       du[i] = d[i] * g[i] * s;
     }

@@ -13,6 +13,7 @@
 // -> global) so the epilogue of tile i overlaps the main loop of tile i+1.  One
 // CTA per SM walks the tile list with a grid stride; tiles are rasterised in
 // bands of 8 M-tiles for L2 reuse of B.
+#include "common.cuh"
 #include "peer.cuh"
 #include "tmap.h"
 
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int e = 0; e < 8; ++e) {
               g[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[q * 8 + e])));
               u[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[q * 8 + e])));
-              const float sg = 1.f / (1.f + __expf(-g[e]));
+              const float sg = sigmoid_fast(g[e]);
               h[e] = g[e] * sg * u[e];
             }
             reinterpret_cast<uint4*>(G)[q] = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]),
