@@ -103,6 +103,8 @@ def parse():
     p.add_argument("--config", default="qwen3-1.7b", choices=sorted(CONFIGS))
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--kernel-table", default=None,
+                   help="ours: write per-kernel device time of the profiled extra step (markdown) to this path")
     p.add_argument("--overlap", action="store_true",
                    help="ours, dp p2p: reduce-scatter per block during the backward instead of after it")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
@@ -333,12 +335,35 @@ def count_launches(step_fn, ids):
         step_fn(ids)
         torch.cuda.synchronize()
     ours = total = 0
+    per_kernel = {}
     for ev in prof.events():
         if ev.device_type is not None and str(ev.device_type).endswith("CUDA"):
             total += 1
             if "nq::" in ev.name:
                 ours += 1
+            a = per_kernel.setdefault(ev.name, [0, 0.0])
+            a[0] += 1
+            a[1] += getattr(ev, "device_time_total", 0.0)
+    if KERNEL_TABLE:
+        write_kernel_table(KERNEL_TABLE, per_kernel)
     return {"ours": ours, "all": total}
+
+
+KERNEL_TABLE = None  # --kernel-table PATH (rank 0)
+
+
+def write_kernel_table(path, per_kernel):
+    """Device time per kernel over the profiled (untimed) step, largest first.
+    Profiler timestamps: use the shares, not the absolute step time."""
+    tot = sum(t for _, t in per_kernel.values()) or 1.0
+    with open(path, "w") as f:
+        f.write(f"# one training step, kernel device time total {tot / 1e3:.1f} ms\n")
+        f.write("| kernel | launches | ms | share |\n|---|---|---|---|\n")
+        for name, (n, t) in sorted(per_kernel.items(), key=lambda x: -x[1][1]):
+            if t / tot < 0.001:
+                continue
+            short = name.split("(")[0].replace("void ", "")[:90]
+            f.write(f"| `{short}` | {n} | {t / 1e3:.2f} | {100 * t / tot:.1f}% |\n")
 
 
 def run_e2e_ours(eng, args, B, S, V, dev, rank):
@@ -459,6 +484,8 @@ def main():
         print(json.dumps({"error": "launch N>1 with torch.distributed.run"}))
         return 2
     mk, B, S, par = CONFIGS[args.config]
+    global KERNEL_TABLE
+    KERNEL_TABLE = args.kernel_table if rank == 0 else None
     if args.impl == "reference" and par == "cp" and world > 1:
         maybe_init_pg(world, local)
         if rank == 0:
