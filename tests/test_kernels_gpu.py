@@ -63,7 +63,8 @@ def test_gemm_nn(E, M, N, K):
     assert rel_err(C, A.float() @ B.float()) < 1e-2
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (136, 200, 72), (520, 1000, 1032)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (136, 200, 72), (520, 1000, 1032),
+                                   (4096, 2048, 16384)])
 def test_gemm_tn_acc(E, M, N, K):
     torch.manual_seed(2)
     A = torch.randn(K, M, device=DEV).bfloat16()
