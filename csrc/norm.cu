@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_bwd_kernel(
   for (int row = blockIdx.x; row < T; row += gridDim.x) {
     const int64_t base = static_cast<int64_t>(row) * H;
     const float r = rstd[row];
-    float xh[NCH][8], g[NCH][8];
+    float xh[NCH][8], g[NCH][8], res[NCH][8];
     float dot = 0.f;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_bwd_kernel(
         float hv[8], d[8];
         ld8(h + base + col, hv);
         ld8(dy + base + col, d);
+        // the incoming residual gradient is loaded with the row, before the
+        // block reduction, so each row costs one memory round trip
+        if (dh != nullptr) ld8(dh + base + col, res[c]);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           xh[c][i] = hv[i] * r;
@@ -108,11 +111,9 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_bwd_kernel(
       const int col = (c * kNormThreads + threadIdx.x) * 8;
       if (col < H) {
         float o[8];
-        float res[8];
-        if (dh != nullptr) ld8(dh + base + col, res);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          o[i] = r * (g[c][i] - xh[c][i] * dot) + (dh != nullptr ? res[i] : 0.f);
+          o[i] = r * (g[c][i] - xh[c][i] * dot) + (dh != nullptr ? res[c][i] : 0.f);
         }
         st8(dx + base + col, o);
         if (dx_bf16 != nullptr) st8(dx_bf16 + base + col, o);

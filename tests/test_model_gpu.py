@@ -54,12 +54,13 @@ def _force_routing(cpu_model, gpu_model):
             m.register_forward_hook(force(n))
 
 
-@pytest.mark.parametrize("moe", [False, True])
-def test_loss_and_grads_match_cpu(moe):
+@pytest.mark.parametrize("moe,head_dim", [(False, 64), (True, 64), (False, 128)])
+def test_loss_and_grads_match_cpu(moe, head_dim):
+    """head_dim 128 runs the flagship attention kernels (ping-pong backward)."""
     from nano_qwen_b200.models import Qwen3Model
     from nano_qwen_b200.training.optimizer import attach_param_store
     torch.manual_seed(0)
-    cfg = _cfg(moe)
+    cfg = _cfg(moe, head_dim=head_dim)
     cpu = Qwen3Model(cfg)
     gpu = Qwen3Model(cfg)
     gpu.load_state_dict(cpu.state_dict())
