@@ -905,32 +905,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// delta[b,h,q] = sum_d dO * O ; also zeroes the dq part of dqk.
+// delta[b,h,q] = sum_d dO * O ; also zeroes the dq part of dqk.  D/8 lanes per
+// (token, head) row, 16-byte loads, a shuffle reduction inside the lane group;
+// every lane of a warp runs the same number of iterations (full-mask shuffles).
 template <int D>
 __global__ void attn_bwd_pre_kernel(const __nv_bfloat16* __restrict__ dO, const __nv_bfloat16* __restrict__ O,
                                     float* __restrict__ delta, float* __restrict__ dqk, int B, int S,
                                     int Hq, int Hk) {
-  const int warps = (gridDim.x * blockDim.x) >> 5;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  constexpr int G = D / 8;             // lanes per row
+  constexpr int RPW = 32 / G;          // rows per warp and iteration
   const int lane = threadIdx.x & 31;
+  const int sub = lane % G;
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t items = static_cast<int64_t>(B) * S * Hq;
-  for (int64_t it = gw; it < items; it += warps) {
-    const int64_t t = it / Hq;
-    const int h = static_cast<int>(it - t * Hq);
-    const __nv_bfloat16* a = dO + (t * Hq + h) * D;
-    const __nv_bfloat16* o = O + (t * Hq + h) * D;
+  for (int64_t base = gw * RPW; base < items; base += warps * RPW) {
+    const int64_t it = base + lane / G;
+    const bool ok = it < items;
+    const int64_t t = ok ? it / Hq : 0;
+    const int h = ok ? static_cast<int>(it - t * Hq) : 0;
+    float x[8], y[8];
     float s = 0.f;
-    for (int d = lane * 2; d < D; d += 64) {
-      const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + d));
-      const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(o + d));
-      s += x.x * y.x + x.y * y.y;
+    if (ok) {
+      load8(dO + (t * Hq + h) * D + sub * 8, x);
+      load8(O + (t * Hq + h) * D + sub * 8, y);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += x[i] * y[i];
     }
-    s = warp_sum(s);
-    const int b = static_cast<int>(t / S);
-    const int q = static_cast<int>(t - static_cast<int64_t>(b) * S);
-    if (lane == 0) delta[(static_cast<int64_t>(b) * Hq + h) * S + q] = s;
-    float* dq = dqk + (t * (Hq + Hk) + h) * D;
-    for (int d = lane * 4; d < D; d += 128) *reinterpret_cast<float4*>(dq + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (ok) {
+      const int b = static_cast<int>(t / S);
+      const int q = static_cast<int>(t - static_cast<int64_t>(b) * S);
+      if (sub == 0) delta[(static_cast<int64_t>(b) * Hq + h) * S + q] = s;
+      float4* dq = reinterpret_cast<float4*>(dqk + (t * (Hq + Hk) + h) * D + sub * 8);
+      dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
 }
 
@@ -952,8 +963,9 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
   auto delta = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
   auto st = at::cuda::getCurrentCUDAStream();
   {
-    const int64_t items = T * Hq;
-    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((items + 7) / 8, num_sms() * 8)));
+    const int64_t rows_per_block = 256 / (D / 8);
+    const int64_t blocks = (T * Hq + rows_per_block - 1) / rows_per_block;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, num_sms() * 8)));
     attn_bwd_pre_kernel<D><<<grid, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(dO.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(O.data_ptr()),
         delta.data_ptr<float>(), dqk.data_ptr<float>(), B, S, Hq, Hk);
