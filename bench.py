@@ -336,6 +336,7 @@ def count_launches(step_fn, ids):
         torch.cuda.synchronize()
     ours = total = 0
     per_kernel = {}
+    spans = []
     for ev in prof.events():
         if ev.device_type is not None and str(ev.device_type).endswith("CUDA"):
             total += 1
@@ -344,20 +345,39 @@ def count_launches(step_fn, ids):
             a = per_kernel.setdefault(ev.name, [0, 0.0])
             a[0] += 1
             a[1] += getattr(ev, "device_time_total", 0.0)
+            tr = getattr(ev, "time_range", None)
+            if tr is not None:
+                spans.append((tr.start, tr.end))
     if KERNEL_TABLE:
-        write_kernel_table(KERNEL_TABLE, per_kernel)
+        write_kernel_table(KERNEL_TABLE, per_kernel, spans)
     return {"ours": ours, "all": total}
 
 
 KERNEL_TABLE = None  # --kernel-table PATH (rank 0)
 
 
-def write_kernel_table(path, per_kernel):
-    """Device time per kernel over the profiled (untimed) step, largest first.
-    Profiler timestamps: use the shares, not the absolute step time."""
+def write_kernel_table(path, per_kernel, spans=()):
+    """Device time per kernel over the profiled (untimed) step, largest first,
+    and the device time with no kernel running (union of the kernels'
+    intervals against first start .. last end).  Profiler timestamps: use the
+    shares, not the absolute step time."""
     tot = sum(t for _, t in per_kernel.values()) or 1.0
+    busy = idle = 0.0
+    if spans:
+        spans = sorted(spans)
+        cur_s, cur_e = spans[0]
+        for s0, e0 in spans[1:]:
+            if s0 > cur_e:
+                busy += cur_e - cur_s
+                cur_s, cur_e = s0, e0
+            else:
+                cur_e = max(cur_e, e0)
+        busy += cur_e - cur_s
+        idle = max(e for _, e in spans) - spans[0][0] - busy
     with open(path, "w") as f:
         f.write(f"# one training step, kernel device time total {tot / 1e3:.1f} ms\n")
+        if spans:
+            f.write(f"# device busy {busy / 1e3:.1f} ms, idle between kernels {idle / 1e3:.1f} ms\n")
         f.write("| kernel | launches | ms | share |\n|---|---|---|---|\n")
         for name, (n, t) in sorted(per_kernel.items(), key=lambda x: -x[1][1]):
             if t / tot < 0.001:
