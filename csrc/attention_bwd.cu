@@ -29,7 +29,7 @@
 // warpgroups, each with its own S^T / dP^T region in TMEM, so the tensor pipe
 // works on one warpgroup's iteration while the other computes P^T / dS^T
 // (4 x 4096 tokens, 16/8 heads: 1159 -> 1067 us on B200; 984 us with the
-// grouped heaviest-first block order).
+// grouped heaviest-first block order; 926 us with dQ^T issued ahead of dV/dK).
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -681,6 +681,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         NQ_BTS(8 * it + 2);
         const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s)), aDS = smem_u32(sDS(w));
         const uint32_t tS = tmem + 128 * w, tP = tS + 64;
+        // dQ^T = K^T dS^T (M = head dims, N = queries, K = keys): A = K read
+        // MN-major, B = dS^T read MN-major; lands over the consumed dP^T[w].
+        // Issued first so the warpgroup can drain it while dV / dK run.
+#pragma unroll
+        for (int kk = 0; kk < BKN / 16; ++kk) {
+          umma_bf16(tP, sdesc_sw128(aK + kk * 2048, 128 * 128, 1024), sdesc_sw128(aDS + kk * 2048, L::kDS, 1024),
+                    id_q, kk > 0);
+        }
+        umma_commit(&dq_full[w]);
 #pragma unroll
         for (int kk = 0; kk < PBQ / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
@@ -690,14 +699,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_bf16(tDK, sdesc_sw128(aDS + kk * 32, 16, 1024), sdesc_sw128(aQ + kk * 2048, PBQ * 128, 1024),
                     id_kv, acc);
         }
-        // dQ^T = K^T dS^T (M = head dims, N = queries, K = keys): A = K read
-        // MN-major, B = dS^T read MN-major; lands over the consumed dP^T[w]
-#pragma unroll
-        for (int kk = 0; kk < BKN / 16; ++kk) {
-          umma_bf16(tP, sdesc_sw128(aK + kk * 2048, 128 * 128, 1024), sdesc_sw128(aDS + kk * 2048, L::kDS, 1024),
-                    id_q, kk > 0);
-        }
-        umma_commit(&dq_full[w]);
         umma_commit(&qdo_empty[s]);
       }
       if (ok) umma_commit(acc_done);
@@ -823,9 +824,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (threadIdx.x == 128) NQ_BTS(8 * it + 4);
       if (lane == 0) mbar_arrive(&pds_ready[w]);
       // dQ^T drain: thread = head dim r, 64 query columns -> fp32 staging in the
-      // Q/dO stage of this iteration (all of its MMAs are done) as four
-      // 64-row x 32-column 128B-swizzled boxes; the lanes of a warp write one
-      // 128-byte row per store.
+      // Q/dO stage of this iteration (once its dV / dK MMAs have released the
+      // stage) as four 64-row x 32-column 128B-swizzled boxes; the lanes of a
+      // warp write one 128-byte row per store.
       if (!mbar_wait(&dq_full[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       tc_fence_after();
       if (threadIdx.x == 128) NQ_BTS(8 * it + 5);
@@ -837,6 +838,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&dq_free[w]);
+        // dV / dK of this iteration may still read Q / dO from the stage
+        if (!mbar_wait(&qdo_empty[s], static_cast<uint32_t>(it / PNS) & 1, err, kErrTimeoutSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
         uint8_t* box = (quarter < 2 ? sQ(s) : sDO(s)) + (quarter & 1) * (PBQ * 128);
         const int chunk = lane >> 2, sub = (lane & 3) * 4;
 #pragma unroll
