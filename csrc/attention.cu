@@ -6,20 +6,23 @@
 // GQA is native: q head h reads kv head h / (Hq/Hk).
 //
 // CTA = (batch, q-head, 256 queries) = two 128-row query tiles, 12 warps:
-//   warp 0     : TMA producer: Q0/Q1 once, then K_j / V_j into a 2-stage ring;
-//   warp 1     : MMA issuer (one thread).  Per key block j and tile t it issues
-//                O_t += P_t(j-1) V(j-1)   (A operand P read from TMEM)
-//                S_t  = Q_t K_j^T         (into the same TMEM columns P used)
-//                so the tensor core alternates between the two tiles while the
-//                other tile's softmax runs;
+//   warp 0     : TMA producer: Q0/Q1 once, then 64-key K_j / V_j tiles into a
+//                4-stage ring;
+//   warp 1     : MMA issuer (one thread).  S_t(j) = Q_t K_j^T goes to buffer
+//                j % 2 of tile t; once tile t's softmax published P_t(j) it
+//                issues O_t += P_t(j) V(j) (A operand P read from TMEM) and
+//                then S_t(j+2) into the buffer P_t(j) occupied, so S_t(j+1)
+//                is already in TMEM when the softmax finishes block j and the
+//                tensor core alternates between the two tiles;
 //   warps 4-7  : softmax warpgroup for tile 0, warps 8-11 for tile 1; thread =
 //                query row = TMEM lane.  Reads S (fp32), masks, exponentiates
 //                in the exp2 domain with tree reductions, writes P as packed
 //                bf16 back into TMEM over S, and rescales O in TMEM only when
 //                the running max grew by more than 2^8 (exact: the final O / l
 //                uses the same reference max).
-// TMEM: S/P tile 0 cols [0,128), tile 1 [128,256), O tile 0 [256,256+D),
-// O tile 1 [384,384+D).  Outputs bf16 O [T, Hq*D] and fp32 LSE [B, Hq, S].
+// TMEM: tile t's two S/P buffers at cols [128t, 128t+64) and [128t+64,
+// 128t+128) (64 keys each; P packed bf16 in a buffer's first 32 columns),
+// O tile 0 [256,256+D), O tile 1 [384,384+D).  Outputs bf16 O [T, Hq*D] and fp32 LSE [B, Hq, S].
 #include "common.cuh"
 #include "peer.cuh"
 #include "tmap.h"
@@ -27,7 +30,8 @@
 namespace nq {
 
 constexpr int ABM = 128;        // queries per tile
-constexpr int ABN = 128;        // keys per block
+constexpr int ABN = 64;         // keys per block
+constexpr int NKV = 4;          // K/V ring stages
 constexpr int kTilesPerCta = 2;
 constexpr int kAttnThreads = 384;
 constexpr float kRescaleThresh = 8.0f;  // log2 units
@@ -38,8 +42,8 @@ struct AttnFwdSmem {
   static constexpr int kKVBytes = ABN * D * 2;  // K or V per stage
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kTilesPerCta * kQBytes;
-  static constexpr int kVOff = kKOff + 2 * kKVBytes;
-  static constexpr int kBarOff = kVOff + 2 * kKVBytes;
+  static constexpr int kVOff = kKOff + NKV * kKVBytes;
+  static constexpr int kBarOff = kVOff + NKV * kKVBytes;
   static constexpr int kBytes = kBarOff + 256 + 1024;
 };
 
@@ -120,14 +124,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sV = smem + L::kVOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2] per tile
-  uint64_t* p_full = bars + 9;    // [2] per tile (P written, S consumed)
-  uint64_t* o_done = bars + 11;   // [2] per tile: PV(j) complete
-  uint64_t* turn = bars + 15;     // [2] softmax ping-pong: turn[t] = tile t may exponentiate
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_full = bars + 1;    // [NKV]
+  uint64_t* v_full = bars + 5;    // [NKV]
+  uint64_t* kv_empty = bars + 9;  // [NKV]
+  uint64_t* s_full = bars + 13;   // [tile * 2 + buffer]
+  uint64_t* p_full = bars + 17;   // [2] per tile (P written, S consumed)
+  uint64_t* o_done = bars + 19;   // [2] per tile: PV(j) complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -158,14 +161,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NKV; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&p_full[s], 4);
       mbar_init(&o_done[s], 1);
-      mbar_init(&turn[s], 4);
     }
     fence_barrier_init();
     tma_prefetch_desc(&tmQK);
@@ -192,8 +196,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tma_load_3d(sQ + t * L::kQBytes + c * ABM * 128, &tmQK, q_full, c * 64, h, tok0 + q0 + t * ABM);
       int waited = -1;
       for (int j = 0; j < n_kblk && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % NKV;
+        const uint32_t ph = static_cast<uint32_t>(j / NKV) & 1;
         if (!mbar_wait(&kv_empty[st], ph ^ 1, err, kErrTimeoutProducer)) { ok = false; break; }
         if (args.kv_flags != nullptr) {
           const int chunk = (j * ABN) / args.cp_c;
@@ -222,48 +226,50 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = mbar_wait(q_full, 0, err, kErrTimeoutMma);
       tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ);
-      // iteration j issues, per tile: PV(j-1) then QK(j); after the loop, PV(n-1).
-      for (int j = 0; j <= n_kblk && ok; ++j) {
-        const int st = j & 1;
-        const int pst = (j - 1) & 1;
-        if (j < n_kblk) {
-          if (!mbar_wait(&k_full[st], (j >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
-          NQ_TS(8 * j + 1);
+      // S_t(j) into buffer j % 2 of tile t (after P_t(j-2) was consumed by
+      // PV_t(j-2), issued earlier on this thread: MMAs execute in order).
+      auto issue_qk = [&](int j, int t) -> bool {
+        const int st = j % NKV;
+        if (!mbar_wait(&k_full[st], static_cast<uint32_t>(j / NKV) & 1, err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t tS = tmem + t * 128 + (j & 1) * ABN;
+        const uint32_t k_addr = smem_u32(sK + st * L::kKVBytes);
+        const uint32_t qa = q_addr + t * L::kQBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * (ABM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * (ABN * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        if (j > 0) {
-          if (!mbar_wait(&v_full[pst], ((j - 1) >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
-        }
+        umma_commit(&s_full[t * 2 + (j & 1)]);
+        return true;
+      };
+      for (int j = 0; j < min(2, n_kblk) && ok; ++j) {
+        if (j == 0) NQ_TS(1);
+        for (int t = 0; t < kTilesPerCta && ok; ++t) ok = issue_qk(j, t);
+      }
+      for (int j = 0; j < n_kblk && ok; ++j) {
+        const int st = j % NKV;
+        if (!mbar_wait(&v_full[st], static_cast<uint32_t>(j / NKV) & 1, err, kErrTimeoutMma)) { ok = false; break; }
+        const uint32_t v_addr = smem_u32(sV + st * L::kKVBytes);
 #pragma unroll
         for (int t = 0; t < kTilesPerCta; ++t) {
-          const uint32_t tS = tmem + t * ABN;
+          const uint32_t tP = tmem + t * 128 + (j & 1) * ABN;
           const uint32_t tO = tmem + 256 + t * 128;
-          if (j > 0) {
-            // P_t(j-1) is ready once its softmax finished
-            if (!mbar_wait(&p_full[t], (j - 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
-            NQ_TS(8 * j + 2 + t);
-            tc_fence_after();
-            const uint32_t v_addr = smem_u32(sV + pst * L::kKVBytes);
+          // P_t(j) is ready once its softmax finished
+          if (!mbar_wait(&p_full[t], j & 1, err, kErrTimeoutMma)) { ok = false; break; }
+          NQ_TS(8 * j + 2 + t);
+          tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < ABN / 16; ++kk) {
-              const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, ABN * 128, 1024);
-              umma_bf16_ts(tO, tS + kk * 8, bd, idesc_pv, (j > 1 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(&o_done[t]);
+          for (int kk = 0; kk < ABN / 16; ++kk) {
+            const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, ABN * 128, 1024);
+            umma_bf16_ts(tO, tP + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
           }
-          if (j < n_kblk) {
-            const uint32_t k_addr = smem_u32(sK + st * L::kKVBytes);
-            const uint32_t qa = q_addr + t * L::kQBytes;
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint64_t ad = sdesc_sw128(qa + (kk >> 2) * (ABM * 128) + (kk & 3) * 32, 16, 1024);
-              const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * (ABN * 128) + (kk & 3) * 32, 16, 1024);
-              umma_bf16(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-            }
-            umma_commit(&s_full[t]);
-          }
+          umma_commit(&o_done[t]);
+          if (j + 2 < n_kblk && !issue_qk(j + 2, t)) { ok = false; break; }
         }
         if (!ok) break;
-        if (j > 0) umma_commit(&kv_empty[pst]);  // K(j-1) and V(j-1) no longer read
+        umma_commit(&kv_empty[st]);  // K(j) and V(j) no longer read
       }
     }
   } else if (warp >= 4) {
@@ -273,25 +279,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = quarter * 32 + lane;      // row in tile == TMEM lane
     const int qi = q0 + t * ABM + r;        // query position in the sequence
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tS = tmem + t * ABN + lane_base;
     const uint32_t tO = tmem + 256 + t * 128 + lane_base;
     float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kblk; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, err, kErrTimeoutSoftmax)) { ok = false; break; }
+      if (!mbar_wait(&s_full[t * 2 + (j & 1)], static_cast<uint32_t>(j >> 1) & 1, err, kErrTimeoutSoftmax)) {
+        ok = false;
+        break;
+      }
+      const uint32_t tS = tmem + t * 128 + (j & 1) * ABN + lane_base;
       if (threadIdx.x % 128 == 0) NQ_TS(8 * j + 4 + 2 * t);
       tc_fence_after();
-      // Ping-pong: tile 0 exponentiates block j after tile 1 finished block j-1,
-      // tile 1 after tile 0 finished block j, so the two tiles' MUFU phases
-      // alternate and each overlaps the other tile's MMAs.
-      if (t == 0 ? j > 0 : true) {
-        const uint32_t par = (t == 0) ? ((j - 1) & 1) : (j & 1);
-        if (!mbar_wait(&turn[t], par, err, kErrTimeoutSoftmax)) { ok = false; break; }
-      }
-      uint32_t u[4][32];
+      // The two tiles exponentiate independently: with S double-buffered, a
+      // tile whose next S is ready starts at once (forcing the two tiles'
+      // exponential phases to alternate measured 10% slower).
+      constexpr int NCK = ABN / 32;  // 32-column chunks of a block
+      uint32_t u[NCK][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, u[c]);
+      for (int c = 0; c < NCK; ++c) tmem_ld32(tS + c * 32, u[c]);
       tmem_wait_ld();
       if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 0);
       const int k0 = j * ABN;
@@ -300,7 +306,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // folded into the exponent's FFMA.
       if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < NCK; ++c)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int kj = k0 + c * 32 + i;
@@ -309,7 +315,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < NCK; ++c)
 #pragma unroll
         for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(u[c][i]));
       const float sl2 = args.scale_log2;
@@ -319,11 +325,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float m_new = grow ? mx : m_ref;
       const bool dead = (m_new == -INFINITY);
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      // P overwrites the first 64 columns of this tile's S region as packed bf16
-      // pairs.  PV(j-1) read the previous P before QK(j) wrote S (MMAs of one
-      // issuing thread execute in order), so the columns are free already.
+      // P overwrites the first ABN/2 columns of this buffer as packed bf16
+      // pairs.  PV(j-2) read the buffer's previous P before QK(j) wrote S
+      // (MMAs of one issuing thread execute in order), so they are free.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < NCK; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
@@ -340,7 +346,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float rowsum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&turn[t ^ 1]);
       if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 2);
       // O and the P columns are busy until PV(j-1) of this tile completes.
       if (j > 0) {
@@ -439,7 +444,7 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
   } else {
     a.kv_flags = nullptr; a.kv_seq = 0; a.cp_c = 1; a.cp_world = 1;
     tv = make_tmap_3d_bf16(qkv.data_ptr(), D, Hq + 2 * Hk, T, D, (int64_t)(Hq + 2 * Hk) * D, 64, 1, ABN);
-    tk = tq;
+    tk = make_tmap_3d_bf16(qk.data_ptr(), D, Hq + Hk, T, D, (int64_t)(Hq + Hk) * D, 64, 1, ABN);  // ABN-row boxes
     a.Sk = S; a.k_head = Hq; a.v_head = Hq + Hk;
     a.off0 = 0; a.off1 = 0; a.split = S;
   }
