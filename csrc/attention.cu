@@ -54,8 +54,6 @@ struct AttnArgs {
   __nv_bfloat16* O;  // [T, Hq*D]
   float* lse;        // [B, Hq, S]
   int* err;
-  unsigned long long* dbg;  // optional per-event timestamps of CTA 0 (profiling aid)
-  int head_major;           // 1: blocks of one head adjacent (profiling comparison)
   // Keys/values: rows per batch (Sk), head index of K and V in their tensor
   // maps.  Queries: key-space position of query row i is i + off0 for
   // i < split, else i + off1 (context parallelism: a rank's two zigzag chunks
@@ -68,11 +66,6 @@ struct AttnArgs {
   unsigned kv_seq;
   int cp_c, cp_world;
 };
-
-#define NQ_TS(slot)                                                         \
-  do {                                                                      \
-    if (args.dbg != nullptr && blockIdx.x == 0) args.dbg[(slot)] = globaltimer(); \
-  } while (0)
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -94,24 +87,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, used for a share of the softmax exponentials so the
-// MUFU unit is not the only bottleneck.  x = n + f with n = round(x) obtained by
-// the 1.5*2^23 rounding trick and f in [-0.5, 0.5]; 2^f is a cubic fitted in
-// this repository by iteratively reweighted least squares for minimum max
-// relative error on [-0.5, 0.5] (max relative error 7.5e-5); 2^n is applied by
-// adding n to the exponent field (the low bits of the rounded value hold n).
-// Inputs below -126 are clamped (result ~1e-38, i.e. zero for softmax).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;
-  const float f = x - (t - 12582912.0f);
-  float p = fmaf(0.05517150089f, f, 0.24261096120f);
-  p = fmaf(p, f, 0.69326096773f);
-  p = fmaf(p, f, 0.99992805719f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
-template <int D, int MODE>
+template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmV,
                     const __grid_constant__ CUtensorMap tmK, const AttnArgs args) {
@@ -144,10 +120,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // scheduling by the hardware block scheduler); adjacent blocks are adjacent
   // heads, which share K/V under GQA.
   const int n_bh = gridDim.x / n_mblk;
-  const int mb = args.head_major ? n_mblk - 1 - static_cast<int>(blockIdx.x) % n_mblk
-                                 : n_mblk - 1 - static_cast<int>(blockIdx.x) / n_bh;
-  const int bh = args.head_major ? static_cast<int>(blockIdx.x) / n_mblk
-                                 : static_cast<int>(blockIdx.x) % n_bh;
+  const int mb = n_mblk - 1 - static_cast<int>(blockIdx.x) / n_bh;
+  const int bh = static_cast<int>(blockIdx.x) % n_bh;
   const int b = bh / args.Hq;
   const int h = bh - b * args.Hq;
   const int hk = h / (args.Hq / args.Hk);
@@ -208,7 +182,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             waited = owner;
           }
         }
-        NQ_TS(8 * j + 0);
         mbar_arrive_expect_tx(&k_full[st], L::kKVBytes);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
@@ -245,7 +218,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         return true;
       };
       for (int j = 0; j < min(2, n_kblk) && ok; ++j) {
-        if (j == 0) NQ_TS(1);
         for (int t = 0; t < kTilesPerCta && ok; ++t) ok = issue_qk(j, t);
       }
       for (int j = 0; j < n_kblk && ok; ++j) {
@@ -258,7 +230,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint32_t tO = tmem + 256 + t * 128;
           // P_t(j) is ready once its softmax finished
           if (!mbar_wait(&p_full[t], j & 1, err, kErrTimeoutMma)) { ok = false; break; }
-          NQ_TS(8 * j + 2 + t);
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < ABN / 16; ++kk) {
@@ -289,7 +260,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         break;
       }
       const uint32_t tS = tmem + t * 128 + (j & 1) * ABN + lane_base;
-      if (threadIdx.x % 128 == 0) NQ_TS(8 * j + 4 + 2 * t);
       tc_fence_after();
       // The two tiles exponentiate independently: with S double-buffered, a
       // tile whose next S is ready starts at once (forcing the two tiles'
@@ -299,7 +269,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < NCK; ++c) tmem_ld32(tS + c * 32, u[c]);
       tmem_wait_ld();
-      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 0);
       const int k0 = j * ABN;
       const bool need_mask = (args.causal && k0 + ABN - 1 > q0 + qoff + t * ABM) || (k0 + ABN > Sk);
       // Raw scores stay in registers; the scale (> 0) is applied to the max and
@@ -320,7 +289,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(u[c][i]));
       const float sl2 = args.scale_log2;
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
-      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 1);
       const bool grow = mx > m_ref + kRescaleThresh;
       const float m_new = grow ? mx : m_ref;
       const bool dead = (m_new == -INFINITY);
@@ -335,10 +303,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 32; i += 2) {
           const float x0 = fmaf(__uint_as_float(u[c][i]), sl2, -m_new);
           const float x1 = fmaf(__uint_as_float(u[c][i + 1]), sl2, -m_new);
-          // MODE 1 / 2: one exponential in four / eight runs on the FMA pipe (exp2_poly).
           const float p0 = dead ? 0.f : ex2_approx(x0);
-          const bool poly = (MODE == 1 && (i & 2)) || (MODE == 2 && (i & 6) == 6);
-          const float p1 = dead ? 0.f : (poly ? exp2_poly(x1) : ex2_approx(x1));
+          const float p1 = dead ? 0.f : ex2_approx(x1);
           sum4[(i >> 1) & 3] += p0 + p1;
           pk[i >> 1] = pack_bf16(p0, p1);
         }
@@ -346,7 +312,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float rowsum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       __syncwarp();
-      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 2);
       // O and the P columns are busy until PV(j-1) of this tile completes.
       if (j > 0) {
         if (!mbar_wait(&o_done[t], (j - 1) & 1, err, kErrTimeoutSoftmax)) { ok = false; break; }
@@ -367,11 +332,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float alpha = (m_ref == -INFINITY) ? 0.f : (grow ? exp2f(m_ref - m_new) : 1.f);
       l = l * alpha + rowsum;
       m_ref = m_new;
-      if (threadIdx.x == 128) NQ_TS(4096 + 4 * j + 3);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (threadIdx.x % 128 == 0) NQ_TS(8 * j + 5 + 2 * t);
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // --------------------------------------------------------- epilogue
@@ -424,10 +387,9 @@ struct AttnKV {
   int cp_c = 1, cp_world = 1;
 };
 
-template <int D, int MODE = 0>
+template <int D>
 static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, torch::Tensor& o,
                             torch::Tensor& lse, int B, int S, int Hq, int Hk, bool causal, float scale,
-                            unsigned long long* dbg = nullptr, int head_major = 0,
                             const AttnKV& cp = AttnKV()) {
   using L = AttnFwdSmem<D>;
   const int64_t T = static_cast<int64_t>(B) * S;
@@ -454,14 +416,8 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
   a.O = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   a.lse = lse.data_ptr<float>();
   a.err = error_flag_ptr();
-  a.dbg = dbg;
-  a.head_major = head_major;
-  auto kern = attn_fwd_kernel<D, MODE>;
-  static bool attr = false;
-  if (!attr) {
-    NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-    attr = true;
-  }
+  auto kern = attn_fwd_kernel<D>;
+  set_max_smem_once(reinterpret_cast<const void*>(kern), L::kBytes);
   const int grid = B * Hq * ((S + ABM * kTilesPerCta - 1) / (ABM * kTilesPerCta));
   kern<<<grid, kAttnThreads, L::kBytes, at::cuda::getCurrentCUDAStream()>>>(tq, tv, tk, a);
   NQ_CHECK_CUDA(cudaGetLastError());
@@ -513,29 +469,10 @@ std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor qk, torch::Tensor kv, int64
     cp.cp_world = static_cast<int>(cp_world);
     cp.cp_c = static_cast<int>(Sk / (2 * cp_world));
   }
-  if (D == 128) launch_attn_fwd<128>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, nullptr, 0, cp);
-  else if (D == 64) launch_attn_fwd<64>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, nullptr, 0, cp);
+  if (D == 128) launch_attn_fwd<128>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, cp);
+  else if (D == 64) launch_attn_fwd<64>(qk, qk, o, lse, B, S, Hq, Hk, true, (float)scale, cp);
   else TORCH_CHECK(false, "attn_fwd_cp: head_dim must be 64 or 128");
   return {o, lse};
-}
-
-// Same as attn_fwd, plus globaltimer stamps of pipeline events of CTA 0
-// (8 slots per key block: load issue, K ready, P0 ready, P1 ready, S0 ready,
-// P0 written, S1 ready, P1 written).  Profiling aid only.
-std::vector<torch::Tensor> attn_fwd_timeline(torch::Tensor qk, torch::Tensor qkv, int64_t B, int64_t S,
-                                             int64_t Hq, int64_t Hk, int64_t D, bool causal, double scale,
-                                             int64_t mode) {
-  c10::cuda::CUDAGuard g(qk.device());
-  auto o = torch::empty({B * S, Hq * D}, qk.options());
-  auto lse = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
-  auto ts = torch::zeros({8192}, qk.options().dtype(torch::kInt64));
-  auto* p = reinterpret_cast<unsigned long long*>(ts.data_ptr<int64_t>());
-  // mode bit 3: head-major block order (comparison with the default order)
-  const int hm = (mode & 8) ? 1 : 0;
-  if ((mode & 7) == 1) launch_attn_fwd<128, 1>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p, hm);
-  else if ((mode & 7) == 2) launch_attn_fwd<128, 2>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p, hm);
-  else launch_attn_fwd<128, 0>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, p, hm);
-  return {o, lse, ts};
 }
 
 }  // namespace nq

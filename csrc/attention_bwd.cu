@@ -64,7 +64,6 @@ struct AttnBwdArgs {
   float* dqk;         // [T, (Hq+Hk)*D] fp32: dq accumulated by atomics, dk written
   __nv_bfloat16* dqkv;  // [T, (Hq+2Hk)*D]: dv written into the v slot
   int* err;
-  unsigned long long* dbg;  // optional event timestamps of CTA 0 (profiling aid)
   // Context parallelism (see AttnArgs in attention.cu): keys/values come from
   // a gathered [B*Sk, 2*Hk*D] buffer (heads k_head / v_head of the tmK map);
   // query row i sits at key position i + off0 (i < split) or i + off1; dK and
@@ -73,11 +72,6 @@ struct AttnBwdArgs {
   int Sk, k_head, v_head, off0, off1, split;
   float* dkv_cp;
 };
-
-#define NQ_BTS(slot)                                                              \
-  do {                                                                            \
-    if (args.dbg != nullptr && blockIdx.x == 0) args.dbg[(slot)] = globaltimer(); \
-  } while (0)
 
 __device__ __forceinline__ float bwd_ex2(float x) {
   float y;
@@ -239,7 +233,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int bf = it & 1;
         const uint32_t aQ = smem_u32(sQ + bf * L::kTile), aDO = smem_u32(sDO + bf * L::kTile);
         if (!mbar_wait(&qdo_full[bf], (it >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
-        NQ_BTS(8 * it + 0);
         tc_fence_after();
         // S^T (tST is free: P^T(it-1) was read by dV(it-1), issued earlier on this thread)
 #pragma unroll
@@ -249,7 +242,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         // dP^T overwrites dQ(it-1): wait until the compute warps drained it
         if (!mbar_wait(dq_free, (it & 1) ^ 1, err, kErrTimeoutMma)) { ok = false; break; }
-        NQ_BTS(8 * it + 1);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -258,7 +250,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         umma_commit(s_full);
         if (!mbar_wait(pt_full, it & 1, err, kErrTimeoutMma)) { ok = false; break; }
-        NQ_BTS(8 * it + 2);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQM / 16; ++kk) {
@@ -335,7 +326,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int q0 = mb * BQM;
       if (!mbar_wait(lse_rdy, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       if (!mbar_wait(s_full, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 3);
       tc_fence_after();
       const int qoff = qoff_of(q0);
       const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + BQM > S) || (k0 + BKN > Sk);
@@ -389,14 +379,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 4);
       if (lane == 0) mbar_arrive(pt_full);
       // dQ drain: TMEM -> fp32 staging in the dS tile (free once the dQ MMA
       // completed, which dq_full implies) -> TMA bulk reduce-add into the fp32 dq
       // buffer.  Rounds of 64 head-dim columns; each warpgroup stages one
       // 128-row x 32-column box (128B-swizzled, bank-conflict free).
       if (!mbar_wait(dq_full, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 5);
       tc_fence_after();
       {
         const int bf = it & 1;
@@ -423,7 +411,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(staged);
       }
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 6);
     }
     // ------------------------------------------------------- dK / dV out
     if (ok && n_iter > 0 && mbar_wait(acc_done, 0, err, kErrTimeoutSoftmax)) {
@@ -653,7 +640,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // dP^T[w] is where dQ^T of iteration j-2 waits to be drained
         if (!mbar_wait(&dq_free[w], static_cast<uint32_t>((j >> 1) & 1) ^ 1, err, kErrTimeoutMma)) return false;
         tc_fence_after();
-        NQ_BTS(8 * j + 0);
         const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s));
         const uint32_t tS = tmem + 128 * w, tP = tS + 64;
 #pragma unroll
@@ -669,7 +655,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_bf16(tP, sdesc_sw128(aV + oa, 16, 1024), sdesc_sw128(aDO + ob, 16, 1024), id_s, kk > 0);
         }
         umma_commit(&s_full[w]);
-        NQ_BTS(8 * j + 1);
         return true;
       };
       if (ok && n_iter > 0) ok = issue_sdp(0);
@@ -678,7 +663,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (it + 1 < n_iter && !issue_sdp(it + 1)) { ok = false; break; }
         if (!mbar_wait(&pds_ready[w], static_cast<uint32_t>(it >> 1) & 1, err, kErrTimeoutMma)) { ok = false; break; }
         tc_fence_after();
-        NQ_BTS(8 * it + 2);
         const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s)), aDS = smem_u32(sDS(w));
         const uint32_t tS = tmem + 128 * w, tP = tS + 64;
         // dQ^T = K^T dS^T (M = head dims, N = queries, K = keys): A = K read
@@ -762,7 +746,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!mbar_wait(&lse_rdy[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       if (!mbar_wait(&s_full[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       tc_fence_after();
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 3);
       const int qoff = qoff_of(q0);
       const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + PBQ > S) || (k0 + BKN > Sk);
       uint32_t us2[2][32], ud2[2][32];
@@ -821,7 +804,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 4);
       if (lane == 0) mbar_arrive(&pds_ready[w]);
       // dQ^T drain: thread = head dim r, 64 query columns -> fp32 staging in the
       // Q/dO stage of this iteration (once its dV / dK MMAs have released the
@@ -829,7 +811,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // warp write one 128-byte row per store.
       if (!mbar_wait(&dq_full[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       tc_fence_after();
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 5);
       {
         uint32_t u[2][32];
         tmem_ld32(tP, u[0]);
@@ -858,7 +839,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&staged[s]);
       }
-      if (threadIdx.x == 128) NQ_BTS(8 * it + 6);
     }
     // ------------------------------------------------------- dK / dV out
     if (ok && n_iter > 0 && mbar_wait(acc_done, 0, err, kErrTimeoutSoftmax)) {
@@ -962,7 +942,7 @@ template <int D>
 static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tensor& qk, const torch::Tensor& qkv,
                                      const torch::Tensor& O, const torch::Tensor& lse, torch::Tensor& dqkv,
                                      int B, int S, int Hq, int Hk, bool causal, float scale,
-                                     unsigned long long* dbg = nullptr, const AttnBwdKV& cp = AttnBwdKV()) {
+                                     const AttnBwdKV& cp = AttnBwdKV()) {
   using L = AttnBwdSmem<D>;
   static_assert(L::kBytes <= 232448 && AttnBwdPPSmem::kBytes <= 232448, "attention backward shared memory budget");
   const int64_t T = static_cast<int64_t>(B) * S;
@@ -1009,18 +989,13 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
   a.dqk = dqk.data_ptr<float>();
   a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   a.err = error_flag_ptr();
-  a.dbg = dbg;
   auto kern = attn_bwd_pp_kernel;
   int bytes = AttnBwdPPSmem::kBytes;
   if constexpr (!kPP) {
     kern = attn_bwd_kernel<D>;
     bytes = L::kBytes;
   }
-  static bool attr = false;
-  if (!attr) {
-    NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    attr = true;
-  }
+  set_max_smem_once(reinterpret_cast<const void*>(kern), bytes);
   const int grid = B * Hk * ((a.Sk + BKN - 1) / BKN);
   kern<<<grid, kBwdThreads, bytes, st>>>(tq, tv, tdo, tdq, tk, a);
   NQ_CHECK_CUDA(cudaGetLastError());
@@ -1069,24 +1044,10 @@ std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor dO, torch::Tensor qk, torch
   cp.split = static_cast<int>(split);
   torch::Tensor dummy_qkv = qk;  // unused V source in this mode
   torch::Tensor dq;
-  if (D == 128) dq = launch_attn_bwd<128>(dO, qk, qk, O, lse, dummy_qkv, B, S, Hq, Hk, true, (float)scale, nullptr, cp);
-  else if (D == 64) dq = launch_attn_bwd<64>(dO, qk, qk, O, lse, dummy_qkv, B, S, Hq, Hk, true, (float)scale, nullptr, cp);
+  if (D == 128) dq = launch_attn_bwd<128>(dO, qk, qk, O, lse, dummy_qkv, B, S, Hq, Hk, true, (float)scale, cp);
+  else if (D == 64) dq = launch_attn_bwd<64>(dO, qk, qk, O, lse, dummy_qkv, B, S, Hq, Hk, true, (float)scale, cp);
   else TORCH_CHECK(false, "attn_bwd_cp: head_dim must be 64 or 128");
   return {dq, dkv};
-}
-
-// attn_bwd plus globaltimer stamps of CTA 0's pipeline events (8 per
-// iteration: Q/dO ready, dQ drained, P/dS ready (MMA view), S ready, P/dS
-// written, dQ ready, dQ drained (compute view)).  Profiling aid only.
-std::vector<torch::Tensor> attn_bwd_timeline(torch::Tensor dO, torch::Tensor qk, torch::Tensor qkv,
-                                             torch::Tensor O, torch::Tensor lse, torch::Tensor dqkv,
-                                             int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
-                                             bool causal, double scale) {
-  c10::cuda::CUDAGuard g(qk.device());
-  auto ts = torch::zeros({16384}, qk.options().dtype(torch::kInt64));
-  auto* p = reinterpret_cast<unsigned long long*>(ts.data_ptr<int64_t>());
-  auto dqk = launch_attn_bwd<128>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale, p);
-  return {dqk, ts};
 }
 
 }  // namespace nq

@@ -33,11 +33,8 @@ void qknorm_rope_bwd(torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>,
                      int64_t, int64_t);
 // attention
 std::vector<torch::Tensor> attn_fwd(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
-std::vector<torch::Tensor> attn_fwd_timeline(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double, int64_t);
 torch::Tensor attn_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
                        int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
-std::vector<torch::Tensor> attn_bwd_timeline(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
-                                             torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
 std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t,
                                        int64_t, int64_t, int64_t, int64_t, double, int64_t, int64_t, int64_t);
 std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
@@ -54,6 +51,8 @@ torch::Tensor decode_attn(torch::Tensor, torch::Tensor, torch::Tensor, torch::Te
 // elementwise.cu
 int64_t error_flag_read();
 void error_flag_clear();
+void wait_limits_set(int64_t, int64_t);
+std::vector<int64_t> wait_limits_get();
 torch::Tensor swiglu_fwd(torch::Tensor);
 torch::Tensor swiglu_bwd(torch::Tensor, torch::Tensor);
 torch::Tensor gelu_fwd(torch::Tensor);
@@ -68,7 +67,7 @@ void ce_lse_chunk(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor);
 void ce_grad_chunk(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor);
 torch::Tensor sum_squares(torch::Tensor);
 void adamw_flat(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
-                int64_t, int64_t, int64_t, double, double, double, double, double, double, double, double);
+                int64_t, int64_t, int64_t, int64_t, double, double, double, double, double, double, double, double);
 // moe.cu
 std::vector<torch::Tensor> router_fwd(torch::Tensor, int64_t, bool);
 torch::Tensor router_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, bool);
@@ -108,8 +107,8 @@ void zero_rs(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, i
              torch::Tensor, int64_t, int64_t);
 void zero_clip(torch::Tensor, double, torch::Tensor, torch::Tensor);
 void zero_adamw_ag(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor,
-                   torch::Tensor, torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, double, double,
-                   double, double, double, double, double, double);
+                   torch::Tensor, torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, double,
+                   double, double, double, double, double, double, double);
 void zero_publish(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t);
 }  // namespace nq
 
@@ -134,8 +133,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qknorm_rope_bwd", &nq::qknorm_rope_bwd);
   m.def("attn_fwd", &nq::attn_fwd);
   m.def("attn_bwd", &nq::attn_bwd);
-  m.def("attn_fwd_timeline", &nq::attn_fwd_timeline);
-  m.def("attn_bwd_timeline", &nq::attn_bwd_timeline);
   m.def("attn_fwd_cp", &nq::attn_fwd_cp, "context-parallel attention forward (local queries, gathered keys)");
   m.def("attn_bwd_cp", &nq::attn_bwd_cp, "context-parallel attention backward");
   m.def("cp_kv_scatter", &nq::cp_kv_scatter, "store local k|v rows into every CP rank's gathered buffer (P2P)");
@@ -144,6 +141,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attn", &nq::decode_attn);
   m.def("error_flag_read", &nq::error_flag_read);
   m.def("error_flag_clear", &nq::error_flag_clear);
+  m.def("wait_limits_set", &nq::wait_limits_set,
+        "bounded-wait limits of the current device in ns (mbarrier, peer flag); <= 0 keeps a value");
+  m.def("wait_limits_get", &nq::wait_limits_get);
   m.def("swiglu_fwd", &nq::swiglu_fwd);
   m.def("swiglu_bwd", &nq::swiglu_bwd);
   m.def("gelu_fwd", &nq::gelu_fwd);

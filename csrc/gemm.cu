@@ -389,11 +389,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
                         int max_tiles, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
   auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    NQ_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-    attr_set = true;
-  }
+  set_max_smem_once(reinterpret_cast<const void*>(kern), L::kBytes);
   int grid = std::min(num_sms(), std::max(1, max_tiles));
   kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, a);
   NQ_CHECK_CUDA(cudaGetLastError());

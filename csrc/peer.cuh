@@ -3,17 +3,15 @@
 // sequence number: the producer publishes `seq` with a system-scope release
 // store after its data stores; a consumer polls with system-scope acquire loads
 // until the value has reached `seq` (wrap-safe comparison).  Every wait is
-// bounded by NQ_PEER_TIMEOUT_NS: on timeout the kernel records kErrTimeoutPeer
-// in the device error word and gives up instead of hanging the GPU.
+// bounded by the peer-flag limit (a run-time value next to the device error
+// word, 20 s by default: ranks can be far apart at start-up): on timeout the
+// kernel records kErrTimeoutPeer in the error word and gives up instead of
+// hanging the GPU.
 #pragma once
 
 #include "sm100.cuh"
 
 namespace nq {
-
-#ifndef NQ_PEER_TIMEOUT_NS
-#define NQ_PEER_TIMEOUT_NS 20000000000ull  // 20 s: ranks can be far apart at start-up
-#endif
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -34,11 +32,12 @@ __device__ __forceinline__ bool seq_reached(unsigned v, unsigned seq) {
 __device__ __forceinline__ bool wait_flag(const unsigned* f, unsigned seq, int* err) {
   if (seq_reached(ld_acquire_sys(f), seq)) return true;
   const uint64_t t0 = globaltimer();
+  const uint64_t limit = peer_limit_ns(err);
   uint32_t spins = 0;
   while (!seq_reached(ld_acquire_sys(f), seq)) {
     if ((++spins & 63u) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (globaltimer() - t0 > NQ_PEER_TIMEOUT_NS) {
+      if (globaltimer() - t0 > limit) {
         atomicCAS(err, 0, kErrTimeoutPeer);
         return false;
       }

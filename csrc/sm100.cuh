@@ -2,20 +2,27 @@
 // copies, tcgen05 (TMEM alloc, UMMA issue/commit, TMEM loads) and the shared
 // memory matrix descriptors consumed by tcgen05.mma.
 //
-// Every wait in this file is bounded: after NQ_WAIT_TIMEOUT_NS of spinning it
-// records an error code in a global word and returns false so the kernel can
-// unwind (free TMEM, drain its own copies) instead of hanging the GPU.
+// Every wait in this file is bounded: after the mbarrier wait limit (a run-time
+// value stored next to the error word, 2 s by default) it records an error code
+// in that word and returns false so the kernel can unwind (free TMEM, drain its
+// own copies) instead of hanging the GPU.
 #pragma once
 
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#ifndef NQ_WAIT_TIMEOUT_NS
-#define NQ_WAIT_TIMEOUT_NS 2000000000ull  // 2 s
-#endif
-
 namespace nq {
+
+// Wait limits live in the error block: err[2..3] = mbarrier limit (ns),
+// err[4..5] = peer-flag limit (ns).  Read only once a wait did not succeed at
+// once, so the fast path costs nothing.
+__device__ __forceinline__ uint64_t mbar_limit_ns(const int* err) {
+  return *reinterpret_cast<const volatile unsigned long long*>(err + 2);
+}
+__device__ __forceinline__ uint64_t peer_limit_ns(const int* err) {
+  return *reinterpret_cast<const volatile unsigned long long*>(err + 4);
+}
 
 enum ErrCode : int {
   kErrNone = 0,
@@ -86,12 +93,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
+  const uint64_t limit = mbar_limit_ns(err);
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (globaltimer() - t0 > NQ_WAIT_TIMEOUT_NS) {
+      if (globaltimer() - t0 > limit) {
         atomicCAS(err, 0, code);
         return false;
       }

@@ -9,6 +9,8 @@
 #include <torch/extension.h>
 
 #include <mutex>
+#include <set>
+#include <utility>
 #include <stdexcept>
 #include <string>
 
@@ -93,19 +95,13 @@ inline CUtensorMap make_tmap_3d_f32(const void* base, int64_t d0, int64_t d1, in
   return m;
 }
 
-inline int num_sms() {
-  static int n = -1;
-  if (n < 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
-
-// Device-side error word shared by all kernels of the extension; a kernel that
-// gives up on a bounded wait writes its code here.  Host code reads it with
-// `error_flag_read` (tests, watchdog) and resets it with `error_flag_clear`.
+// Device-side error block shared by all kernels of the extension (int32
+// words, one block per device): word 0 is the error code a kernel writes when
+// it gives up on a bounded wait; words 2-3 hold the mbarrier wait limit and
+// words 4-5 the peer-flag wait limit, in nanoseconds (u64), which the waits in
+// sm100.cuh / peer.cuh read at run time.  Host code reads the code with
+// `error_flag_read` (tests, watchdog), resets it with `error_flag_clear` and
+// changes the limits with `wait_limits_set`.
 int* error_flag_ptr();
 
 #define NQ_CHECK_CUDA(expr)                                                          \
@@ -115,6 +111,42 @@ int* error_flag_ptr();
                                                     cudaGetErrorString(_e) + " at " + \
                                                     __FILE__ + ":" + std::to_string(__LINE__)); \
   } while (0)
+
+constexpr int kMaxDevices = 64;
+
+// Current device ordinal, checked against the per-device tables' size.
+inline int current_device() {
+  int dev = 0;
+  NQ_CHECK_CUDA(cudaGetDevice(&dev));
+  TORCH_CHECK(dev >= 0 && dev < kMaxDevices, "device ordinal ", dev, " beyond the library's limit of ",
+              kMaxDevices);
+  return dev;
+}
+
+// SM count of the current device (cached per device).
+inline int num_sms() {
+  static int n[kMaxDevices] = {};
+  const int dev = current_device();
+  if (n[dev] == 0) {
+    int v = 0;
+    NQ_CHECK_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    n[dev] = v;
+  }
+  return n[dev];
+}
+
+// Raise a kernel's dynamic shared-memory limit on the current device.  The
+// attribute belongs to the device's context, so a process that launches the
+// kernel on several GPUs must set it on each; done once per (kernel, device).
+inline void set_max_smem_once(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({kernel, dev})) return;
+  NQ_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert({kernel, dev});
+}
 
 inline void check_bf16(const torch::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");

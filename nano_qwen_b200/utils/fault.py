@@ -11,8 +11,9 @@ minutes (reference: distributed/comm.py:14, :33-35).  Here:
 * ``StepWatchdog``: a host thread that calls a handler (default: log and raise
   in the main thread at the next ``check()``) when a step exceeds its budget.
 * ``check_device_errors``: every spin-wait in this library's kernels is bounded
-  (by ``%globaltimer``); a wait that runs out records a code in a device error
-  word and returns instead of hanging.  This reads the word and raises.
+  (by ``%globaltimer``, with limits set at run time by ``set_wait_limits``); a
+  wait that runs out records a code in a device error word and returns instead
+  of hanging.  This reads the word and raises.
 * ``FaultInjector``: ``NQ_FAULT="rank:step:kind"`` makes that rank raise
   (``raise``), exit (``exit``) or stop heart-beating (``silent``) at that step.
   Injection is host-only; nothing here faults or stalls a GPU.
@@ -79,6 +80,29 @@ class HeartbeatMonitor:
         bad = self.stale_ranks()
         if bad:
             raise PeerFailure(bad, f"no heartbeat for > {self.timeout_s:.1f} s")
+
+    def gate(self, step: int) -> None:
+        """Step gate, called between steps before any collective of ``step``:
+        announce this rank at ``step`` and wait (at most ``timeout_s``) until
+        every peer has announced it too.  A rank that left, crashed or hangs
+        in its previous step never announces, and the survivors get a
+        ``PeerFailure`` naming it here, on the host, instead of blocking in
+        their next collective or peer-memory wait."""
+        if not self.silent:
+            self.store.set(f"{self.prefix}/step/{step}/{self.rank}", "1")
+        peers = [r for r in range(self.world) if r != self.rank]
+        keys = [f"{self.prefix}/step/{step}/{r}" for r in peers]
+        try:
+            self.store.wait(keys, _td(self.timeout_s))
+            return
+        except Exception:
+            pass
+        try:
+            missing = [r for r, k in zip(peers, keys) if not self.store.check([k])]
+        except Exception as e:  # the store's host rank is gone too
+            raise PeerFailure(peers, f"store unreachable at step {step}: {e}") from e
+        if missing:
+            raise PeerFailure(missing, f"did not reach step {step} within {self.timeout_s:.1f} s")
 
 
 def _td(s: float):
@@ -161,6 +185,23 @@ def check_device_errors(clear: bool = True) -> None:
         if clear:
             E.error_flag_clear()
         raise DeviceWaitTimeout(f"device error word {code}: {_ERR_NAMES.get(code & 0xff, 'unknown')}")
+
+
+def set_wait_limits(mbar_s: Optional[float] = None, peer_s: Optional[float] = None) -> None:
+    """Change the bounded-wait limits of the current GPU's kernels (seconds;
+    ``None`` keeps a value).  Defaults: 2 s for waits on a CTA's own pipeline
+    (mbarriers), 20 s for flags written by another GPU.  A watchdog that wants
+    a dead peer to surface sooner lowers the peer limit; the kernels read the
+    values at run time, so no rebuild is needed."""
+    from ..ops._ext import ext
+    ext().wait_limits_set(int(mbar_s * 1e9) if mbar_s else 0, int(peer_s * 1e9) if peer_s else 0)
+
+
+def get_wait_limits() -> tuple:
+    """(mbarrier limit, peer-flag limit) of the current GPU, in seconds."""
+    from ..ops._ext import ext
+    m, p = ext().wait_limits_get()
+    return m / 1e9, p / 1e9
 
 
 class FaultInjector:

@@ -314,3 +314,75 @@ def global_balance_worker(rank, world, port):
     assert torch.allclose(aux0, expect, rtol=1e-5, atol=1e-6), (float(aux0), float(expect))
     assert torch.isfinite(out["loss"])
     dist.destroy_process_group()
+
+
+def rank_leave_worker(rank, world, port):
+    """The last rank leaves between training steps (exits without a word); the
+    survivors' step gate names it before they issue their next collective."""
+    init(rank, world, port)
+    from nano_qwen_b200.training.engine import TrainEngine
+    from nano_qwen_b200.utils.fault import HeartbeatMonitor, PeerFailure
+    store = dist.distributed_c10d._get_default_store()
+    hb = HeartbeatMonitor(store, rank, world, timeout_s=2.0, prefix="leave")
+    cfg = tiny_cfg()
+    eng = TrainEngine(build(cfg), {"optimizer": {"lr": 1e-3}, "scheduler": {"warmup_steps": 0}},
+                      torch.device("cpu"), dp_mode="shard")
+    ids = batch(cfg, 2, 16, seed=rank)
+    leaver = world - 1
+    for step in range(4):
+        if rank == leaver and step == 2:
+            os._exit(0)  # between steps: nothing in flight, no goodbye
+        try:
+            hb.gate(step)
+        except PeerFailure as e:
+            assert rank != leaver and step == 2 and e.ranks == [leaver], (rank, step, e.ranks)
+            # stop before the next collective; rank 0 hosts the store, so it
+            # leaves after the other survivors have seen the failure
+            store.set(f"leave/seen/{rank}", "1")
+            if rank == 0:
+                store.wait([f"leave/seen/{r}" for r in range(1, leaver)], datetime.timedelta(seconds=30))
+            os._exit(0)
+        eng.train_step([{"input_ids": ids, "labels": ids}])
+    raise AssertionError("the departed rank was not detected")
+
+
+def zero_checkpoint_worker(rank, world, port, tmp):
+    """ZeRO shard mode keeps only this rank's slice of the Adam moments.  A
+    checkpoint gathers them, and a fresh engine that loads it continues the
+    run exactly: the next step's loss and every parameter match the engine
+    that was never interrupted."""
+    init(rank, world, port)
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg()
+    tc = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+          "scheduler": {"warmup_steps": 1, "total_steps": 20}}
+
+    def engine():
+        return TrainEngine(build(cfg), tc, torch.device("cpu"), dp_mode="shard")
+
+    a = engine()
+    assert a.optimizer.sharded and a.optimizer.exp_avg.numel() < a.store.numel
+    data = [batch(cfg, 2, 16, seed=10 * s + rank) for s in range(4)]
+    for s in range(3):
+        a.train_step([{"input_ids": data[s], "labels": data[s]}])
+    mgr = CheckpointManager(save_dir=tmp, async_save=False)
+    m, o, sch = a.state_for_save()
+    full_m = o.state[next(iter(o.state))]["exp_avg"].clone()
+    d = mgr.save(3, m, o, sch)
+    assert "exp_avg" not in o.state[next(iter(o.state))]  # full views released after the save
+    # the saved moments are the gathered ones, nonzero outside this rank's shard
+    assert full_m.abs().sum() > 0
+    b = engine()
+    mgr.load(b.model, b.optimizer, b.scheduler, checkpoint_dir=str(d))
+    assert b.optimizer.step_count == a.optimizer.step_count
+    assert torch.equal(b.optimizer.exp_avg, a.optimizer.exp_avg)
+    assert torch.equal(b.optimizer.exp_avg_sq, a.optimizer.exp_avg_sq)
+    ra = a.train_step([{"input_ids": data[3], "labels": data[3]}])
+    rb = b.train_step([{"input_ids": data[3], "labels": data[3]}])
+    assert torch.equal(ra["loss"], rb["loss"]), (ra["loss"], rb["loss"])
+    a.dp.gather_master()
+    b.dp.gather_master()
+    assert torch.equal(a.store.master, b.store.master)
+    dist.barrier()
+    dist.destroy_process_group()

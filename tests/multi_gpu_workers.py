@@ -96,10 +96,15 @@ def tp_fused_worker(rank, world, port):
     from nano_qwen_b200.ops import ext
     from nano_qwen_b200.parallel.tensor_parallel import apply_tensor_parallel, sync_replicated_grads
     from nano_qwen_b200.training.optimizer import attach_param_store
-    cfg = _cfg()
+    from nano_qwen_b200.config import ModelConfig
+    # 16 Q / 8 KV heads divide by every tp size up to 8; 2 x 512 tokens give
+    # each rank a multiple of 128 rows under sequence parallelism
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=16,
+                      num_key_value_heads=8, head_dim=64, intermediate_size=1024,
+                      vocab_size=4096, max_position_embeddings=1024, tie_word_embeddings=True)
     grp = dist.new_group(list(range(world)))
     g = torch.Generator().manual_seed(7)
-    ids = torch.randint(0, cfg.vocab_size, (2, 256), generator=g).cuda()
+    ids = torch.randint(0, cfg.vocab_size, (2, 512), generator=g).cuda()
 
     def build(tp, fused):
         torch.manual_seed(0)
@@ -212,7 +217,7 @@ def ep_fused_worker(rank, world, port):
 
 
 def cp_kernel_worker(rank, world, port):
-    """Context parallelism on the attention kernels (2 ranks, zigzag) against
+    """Context parallelism on the attention kernels (zigzag over the ranks) against
     the single-GPU model on the full sequence: loss and gradients."""
     init(rank, world, port)
     from nano_qwen_b200.models import Qwen3Model
@@ -261,3 +266,39 @@ def cp_kernel_worker(rank, world, port):
         assert err < 5e-2, (n, err)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def rank_leave_worker(rank, world, port):
+    """One process per GPU trains with NCCL data parallelism; the last rank
+    leaves between steps (synchronised, then exits without a word).  The
+    survivors' host-side step gate names it before they launch their next
+    collective.  NVLS is off and no buffer is bound to a multicast object, so
+    the departed rank's memory is not part of anything the survivors touch."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
+    init(rank, world, port)
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.utils.fault import HeartbeatMonitor, PeerFailure
+    store = dist.distributed_c10d._get_default_store()
+    hb = HeartbeatMonitor(store, rank, world, timeout_s=3.0, prefix="leave")
+    eng = _engine("shard", None)  # NCCL reduce-scatter / all-gather, no peer-memory kernels
+    g = torch.Generator().manual_seed(21 + rank)
+    ids = torch.randint(0, 4096, (2, 128), generator=g).cuda()
+    leaver = world - 1
+    for step in range(4):
+        if rank == leaver and step == 2:
+            torch.cuda.synchronize()  # nothing of this rank in flight
+            os._exit(0)
+        try:
+            hb.gate(step)
+        except PeerFailure as e:
+            assert rank != leaver and step == 2 and e.ranks == [leaver], (rank, step, e.ranks)
+            torch.cuda.synchronize()
+            assert ext().error_flag_read() == 0
+            store.set(f"leave/seen/{rank}", "1")
+            if rank == 0:  # hosts the store: leaves after the other survivors
+                store.wait([f"leave/seen/{r}" for r in range(1, leaver)], datetime.timedelta(seconds=30))
+            os._exit(0)
+        out = eng.train_step([{"input_ids": ids, "labels": ids}])
+        assert torch.isfinite(out["loss"]).item()
+    raise AssertionError("the departed rank was not detected")

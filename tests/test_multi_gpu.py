@@ -1,5 +1,6 @@
 """Tests that need two or more GPUs of one node (NCCL + NVLink peer memory).
-Skipped when fewer GPUs are visible."""
+Each runs at 2, 4 and 8 ranks; a world larger than the number of visible
+GPUs is skipped."""
 
 import socket
 
@@ -9,8 +10,12 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-needs2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                            reason="needs 2 GPUs")
+WORLDS = [2, 4, 8]
+
+
+def _need(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
 
 
 def _port():
@@ -21,25 +26,36 @@ def _port():
     return p
 
 
-@needs2
-def test_peer_memory_zero_step_matches_single_process():
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_memory_zero_step_matches_single_process(world):
+    _need(world)
     import multi_gpu_workers as W
-    mp.spawn(W.peer_dp_worker, args=(2, _port()), nprocs=2, join=True)
+    mp.spawn(W.peer_dp_worker, args=(world, _port()), nprocs=world, join=True)
 
 
-@needs2
-def test_fused_tensor_parallel_matches_single_gpu():
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_tensor_parallel_matches_single_gpu(world):
+    _need(world)
     import multi_gpu_workers as W
-    mp.spawn(W.tp_fused_worker, args=(2, _port()), nprocs=2, join=True)
+    mp.spawn(W.tp_fused_worker, args=(world, _port()), nprocs=world, join=True)
 
 
-@needs2
-def test_fused_expert_parallel_matches_single_gpu():
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_expert_parallel_matches_single_gpu(world):
+    _need(world)
     import multi_gpu_workers as W
-    mp.spawn(W.ep_fused_worker, args=(2, _port()), nprocs=2, join=True)
+    mp.spawn(W.ep_fused_worker, args=(world, _port()), nprocs=world, join=True)
 
 
-@needs2
-def test_context_parallel_kernels_match_single_gpu():
+@pytest.mark.parametrize("world", WORLDS)
+def test_context_parallel_kernels_match_single_gpu(world):
+    _need(world)
     import multi_gpu_workers as W
-    mp.spawn(W.cp_kernel_worker, args=(2, _port()), nprocs=2, join=True)
+    mp.spawn(W.cp_kernel_worker, args=(world, _port()), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_rank_leaving_between_steps_is_detected(world):
+    _need(world)
+    import multi_gpu_workers as W
+    mp.spawn(W.rank_leave_worker, args=(world, _port()), nprocs=world, join=True)

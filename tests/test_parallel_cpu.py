@@ -60,3 +60,11 @@ def test_tensor_parallel_checkpoint_roundtrip(tmp_path):
 
 def test_global_batch_moe_balance():
     _run(W.global_balance_worker, 2)
+
+
+def test_rank_leaving_between_steps_is_detected():
+    _run(W.rank_leave_worker, 3)
+
+
+def test_zero_shard_checkpoint_resumes_exactly(tmp_path):
+    _run(W.zero_checkpoint_worker, 2, str(tmp_path))
