@@ -9,14 +9,48 @@
 namespace nq {
 
 // ------------------------------------------------------------- error word
+// Default wait limits: 2 s for mbarrier waits inside one CTA (a pipeline stage
+// that has not arrived by then never will), 20 s for flags written by another
+// GPU (ranks can be far apart at start-up, e.g. one still compiling or loading).
+constexpr uint64_t kDefaultMbarLimitNs = 2000000000ull;
+constexpr uint64_t kDefaultPeerLimitNs = 20000000000ull;
+
 int* error_flag_ptr() {
-  static torch::Tensor flags[64];
-  int dev;
-  cudaGetDevice(&dev);
-  if (!flags[dev].defined()) {
-    flags[dev] = torch::zeros({4}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
+  static std::mutex mu;
+  static int* block[kMaxDevices] = {};
+  static torch::Tensor owner[kMaxDevices];
+  const int dev = current_device();
+  if (block[dev] != nullptr) return block[dev];
+  std::lock_guard<std::mutex> lk(mu);
+  if (block[dev] == nullptr) {
+    auto t = torch::zeros({8}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
+    const uint64_t lim[2] = {kDefaultMbarLimitNs, kDefaultPeerLimitNs};
+    NQ_CHECK_CUDA(cudaMemcpy(t.data_ptr<int>() + 2, lim, sizeof(lim), cudaMemcpyHostToDevice));
+    owner[dev] = t;
+    block[dev] = t.data_ptr<int>();
   }
-  return flags[dev].data_ptr<int>();
+  return block[dev];
+}
+
+// Set the bounded-wait limits of the current device (nanoseconds; <= 0 keeps
+// the current value).  Takes effect for kernels launched afterwards.
+void wait_limits_set(int64_t mbar_ns, int64_t peer_ns) {
+  int* p = error_flag_ptr();
+  NQ_CHECK_CUDA(cudaDeviceSynchronize());
+  if (mbar_ns > 0) {
+    const uint64_t v = static_cast<uint64_t>(mbar_ns);
+    NQ_CHECK_CUDA(cudaMemcpy(p + 2, &v, sizeof(v), cudaMemcpyHostToDevice));
+  }
+  if (peer_ns > 0) {
+    const uint64_t v = static_cast<uint64_t>(peer_ns);
+    NQ_CHECK_CUDA(cudaMemcpy(p + 4, &v, sizeof(v), cudaMemcpyHostToDevice));
+  }
+}
+
+std::vector<int64_t> wait_limits_get() {
+  uint64_t lim[2];
+  NQ_CHECK_CUDA(cudaMemcpy(lim, error_flag_ptr() + 2, sizeof(lim), cudaMemcpyDeviceToHost));
+  return {static_cast<int64_t>(lim[0]), static_cast<int64_t>(lim[1])};
 }
 
 int64_t error_flag_read() {
@@ -490,9 +524,13 @@ template <bool WRITE_BF16>
 __global__ void adamw_flat_kernel(float* __restrict__ p, const float* __restrict__ g,
                                   float* __restrict__ m, float* __restrict__ v,
                                   __nv_bfloat16* __restrict__ comp, const float* __restrict__ clip,
-                                  int64_t begin, int64_t end, int64_t decay_end, float lr_d,
-                                  float lr_n, float b1, float b2, float eps, float wd, float bc1,
-                                  float bc2) {
+                                  int64_t begin, int64_t end, int64_t sbase, int64_t decay_end,
+                                  float lr_d, float lr_n, float b1, float b2, float eps, float wd,
+                                  float bc1, float bc2) {
+  // m / v hold the optimizer state of flat elements [sbase, sbase + numel):
+  // the whole store (sbase 0) or only this rank's shard (sbase = begin).
+  m -= sbase;
+  v -= sbase;
   const float cs = *clip;
   const float rbc1 = 1.f / bc1, rbc2 = 1.f / bc2;
   const int64_t n4 = (end - begin) / 4;
@@ -529,10 +567,12 @@ __global__ void adamw_flat_kernel(float* __restrict__ p, const float* __restrict
 }
 
 void adamw_flat(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v,
-                torch::Tensor comp, torch::Tensor clip, int64_t begin, int64_t end,
+                torch::Tensor comp, torch::Tensor clip, int64_t begin, int64_t end, int64_t sbase,
                 int64_t decay_end, double lr_d, double lr_n, double b1, double b2, double eps,
                 double wd, double bc1, double bc2) {
-  TORCH_CHECK(begin % 4 == 0 && end % 4 == 0, "adamw range must be 4-aligned");
+  TORCH_CHECK(begin % 4 == 0 && end % 4 == 0 && sbase % 4 == 0, "adamw range must be 4-aligned");
+  TORCH_CHECK(sbase <= begin && end - sbase <= m.numel() && m.numel() == v.numel(),
+              "adamw: optimizer state does not cover the updated range");
   c10::cuda::CUDAGuard gd(p.device());
   const int64_t n = end - begin;
   if (n <= 0) return;
@@ -541,12 +581,12 @@ void adamw_flat(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
   if (comp.numel() > 0) {
     adamw_flat_kernel<true><<<ew_grid(n / 4, 256), 256, 0, st>>>(
         p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
-        reinterpret_cast<__nv_bfloat16*>(comp.data_ptr()), cl.data_ptr<float>(), begin, end, decay_end,
+        reinterpret_cast<__nv_bfloat16*>(comp.data_ptr()), cl.data_ptr<float>(), begin, end, sbase, decay_end,
         (float)lr_d, (float)lr_n, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2);
   } else {
     adamw_flat_kernel<false><<<ew_grid(n / 4, 256), 256, 0, st>>>(
         p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), nullptr,
-        cl.data_ptr<float>(), begin, end, decay_end, (float)lr_d, (float)lr_n, (float)b1, (float)b2,
+        cl.data_ptr<float>(), begin, end, sbase, decay_end, (float)lr_d, (float)lr_n, (float)b1, (float)b2,
         (float)eps, (float)wd, (float)bc1, (float)bc2);
   }
   NQ_CHECK_CUDA(cudaGetLastError());

@@ -112,8 +112,11 @@ __global__ void zero_clip_kernel(const float* __restrict__ sq, float max_norm, f
 template <int W>
 __global__ void __launch_bounds__(256) zero_adamw_ag_kernel(
     ZeroPeers P, float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
-    const float* __restrict__ clip, int64_t begin, int64_t end, int64_t decay_end, float lr_d,
-    float lr_n, float b1, float b2, float eps, float wd, float bc1, float bc2) {
+    const float* __restrict__ clip, int64_t begin, int64_t end, int64_t sbase, int64_t decay_end,
+    float lr_d, float lr_n, float b1, float b2, float eps, float wd, float bc1, float bc2) {
+  // m / v cover flat elements [sbase, ...): the shard (sbase = begin) or all
+  m -= sbase;
+  v -= sbase;
   const float* g = P.grad[P.rank];
   const float cs = *clip;
   const float rbc1 = 1.f / bc1, rbc2 = 1.f / bc2;
@@ -215,16 +218,19 @@ void zero_clip(torch::Tensor sq, double max_norm, torch::Tensor clip, torch::Ten
 
 void zero_adamw_ag(std::vector<int64_t> grad, std::vector<int64_t> comp, std::vector<int64_t> flags,
                    int64_t rank, torch::Tensor master, torch::Tensor m, torch::Tensor v,
-                   torch::Tensor clip, int64_t begin, int64_t end, int64_t decay_end, double lr_d,
-                   double lr_n, double b1, double b2, double eps, double wd, double bc1, double bc2) {
+                   torch::Tensor clip, int64_t begin, int64_t end, int64_t sbase, int64_t decay_end,
+                   double lr_d, double lr_n, double b1, double b2, double eps, double wd, double bc1,
+                   double bc2) {
   auto P = make_peers(grad, comp, flags, rank);
-  TORCH_CHECK(begin % 4 == 0 && end % 4 == 0 && end >= begin, "zero_adamw_ag: 4-aligned shard");
+  TORCH_CHECK(begin % 4 == 0 && end % 4 == 0 && end >= begin && sbase % 4 == 0, "zero_adamw_ag: 4-aligned shard");
+  TORCH_CHECK(sbase <= begin && end - sbase <= m.numel() && m.numel() == v.numel(),
+              "zero_adamw_ag: optimizer state does not cover the shard");
   auto st = at::cuda::getCurrentCUDAStream();
   const int64_t n4 = (end - begin) / 4;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n4 + 255) / 256, num_sms() * 8)));
   NQ_W_DISPATCH(P.world, zero_adamw_ag_kernel<WW><<<grid, 256, 0, st>>>(
       P, master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), clip.data_ptr<float>(),
-      begin, end, decay_end, (float)lr_d, (float)lr_n, (float)b1, (float)b2, (float)eps, (float)wd,
+      begin, end, sbase, decay_end, (float)lr_d, (float)lr_n, (float)b1, (float)b2, (float)eps, (float)wd,
       (float)bc1, (float)bc2));
   NQ_CHECK_CUDA(cudaGetLastError());
 }

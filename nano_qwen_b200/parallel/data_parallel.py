@@ -14,8 +14,10 @@ packing copies):
   all-gather at all; the fp32 master/Adam state (16 B/param) is what gets
   sharded.
 
-Shard boundaries are multiples of 64 elements.  ``gather_master`` all-gathers
-the fp32 master weights (needed before a full state-dict save).
+Shard boundaries are multiples of 64 elements.  The Adam moments exist only
+for the shard (see ``FusedAdamW``); ``gather_master`` / ``gather_flat_``
+all-gather the fp32 master weights and the moments before a full state-dict
+save.
 """
 
 from __future__ import annotations
@@ -161,14 +163,20 @@ class DataParallel:
 
     @torch.no_grad()
     def gather_master(self) -> None:
+        self.gather_flat_(self.store.master)
+
+    @torch.no_grad()
+    def gather_flat_(self, buf: torch.Tensor) -> None:
+        """All-gather a store-sized fp32 buffer in which each rank holds its
+        own shard [b, e) (in place): the master weights, or the Adam moments
+        before a checkpoint save."""
         if self.world == 1 or self.mode != "shard":
             return
-        m = self.store.master
-        mp = self._padded(m, "_master_pad")
-        mine = mp[self.rank * self.per:(self.rank + 1) * self.per].clone()
-        all_gather_flat_(mp, mine, self.group)
-        if mp.data_ptr() != m.data_ptr():
-            m.copy_(mp[: m.numel()])
+        bp = self._padded(buf, "_master_pad")
+        mine = bp[self.rank * self.per:(self.rank + 1) * self.per].clone()
+        all_gather_flat_(bp, mine, self.group)
+        if bp.data_ptr() != buf.data_ptr():
+            buf.copy_(bp[: buf.numel()])
 
     @torch.no_grad()
     def broadcast_params(self, src: int = 0) -> None:

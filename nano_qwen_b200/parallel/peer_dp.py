@@ -14,8 +14,9 @@ comes from PyTorch).  One step is:
    every peer's compute copy (all-gather fused into the optimizer);
 4. ``zero_publish``: flag barrier so the next forward reads complete weights.
 
-The fp32 master weights and Adam moments stay sharded by use (each rank only
-updates its slice).  Same interface as ``DataParallel``; the engine calls
+The Adam moments are allocated for this rank's shard only; the fp32 master
+is updated only in the shard (the rest is refreshed by ``gather_master``
+before a save).  Same interface as ``DataParallel``; the engine calls
 ``fused_step`` instead of sync + clip + step + gather.  Requires 1, 2, 4 or 8
 ranks on one NVSwitch domain.
 """
@@ -197,10 +198,15 @@ class PeerDataParallel(DataParallel):
         E.zero_clip(sq, float(max_norm or 0.0), self.clip, self.norm)
         optimizer.clip_scale = self.clip
         optimizer.last_grad_norm = self.norm
-        lr_d, lr_n, b1, b2, eps, wd, bc1, bc2 = optimizer.advance()
-        E.zero_adamw_ag(self.p_grad, self.p_comp, self.p_flags, self.rank, self.store.master,
-                        optimizer.exp_avg, optimizer.exp_avg_sq, self.clip, b, e,
-                        self.store.decay_end, lr_d, lr_n, b1, b2, eps, wd, bc1, bc2)
+
+        def update(hp):
+            lr_d, lr_n, b1, b2, eps, wd, bc1, bc2 = hp
+            E.zero_adamw_ag(self.p_grad, self.p_comp, self.p_flags, self.rank, self.store.master,
+                            optimizer.exp_avg, optimizer.exp_avg_sq, self.clip, b, e,
+                            optimizer.state_base, self.store.decay_end, lr_d, lr_n, b1, b2, eps, wd,
+                            bc1, bc2)
+
+        optimizer.step(update=update)
         E.zero_publish(self.p_grad, self.p_comp, self.p_flags, self.rank, self.epoch)
         self.sync_fp32_span()
         return self.norm

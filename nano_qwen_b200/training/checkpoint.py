@@ -83,6 +83,11 @@ class CheckpointManager:
              extra_state: Optional[Dict[str, Any]] = None, sampler=None) -> Path:
         d = self.save_dir / f"step_{step:08d}"
         self.wait()
+        # a sharded optimizer exposes full-shape moments only while a save or
+        # load runs (gathered by the engine's state_for_save, or here)
+        self._release = getattr(optimizer, "release_full_state", None)
+        if self._release is not None:
+            optimizer.gather_full_state()
         if model_parallel(model):
             self._save_sharded(d, model, optimizer)
         elif self.use_dcp:
@@ -101,8 +106,15 @@ class CheckpointManager:
             with open(d / "meta.json", "w") as f:
                 json.dump(meta, f)
             self._cleanup()
+        if self._pending is None:
+            self._release_full()
         barrier()
         return d
+
+    def _release_full(self) -> None:
+        rel, self._release = getattr(self, "_release", None), None
+        if rel is not None:
+            rel()
 
     def _save_sharded(self, d: Path, model, optimizer):
         """Model-parallel runs (tensor / expert / pipeline): every rank writes
@@ -148,6 +160,7 @@ class CheckpointManager:
         if self._pending is not None:
             self._pending.result()
             self._pending = None
+        self._release_full()
 
     # ------------------------------------------------------------------ load
     def load(self, model: nn.Module, optimizer=None, scheduler=None,
@@ -168,13 +181,20 @@ class CheckpointManager:
         elif (d / "checkpoint.pt").exists() and not (d / ".metadata").exists():
             out = self._load_plain(d, model, optimizer, scheduler)
         else:
-            sd = {"model": get_model_state_dict(model)}
-            if optimizer is not None:
-                sd["optimizer"] = get_optimizer_state_dict(model, optimizer)
-            dcp.load(sd, checkpoint_id=str(d))
-            set_model_state_dict(model, sd["model"])
-            if optimizer is not None:
-                set_optimizer_state_dict(model, optimizer, sd["optimizer"])
+            full = getattr(optimizer, "gather_full_state", None)
+            if full is not None:
+                full()  # full-shape views for DCP to load into
+            try:
+                sd = {"model": get_model_state_dict(model)}
+                if optimizer is not None:
+                    sd["optimizer"] = get_optimizer_state_dict(model, optimizer)
+                dcp.load(sd, checkpoint_id=str(d))
+                set_model_state_dict(model, sd["model"])
+                if optimizer is not None:
+                    set_optimizer_state_dict(model, optimizer, sd["optimizer"])
+            finally:
+                if full is not None:
+                    optimizer.release_full_state(scatter=True)
             out = {}
         store = getattr(model, "param_store", None)
         if store is not None:

@@ -101,6 +101,8 @@ class TrainEngine:
             self.model, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),
             beta1=opt.get("beta1", 0.9), beta2=opt.get("beta2", 0.95), eps=opt.get("eps", 1e-8),
             fused=True, store=self.store, shard=self.dp.shard if self.dp is not None else None)
+        if self.dp is not None and hasattr(self.optimizer, "state_gather"):
+            self.optimizer.state_gather = self.dp.gather_flat_
         sch = training_config.get("scheduler", {}) or {}
         self.scheduler = build_scheduler(self.optimizer, scheduler_type=sch.get("type", "cosine"),
                                          warmup_steps=sch.get("warmup_steps", 2000),
@@ -193,6 +195,12 @@ class TrainEngine:
         return sq
 
     def state_for_save(self):
+        """Model, optimizer and scheduler with complete state on every rank:
+        the fp32 master and, when the optimizer keeps only this rank's shard
+        of the Adam moments, full-size gathered moments (released again by the
+        checkpoint manager once the save has consumed them)."""
         if self.dp is not None:
             self.dp.gather_master()
+            if getattr(self.optimizer, "sharded", False):
+                self.optimizer.gather_full_state()
         return self.model, self.optimizer, self.scheduler

@@ -26,8 +26,13 @@ class FusedAdamW(torch.optim.Optimizer):
     """AdamW on a FlatParamStore.
 
     ``shard`` = (begin, end) restricts the update to a slice of the flat
-    buffers (ZeRO-1 style: each data-parallel rank updates its slice and the
-    updated compute copy is all-gathered by the caller).
+    buffers (each data-parallel rank updates its slice and the updated compute
+    copy is all-gathered by the caller).  With a proper slice the Adam moments
+    are allocated for that slice only (``sharded``): 8 B per parameter divided
+    by the data-parallel world instead of 8 B per parameter on every rank.
+    Full-shape per-parameter views of the moments (what ``state_dict`` and DCP
+    see) then exist only between ``gather_full_state`` and
+    ``release_full_state``, which checkpointing calls around a save or load.
     """
 
     def __init__(self, store: FlatParamStore, lr: float = 3e-4, betas=(0.9, 0.95),
@@ -44,18 +49,67 @@ class FusedAdamW(torch.optim.Optimizer):
         super().__init__(groups, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
         dev = store.master.device
         self.shard = shard or (0, store.numel)
-        self.exp_avg = torch.zeros(store.numel, dtype=torch.float32, device=dev)
-        self.exp_avg_sq = torch.zeros(store.numel, dtype=torch.float32, device=dev)
+        b, e = self.shard
+        self.sharded = (b, e) != (0, store.numel)
+        # flat index of element 0 of exp_avg / exp_avg_sq
+        self.state_base = b if self.sharded else 0
+        n = e - b if self.sharded else store.numel
+        self.exp_avg = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(n, dtype=torch.float32, device=dev)
+        self._full = None
+        # completes a full-size buffer across the data-parallel group (set by
+        # the training engine; ``gather_full_state`` uses it by default)
+        self.state_gather = None
         self.step_count = 0
         self.clip_scale = torch.ones((), dtype=torch.float32, device=dev)
         self.last_grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
         for p in store.params:
-            o = store.offset(p)
-            self.state[p] = {
-                "step": torch.zeros((), dtype=torch.float32),
-                "exp_avg": self.exp_avg[o:o + p.numel()].view(p.shape),
-                "exp_avg_sq": self.exp_avg_sq[o:o + p.numel()].view(p.shape),
-            }
+            self.state[p] = {"step": torch.zeros((), dtype=torch.float32)}
+        if not self.sharded:
+            self._bind_views(self.exp_avg, self.exp_avg_sq)
+
+    # ------------------------------------------------------- moment views
+    def _bind_views(self, m: torch.Tensor, v: torch.Tensor) -> None:
+        for p in self.store.params:
+            o = self.store.offset(p)
+            self.state[p]["exp_avg"] = m[o:o + p.numel()].view(p.shape)
+            self.state[p]["exp_avg_sq"] = v[o:o + p.numel()].view(p.shape)
+
+    @torch.no_grad()
+    def gather_full_state(self, gather=None) -> None:
+        """Sharded state: build full-size moment buffers (this rank's slice
+        filled in, the rest zero), let ``gather(buf)`` complete them across the
+        data-parallel group (all-gather), and expose per-parameter views of
+        them in ``self.state``.  No-op for unsharded state."""
+        if not self.sharded or self._full is not None:
+            return
+        b, e = self.shard
+        gather = gather or self.state_gather
+        full = []
+        for shard in (self.exp_avg, self.exp_avg_sq):
+            buf = torch.zeros(self.store.numel, dtype=torch.float32, device=shard.device)
+            buf[b:e].copy_(shard)
+            if gather is not None:
+                gather(buf)
+            full.append(buf)
+        self._full = full
+        self._bind_views(*full)
+
+    @torch.no_grad()
+    def release_full_state(self, scatter: bool = False) -> None:
+        """Drop the full-size buffers of ``gather_full_state``; with
+        ``scatter`` first copy this rank's slice of them back into the shard
+        (after a load wrote into the views)."""
+        if self._full is None:
+            return
+        if scatter:
+            b, e = self.shard
+            self.exp_avg.copy_(self._full[0][b:e])
+            self.exp_avg_sq.copy_(self._full[1][b:e])
+        for p in self.store.params:
+            self.state[p].pop("exp_avg", None)
+            self.state[p].pop("exp_avg_sq", None)
+        self._full = None
 
     # ----------------------------------------------------------- clipping
     @torch.no_grad()
@@ -67,7 +121,7 @@ class FusedAdamW(torch.optim.Optimizer):
         if g.is_cuda:
             sq = ext().sum_squares(g)
         else:
-            sq = (g.double() ** 2).sum().float().reshape(())
+            sq = torch.linalg.vector_norm(g).square().reshape(())
         if norm_sq_reduce is not None:
             sq = norm_sq_reduce(sq)
         norm = sq.sqrt()
@@ -94,16 +148,24 @@ class FusedAdamW(torch.optim.Optimizer):
                 1.0 - beta1 ** t, 1.0 - beta2 ** t)
 
     @torch.no_grad()
-    def step(self, closure=None):
+    def step(self, closure=None, update=None):
+        """One AdamW step over this rank's range.  ``update(hparams)``, when
+        given, performs the update instead of the local kernel (the
+        peer-memory data-parallel step fuses it with the all-gather); going
+        through ``step`` keeps the LR scheduler's step bookkeeping intact."""
         loss = closure() if closure is not None else None
         st = self.store
         b, e = self.shard
-        lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2 = self.advance()
+        hp = self.advance()
+        if update is not None:
+            update(hp)
+            return loss
+        lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2 = hp
         if st.master.is_cuda:
             comp = st.compute if st.compute is not None else torch.empty(0, device=st.master.device)
             ext().adamw_flat(st.master, st.grad, self.exp_avg, self.exp_avg_sq, comp,
-                             self.clip_scale, b, e, st.decay_end, lr_decay, lr_nodecay, beta1,
-                             beta2, eps, wd, bc1, bc2)
+                             self.clip_scale, b, e, self.state_base, st.decay_end, lr_decay,
+                             lr_nodecay, beta1, beta2, eps, wd, bc1, bc2)
         else:
             self._step_cpu(b, e, lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2)
         return loss
@@ -116,8 +178,9 @@ class FusedAdamW(torch.optim.Optimizer):
                 continue
             p = st.master[lo:hi]
             g = st.grad[lo:hi] * self.clip_scale
-            m = self.exp_avg[lo:hi]
-            v = self.exp_avg_sq[lo:hi]
+            sb = self.state_base
+            m = self.exp_avg[lo - sb:hi - sb]
+            v = self.exp_avg_sq[lo - sb:hi - sb]
             p.mul_(1 - lr * w)
             m.mul_(beta1).add_(g, alpha=1 - beta1)
             v.mul_(beta2).addcmul_(g, g, value=1 - beta2)
@@ -131,7 +194,18 @@ class FusedAdamW(torch.optim.Optimizer):
 
     # ------------------------------------------------------- state dict
     def load_state_dict(self, state_dict):
-        """Copy loaded moments into the flat buffers (keeps the views valid)."""
+        """Copy loaded moments into the flat buffers (keeps the views valid);
+        sharded state keeps this rank's slice of them."""
+        materialized = self.sharded and self._full is None
+        if materialized:
+            self.gather_full_state()
+        try:
+            self._load_moments(state_dict)
+        finally:
+            if materialized:
+                self.release_full_state(scatter=True)
+
+    def _load_moments(self, state_dict):
         groups = self.param_groups
         saved_groups = state_dict["param_groups"]
         id_map = {}

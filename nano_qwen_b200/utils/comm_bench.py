@@ -82,7 +82,7 @@ def main(argv=None) -> None:
     clip = torch.ones((), device=dev)
 
     def ag():
-        E.zero_adamw_ag(pg, pc, pf, rank, master, m, v, clip, b, e, e, 1e-4, 1e-4, 0.9, 0.95,
+        E.zero_adamw_ag(pg, pc, pf, rank, master, m, v, clip, b, e, 0, e, 1e-4, 1e-4, 0.9, 0.95,
                         1e-8, 0.1, 0.1, 0.05)
         epoch[0] += 1
         E.zero_publish(pg, pc, pf, rank, epoch[0])
@@ -96,7 +96,7 @@ def main(argv=None) -> None:
         E.sum_squares(out)
 
     def nccl_ag():
-        E.adamw_flat(master, plain, m, v, comp_plain, clip, b, e, e, 1e-4, 1e-4, 0.9, 0.95, 1e-8,
+        E.adamw_flat(master, plain, m, v, comp_plain, clip, b, e, 0, e, 1e-4, 1e-4, 0.9, 0.95, 1e-8,
                      0.1, 0.1, 0.05)
         dist.all_gather_into_tensor(comp_plain, comp_plain[b:e].clone())
 

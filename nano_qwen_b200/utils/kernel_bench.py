@@ -160,7 +160,7 @@ def cases(T: int, H: int, Hq: int, Hk: int, D: int, I: int, B: int, S: int) -> D
         p, g, m, v = (torch.randn(n, device=dev) for _ in range(4))
         comp = torch.empty(n, device=dev, dtype=torch.bfloat16)
         clip = torch.ones((), device=dev)
-        return (lambda: E.adamw_flat(p, g, m, v, comp, clip, 0, n, n, 1e-4, 1e-4, 0.9, 0.95, 1e-8,
+        return (lambda: E.adamw_flat(p, g, m, v, comp, clip, 0, n, 0, n, 1e-4, 1e-4, 0.9, 0.95, 1e-8,
                                      0.1, 0.1, 0.05)), None, n * (16 + 12 + 2)
     out["adamw_flat"] = adamw_flat
     return out

@@ -320,10 +320,32 @@ def test_adamw_flat(E):
     pr.grad = g.clone()
     opt.step()
     clip = torch.ones((), device=DEV)
-    E.adamw_flat(p, g, m, v, comp, clip, 0, n, n, 1e-2, 1e-2, 0.9, 0.95, 1e-8, 0.1, 0.1, 0.05)
+    E.adamw_flat(p, g, m, v, comp, clip, 0, n, 0, n, 1e-2, 1e-2, 0.9, 0.95, 1e-8, 0.1, 0.1, 0.05)
     assert rel_err(p, pr.detach()) < 1e-6
     assert rel_err(comp, pr.detach()) < 1e-2
     assert abs(E.sum_squares(g).item() - (g * g).sum().item()) / (g * g).sum().item() < 1e-5
+
+
+def test_adamw_flat_shard_state(E):
+    """Optimizer state held for a shard only (sbase = begin): the same update
+    as full-size state over that range, and nothing outside it is touched."""
+    torch.manual_seed(14)
+    n, b, e = 4096 * 4, 1024 * 4, 3072 * 4
+    p = torch.randn(n, device=DEV)
+    g = torch.randn(n, device=DEV)
+    clip = torch.full((), 0.5, device=DEV)
+    full = [p.clone(), torch.randn(n, device=DEV).abs(), torch.rand(n, device=DEV)]
+    shard = [p.clone(), full[1][b:e].clone(), full[2][b:e].clone()]
+    cf = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    cs = torch.zeros(n, device=DEV, dtype=torch.bfloat16)
+    args = (2e-3, 1e-3, 0.9, 0.95, 1e-8, 0.1, 0.3, 0.2)
+    E.adamw_flat(full[0], g, full[1], full[2], cf, clip, b, e, 0, 2 * n // 3, *args)
+    E.adamw_flat(shard[0], g, shard[1], shard[2], cs, clip, b, e, b, 2 * n // 3, *args)
+    assert torch.equal(shard[0], full[0])
+    assert torch.equal(shard[1], full[1][b:e]) and torch.equal(shard[2], full[2][b:e])
+    assert torch.equal(cs[b:e], cf[b:e]) and not cs[:b].any() and not cs[e:].any()
+    with pytest.raises(Exception):
+        E.adamw_flat(shard[0], g, shard[1], shard[2], cs, clip, b - 4, e, b, n, *args)
 
 
 # ------------------------------------------------------------------- MoE
