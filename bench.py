@@ -43,6 +43,8 @@ DP_LABEL = {"p2p": "ZeRO-2, fused peer-memory reduce-scatter + sharded AdamW + a
             "replicate": "NCCL all-reduce"}
 
 BASELINE_METRIC = "train tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; MFU"
+# the only measured reference number: its CPU fp32 debug step (BASELINE config #1)
+CPU_BASELINE_TOKS = 1169.0
 
 CONFIGS = {
     # name: (model kwargs, per-GPU micro batch, seq, parallel label)
@@ -111,6 +113,8 @@ def parse():
                    help="ours, tp/ep configs: peer-memory fused kernels or NCCL collectives")
     p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate"],
                    help="ours, N>1: peer-memory fused ZeRO step (p2p) or NCCL ZeRO-2 / all-reduce")
+    p.add_argument("--device", default="cuda", choices=["cuda", "cpu"],
+                   help="cpu: fp32 on the host, world size 1 (BASELINE config #1 with --config debug)")
     return p.parse_args()
 
 
@@ -169,13 +173,16 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ common
+DEVICE = "cuda"  # --device
+
+
 def dist_setup():
     import torch
-    import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
+    if DEVICE == "cuda":
+        torch.cuda.set_device(local)
     return world, rank, local
 
 
@@ -246,6 +253,14 @@ def synthetic_batches(n, B, S, V, device, seed=1234, pinned=False):
 def timed_loop(step_fn, inputs, K, W, local):
     """Warm-up W, then K device-timed steps; returns ms/step (max over ranks) and clocks."""
     import torch
+    if DEVICE == "cpu":  # host-timed (fp32 on the CPU, one process)
+        for i in range(W):
+            step_fn(inputs[i % len(inputs)])
+        t0 = time.perf_counter()
+        for i in range(K):
+            step_fn(inputs[i % len(inputs)])
+        return (time.perf_counter() - t0) * 1e3 / K, {"sm_mhz": None, "sm_max_mhz": None,
+                                                       "reasons": ["cpu run"]}
     for i in range(W):
         step_fn(inputs[i % len(inputs)])
     barrier()
@@ -280,7 +295,7 @@ def run_ours(args, world, rank, local):
 
     mk, B, S, par = CONFIGS[args.config]
     init_distributed()
-    dev = torch.device("cuda", local)
+    dev = torch.device("cuda", local) if DEVICE == "cuda" else torch.device("cpu")
     torch.manual_seed(0)
     cfg = ModelConfig(**mk)
     with torch.device(dev):
@@ -306,6 +321,10 @@ def run_ours(args, world, rank, local):
     def step(ids):
         eng.train_step([{"input_ids": ids, "labels": ids}])
 
+    if DEVICE == "cpu":
+        ms, clocks = timed_loop(step, inputs, args.steps, args.warmup, local)
+        return ms, clocks, {"kernel_error_flag": 0, "gpu_launches_per_step": {"ours": 0, "all": 0},
+                            "dp_mode": None}, None
     ext().error_flag_clear()
     ms, clocks = timed_loop(step, inputs, args.steps, args.warmup, local)
     err = ext().error_flag_read()
@@ -425,6 +444,8 @@ def run_reference(args, world, rank, local):
     from training.scheduler import build_scheduler
 
     mk, B, S, par = CONFIGS[args.config]
+    if DEVICE == "cpu":
+        return run_reference_cpu(args, mk, B, S)
     if par == "tp":
         # substituted baseline (the reference's TP path does not run): FSDP2 over the
         # same global batch, i.e. B / N sequences per rank
@@ -479,6 +500,30 @@ def run_reference(args, world, rank, local):
     return ms, clocks, {}, e2e
 
 
+def run_reference_cpu(args, mk, B, S):
+    """BASELINE config #1: the reference's Qwen3Model + build_optimizer (unfused
+    AdamW on the CPU) + clip_grad_norm_, fp32, one process, host-timed."""
+    import torch
+    import torch.nn as nn
+    from model.config import ModelConfig as RC  # noqa: E402  (reference code)
+    from model.transformer import Qwen3Model as RM
+    from training.optimizer import build_optimizer
+    torch.manual_seed(0)
+    model = RM(RC(**mk))
+    opt = build_optimizer(model, lr=3e-4, weight_decay=0.1, fused=False)
+    inputs = synthetic_batches(4, B, S, mk["vocab_size"], None, seed=1234)
+
+    def step(ids):
+        opt.zero_grad()
+        out = model(input_ids=ids, labels=ids)
+        out["loss"].backward()
+        nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+
+    ms, clocks = timed_loop(step, inputs, args.steps, args.warmup, 0)
+    return ms, clocks, {}, None
+
+
 def parallel_label(par, world, impl, mode):
     if world == 1:
         return "dp1"
@@ -499,7 +544,12 @@ def parallel_label(par, world, impl, mode):
 def main():
     args = parse()
     import torch
+    global DEVICE
+    DEVICE = args.device
     world, rank, local = dist_setup()
+    if DEVICE == "cpu" and world > 1:
+        print(json.dumps({"error": "--device cpu runs one process"}))
+        return 2
     if args.gpus != world and world == 1 and args.gpus > 1:
         print(json.dumps({"error": "launch N>1 with torch.distributed.run"}))
         return 2
@@ -525,7 +575,7 @@ def main():
     tokens_per_step = B * S * (1 if par in ("tp", "cp") else world)
     value = tokens_per_step / (ms / 1e3)
     fpt = flops_per_token(mk, S)
-    mfu = value * fpt / (measured_peak() * world)
+    mfu = value * fpt / (measured_peak() * world) if DEVICE == "cuda" else None
     line = {
         "metric": BASELINE_METRIC,
         "value": round(value, 1),
@@ -536,15 +586,16 @@ def main():
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
         "scaling": "strong" if par in ("tp", "cp") else "weak",
-        "vs_baseline": None,
-        "dtype": "bf16",
+        "vs_baseline": (round(value / CPU_BASELINE_TOKS, 3)
+                        if DEVICE == "cpu" and args.config == "debug" else None),
+        "dtype": "bf16" if DEVICE == "cuda" else "fp32",
         "data": "synthetic uniform-random token ids, random-init weights",
         "config": {"model": f"{args.config} (Qwen3-1.7B shape: L28 h2048 16Q/8KV hd128 I6144 V151936 tied)"
                    if args.config == "qwen3-1.7b" else args.config,
                    "global_batch": B * (1 if par in ("tp", "cp") else world), "seq_len": S,
                    "parallelism": parallel_label(par, world, args.impl, extra.get("dp_mode")),
                    "l2": "no flush: per-step working set (weights + activations) >> 126 MB L2"},
-        "mfu": round(mfu, 4),
+        "mfu": round(mfu, 4) if mfu is not None else None,
         "flops_per_token": fpt,
         "clocks": clocks,
     }

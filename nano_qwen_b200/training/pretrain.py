@@ -143,11 +143,11 @@ class PreTrainer:
                 dt = max_over_ranks(dt)
                 tps = ntok / dt
                 n_params = sum(p.numel() for p in self.model.parameters())
-                self.logger.log_step(step=step, loss=float(out["loss"]),
+                # device scalars: the logger reads them back in one copy
+                self.logger.log_step(step=step, loss=out["loss"],
                                      lr=self.scheduler.get_last_lr()[0],
-                                     grad_norm=float(out["grad_norm"]), tokens_per_sec=tps,
-                                     aux_loss=(float(out["aux_loss"]) if out["aux_loss"] is not None
-                                               else None),
+                                     grad_norm=out["grad_norm"], tokens_per_sec=tps,
+                                     aux_loss=out["aux_loss"],
                                      mfu=mfu(self.model_config, seq_len, tps, self.world_size))
             if self.ckpt_mgr.should_save(step):
                 model, opt, sch = self.engine.state_for_save()

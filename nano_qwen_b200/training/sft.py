@@ -144,9 +144,9 @@ class SFTTrainer:
             out = self.engine.train_step(mbs)
             step += 1
             if step % self.logger.log_interval == 0:
-                self.logger.log_step(step=step, loss=float(out["loss"]),
+                self.logger.log_step(step=step, loss=out["loss"],
                                      lr=self.scheduler.get_last_lr()[0],
-                                     grad_norm=float(out["grad_norm"]))
+                                     grad_norm=out["grad_norm"])
             if self.ckpt_mgr.should_save(step):
                 m, o, s = self.engine.state_for_save()
                 self.ckpt_mgr.save(step, m, o, s, extra_state={"step": step})
