@@ -41,13 +41,17 @@ class ImageProcessor:
         if isinstance(image, str):
             image = Image.open(image)
         image = image.convert("RGB")
+        n = self.image_size
         w, h = image.size
-        s = self.image_size / min(w, h)
-        image = image.resize((max(self.image_size, round(w * s)), max(self.image_size, round(h * s))),
-                             Image.BICUBIC)
+        # shorter side -> n, longer side scaled and truncated (the reference's
+        # torchvision Resize(n) rule), bicubic; then a centre crop whose offset
+        # rounds half to even like the reference's CenterCrop
+        size = (n, int(n * h / w)) if w <= h else (int(n * w / h), n)
+        if size != (w, h):
+            image = image.resize(size, Image.BICUBIC)
         w, h = image.size
-        left, top = (w - self.image_size) // 2, (h - self.image_size) // 2
-        image = image.crop((left, top, left + self.image_size, top + self.image_size))
+        left, top = int(round((w - n) / 2.0)), int(round((h - n) / 2.0))
+        image = image.crop((left, top, left + n, top + n))
         import numpy as np
         x = torch.from_numpy(np.asarray(image, dtype="float32") / 255.0).permute(2, 0, 1)
         return (x - self.mean) / self.std

@@ -31,7 +31,10 @@ class Linear(nn.Module):
 
 
 def compute_dtype_of(x: torch.Tensor) -> torch.dtype:
-    return torch.float32 if x.dtype == torch.float32 and not x.is_cuda else x.dtype
+    """GEMM input dtype: bf16 on the GPU (the tcgen05 kernels' operand type,
+    whatever the activation's dtype, e.g. an fp32 residual stream), the
+    input's own dtype on the CPU."""
+    return torch.bfloat16 if x.is_cuda else x.dtype
 
 
 def fused_linear(x: torch.Tensor, linears: Sequence[Linear], dtype: torch.dtype) -> torch.Tensor:

@@ -116,10 +116,32 @@ class DataParallel:
         return [(0, xb), (xe, n)]
 
     def norm_sq_reduce(self, sq: torch.Tensor) -> torch.Tensor:
-        """Sum a per-rank squared norm (shard mode) over the group."""
-        if self.world > 1 and self.mode == "shard":
+        """Global squared gradient norm from this rank's part.
+
+        Shard mode: each rank holds a disjoint shard, so the parts add up.
+        Replicate mode with an expert span (expert parallelism): the dense
+        gradient is the same on every rank after the reduction, but each rank
+        holds other experts, so the expert part is summed over the group and
+        divided by the number of ranks holding each expert set.  Without that,
+        every rank would clip with its own norm and the replicated weights
+        would drift apart."""
+        if self.world <= 1:
+            return sq
+        if self.mode == "shard":
             sq = sq.clone()
             dist.all_reduce(sq, group=self.group)
+        elif self.expert_span is not None:
+            xb, xe = self.expert_span
+            g = self.store.grad[xb:xe]
+            if g.is_cuda:
+                from ..ops._ext import ext
+                part = ext().sum_squares(g).reshape(sq.shape)
+            else:
+                part = torch.linalg.vector_norm(g).square().reshape(sq.shape)
+            tot = part.clone()
+            dist.all_reduce(tot, group=self.group)
+            reps = get_world_size(self.expert_group) if self.expert_group is not None else 1
+            sq = sq - part + tot / reps
         return sq
 
     # ------------------------------------------------------------ parameters

@@ -11,8 +11,12 @@ Additions over the reference: the full CPU/CUDA RNG state and sampler state are
 saved and restored (the reference saves 8 bytes of CPU RNG and never restores
 them), ``async_save`` really runs DCP's ``async_save`` and the plain path keeps
 ``step`` on resume (reference: training/checkpoint.py:174 loses it).
-Model-parallel runs (tensor / expert / pipeline shards) write one
-``shard_{rank:05d}.pt`` per rank in the same step directory.
+Model-parallel runs (tensor / expert / pipeline shards) save through DCP
+as well, under the single-process model's parameter names with TP shards as
+DTensors (``dcp_state``), so a checkpoint of one layout loads into another;
+their optimizer hyper-parameters go to ``meta.json``.  Loading always asks
+DCP for the logical names, which also reads replicated and reference-written
+checkpoints.
 """
 
 from __future__ import annotations
@@ -88,8 +92,12 @@ class CheckpointManager:
         self._release = getattr(optimizer, "release_full_state", None)
         if self._release is not None:
             optimizer.gather_full_state()
-        if model_parallel(model):
-            self._save_sharded(d, model, optimizer)
+        groups = None
+        if optimizer is not None:
+            groups = [{k: v for k, v in g.items() if k != "params" and isinstance(v, (int, float, list, tuple))}
+                      for g in optimizer.param_groups]
+        if model_parallel(model) and HAS_DCP:
+            self._save_logical(d, model, optimizer)
         elif self.use_dcp:
             self._save_dcp(d, model, optimizer)
         else:
@@ -103,6 +111,8 @@ class CheckpointManager:
                 "rng": _rng_state(),
                 "sampler": sampler.state_dict() if sampler is not None else None,
             }
+            if groups is not None:
+                meta["optimizer_param_groups"] = groups
             with open(d / "meta.json", "w") as f:
                 json.dump(meta, f)
             self._cleanup()
@@ -116,18 +126,15 @@ class CheckpointManager:
         if rel is not None:
             rel()
 
-    def _save_sharded(self, d: Path, model, optimizer):
-        """Model-parallel runs (tensor / expert / pipeline): every rank writes
-        its own shard file with the local parameter names; loading expects the
-        same parallel layout (same world size and axis sizes)."""
-        d.mkdir(parents=True, exist_ok=True)
-        state = {"model": {k: v.detach().cpu() for k, v in model.state_dict().items()}}
-        if optimizer is not None:
-            state["optimizer"] = optimizer.state_dict()
-        torch.save(state, d / f"shard_{get_rank():05d}.pt")
-        if is_main_process():
-            with open(d / "sharded.json", "w") as f:
-                json.dump({"world_size": get_world_size()}, f)
+    def _save_logical(self, d: Path, model, optimizer):
+        """Model-parallel runs: DCP save of the logical (single-process) state
+        (the optimizer's hyper-parameters go to ``meta.json``)."""
+        from .dcp_state import model_parallel_state
+        sd = model_parallel_state(model, optimizer)
+        if self.async_save and torch.distributed.is_initialized():
+            self._pending = dcp.async_save(sd, checkpoint_id=str(d))
+        else:
+            dcp.save(sd, checkpoint_id=str(d))
 
     def _save_dcp(self, d: Path, model, optimizer):
         sd = {"model": get_model_state_dict(model)}
@@ -181,20 +188,7 @@ class CheckpointManager:
         elif (d / "checkpoint.pt").exists() and not (d / ".metadata").exists():
             out = self._load_plain(d, model, optimizer, scheduler)
         else:
-            full = getattr(optimizer, "gather_full_state", None)
-            if full is not None:
-                full()  # full-shape views for DCP to load into
-            try:
-                sd = {"model": get_model_state_dict(model)}
-                if optimizer is not None:
-                    sd["optimizer"] = get_optimizer_state_dict(model, optimizer)
-                dcp.load(sd, checkpoint_id=str(d))
-                set_model_state_dict(model, sd["model"])
-                if optimizer is not None:
-                    set_optimizer_state_dict(model, optimizer, sd["optimizer"])
-            finally:
-                if full is not None:
-                    optimizer.release_full_state(scatter=True)
+            self._load_logical(d, model, optimizer)
             out = {}
         store = getattr(model, "param_store", None)
         if store is not None:
@@ -203,6 +197,9 @@ class CheckpointManager:
         if meta_p.exists():
             with open(meta_p) as f:
                 meta = json.load(f)
+            if optimizer is not None and meta.get("optimizer_param_groups"):
+                for g, sg in zip(optimizer.param_groups, meta["optimizer_param_groups"]):
+                    g.update({k: tuple(v) if k == "betas" else v for k, v in sg.items()})
             if scheduler is not None and meta.get("scheduler"):
                 scheduler.load_state_dict(meta["scheduler"])
             if meta.get("rng"):
@@ -211,6 +208,27 @@ class CheckpointManager:
                 sampler.load_state_dict(meta["sampler"])
             out.update(meta)
         return out
+
+    def _load_logical(self, d: Path, model, optimizer):
+        """DCP load by logical parameter names into whatever layout this run
+        has (TP shards read their chunks, EP ranks their experts, PP stages
+        their layers).  Works for model-parallel, replicated and
+        reference-written checkpoints alike."""
+        from .dcp_state import logical_load_state
+        full = getattr(optimizer, "gather_full_state", None)
+        if full is not None:
+            full()  # full-shape moment views for DCP to load into
+        try:
+            sd = logical_load_state(model, optimizer)
+            if optimizer is not None and not sd.get("optimizer", {}).get("state"):
+                sd.pop("optimizer", None)
+            dcp.load(sd, checkpoint_id=str(d))
+        finally:
+            if full is not None:
+                optimizer.release_full_state(scatter=True)
+        if optimizer is not None and hasattr(optimizer, "step_count"):
+            steps = [float(st["step"]) for st in optimizer.state.values() if "step" in st]
+            optimizer.step_count = int(max(steps)) if steps else 0
 
     def _load_plain(self, d, model, optimizer, scheduler):
         st = torch.load(d / "checkpoint.pt", map_location="cpu", weights_only=False)

@@ -274,9 +274,81 @@ def tp_checkpoint_worker(rank, world, port, tmp):
     mgr.load(e2.model, e2.optimizer, e2.scheduler, str(path))
     for (n, p), q in zip(e1.model.named_parameters(), e2.model.parameters()):
         assert torch.equal(p, q), n
+    # the same checkpoint loads at tp1 (the single-process layout): weights and
+    # Adam moments are the concatenation of the tp2 shards
+    e3 = TrainEngine(build(cfg, seed=9), tcfg, torch.device("cpu"), dp_group=singles[rank])
+    mgr.load(e3.model, e3.optimizer, e3.scheduler, str(path))
+    full = dict(e3.model.named_parameters())
+    for n, p in e1.model.named_parameters():
+        q = full[n]
+        mom = (e1.optimizer.state[p]["exp_avg"], e3.optimizer.state[q]["exp_avg"])
+        if getattr(p, "_tp_sharded", False):
+            dim = 0 if p.shape[0] != q.shape[0] else 1
+            k = p.shape[dim]
+            q = q.narrow(dim, rank * k, k)
+            mom = (mom[0], mom[1].narrow(dim, rank * k, k))
+        assert torch.equal(p, q), n
+        assert torch.equal(*mom), n
+    assert e3.optimizer.step_count == e1.optimizer.step_count
     a = e1.train_step([{"input_ids": ids, "labels": ids}])
     b = e2.train_step([{"input_ids": ids, "labels": ids}])
+    c = e3.train_step([{"input_ids": ids, "labels": ids}])
     assert torch.allclose(a["loss"], b["loss"])
+    assert torch.allclose(a["loss"], c["loss"], rtol=1e-5, atol=1e-6), (a["loss"], c["loss"])
+    # and back: the tp1 engine's checkpoint loads at tp2
+    mgr2 = CheckpointManager(save_dir=tmp + "/tp1", save_interval=1, async_save=False)
+    path2 = mgr2.save(2, *e3.state_for_save(), extra_state={"step": 2})
+    e4 = TrainEngine(apply_tensor_parallel(build(cfg, seed=7), grp, sequence_parallel=True), tcfg,
+                     torch.device("cpu"), dp_group=singles[rank])
+    e4.tp_group = grp
+    mgr2.load(e4.model, e4.optimizer, e4.scheduler, str(path2))
+    full = dict(e3.model.named_parameters())
+    for n, p in e4.model.named_parameters():
+        q = full[n]
+        if getattr(p, "_tp_sharded", False):
+            dim = 0 if p.shape[0] != q.shape[0] else 1
+            q = q.narrow(dim, rank * p.shape[dim], p.shape[dim])
+        assert torch.equal(p, q), n
+    dist.destroy_process_group()
+
+
+def ep_checkpoint_worker(rank, world, port, tmp):
+    """An expert-parallel checkpoint names experts by their global index, so it
+    loads into the single-process layout (every rank holding all experts)."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.expert_parallel import apply_expert_parallel
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg(moe=True)
+    grp = dist.new_group(list(range(world)))
+    tcfg = {"optimizer": {"lr": 1e-2}, "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    # data parallel over both ranks keeps the replicated (dense) weights equal
+    e1 = TrainEngine(apply_expert_parallel(build(cfg), grp, fused=False), tcfg, torch.device("cpu"))
+    ids = batch(cfg, 2, 16, seed=rank)
+    e1.train_step([{"input_ids": ids, "labels": ids}])
+    mgr = CheckpointManager(save_dir=tmp, save_interval=1, async_save=False)
+    path = mgr.save(1, *e1.state_for_save(), extra_state={"step": 1})
+    # single layout, ZeRO-sharded Adam moments over the two ranks
+    e2 = TrainEngine(build(cfg, seed=3), tcfg, torch.device("cpu"))
+    assert e2.optimizer.sharded
+    mgr.load(e2.model, e2.optimizer, e2.scheduler, str(path))
+    e2.optimizer.gather_full_state()
+    full = dict(e2.model.named_parameters())
+    e_loc = cfg.num_experts // world
+    n_checked = 0
+    for n, p in e1.model.named_parameters():
+        if ".experts." in n:
+            pre, rest = n.split(".experts.", 1)
+            e, tail = rest.split(".", 1)
+            n = f"{pre}.experts.{int(e) + rank * e_loc}.{tail}"
+            n_checked += 1
+            assert torch.equal(p, full[n]), n
+            assert torch.equal(e1.optimizer.state[p]["exp_avg"], e2.optimizer.state[full[n]]["exp_avg"]), n
+        else:
+            assert torch.equal(p, full[n]), n
+            assert torch.equal(e1.optimizer.state[p]["exp_avg"], e2.optimizer.state[full[n]]["exp_avg"]), n
+    assert n_checked > 0
+    e2.optimizer.release_full_state()
     dist.destroy_process_group()
 
 
@@ -385,4 +457,35 @@ def zero_checkpoint_worker(rank, world, port, tmp):
     b.dp.gather_master()
     assert torch.equal(a.store.master, b.store.master)
     dist.barrier()
+    dist.destroy_process_group()
+
+
+def pp_checkpoint_worker(rank, world, port, tmp):
+    """A pipeline-parallel checkpoint names layers by their global index, so
+    it loads into the single-process layout."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.pipeline_parallel import apply_pipeline_parallel
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg(num_hidden_layers=4)
+    grp = dist.new_group(list(range(world)))
+    singles = [dist.new_group([r]) for r in range(world)]
+    tcfg = {"optimizer": {"lr": 1e-2}, "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    pm = apply_pipeline_parallel(build(cfg), grp, list(range(world)), n_microbatches=2)
+    e1 = TrainEngine(pm, tcfg, torch.device("cpu"), dp_group=singles[rank])
+    e1.pp_group = grp
+    ids = batch(cfg, 4, 16)
+    e1.train_step([{"input_ids": ids, "labels": ids}])
+    mgr = CheckpointManager(save_dir=tmp, save_interval=1, async_save=False)
+    path = mgr.save(1, *e1.state_for_save(), extra_state={"step": 1})
+    e2 = TrainEngine(build(cfg, seed=3), tcfg, torch.device("cpu"), dp_group=singles[rank])
+    mgr.load(e2.model, e2.optimizer, e2.scheduler, str(path))
+    full = dict(e2.model.named_parameters())
+    off = pm.stage_layers[rank][0]
+    for n, p in pm.model.named_parameters():
+        if n.startswith("layers."):
+            i, tail = n[len("layers."):].split(".", 1)
+            n = f"layers.{int(i) + off}.{tail}"
+        assert torch.equal(p, full[n]), n
+        assert torch.equal(e1.optimizer.state[p]["exp_avg"], e2.optimizer.state[full[n]]["exp_avg"]), n
     dist.destroy_process_group()

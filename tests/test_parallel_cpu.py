@@ -54,8 +54,12 @@ def test_heartbeat_detects_silent_rank():
     _run(W.heartbeat_worker, 3, 1)
 
 
-def test_tensor_parallel_checkpoint_roundtrip(tmp_path):
+def test_tensor_parallel_checkpoint_roundtrip_and_reshard(tmp_path):
     _run(W.tp_checkpoint_worker, 2, str(tmp_path))
+
+
+def test_expert_parallel_checkpoint_loads_single_layout(tmp_path):
+    _run(W.ep_checkpoint_worker, 2, str(tmp_path))
 
 
 def test_global_batch_moe_balance():
@@ -68,3 +72,7 @@ def test_rank_leaving_between_steps_is_detected():
 
 def test_zero_shard_checkpoint_resumes_exactly(tmp_path):
     _run(W.zero_checkpoint_worker, 2, str(tmp_path))
+
+
+def test_pipeline_parallel_checkpoint_loads_single_layout(tmp_path):
+    _run(W.pp_checkpoint_worker, 2, str(tmp_path))
