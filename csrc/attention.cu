@@ -65,6 +65,10 @@ struct AttnArgs {
   const unsigned* kv_flags;
   unsigned kv_seq;
   int cp_c, cp_world;
+  // Key-range mask (document packing, left padding): query token i sees keys
+  // [kv_lo[i], i] of its row; kv_lo is non-decreasing along a row.  The CTA
+  // skips every key block before kv_lo of its first query.  null: causal only.
+  const int* kv_lo;
 };
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -130,8 +134,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int Sk = args.Sk;
   const int ktok0 = b * Sk;
   const int qoff = (q0 < args.split) ? args.off0 : args.off1;  // CTA rows share one chunk
-  const int n_kblk = args.causal ? min((q0 + qoff + CTA_M + ABN - 1) / ABN, (Sk + ABN - 1) / ABN)
+  const int n_kend = args.causal ? min((q0 + qoff + CTA_M + ABN - 1) / ABN, (Sk + ABN - 1) / ABN)
                                  : (Sk + ABN - 1) / ABN;
+  // first key block (key-range mask); the loops below count iterations j from
+  // 0 and read key block jb + j
+  const int jb = (args.kv_lo != nullptr) ? min(args.kv_lo[tok0 + q0] / ABN, n_kend) : 0;
+  const int n_kblk = n_kend - jb;
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
@@ -174,7 +182,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t ph = static_cast<uint32_t>(j / NKV) & 1;
         if (!mbar_wait(&kv_empty[st], ph ^ 1, err, kErrTimeoutProducer)) { ok = false; break; }
         if (args.kv_flags != nullptr) {
-          const int chunk = (j * ABN) / args.cp_c;
+          const int chunk = ((jb + j) * ABN) / args.cp_c;
           const int owner = chunk < args.cp_world ? chunk : 2 * args.cp_world - 1 - chunk;
           if (owner != waited) {
             if (!wait_flag(args.kv_flags + owner, args.kv_seq, err)) { ok = false; break; }
@@ -185,11 +193,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive_expect_tx(&k_full[st], L::kKVBytes);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-          tma_load_3d(sK + st * L::kKVBytes + c * ABN * 128, &tmK, &k_full[st], c * 64, args.k_head + hk, ktok0 + j * ABN);
+          tma_load_3d(sK + st * L::kKVBytes + c * ABN * 128, &tmK, &k_full[st], c * 64, args.k_head + hk, ktok0 + (jb + j) * ABN);
         mbar_arrive_expect_tx(&v_full[st], L::kKVBytes);
 #pragma unroll
         for (int c = 0; c < KCH; ++c)
-          tma_load_3d(sV + st * L::kKVBytes + c * ABN * 128, &tmV, &v_full[st], c * 64, args.v_head + hk, ktok0 + j * ABN);
+          tma_load_3d(sV + st * L::kKVBytes + c * ABN * 128, &tmV, &v_full[st], c * 64, args.v_head + hk, ktok0 + (jb + j) * ABN);
       }
     }
   } else if (warp == 1) {
@@ -254,6 +262,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float m_ref = -INFINITY;
     float l = 0.f;
     bool ok = true;
+    const int lo = (args.kv_lo != nullptr) ? args.kv_lo[tok0 + min(qi, S - 1)] : 0;
     for (int j = 0; j < n_kblk; ++j) {
       if (!mbar_wait(&s_full[t * 2 + (j & 1)], static_cast<uint32_t>(j >> 1) & 1, err, kErrTimeoutSoftmax)) {
         ok = false;
@@ -269,8 +278,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < NCK; ++c) tmem_ld32(tS + c * 32, u[c]);
       tmem_wait_ld();
-      const int k0 = j * ABN;
-      const bool need_mask = (args.causal && k0 + ABN - 1 > q0 + qoff + t * ABM) || (k0 + ABN > Sk);
+      const int k0 = (jb + j) * ABN;
+      const bool need_mask = (args.causal && k0 + ABN - 1 > q0 + qoff + t * ABM) || (k0 + ABN > Sk) ||
+                             (k0 < lo);
       // Raw scores stay in registers; the scale (> 0) is applied to the max and
       // folded into the exponent's FFMA.
       if (need_mask) {
@@ -279,7 +289,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int kj = k0 + c * 32 + i;
-            if (kj >= Sk || (args.causal && kj > qi + qoff)) u[c][i] = 0xff800000u;  // -inf
+            if (kj >= Sk || (args.causal && kj > qi + qoff) || kj < lo) u[c][i] = 0xff800000u;  // -inf
           }
       }
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -385,6 +395,7 @@ struct AttnKV {
   const unsigned* kv_flags = nullptr;
   unsigned kv_seq = 0;
   int cp_c = 1, cp_world = 1;
+  const int* kv_lo = nullptr;  // key-range mask (self-attention only)
 };
 
 template <int D>
@@ -410,6 +421,7 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
     a.Sk = S; a.k_head = Hq; a.v_head = Hq + Hk;
     a.off0 = 0; a.off1 = 0; a.split = S;
   }
+  a.kv_lo = cp.kv_lo;
   a.B = B; a.S = S; a.Hq = Hq; a.Hk = Hk;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.causal = causal ? 1 : 0;
@@ -424,7 +436,8 @@ static void launch_attn_fwd(const torch::Tensor& qk, const torch::Tensor& qkv, t
 }
 
 std::vector<torch::Tensor> attn_fwd(torch::Tensor qk, torch::Tensor qkv, int64_t B, int64_t S,
-                                    int64_t Hq, int64_t Hk, int64_t D, bool causal, double scale) {
+                                    int64_t Hq, int64_t Hk, int64_t D, bool causal, double scale,
+                                    c10::optional<torch::Tensor> kv_lo) {
   check_bf16(qk, "qk"); check_bf16(qkv, "qkv");
   TORCH_CHECK(qk.is_contiguous() && qkv.is_contiguous(), "attn_fwd: contiguous inputs");
   TORCH_CHECK(qk.size(1) == (Hq + Hk) * D && qkv.size(1) == (Hq + 2 * Hk) * D, "attn_fwd: widths");
@@ -433,8 +446,15 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qk, torch::Tensor qkv, int64_t
   auto o = torch::empty({B * S, Hq * D}, qk.options());
   auto lse = torch::empty({B, Hq, S}, qk.options().dtype(torch::kFloat32));
   if (B * S == 0) return {o, lse};
-  if (D == 128) launch_attn_fwd<128>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale);
-  else if (D == 64) launch_attn_fwd<64>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale);
+  AttnKV self;
+  if (kv_lo.has_value() && kv_lo->defined()) {
+    TORCH_CHECK(causal, "attn_fwd: the key-range mask applies to causal attention");
+    TORCH_CHECK(kv_lo->is_cuda() && kv_lo->scalar_type() == torch::kInt32 && kv_lo->is_contiguous() &&
+                    kv_lo->numel() == B * S, "attn_fwd: kv_lo int32 [B*S]");
+    self.kv_lo = kv_lo->data_ptr<int>();
+  }
+  if (D == 128) launch_attn_fwd<128>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, self);
+  else if (D == 64) launch_attn_fwd<64>(qk, qkv, o, lse, B, S, Hq, Hk, causal, (float)scale, self);
   else TORCH_CHECK(false, "attn_fwd: head_dim must be 64 or 128");
   return {o, lse};
 }

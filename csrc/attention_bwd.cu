@@ -71,6 +71,11 @@ struct AttnBwdArgs {
   // Self-attention: Sk = S, offsets 0, dkv_cp null.
   int Sk, k_head, v_head, off0, off1, split;
   float* dkv_cp;
+  // Key-range mask (the forward's kv_lo, seen from the keys): key token j is
+  // seen by queries [j, q_hi[j]) of its row; q_hi is non-decreasing along a
+  // row, so a key block's last key bounds the query blocks to visit.
+  // null: causal only.
+  const int* q_hi;
 };
 
 __device__ __forceinline__ float bwd_ex2(float x) {
@@ -146,6 +151,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   // blocks [0, split/BQM) at offset off0, chunk 1 the rest at offset off1.
   const int split_mb = (args.split + BQM - 1) / BQM;
   int b0 = 0, e0 = split_mb, b1 = split_mb, e1 = n_mblk;
+  if (args.q_hi != nullptr) e0 = min(e0, (args.q_hi[ktok0 + min(k0 + BKN, Sk) - 1] + BQM - 1) / BQM);
   if (args.causal) {
     // first block with a query at key position >= k0 (floor division of possibly negative values)
     const int f0 = k0 - args.off0, f1 = k0 - args.off1;
@@ -318,6 +324,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int col0 = wg * 64;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int kj = k0 + r;              // this thread's key position
+    const int qhi = (args.q_hi != nullptr) ? args.q_hi[ktok0 + min(kj, Sk - 1)] : 0x7fffffff;
     bool ok = true;
     for (int it = 0; it < n_iter; ++it) {
       int hq, mb;
@@ -328,7 +335,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!mbar_wait(s_full, ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       tc_fence_after();
       const int qoff = qoff_of(q0);
-      const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + BQM > S) || (k0 + BKN > Sk);
+      const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + BQM > S) || (k0 + BKN > Sk) ||
+                             (q0 + BQM > qhi);
       uint32_t us2[2][32], ud2[2][32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -361,7 +369,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int qi = q0 + col0 + c + i;
-            const bool m = (qi >= S) || (kj >= Sk) || (args.causal && kj > qi + qoff);
+            const bool m = (qi >= S) || (kj >= Sk) || (args.causal && kj > qi + qoff) || (qi >= qhi);
             p[i] = m ? 0.f : p[i];
             ds[i] = m ? 0.f : ds[i];
           }
@@ -550,6 +558,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int n_mblk = (S + PBQ - 1) / PBQ;
   const int split_mb = (args.split + PBQ - 1) / PBQ;
   int b0 = 0, e0 = split_mb, b1 = split_mb, e1 = n_mblk;
+  if (args.q_hi != nullptr) e0 = min(e0, (args.q_hi[ktok0 + min(k0 + BKN, Sk) - 1] + PBQ - 1) / PBQ);
   if (args.causal) {
     const int f0 = k0 - args.off0, f1 = k0 - args.off1;
     b0 = max(b0, f0 >= 0 ? f0 / PBQ : 0);
@@ -733,6 +742,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tS = tmem + 128 * w + lane_base, tP = tS + 64;
     const int kj = k0 + r;
+    const int qhi = (args.q_hi != nullptr) ? args.q_hi[ktok0 + min(kj, Sk - 1)] : 0x7fffffff;
     const float* lse = sLse(w);
     const float* dlt = lse + PBQ;
     uint8_t* ds_tile = sDS(w);
@@ -747,7 +757,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!mbar_wait(&s_full[w], ph, err, kErrTimeoutSoftmax)) { ok = false; break; }
       tc_fence_after();
       const int qoff = qoff_of(q0);
-      const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + PBQ > S) || (k0 + BKN > Sk);
+      const bool need_mask = (args.causal && k0 + BKN - 1 > q0 + qoff) || (q0 + PBQ > S) || (k0 + BKN > Sk) ||
+                             (q0 + PBQ > qhi);
       uint32_t us2[2][32], ud2[2][32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -777,7 +788,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int qi = q0 + 32 * c + i;
-            const bool m = (qi >= S) || (kj >= Sk) || (args.causal && kj > qi + qoff);
+            const bool m = (qi >= S) || (kj >= Sk) || (args.causal && kj > qi + qoff) || (qi >= qhi);
             p[i] = m ? 0.f : p[i];
             ds[i] = m ? 0.f : ds[i];
           }
@@ -936,6 +947,7 @@ struct AttnBwdKV {           // context parallelism (see AttnBwdArgs)
   const torch::Tensor* kv = nullptr;
   torch::Tensor* dkv = nullptr;
   int Sk = 0, off0 = 0, off1 = 0, split = 0;
+  const int* q_hi = nullptr;  // key-range mask (self-attention only)
 };
 
 template <int D>
@@ -980,6 +992,7 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
     a.off0 = 0; a.off1 = 0; a.split = S;
     a.dkv_cp = nullptr;
   }
+  a.q_hi = cp.q_hi;
   a.B = B; a.S = S; a.Hq = Hq; a.Hk = Hk;
   a.scale = scale;
   a.scale_log2 = scale * 1.4426950408889634f;
@@ -1005,12 +1018,19 @@ static torch::Tensor launch_attn_bwd(const torch::Tensor& dO, const torch::Tenso
 // Returns dq|dk fp32 [T, (Hq+Hk)*D]; writes dv (bf16) into the v slot of dqkv.
 torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qk, torch::Tensor qkv, torch::Tensor O,
                        torch::Tensor lse, torch::Tensor dqkv, int64_t B, int64_t S, int64_t Hq,
-                       int64_t Hk, int64_t D, bool causal, double scale) {
+                       int64_t Hk, int64_t D, bool causal, double scale, c10::optional<torch::Tensor> q_hi) {
   check_bf16(dO, "dO"); check_bf16(qk, "qk"); check_bf16(qkv, "qkv"); check_bf16(O, "O"); check_bf16(dqkv, "dqkv");
   TORCH_CHECK(dO.is_contiguous() && O.is_contiguous() && dqkv.is_contiguous(), "attn_bwd: contiguous");
   c10::cuda::CUDAGuard g(qk.device());
-  if (D == 128) return launch_attn_bwd<128>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale);
-  if (D == 64) return launch_attn_bwd<64>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale);
+  AttnBwdKV self;
+  if (q_hi.has_value() && q_hi->defined()) {
+    TORCH_CHECK(causal, "attn_bwd: the key-range mask applies to causal attention");
+    TORCH_CHECK(q_hi->is_cuda() && q_hi->scalar_type() == torch::kInt32 && q_hi->is_contiguous() &&
+                    q_hi->numel() == B * S, "attn_bwd: q_hi int32 [B*S]");
+    self.q_hi = q_hi->data_ptr<int>();
+  }
+  if (D == 128) return launch_attn_bwd<128>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale, self);
+  if (D == 64) return launch_attn_bwd<64>(dO, qk, qkv, O, lse, dqkv, B, S, Hq, Hk, causal, (float)scale, self);
   TORCH_CHECK(false, "attn_bwd: head_dim must be 64 or 128");
   return torch::Tensor();
 }

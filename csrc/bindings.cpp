@@ -32,9 +32,10 @@ void qknorm_rope_bwd(torch::Tensor, torch::Tensor, c10::optional<torch::Tensor>,
                      c10::optional<torch::Tensor>, c10::optional<torch::Tensor>, int64_t, int64_t, int64_t,
                      int64_t, int64_t);
 // attention
-std::vector<torch::Tensor> attn_fwd(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
+std::vector<torch::Tensor> attn_fwd(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t, bool, double,
+                                    c10::optional<torch::Tensor>);
 torch::Tensor attn_bwd(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
-                       int64_t, int64_t, int64_t, int64_t, int64_t, bool, double);
+                       int64_t, int64_t, int64_t, int64_t, int64_t, bool, double, c10::optional<torch::Tensor>);
 std::vector<torch::Tensor> attn_fwd_cp(torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, int64_t,
                                        int64_t, int64_t, int64_t, int64_t, double, int64_t, int64_t, int64_t);
 std::vector<torch::Tensor> attn_bwd_cp(torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor,
@@ -131,8 +132,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_bwd", &nq::layernorm_bwd);
   m.def("qknorm_rope_fwd", &nq::qknorm_rope_fwd);
   m.def("qknorm_rope_bwd", &nq::qknorm_rope_bwd);
-  m.def("attn_fwd", &nq::attn_fwd);
-  m.def("attn_bwd", &nq::attn_bwd);
+  m.def("attn_fwd", &nq::attn_fwd, "causal / full GQA flash attention forward; kv_lo: per-query first visible key",
+        py::arg("qk"), py::arg("qkv"), py::arg("B"), py::arg("S"), py::arg("Hq"), py::arg("Hk"), py::arg("D"),
+        py::arg("causal"), py::arg("scale"), py::arg("kv_lo") = py::none());
+  m.def("attn_bwd", &nq::attn_bwd, "attention backward; q_hi: per-key end of the queries that see it",
+        py::arg("dO"), py::arg("qk"), py::arg("qkv"), py::arg("O"), py::arg("lse"), py::arg("dqkv"), py::arg("B"),
+        py::arg("S"), py::arg("Hq"), py::arg("Hk"), py::arg("D"), py::arg("causal"), py::arg("scale"),
+        py::arg("q_hi") = py::none());
   m.def("attn_fwd_cp", &nq::attn_fwd_cp, "context-parallel attention forward (local queries, gathered keys)");
   m.def("attn_bwd_cp", &nq::attn_bwd_cp, "context-parallel attention backward");
   m.def("cp_kv_scatter", &nq::cp_kv_scatter, "store local k|v rows into every CP rank's gathered buffer (P2P)");

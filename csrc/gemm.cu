@@ -13,6 +13,8 @@
 // -> global) so the epilogue of tile i overlaps the main loop of tile i+1.  One
 // CTA per SM walks the tile list with a grid stride; tiles are rasterised in
 // bands of 8 M-tiles for L2 reuse of B.
+#include <cstring>
+
 #include "common.cuh"
 #include "peer.cuh"
 #include "tmap.h"
@@ -61,7 +63,18 @@ struct GemmArgs {
   unsigned rs_seq;
   unsigned* rs_counter;
   unsigned rs_target;
+  // 1: the epilogue writes C (and H) through shared memory with TMA stores
+  // (bf16) or TMA add-reductions (fp32 accumulate) using the tmC / tmH maps
+  // (box 32 x 32 rows).  0: register-to-global stores.
+  int tma_epi;
 };
+
+// Epilogue staging for TMA stores: per epilogue warp (32 rows) three 2 KB
+// boxes of 32 rows x 64 B (bf16: 32 columns; SwiGLU: g, u and h), or one
+// 4 KB box of 32 rows x 32 fp32 columns.  Rows are dense (no swizzle); each
+// lane writes its row's 16-byte pieces in a lane-rotated order, so a warp's
+// shared-memory stores are free of bank conflicts.
+constexpr int kEpiWarpBytes = 6144;
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -69,7 +82,8 @@ struct GemmSmem {
   static constexpr int kBBytes = BN * GBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOff = STAGES * kStageBytes;
-  static constexpr int kBytes = kBarOff + 1024 + 4 * (kMaxGroups + 1) + 1024;  // + align slack
+  static constexpr int kEpiOff = (kBarOff + 1024 + 4 * (kMaxGroups + 1) + 1023) / 1024 * 1024;
+  static constexpr int kBytes = kEpiOff + 4 * kEpiWarpBytes + 1024;  // + align slack
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mt, int& nt) {
@@ -85,6 +99,7 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH,
                 const GemmArgs args) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -120,6 +135,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (args.tma_epi) {
+      tma_prefetch_desc(&tmC);
+      if (EPI == kEpiSwiGLU) tma_prefetch_desc(&tmH);
+    }
   }
   constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
   if (warp == 1) {
@@ -280,7 +299,117 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m_limit = (args.group_mode == kGroupM) ? s_off[args.num_groups] : args.M;
       const bool row_ok = row < m_limit;
       const bool has_acc = ke > kb;
-      if (EPI == kEpiSwiGLU) {
+      if (args.tma_epi) {
+        // ------------------------------------------------ TMA-store epilogue
+        uint8_t* stg = smem + L::kEpiOff + quarter * kEpiWarpBytes;
+        const int ty = m0 + quarter * 32;
+        const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+        if (EPI == kEpiSwiGLU) {
+          const int I = args.N >> 1;
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 32) {
+            uint32_t rg[32], ru[32];
+            tmem_ld32(trow + c, rg);
+            tmem_ld32(trow + BN / 2 + c, ru);
+            tmem_wait_ld();
+            const int jc = n0 / 2 + c;
+            if (jc >= I) continue;
+            uint4 vg[4], vu[4], vh[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float g[8], u[8], h[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                g[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[q * 8 + e])));
+                u[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[q * 8 + e])));
+                h[e] = g[e] * sigmoid_fast(g[e]) * u[e];
+              }
+              vg[q] = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]),
+                                 pack_bf16(g[6], g[7]));
+              vu[q] = make_uint4(pack_bf16(u[0], u[1]), pack_bf16(u[2], u[3]), pack_bf16(u[4], u[5]),
+                                 pack_bf16(u[6], u[7]));
+              vh[q] = make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]),
+                                 pack_bf16(h[6], h[7]));
+            }
+            if (lane == 0) bulk_wait_read_all();  // the previous chunk's stores have read the staging
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int q = (j + lane) & 3;
+              const uint4 a = q == 0 ? vg[0] : q == 1 ? vg[1] : q == 2 ? vg[2] : vg[3];
+              const uint4 b = q == 0 ? vu[0] : q == 1 ? vu[1] : q == 2 ? vu[2] : vu[3];
+              const uint4 d = q == 0 ? vh[0] : q == 1 ? vh[1] : q == 2 ? vh[2] : vh[3];
+              *reinterpret_cast<uint4*>(stg + lane * 64 + q * 16) = a;
+              *reinterpret_cast<uint4*>(stg + 2048 + lane * 64 + q * 16) = b;
+              *reinterpret_cast<uint4*>(stg + 4096 + lane * 64 + q * 16) = d;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, stg, jc, ty);
+              tma_store_2d(&tmC, stg + 2048, I + jc, ty);
+              tma_store_2d(&tmH, stg + 4096, jc, ty);
+              bulk_commit();
+            }
+          }
+        } else if (EPI == kEpiBF16 && has_acc) {
+          int half = 0;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(trow + c, r);
+            tmem_wait_ld();
+            if (n0 + c >= args.N) continue;
+            uint4 v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              v[q] = make_uint4(pack_bf16(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1])),
+                                pack_bf16(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3])),
+                                pack_bf16(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5])),
+                                pack_bf16(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7])));
+            uint8_t* dst = stg + half * 2048;
+            if (lane == 0) bulk_wait_read_1();  // the store that last read this half is done reading
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int q = (j + lane) & 3;
+              *reinterpret_cast<uint4*>(dst + lane * 64 + q * 16) = q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, dst, n0 + c, ty);
+              bulk_commit();
+            }
+            half ^= 1;
+          }
+        } else if (EPI == kEpiAccF32 && has_acc) {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(trow + c, r);
+            tmem_wait_ld();
+            if (n0 + c >= args.N) continue;
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int q = (j + lane) & 7;
+              uint4 v = make_uint4(r[0], r[1], r[2], r[3]);
+#pragma unroll
+              for (int t = 1; t < 8; ++t)
+                if (q == t) v = make_uint4(r[4 * t], r[4 * t + 1], r[4 * t + 2], r[4 * t + 3]);
+              *reinterpret_cast<uint4*>(stg + lane * 128 + q * 16) = v;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_reduce_add_2d(&tmC, stg, n0 + c, ty);
+              bulk_commit();
+            }
+          }
+        }
+      } else if (EPI == kEpiSwiGLU) {
         const int I = args.N >> 1;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
@@ -370,6 +499,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
+    // TMA stores complete before the CTA's shared memory goes away
+    if (args.tma_epi && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -386,13 +517,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ----------------------------------------------------------------------- host
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
-                        int max_tiles, cudaStream_t stream) {
+                        int max_tiles, cudaStream_t stream, const CUtensorMap* tc = nullptr,
+                        const CUtensorMap* th = nullptr) {
   using L = GemmSmem<BN, STAGES>;
+  static_assert(L::kBytes <= 232448, "GEMM shared memory budget");
   auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   set_max_smem_once(reinterpret_cast<const void*>(kern), L::kBytes);
   int grid = std::min(num_sms(), std::max(1, max_tiles));
-  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, a);
+  CUtensorMap none;
+  std::memset(&none, 0, sizeof(none));
+  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, tc ? *tc : none, th ? *th : none, a);
   NQ_CHECK_CUDA(cudaGetLastError());
+}
+
+// TMA-store epilogue maps: C (bf16 or fp32) in 32 x 32 boxes, when its base
+// and row stride meet TMA's 16-byte rules.
+static bool tma_epi_ok(const void* p, int64_t ld, int elem) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld * elem) % 16 == 0;
 }
 
 constexpr int kBN = 256;
@@ -403,6 +544,7 @@ static GemmArgs base_args(int M, int N, int K, void* C, int64_t ldc) {
   a.M = M; a.N = N; a.K = K; a.C = C; a.ldc = ldc;
   a.group_mode = kGroupNone; a.num_groups = 1; a.offsets = nullptr;
   a.c_group_stride = 0; a.b_group_rows = 0; a.err = error_flag_ptr();
+  a.tma_epi = 0;
   return a;
 }
 
@@ -421,8 +563,14 @@ void gemm_nt_out(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
   auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, GBM);
   auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, kBN);
   auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
+  CUtensorMap tc;
+  if (tma_epi_ok(C.data_ptr(), C.stride(0), 2)) {
+    tc = make_tmap_2d_bf16(C.data_ptr(), M, N, C.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+    a.tma_epi = 1;
+  }
   launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
-                                                    at::cuda::getCurrentCUDAStream());
+                                                    at::cuda::getCurrentCUDAStream(),
+                                                    a.tma_epi ? &tc : nullptr);
 }
 
 torch::Tensor gemm_nt(torch::Tensor A, torch::Tensor B) {
@@ -448,8 +596,12 @@ std::vector<torch::Tensor> gemm_nt_swiglu(torch::Tensor A, torch::Tensor B) {
   auto a = base_args(M, N, K, gu.data_ptr(), gu.stride(0));
   a.H = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
   a.ldh = N / 2;
+  // N is a multiple of 256, so both outputs meet the TMA stride rules
+  auto tc = make_tmap_2d_bf16(gu.data_ptr(), M, N, gu.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+  auto th = make_tmap_2d_bf16(h.data_ptr(), M, N / 2, N / 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+  a.tma_epi = 1;
   launch_gemm<kBN, kStages, false, false, kEpiSwiGLU>(ta, tb, a, cdiv(M, GBM) * (N / kBN),
-                                                      at::cuda::getCurrentCUDAStream());
+                                                      at::cuda::getCurrentCUDAStream(), &tc, &th);
   return {gu, h};
 }
 
@@ -466,8 +618,14 @@ void gemm_nn_out(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
   auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, GBM);
   auto tb = make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, 64);
   auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
+  CUtensorMap tc;
+  if (tma_epi_ok(C.data_ptr(), C.stride(0), 2)) {
+    tc = make_tmap_2d_bf16(C.data_ptr(), M, N, C.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+    a.tma_epi = 1;
+  }
   launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
-                                                   at::cuda::getCurrentCUDAStream());
+                                                   at::cuda::getCurrentCUDAStream(),
+                                                   a.tma_epi ? &tc : nullptr);
 }
 
 torch::Tensor gemm_nn(torch::Tensor A, torch::Tensor B) {
@@ -489,8 +647,15 @@ void gemm_tn_acc(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
   auto ta = make_tmap_2d_bf16(A.data_ptr(), K, M, A.stride(0), 64, 64);
   auto tb = make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, 64);
   auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
+  CUtensorMap tc;
+  if (tma_epi_ok(C.data_ptr(), C.stride(0), 4)) {
+    // C += tile through TMA add-reductions (the read-modify-write happens in L2)
+    tc = make_tmap_2d_f32(C.data_ptr(), M, N, C.stride(0), 32, 32);
+    a.tma_epi = 1;
+  }
   launch_gemm<kBN, kStages, true, true, kEpiAccF32>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
-                                                    at::cuda::getCurrentCUDAStream());
+                                                    at::cuda::getCurrentCUDAStream(),
+                                                    a.tma_epi ? &tc : nullptr);
 }
 
 // ------------------------------------------------------ tensor-parallel GEMMs

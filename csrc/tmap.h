@@ -75,6 +75,25 @@ inline CUtensorMap make_tmap_3d_bf16(const void* base, int64_t d0, int64_t d1, i
   return m;
 }
 
+// 2-D fp32 tensor map over a row-major matrix [rows, cols] with row stride
+// `ld` elements (TMA store / reduce-add destinations).
+inline CUtensorMap make_tmap_2d_f32(const void* base, int64_t rows, int64_t cols, int64_t ld,
+                                    int box_cols, int box_rows,
+                                    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base not 16B aligned");
+  if ((ld * 4) % 16 != 0) throw std::runtime_error("TMA row stride not a multiple of 16 bytes");
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled(2d f32) failed: " + std::to_string(r));
+  return m;
+}
+
 // 3-D fp32 tensor map (used as the destination of TMA bulk reductions).
 inline CUtensorMap make_tmap_3d_f32(const void* base, int64_t d0, int64_t d1, int64_t d2,
                                     int64_t s1_elems, int64_t s2_elems, int b0, int b1, int b2,

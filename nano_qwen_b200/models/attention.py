@@ -79,9 +79,11 @@ class Attention(nn.Module):
         cp = getattr(self, "cp_group", None)
         if cp is not None and kv_cache is None:
             o = self._attend_cp(qkv, qw, kw, cos, sin, position_ids, B, S, Hq, Hk, D, eps, cp)
-        elif kv_cache is None and attention_mask is None:
+        elif kv_cache is None and (attention_mask is None or isinstance(attention_mask, ops.KeyRange)):
+            # plain causal, or causal within per-token key ranges (packed
+            # documents, padding) on the same kernels
             o = ops.attention_core(qkv, qw, kw, cos, sin, position_ids, Hq, Hk, D, eps,
-                                   causal=True)
+                                   causal=True, key_range=attention_mask)
         else:
             o = self._attend_general(qkv, qw, kw, cos, sin, position_ids, attention_mask,
                                      kv_cache, B, S, Hq, Hk, D, eps)
@@ -147,7 +149,10 @@ def _masked_attention(q, k, v, attention_mask, past):
     causal = torch.arange(Sk, device=q.device)[None, :] > (torch.arange(Sq, device=q.device)[:, None] + past)
     s = s.masked_fill(causal, float("-inf"))
     m = attention_mask
-    if m.dtype == torch.bool or m.dtype in (torch.int32, torch.int64):
+    if isinstance(m, ops.KeyRange):  # key ranges of the new rows (positions past..past+Sq)
+        early = torch.arange(Sk, device=q.device)[None, None, :] < m.kv_lo[:, :, None]
+        s = s.masked_fill(early[:, None, None, :, :], float("-inf"))
+    elif m.dtype == torch.bool or m.dtype in (torch.int32, torch.int64):
         if m.dim() == 2:  # [B, Sk] key padding, 1 = keep
             s = s.masked_fill(~m.bool()[:, None, None, None, :], float("-inf"))
         else:

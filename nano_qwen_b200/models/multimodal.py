@@ -21,7 +21,7 @@ import torch.nn as nn
 
 from .. import ops
 from ..config import ModelConfig
-from .transformer import Qwen3Model, shift_targets
+from .transformer import Qwen3Model, key_range_mask, shift_targets
 from .vision.deepstack import DeepStack
 from .vision.merger import VisionMerger
 from .vision.mrope import build_mrope_position_ids, mrope_tables
@@ -77,7 +77,7 @@ class Qwen3VLModel(nn.Module):
                 pos = build_mrope_position_ids(base, image_grid_thw, mask)
                 rope = mrope_tables(self.config.head_dim, self.config.rope_theta, pos,
                                     self.mrope_section)
-        x, aux_total, n_moe = lm.hidden(input_ids, position_ids, attention_mask, None,
+        x, aux_total, n_moe = lm.hidden(input_ids, position_ids, key_range_mask(attention_mask), None,
                                         inputs_embeds=h, rope=rope)
         if return_logits is None:
             return_logits = labels is None

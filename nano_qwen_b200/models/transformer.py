@@ -93,6 +93,22 @@ class TransformerBlock(nn.Module):
         return resid + f.to(resid.dtype), aux
 
 
+def key_range_mask(attention_mask, document_ids=None, cached: bool = False):
+    """The attention mask the layers receive: ``document_ids`` or a
+    one-run-per-row 2-D padding mask become an ``ops.KeyRange`` (handled by
+    the flash-attention kernels); anything else is passed through to the
+    general path."""
+    if document_ids is not None:
+        return ops.KeyRange.from_segments(document_ids)
+    if (attention_mask is not None and not cached and torch.is_tensor(attention_mask)
+            and attention_mask.dim() == 2
+            and attention_mask.dtype in (torch.bool, torch.int32, torch.int64)):
+        kr = ops.KeyRange.from_padding_mask(attention_mask)
+        if kr is not None:
+            return kr
+    return attention_mask
+
+
 class Qwen3Model(nn.Module):
     def __init__(self, config: ModelConfig):
         super().__init__()
@@ -170,8 +186,16 @@ class Qwen3Model(nn.Module):
                 attention_mask: Optional[torch.Tensor] = None,
                 kv_caches: Optional[List[KVCache]] = None, labels: Optional[torch.Tensor] = None,
                 return_logits: Optional[bool] = None, logits_to_keep: int = 0,
-                inputs_embeds: Optional[torch.Tensor] = None) -> dict:
+                inputs_embeds: Optional[torch.Tensor] = None,
+                document_ids: Optional[torch.Tensor] = None) -> dict:
+        """``document_ids`` [B, S] (optional): a document id per token of
+        packed rows; each token then attends only within its document.  A 2-D
+        key-padding ``attention_mask`` with one run of real tokens per row
+        (left or right padding) runs on the same masked kernels."""
+        attention_mask = key_range_mask(attention_mask, document_ids, kv_caches is not None)
         if getattr(self, "cp_group", None) is not None and kv_caches is None:
+            if attention_mask is not None:
+                raise NotImplementedError("context parallelism runs plain causal attention")
             return self._forward_cp(input_ids, position_ids, labels, return_logits,
                                     logits_to_keep, inputs_embeds)
         if getattr(self, "tp_fused", False) and kv_caches is None and inputs_embeds is None \

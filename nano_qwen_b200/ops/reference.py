@@ -50,12 +50,14 @@ def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, q_w: Optional[torch.Tensor],
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
               scale: Optional[float] = None, q_offset: int = 0,
-              kv_len: Optional[torch.Tensor] = None) -> torch.Tensor:
+              kv_len: Optional[torch.Tensor] = None,
+              kv_lo: Optional[torch.Tensor] = None) -> torch.Tensor:
     """GQA attention.  q [B,Sq,Hq,D], k/v [B,Sk,Hk,D] -> [B,Sq,Hq,D].
 
     ``q_offset`` is the absolute position of q row 0 (decode / chunked prefill):
     query i may attend key j iff j <= i + q_offset.  ``kv_len`` [B] masks keys
-    at positions >= kv_len[b] (padded caches).
+    at positions >= kv_len[b] (padded caches).  ``kv_lo`` [B, Sq] masks keys
+    before kv_lo[b, i] for query i (document packing, left padding).
     """
     B, Sq, Hq, D = q.shape
     Sk, Hk = k.shape[1], k.shape[2]
@@ -73,6 +75,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
         kj = torch.arange(Sk, device=q.device)
         pad = kj[None, :] >= kv_len[:, None]  # [B, Sk]
         s = s.masked_fill(pad[:, None, None, None, :], float("-inf"))
+    if kv_lo is not None:
+        kj = torch.arange(Sk, device=q.device)
+        early = kj[None, None, :] < kv_lo.to(q.device)[:, :, None]  # [B, Sq, Sk]
+        s = s.masked_fill(early[:, None, None, :, :], float("-inf"))
     p = torch.softmax(s, dim=-1)
     o = torch.einsum("bhgqk,bkhd->bqhgd", p, v.float())
     return o.reshape(B, Sq, Hq, D).to(q.dtype)

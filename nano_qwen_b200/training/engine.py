@@ -115,7 +115,12 @@ class TrainEngine:
 
     # ----------------------------------------------------------------- step
     def forward_backward(self, batch: Dict[str, torch.Tensor], scale: float):
-        out = self.model(input_ids=batch["input_ids"], labels=batch["labels"])
+        # packed documents (``doc_ids`` from DocumentPackingDataset) attend
+        # within their own document; padding masks restrict keys the same way
+        extra = {k: batch[k] for k in ("document_ids", "attention_mask") if batch.get(k) is not None}
+        if "document_ids" not in extra and batch.get("doc_ids") is not None:
+            extra["document_ids"] = batch["doc_ids"]
+        out = self.model(input_ids=batch["input_ids"], labels=batch["labels"], **extra)
         loss = out["loss"] * scale
         loss.backward()
         aux = out.get("aux_loss")

@@ -201,3 +201,34 @@ def test_checkpoint_roundtrip_plain_and_dcp(tmp_path):
     m3 = load_model_for_eval(str(yp), out)
     for (n, p), (_, q) in zip(eng.model.named_parameters(), m3.named_parameters()):
         assert torch.equal(p.detach(), q.detach()), n
+
+
+def test_document_mask_and_padding_key_ranges():
+    """Packed documents attend within themselves (the logits of each document
+    equal its logits alone), and a left-padded row's real tokens ignore the
+    padding; key ranges come from document ids or a one-run padding mask."""
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.ops import KeyRange
+    torch.manual_seed(2)
+    m = Qwen3Model(ModelConfig(**dict(TINY, tie_word_embeddings=False))).eval()
+    a = torch.randint(0, 256, (1, 11))
+    b = torch.randint(0, 256, (1, 9))
+    packed = torch.cat([a, b], 1)
+    doc = torch.tensor([[0] * 11 + [1] * 9])
+    pos = torch.cat([torch.arange(11), torch.arange(9)]).view(1, -1)
+    with torch.no_grad():
+        lp = m(packed, position_ids=pos, document_ids=doc)["logits"]
+        assert torch.allclose(lp[:, :11], m(a)["logits"], atol=1e-5)
+        assert torch.allclose(lp[:, 11:], m(b)["logits"], atol=1e-5)
+        # left padding: 4 pad tokens, positions of the real tokens start at 0
+        mask = torch.tensor([[0] * 4 + [1] * 9])
+        padded = torch.cat([torch.zeros(1, 4, dtype=torch.long), b], 1)
+        pos2 = torch.cat([torch.zeros(4, dtype=torch.long), torch.arange(9)]).view(1, -1)
+        lpad = m(padded, position_ids=pos2, attention_mask=mask)["logits"]
+        assert torch.allclose(lpad[:, 4:], m(b)["logits"], atol=1e-5)
+    kr = KeyRange.from_segments(torch.tensor([[0, 0, 0, 1, 1, 2, 2, 2]]))
+    assert kr.kv_lo.tolist() == [[0, 0, 0, 3, 3, 5, 5, 5]]
+    assert kr.q_hi.tolist() == [[3, 3, 3, 5, 5, 8, 8, 8]]
+    assert KeyRange.from_padding_mask(torch.tensor([[1, 1, 0, 1]])) is None  # two runs of real tokens
+    assert KeyRange.from_padding_mask(torch.tensor([[0, 1, 1, 0]])).kv_lo.tolist() == [[0, 1, 1, 3]]

@@ -76,6 +76,35 @@ def test_gemm_tn_acc(E, M, N, K):
     assert rel_err(C, ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(200, 136, 72), (1000, 520, 1032), (333, 2048, 256)])
+def test_gemm_tma_epilogue_matches_register_epilogue(E, M, N, K):
+    """The TMA-store epilogue (16-byte-aligned output rows) and the
+    register-store epilogue (an output view whose row stride breaks TMA's
+    16-byte rule) write the same bits, for bf16 stores and fp32 accumulation;
+    row / column tails are clipped by the tensor map."""
+    torch.manual_seed(5)
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    c_tma = E.gemm_nt(A, B)
+    wide = torch.zeros(M, N + 4, device=DEV).bfloat16()  # row stride 2N+8 bytes: register path
+    E.gemm_nt_out(A, B, wide[:, :N])
+    assert torch.equal(c_tma, wide[:, :N])
+    assert not wide[:, N:].any()
+    Bk = torch.randn(K, N, device=DEV).bfloat16()
+    wide.zero_()
+    E.gemm_nn_out(A, Bk, wide[:, :N])
+    assert torch.equal(E.gemm_nn(A, Bk), wide[:, :N])
+    At = torch.randn(K, M, device=DEV).bfloat16()
+    c0 = torch.randn(M, N, device=DEV)
+    c_tma = c0.clone()
+    E.gemm_tn_acc(At, Bk, c_tma)
+    widef = torch.zeros(M, N + 1, device=DEV)  # row stride 4N+4 bytes: register path
+    widef[:, :N] = c0
+    E.gemm_tn_acc(At, Bk, widef[:, :N])
+    assert rel_err(c_tma, widef[:, :N]) < 1e-6  # fp32 adds in L2 vs in registers: same sums
+    assert rel_err(c_tma, c0 + At.float().t() @ Bk.float()) < 1e-2
+
+
 def _grouped_inputs(G, R_per, K, seed=3):
     torch.manual_seed(seed)
     sizes = [R_per[g] for g in range(G)]
@@ -243,6 +272,77 @@ def test_attention_fwd_bwd(E, B, S, Hq, Hk, D, causal):
     assert rel_err(dqk[:, :Hq * D].view(B, S, Hq, D), q.grad) < 3e-2
     assert rel_err(dqk[:, Hq * D:].view(B, S, Hk, D), k.grad) < 3e-2
     assert rel_err(dqkv[:, (Hq + Hk) * D:].view(B, S, Hk, D), v.grad) < 3e-2
+
+
+def _segments(B, S, cuts, left_pad=None):
+    seg = torch.zeros(B, S, dtype=torch.int64)
+    for b in range(B):
+        for c in cuts[b]:
+            seg[b, c:] += 1
+    return seg
+
+
+@pytest.mark.parametrize("S,D", [(640, 128), (640, 64), (1024, 128)])
+def test_attention_key_range_mask(E, S, D):
+    """Causal attention within per-token key ranges (packed documents, a
+    left-padded row) against the fp32 statement with the same mask; block
+    skipping and the element masks at document edges both matter here."""
+    from nano_qwen_b200.ops import KeyRange
+    from nano_qwen_b200.ops import reference as R
+    torch.manual_seed(17)
+    B, Hq, Hk = 3, 4, 2
+    # row 0: documents at 0 / 100 / 300 / 301 / 520; row 1: 37 pad tokens then
+    # one document; row 2: a single document (plain causal)
+    seg = _segments(B, S, [[100, 300, 301, 520], [37], []]).to(DEV)
+    kr = KeyRange.from_segments(seg)
+    lo_ref = torch.stack([torch.tensor([int((seg[b, :i + 1] == seg[b, i]).nonzero()[0]) for i in range(S)])
+                          for b in range(B)]).to(DEV)
+    assert torch.equal(kr.kv_lo.long(), lo_ref)
+    qk = torch.randn(B * S, (Hq + Hk) * D, device=DEV).bfloat16()
+    qkv = torch.randn(B * S, (Hq + 2 * Hk) * D, device=DEV).bfloat16()
+    scale = 1.0 / math.sqrt(D)
+    o, lse = E.attn_fwd(qk, qkv, B, S, Hq, Hk, D, True, scale, kr.kv_lo.reshape(-1))
+    q = qk[:, :Hq * D].float().view(B, S, Hq, D).requires_grad_(True)
+    k = qk[:, Hq * D:].float().view(B, S, Hk, D).requires_grad_(True)
+    v = qkv[:, (Hq + Hk) * D:].float().view(B, S, Hk, D).requires_grad_(True)
+    oref = R.attention(q, k, v, causal=True, scale=scale, kv_lo=kr.kv_lo)
+    assert rel_err(o.view(B, S, Hq, D), oref) < 2e-2
+    do = torch.randn(B * S, Hq * D, device=DEV).bfloat16()
+    oref.backward(do.float().view(B, S, Hq, D))
+    dqkv = torch.zeros_like(qkv)
+    dqk = E.attn_bwd(do, qk, qkv, o, lse, dqkv, B, S, Hq, Hk, D, True, scale, kr.q_hi.reshape(-1))
+    assert rel_err(dqk[:, :Hq * D].view(B, S, Hq, D), q.grad) < 3e-2
+    assert rel_err(dqk[:, Hq * D:].view(B, S, Hk, D), k.grad) < 3e-2
+    assert rel_err(dqkv[:, (Hq + Hk) * D:].view(B, S, Hk, D), v.grad) < 3e-2
+    # the unmasked kernel differs on the packed row: the mask is really applied
+    o_plain, _ = E.attn_fwd(qk, qkv, B, S, Hq, Hk, D, True, scale)
+    assert rel_err(o_plain.view(B, S, Hq, D)[0, 300:], oref[0, 300:]) > 0.1
+    assert rel_err(o_plain.view(B, S, Hq, D)[2], oref[2]) < 2e-2
+
+
+def test_model_document_mask_matches_separate_documents():
+    """Model level: a packed row with document ids gives each document the
+    logits it gets alone (positions restart per document)."""
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    torch.manual_seed(3)
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=64, intermediate_size=512, vocab_size=1024, max_position_embeddings=1024,
+                      tie_word_embeddings=True)
+    m = Qwen3Model(cfg).cuda()
+    attach_param_store(m)
+    a = torch.randint(0, 1024, (1, 200), device=DEV)
+    b = torch.randint(0, 1024, (1, 312), device=DEV)
+    packed = torch.cat([a, b], 1)
+    doc = torch.cat([torch.zeros(1, 200), torch.ones(1, 312)], 1).long().to(DEV)
+    pos = torch.cat([torch.arange(200), torch.arange(312)]).view(1, -1).to(DEV)
+    with torch.no_grad():
+        lp = m(packed, position_ids=pos, document_ids=doc)["logits"].float()
+        la = m(a)["logits"].float()
+        lb = m(b)["logits"].float()
+    assert rel_err(lp[:, :200], la) < 2e-2
+    assert rel_err(lp[:, 200:], lb) < 2e-2
 
 
 def test_decode_attention(E):
