@@ -22,6 +22,7 @@ import torch.utils.checkpoint as ckpt
 
 from .. import ops
 from ..config import ModelConfig
+from ..utils.tracing import nvtx_range
 from .attention import Attention
 from .ffn import build_ffn
 from .kv_cache import KVCache
@@ -76,13 +77,15 @@ class TransformerBlock(nn.Module):
             # the gradient of the block input is produced after every weight
             # gradient of the block: the hook may start reducing them
             resid = _GradReady.apply(resid, self.grad_ready_hook)
-        resid, x = ops.add_rms_norm(resid, delta, self.input_layernorm.weight, eps)
-        a = self.attention(x, position_ids, attention_mask, kv_cache, rope)
-        resid, x = ops.add_rms_norm(resid, a, self.post_attention_layernorm.weight, eps)
-        if self._use_moe:
-            f, aux = self.feed_forward(x)
-        else:
-            f, aux = self.feed_forward(x), None
+        with nvtx_range(f"layer{self.layer_idx}.attention"):
+            resid, x = ops.add_rms_norm(resid, delta, self.input_layernorm.weight, eps)
+            a = self.attention(x, position_ids, attention_mask, kv_cache, rope)
+        with nvtx_range(f"layer{self.layer_idx}.mlp"):
+            resid, x = ops.add_rms_norm(resid, a, self.post_attention_layernorm.weight, eps)
+            if self._use_moe:
+                f, aux = self.feed_forward(x)
+            else:
+                f, aux = self.feed_forward(x), None
         return resid, f, aux
 
     def forward(self, hidden_states, position_ids=None, attention_mask=None, kv_cache=None):

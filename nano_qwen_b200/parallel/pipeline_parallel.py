@@ -69,8 +69,12 @@ class PipelineParallel(nn.Module):
             model.norm = None
         self.model = model
         self.n_moe_total = sum(1 for i in range(cfg.num_hidden_layers) if cfg.layer_is_moe(i))
+        self._pending_sends = []
         if self.tied:
             self._sync_tied(weights=True)
+            for r, _ in self._pending_sends:
+                r.wait()
+            self._pending_sends = []
 
     # ---------------------------------------------------------------- p2p
     def _peer(self, d: int) -> int:
@@ -90,6 +94,11 @@ class PipelineParallel(nn.Module):
             reqs = dist.batch_isend_irecv(ops_)
         else:
             reqs = [op.op(op.tensor, op.peer, op.group) for op in ops_]
+        if buf is None and dist.get_backend(self.group) == "nccl":
+            # send only: the compute stream goes on while NCCL's stream sends;
+            # the request (and so the tensor) is kept until the schedule ends
+            self._pending_sends.extend((r, send) for r in reqs)
+            return buf
         for r in reqs:
             r.wait()
         return buf
@@ -180,6 +189,7 @@ class PipelineParallel(nn.Module):
             saved_in[i] = None
             return gin
 
+        self._pending_sends = []
         prev = None if self.first else self._peer(-1)
         nxt = None if self.last else self._peer(1)
         warm = min(self.pp - self.stage - 1, m)
@@ -205,6 +215,9 @@ class PipelineParallel(nn.Module):
             gin = bwd(j, g)
             if prev is not None:
                 self._p2p(send=gin, send_to=prev)
+        for r, _ in self._pending_sends:
+            r.wait()
+        self._pending_sends = []
         if self.tied:
             self._sync_tied()
         # every stage reports the same numbers

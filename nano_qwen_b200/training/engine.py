@@ -18,6 +18,7 @@ import torch.nn as nn
 from ..parallel.comm import get_world_size
 from ..parallel.data_parallel import DataParallel
 from ..runtime.flat_params import ALIGN
+from ..utils.tracing import nvtx_range
 from .optimizer import attach_param_store, build_optimizer
 from .scheduler import build_scheduler
 
@@ -115,6 +116,10 @@ class TrainEngine:
 
     # ----------------------------------------------------------------- step
     def forward_backward(self, batch: Dict[str, torch.Tensor], scale: float):
+        with nvtx_range("forward_backward"):
+            return self._forward_backward(batch, scale)
+
+    def _forward_backward(self, batch: Dict[str, torch.Tensor], scale: float):
         # packed documents (``doc_ids`` from DocumentPackingDataset) attend
         # within their own document; padding masks restrict keys the same way
         extra = {k: batch[k] for k in ("document_ids", "attention_mask") if batch.get(k) is not None}
@@ -150,17 +155,18 @@ class TrainEngine:
         if self.tp_group is not None:
             from ..parallel.tensor_parallel import sync_replicated_grads
             sync_replicated_grads(self.model, self.tp_group)
-        if hasattr(self.dp, "fused_step"):
-            gnorm = self.dp.fused_step(self.optimizer, self.grad_clip)
+        with nvtx_range("optimizer_step"):
+            if hasattr(self.dp, "fused_step"):
+                gnorm = self.dp.fused_step(self.optimizer, self.grad_clip)
+                self.scheduler.step()
+                return {"loss": loss_sum, "grad_norm": gnorm, "aux_loss": aux_sum}
+            if self.dp is not None:
+                self.dp.sync_grads()
+            gnorm = self.optimizer.clip_grad_norm_(self.grad_clip, self._norm_sq_reduce)
+            self.optimizer.step()
+            if self.dp is not None:
+                self.dp.gather_params()
             self.scheduler.step()
-            return {"loss": loss_sum, "grad_norm": gnorm, "aux_loss": aux_sum}
-        if self.dp is not None:
-            self.dp.sync_grads()
-        gnorm = self.optimizer.clip_grad_norm_(self.grad_clip, self._norm_sq_reduce)
-        self.optimizer.step()
-        if self.dp is not None:
-            self.dp.gather_params()
-        self.scheduler.step()
         return {"loss": loss_sum, "grad_norm": gnorm, "aux_loss": aux_sum}
 
     # ------------------------------------------------------- grad norm

@@ -106,6 +106,11 @@ class PreTrainer:
                                      log_interval=lg.get("log_interval", 10))
         self.grad_accum_steps = (training_config.get("batch", {}) or {}).get(
             "gradient_accumulation_steps", 1)
+        # optional torch.profiler window over training steps (training YAML
+        # ``profiling``: enabled / wait / warmup / active / dir)
+        from ..utils.tracing import step_profiler_from_config
+        self.step_profiler = step_profiler_from_config(training_config.get("profiling"),
+                                                       rank=self.rank)
 
     def train(self, dataloader, total_steps: int, start_step: int = 0, sampler=None):
         step = start_step
@@ -129,7 +134,11 @@ class PreTrainer:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
             t0 = time.perf_counter()
-            out = self.engine.train_step(mbs)
+            if self.step_profiler is not None:
+                with self.step_profiler.step(step):
+                    out = self.engine.train_step(mbs)
+            else:
+                out = self.engine.train_step(mbs)
             step += 1
             if cuda:
                 e1.record()

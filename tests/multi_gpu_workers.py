@@ -302,3 +302,57 @@ def rank_leave_worker(rank, world, port):
         out = eng.train_step([{"input_ids": ids, "labels": ids}])
         assert torch.isfinite(out["loss"]).item()
     raise AssertionError("the departed rank was not detected")
+
+
+def pp_worker(rank, world, port):
+    """Pipeline parallelism over NCCL on GPUs (1F1B, micro-batches, tied
+    embeddings across the first and last stage) against the single-GPU model."""
+    init(rank, world, port)
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.parallel.pipeline_parallel import apply_pipeline_parallel
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2 * world, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=64, intermediate_size=512, vocab_size=4096,
+                      max_position_embeddings=512, tie_word_embeddings=True)
+    g = torch.Generator().manual_seed(13)
+    ids = torch.randint(0, cfg.vocab_size, (4, 256), generator=g).cuda()
+
+    def build():
+        torch.manual_seed(0)
+        m = Qwen3Model(cfg).cuda()
+        with torch.no_grad():
+            for p in m.parameters():
+                if p.ndim >= 2:
+                    p.normal_(0.0, 0.05)
+        return m
+
+    ref = build()
+    attach_param_store(ref)
+    loss_ref = 0.0
+    for c in ids.chunk(4):
+        o = ref(c, labels=c)
+        (o["loss"] / 4).backward()
+        loss_ref += float(o["loss"]) / 4
+    grp = dist.new_group(list(range(world)))
+    pm = apply_pipeline_parallel(build(), grp, list(range(world)), n_microbatches=4)
+    attach_param_store(pm.model)
+    loss, _ = pm.pipeline_forward_backward([{"input_ids": ids, "labels": ids}])
+    torch.cuda.synchronize()
+    assert ext().error_flag_read() == 0
+    assert abs(float(loss) - loss_ref) < 1e-2 * loss_ref, (float(loss), loss_ref)
+    rp = dict(ref.named_parameters())
+    off = pm.stage_layers[rank][0]
+    for n, p in pm.model.named_parameters():
+        rn = n
+        if n.startswith("layers."):
+            i, tail = n[len("layers."):].split(".", 1)
+            rn = f"layers.{int(i) + off}.{tail}"
+        if rn == "lm_head.weight":
+            rn = "embed.embed_tokens.weight"
+        gr = rp[rn].grad.float()
+        err = ((p.grad.float() - gr).norm() / (gr.norm() + 1e-12)).item()
+        assert err < 5e-2, (n, err)
+    dist.barrier()
+    dist.destroy_process_group()

@@ -119,3 +119,25 @@ def test_generation_cache_matches_full_forward():
     got = torch.stack(steps, 1).float()
     want = full[:, 29:39].float()
     assert ((got - want).norm() / want.norm()).item() < 3e-2
+
+
+def test_replay_determinism_on_gpu():
+    """Race detection by replay: the forward is bit-identical run to run; a
+    full training step differs at most by the rounding of the two
+    order-free reductions (attention dQ bulk adds, embedding atomics)."""
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.training.engine import TrainEngine
+    from nano_qwen_b200.utils.replay import replay_forward, replay_step
+    torch.manual_seed(0)
+    cfg = _cfg(head_dim=128)
+    eng = TrainEngine(Qwen3Model(cfg), {"optimizer": {"lr": 1e-3}, "scheduler": {"warmup_steps": 0}},
+                      torch.device("cuda"))
+    ids = torch.randint(0, cfg.vocab_size, (2, 512), device="cuda")
+    assert replay_forward(eng.model, ids)
+    eng.train_step([{"input_ids": ids, "labels": ids}])
+    r = replay_step(eng, [{"input_ids": ids, "labels": ids}])
+    assert r["loss_equal"], r["loss"]
+    # Adam's normalised step bounds any difference by a few learning rates
+    assert all(d < 5e-3 for d in r["differs"].values()), r["differs"]
+    assert ext().error_flag_read() == 0

@@ -59,3 +59,10 @@ def test_rank_leaving_between_steps_is_detected(world):
     _need(world)
     import multi_gpu_workers as W
     mp.spawn(W.rank_leave_worker, args=(world, _port()), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_pipeline_parallel_matches_single_gpu(world):
+    _need(world)
+    import multi_gpu_workers as W
+    mp.spawn(W.pp_worker, args=(world, _port()), nprocs=world, join=True)

@@ -131,3 +131,39 @@ def test_generation_greedy_is_deterministic():
     a = g.generate("abc", max_new_tokens=6, temperature=0.0)
     b = g.generate("abc", max_new_tokens=6, temperature=0.0)
     assert a == b
+
+
+def test_tracing_nvtx_and_step_profiler(tmp_path):
+    """NVTX ranges are inert without a GPU and when off; the step profiler
+    writes a trace and a kernel table after its window."""
+    import torch
+    from nano_qwen_b200.utils.tracing import StepProfiler, enable_nvtx, nvtx_range
+    enable_nvtx(True)
+    with nvtx_range("x"):
+        pass
+    enable_nvtx(False)
+    prof = StepProfiler(str(tmp_path), wait=1, warmup=1, active=2)
+    for i in range(5):
+        with prof.step(i):
+            torch.randn(64, 64) @ torch.randn(64, 64)
+    assert prof.done
+    assert (tmp_path / "trace_rank0.json").exists() and (tmp_path / "kernels_rank0.txt").exists()
+
+
+def test_replay_step_is_bitwise_on_cpu():
+    """The replay check restores the full state: on the CPU path a step is
+    bit-identical run to run."""
+    import torch
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.engine import TrainEngine
+    from nano_qwen_b200.utils.replay import replay_step
+    torch.manual_seed(0)
+    cfg = ModelConfig(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=16, intermediate_size=128, vocab_size=256, max_position_embeddings=64)
+    eng = TrainEngine(Qwen3Model(cfg), {"optimizer": {"lr": 1e-2}, "scheduler": {"warmup_steps": 0}},
+                      torch.device("cpu"))
+    ids = torch.randint(0, 256, (2, 16))
+    eng.train_step([{"input_ids": ids, "labels": ids}])
+    r = replay_step(eng, [{"input_ids": ids, "labels": ids}])
+    assert r["loss_equal"] and not r["differs"], r
