@@ -6,6 +6,7 @@
 namespace nq {
 // gemm.cu
 torch::Tensor gemm_nt(torch::Tensor A, torch::Tensor B);
+int64_t gemm_pair_mode(int64_t mode);
 void gemm_nt_out(torch::Tensor A, torch::Tensor B, torch::Tensor C);
 std::vector<torch::Tensor> gemm_nt_swiglu(torch::Tensor A, torch::Tensor B);
 torch::Tensor gemm_nn(torch::Tensor A, torch::Tensor B);
@@ -117,6 +118,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_qwen_b200 sm_100a kernels";
   m.def("gemm_nt", &nq::gemm_nt, "C = A @ B^T (bf16, tcgen05)");
   m.def("gemm_nt_out", &nq::gemm_nt_out);
+  m.def("gemm_pair_mode", &nq::gemm_pair_mode,
+        "CTA-pair (cta_group::2) GEMMs: 1 on, 0 off, <0 query; returns the previous mode");
   m.def("gemm_nt_swiglu", &nq::gemm_nt_swiglu, "gu = A @ [gate; up]^T, h = silu(g) * u (one GEMM)");
   m.def("gemm_nn", &nq::gemm_nn, "C = A @ B (bf16, tcgen05)");
   m.def("gemm_nn_out", &nq::gemm_nn_out);

@@ -13,7 +13,10 @@
 // -> global) so the epilogue of tile i overlaps the main loop of tile i+1.  One
 // CTA per SM walks the tile list with a grid stride; tiles are rasterised in
 // bands of 8 M-tiles for L2 reuse of B.
+#include <atomic>
+#include <cstdlib>
 #include <cstring>
+#include <string>
 
 #include "common.cuh"
 #include "peer.cuh"
@@ -67,6 +70,15 @@ struct GemmArgs {
   // (bf16) or TMA add-reductions (fp32 accumulate) using the tmC / tmH maps
   // (box 32 x 32 rows).  0: register-to-global stores.
   int tma_epi;
+  // Expert-parallel consumer (group M): the A rows of local expert g's
+  // segment arrive from the source ranks in rank order, source s holding
+  // ep_counts[s * ep_E + ep_expert0 + g] rows.  Before loading an m-tile the
+  // producer waits for the dispatch flag ep_flags[s] >= ep_seq of every
+  // source whose rows the tile covers, so tiles start as their rows land.
+  const int* ep_counts;      // null: no wait
+  const unsigned* ep_flags;
+  unsigned ep_seq;
+  int ep_world, ep_E, ep_expert0;
 };
 
 // Epilogue staging for TMA stores: per epilogue warp (32 rows) three 2 KB
@@ -94,6 +106,121 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   const int bm = min(8, tiles_m - m_base);
   mt = m_base + r % bm;
   nt = r / bm;
+}
+
+// TMA-store epilogue of one accumulator tile for one epilogue warp: rows
+// [ty, ty+32) of C, columns [n0, n0+BN) read from TMEM at `trow` (the warp's
+// lane quarter, the tile's accumulator buffer); `stg` is the warp's staging.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tma(uint8_t* stg, uint32_t trow, int ty, int n0, const GemmArgs& args,
+                                             const CUtensorMap* tmC, const CUtensorMap* tmH, bool has_acc,
+                                             int lane, int& half) {
+  if (EPI == kEpiSwiGLU) {
+    const int I = args.N >> 1;
+#pragma unroll 1
+    for (int c = 0; c < BN / 2; c += 32) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32(trow + c, rg);
+      tmem_ld32(trow + BN / 2 + c, ru);
+      tmem_wait_ld();
+      const int jc = n0 / 2 + c;
+      if (jc >= I) continue;
+      uint4 vg[4], vu[4], vh[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float g[8], u[8], h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          g[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[q * 8 + e])));
+          u[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[q * 8 + e])));
+          h[e] = g[e] * sigmoid_fast(g[e]) * u[e];
+        }
+        vg[q] = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]),
+                           pack_bf16(g[6], g[7]));
+        vu[q] = make_uint4(pack_bf16(u[0], u[1]), pack_bf16(u[2], u[3]), pack_bf16(u[4], u[5]),
+                           pack_bf16(u[6], u[7]));
+        vh[q] = make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]),
+                           pack_bf16(h[6], h[7]));
+      }
+      if (lane == 0) bulk_wait_read_all();  // the previous chunk's stores have read the staging
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int q = (j + lane) & 3;
+        const uint4 a = q == 0 ? vg[0] : q == 1 ? vg[1] : q == 2 ? vg[2] : vg[3];
+        const uint4 b = q == 0 ? vu[0] : q == 1 ? vu[1] : q == 2 ? vu[2] : vu[3];
+        const uint4 d = q == 0 ? vh[0] : q == 1 ? vh[1] : q == 2 ? vh[2] : vh[3];
+        *reinterpret_cast<uint4*>(stg + lane * 64 + q * 16) = a;
+        *reinterpret_cast<uint4*>(stg + 2048 + lane * 64 + q * 16) = b;
+        *reinterpret_cast<uint4*>(stg + 4096 + lane * 64 + q * 16) = d;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, stg, jc, ty);
+        tma_store_2d(tmC, stg + 2048, I + jc, ty);
+        tma_store_2d(tmH, stg + 4096, jc, ty);
+        bulk_commit();
+      }
+    }
+  } else if (EPI == kEpiBF16 && has_acc) {
+    // `half` alternates the two staging halves across chunks and tiles, so
+    // the store still in flight always reads the other half
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(trow + c, r);
+      tmem_wait_ld();
+      if (n0 + c >= args.N) continue;
+      uint4 v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        v[q] = make_uint4(pack_bf16(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1])),
+                          pack_bf16(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3])),
+                          pack_bf16(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5])),
+                          pack_bf16(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7])));
+      uint8_t* dst = stg + half * 2048;
+      if (lane == 0) bulk_wait_read_1();  // the store that last read this half is done reading
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int q = (j + lane) & 3;
+        *reinterpret_cast<uint4*>(dst + lane * 64 + q * 16) = q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, dst, n0 + c, ty);
+        bulk_commit();
+      }
+      half ^= 1;
+    }
+  } else if (EPI == kEpiAccF32 && has_acc) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(trow + c, r);
+      tmem_wait_ld();
+      if (n0 + c >= args.N) continue;
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int q = (j + lane) & 7;
+        uint4 v = make_uint4(r[0], r[1], r[2], r[3]);
+#pragma unroll
+        for (int t = 1; t < 8; ++t)
+          if (q == t) v = make_uint4(r[4 * t], r[4 * t + 1], r[4 * t + 2], r[4 * t + 3]);
+        *reinterpret_cast<uint4*>(stg + lane * 128 + q * 16) = v;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_2d(tmC, stg, n0 + c, ty);
+        bulk_commit();
+      }
+    }
+  }
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
@@ -198,10 +325,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int waited_owner = -1;
+      unsigned waited_src = 0;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         int m0, n0, g, kb, ke;
         decode(t, m0, n0, g, kb, ke);
         const int b_row_off = (args.group_mode == kGroupM) ? g * args.b_group_rows : 0;
+        if (args.ep_counts != nullptr && args.group_mode == kGroupM) {
+          const int e = args.ep_expert0 + g;
+          const int r0 = m0 - s_off[g];
+          int pre = 0;
+          for (int src = 0; src < args.ep_world; ++src) {
+            const int c = args.ep_counts[src * args.ep_E + e];
+            if (c > 0 && pre < r0 + GBM && pre + c > r0 && !((waited_src >> src) & 1u)) {
+              if (!wait_flag(args.ep_flags + src, args.ep_seq, err)) { ok = false; break; }
+              waited_src |= 1u << src;
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+            pre += c;
+          }
+          if (!ok) break;
+        }
         if (args.ag_flags != nullptr) {
           const int owner = m0 / args.tp_rows;
           if (owner != waited_owner) {
@@ -288,6 +431,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
+    int stg_half = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       int m0, n0, g, kb, ke;
       decode(t, m0, n0, g, kb, ke);
@@ -300,115 +444,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool row_ok = row < m_limit;
       const bool has_acc = ke > kb;
       if (args.tma_epi) {
-        // ------------------------------------------------ TMA-store epilogue
-        uint8_t* stg = smem + L::kEpiOff + quarter * kEpiWarpBytes;
-        const int ty = m0 + quarter * 32;
-        const uint32_t trow = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-        if (EPI == kEpiSwiGLU) {
-          const int I = args.N >> 1;
-#pragma unroll 1
-          for (int c = 0; c < BN / 2; c += 32) {
-            uint32_t rg[32], ru[32];
-            tmem_ld32(trow + c, rg);
-            tmem_ld32(trow + BN / 2 + c, ru);
-            tmem_wait_ld();
-            const int jc = n0 / 2 + c;
-            if (jc >= I) continue;
-            uint4 vg[4], vu[4], vh[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float g[8], u[8], h[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                g[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[q * 8 + e])));
-                u[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[q * 8 + e])));
-                h[e] = g[e] * sigmoid_fast(g[e]) * u[e];
-              }
-              vg[q] = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]),
-                                 pack_bf16(g[6], g[7]));
-              vu[q] = make_uint4(pack_bf16(u[0], u[1]), pack_bf16(u[2], u[3]), pack_bf16(u[4], u[5]),
-                                 pack_bf16(u[6], u[7]));
-              vh[q] = make_uint4(pack_bf16(h[0], h[1]), pack_bf16(h[2], h[3]), pack_bf16(h[4], h[5]),
-                                 pack_bf16(h[6], h[7]));
-            }
-            if (lane == 0) bulk_wait_read_all();  // the previous chunk's stores have read the staging
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int q = (j + lane) & 3;
-              const uint4 a = q == 0 ? vg[0] : q == 1 ? vg[1] : q == 2 ? vg[2] : vg[3];
-              const uint4 b = q == 0 ? vu[0] : q == 1 ? vu[1] : q == 2 ? vu[2] : vu[3];
-              const uint4 d = q == 0 ? vh[0] : q == 1 ? vh[1] : q == 2 ? vh[2] : vh[3];
-              *reinterpret_cast<uint4*>(stg + lane * 64 + q * 16) = a;
-              *reinterpret_cast<uint4*>(stg + 2048 + lane * 64 + q * 16) = b;
-              *reinterpret_cast<uint4*>(stg + 4096 + lane * 64 + q * 16) = d;
-            }
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmC, stg, jc, ty);
-              tma_store_2d(&tmC, stg + 2048, I + jc, ty);
-              tma_store_2d(&tmH, stg + 4096, jc, ty);
-              bulk_commit();
-            }
-          }
-        } else if (EPI == kEpiBF16 && has_acc) {
-          int half = 0;
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(trow + c, r);
-            tmem_wait_ld();
-            if (n0 + c >= args.N) continue;
-            uint4 v[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              v[q] = make_uint4(pack_bf16(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1])),
-                                pack_bf16(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3])),
-                                pack_bf16(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5])),
-                                pack_bf16(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7])));
-            uint8_t* dst = stg + half * 2048;
-            if (lane == 0) bulk_wait_read_1();  // the store that last read this half is done reading
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int q = (j + lane) & 3;
-              *reinterpret_cast<uint4*>(dst + lane * 64 + q * 16) = q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
-            }
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmC, dst, n0 + c, ty);
-              bulk_commit();
-            }
-            half ^= 1;
-          }
-        } else if (EPI == kEpiAccF32 && has_acc) {
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(trow + c, r);
-            tmem_wait_ld();
-            if (n0 + c >= args.N) continue;
-            if (lane == 0) bulk_wait_read_all();
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int q = (j + lane) & 7;
-              uint4 v = make_uint4(r[0], r[1], r[2], r[3]);
-#pragma unroll
-              for (int t = 1; t < 8; ++t)
-                if (q == t) v = make_uint4(r[4 * t], r[4 * t + 1], r[4 * t + 2], r[4 * t + 3]);
-              *reinterpret_cast<uint4*>(stg + lane * 128 + q * 16) = v;
-            }
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_reduce_add_2d(&tmC, stg, n0 + c, ty);
-              bulk_commit();
-            }
-          }
-        }
+        epilogue_tma<BN, EPI>(smem + L::kEpiOff + quarter * kEpiWarpBytes,
+                              tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN,
+                              m0 + quarter * 32, n0, args, &tmC, &tmH, has_acc, lane, stg_half);
       } else if (EPI == kEpiSwiGLU) {
         const int I = args.N >> 1;
 #pragma unroll 1
@@ -514,6 +552,196 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ---------------------------------------------------------- 2-SM (CTA pair)
+// Same GEMMs on CTA pairs: a cluster of two CTAs computes a 256 x 256 output
+// tile with tcgen05.mma.cta_group::2 (M = 256: 128 rows per CTA; B: each CTA
+// stages 128 of the 256 columns).  Per k-block each SM loads 32 KB (its A rows
+// and its half of B) instead of 48 KB for a 128 x 256 tile on one SM, so a
+// FLOP costs a third less L2-to-shared traffic and shared-memory bandwidth.
+//   warp 0 (both CTAs)  : TMA loads into its own ring; completion bytes count
+//                          on the even CTA's `full` barrier;
+//   warp 1 (even CTA)   : waits `full`, issues the pair MMAs, commits stage
+//                          release and accumulator-ready to both CTAs;
+//   warps 2-5 (both)    : drain the CTA's 128 accumulator rows with the TMA
+//                          epilogue, then arrive on the even CTA's `tempty`.
+// No TMA multicast is used (loads read global memory of this GPU only, but
+// the kernel is meant for multi-GPU jobs too).
+constexpr int kPairStages = 6;
+
+struct GemmPairSmem {
+  static constexpr int kABytes = 128 * GBK * 2;   // this CTA's 128 rows of A
+  static constexpr int kBBytes = 128 * GBK * 2;   // this CTA's 128 columns of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOff = kPairStages * kStageBytes;
+  static constexpr int kEpiOff = kBarOff + 1024;
+  static constexpr int kBytes = kEpiOff + 4 * kEpiWarpBytes + 1024;
+};
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1) __cluster_dims__(2, 1, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH,
+                     const GemmArgs args) {
+  using L = GemmPairSmem;
+  constexpr int STAGES = kPairStages;
+  constexpr int BN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const bool leader = cta == 0;
+  int* err = args.err;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    if (EPI == kEpiSwiGLU) tma_prefetch_desc(&tmH);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  // the peer's loads and arrivals target this CTA's barriers: both CTAs'
+  // barriers are initialised before anyone proceeds
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = (args.M + 255) / 256;
+  const int tiles_n = (args.N + BN - 1) / BN;
+  const int total = tiles_m * tiles_n;
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += pairs) {
+        int mt, nt;
+        tile_coords(t, tiles_m, tiles_n, mt, nt);
+        const int m0 = mt * 256 + 128 * static_cast<int>(cta);  // this CTA's A rows
+        const int n0 = nt * BN;
+        for (int k0 = 0; k0 < args.K; k0 += GBK) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTimeoutProducer)) { ok = false; break; }
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          uint8_t* sA = smem + stage * L::kStageBytes;
+          uint8_t* sB = sA + L::kABytes;
+          if (!A_MN) {
+            tma_load_2d_pair(sA, &tmA, bar, k0, m0);
+          } else {
+            tma_load_2d_pair(sA, &tmA, bar, m0, k0);
+            tma_load_2d_pair(sA + 8192, &tmA, bar, m0 + 64, k0);
+          }
+          if (EPI == kEpiSwiGLU) {
+            // even CTA: the gate rows of this tile, odd CTA: the matching up rows
+            tma_load_2d_pair(sB, &tmB, bar, k0, (cta ? args.N / 2 : 0) + n0 / 2);
+          } else if (!B_MN) {
+            tma_load_2d_pair(sB, &tmB, bar, k0, n0 + 128 * static_cast<int>(cta));
+          } else {
+            tma_load_2d_pair(sB, &tmB, bar, n0 + 128 * static_cast<int>(cta), k0);
+            tma_load_2d_pair(sB + 8192, &tmB, bar, n0 + 128 * static_cast<int>(cta) + 64, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {  // let loads already issued land before the CTA can exit
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 200000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (even CTA only)
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16(256, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += pairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        uint32_t acc = 0;
+        for (int k0 = 0; k0 < args.K; k0 += GBK) {
+          if (!mbar_wait(&full[stage], phase, err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < GBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_addr + kk * 2048, 8192, 1024)
+                                     : sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_addr + kk * 2048, 8192, 1024)
+                                     : sdesc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, acc);
+            acc = 1;
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[buf], 0x3);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    int local = 0;
+    int stg_half = 0;
+    for (int t = pair; t < total; t += pairs, ++local) {
+      int mt, nt;
+      tile_coords(t, tiles_m, tiles_n, mt, nt);
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&tfull[buf], use & 1, err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      epilogue_tma<BN, EPI>(smem + L::kEpiOff + quarter * kEpiWarpBytes,
+                            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN,
+                            mt * 256 + 128 * static_cast<int>(cta) + quarter * 32, nt * BN, args, &tmC, &tmH,
+                            args.K > 0, lane, stg_half);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  // neither CTA leaves while the other may still signal its barriers or read
+  // its shared memory / TMEM
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
 // ----------------------------------------------------------------------- host
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
@@ -527,6 +755,47 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   CUtensorMap none;
   std::memset(&none, 0, sizeof(none));
   kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, tc ? *tc : none, th ? *th : none, a);
+  NQ_CHECK_CUDA(cudaGetLastError());
+}
+
+// CTA-pair GEMM (the default where it applies: TMA epilogue usable and at
+// least one tile per SM pair); NQ_GEMM_PAIR=0 in the environment, or
+// gemm_pair_mode(0), selects the one-SM kernel everywhere.
+static std::atomic<int> g_pair_mode{-1};
+
+static bool pair_enabled() {
+  int m = g_pair_mode.load(std::memory_order_relaxed);
+  if (m < 0) {
+    const char* e = std::getenv("NQ_GEMM_PAIR");
+    m = (e == nullptr || std::string(e) != "0") ? 1 : 0;
+    g_pair_mode.store(m, std::memory_order_relaxed);
+  }
+  return m != 0;
+}
+
+// mode 0 / 1 switches the CTA-pair kernels off / on; returns the mode before
+// the call (a negative mode only queries it).
+int64_t gemm_pair_mode(int64_t mode) {
+  const int before = pair_enabled() ? 1 : 0;
+  if (mode >= 0) g_pair_mode.store(mode ? 1 : 0, std::memory_order_relaxed);
+  return before;
+}
+
+static bool use_pair(int M, int N) {
+  return pair_enabled() && static_cast<int64_t>((M + 255) / 256) * ((N + 255) / 256) >= num_sms() / 2;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                             const CUtensorMap* th, const GemmArgs& a, cudaStream_t stream) {
+  static_assert(GemmPairSmem::kBytes <= 232448, "pair GEMM shared memory budget");
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  set_max_smem_once(reinterpret_cast<const void*>(kern), GemmPairSmem::kBytes);
+  const int tiles = ((a.M + 255) / 256) * ((a.N + 255) / 256);
+  const int grid = 2 * std::max(1, std::min(num_sms() / 2, tiles));
+  CUtensorMap none;
+  std::memset(&none, 0, sizeof(none));
+  kern<<<grid, kGemmThreads, GemmPairSmem::kBytes, stream>>>(ta, tb, tc, th ? *th : none, a);
   NQ_CHECK_CUDA(cudaGetLastError());
 }
 
@@ -545,6 +814,7 @@ static GemmArgs base_args(int M, int N, int K, void* C, int64_t ldc) {
   a.group_mode = kGroupNone; a.num_groups = 1; a.offsets = nullptr;
   a.c_group_stride = 0; a.b_group_rows = 0; a.err = error_flag_ptr();
   a.tma_epi = 0;
+  a.ep_counts = nullptr; a.ep_flags = nullptr; a.ep_seq = 0; a.ep_world = 0; a.ep_E = 0; a.ep_expert0 = 0;
   return a;
 }
 
@@ -561,15 +831,20 @@ void gemm_nt_out(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
   if (K == 0) { C.zero_(); return; }
   c10::cuda::CUDAGuard g(A.device());
   auto ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, GBM);
-  auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, kBN);
   auto a = base_args(M, N, K, C.data_ptr(), C.stride(0));
   CUtensorMap tc;
   if (tma_epi_ok(C.data_ptr(), C.stride(0), 2)) {
     tc = make_tmap_2d_bf16(C.data_ptr(), M, N, C.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
     a.tma_epi = 1;
   }
-  launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
-                                                    at::cuda::getCurrentCUDAStream(),
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (a.tma_epi && use_pair(M, N)) {
+    auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, 128);
+    launch_gemm_pair<false, false, kEpiBF16>(ta, tb, tc, nullptr, a, st);
+    return;
+  }
+  auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, kBN);
+  launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN), st,
                                                     a.tma_epi ? &tc : nullptr);
 }
 
@@ -600,6 +875,10 @@ std::vector<torch::Tensor> gemm_nt_swiglu(torch::Tensor A, torch::Tensor B) {
   auto tc = make_tmap_2d_bf16(gu.data_ptr(), M, N, gu.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
   auto th = make_tmap_2d_bf16(h.data_ptr(), M, N / 2, N / 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
   a.tma_epi = 1;
+  if (use_pair(M, N)) {  // tb already has 128-row boxes (gate / up halves)
+    launch_gemm_pair<false, false, kEpiSwiGLU>(ta, tb, tc, &th, a, at::cuda::getCurrentCUDAStream());
+    return {gu, h};
+  }
   launch_gemm<kBN, kStages, false, false, kEpiSwiGLU>(ta, tb, a, cdiv(M, GBM) * (N / kBN),
                                                       at::cuda::getCurrentCUDAStream(), &tc, &th);
   return {gu, h};
@@ -622,6 +901,10 @@ void gemm_nn_out(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
   if (tma_epi_ok(C.data_ptr(), C.stride(0), 2)) {
     tc = make_tmap_2d_bf16(C.data_ptr(), M, N, C.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
     a.tma_epi = 1;
+  }
+  if (a.tma_epi && use_pair(M, N)) {  // tb: 64 x 64 boxes, the same for both kernels
+    launch_gemm_pair<false, true, kEpiBF16>(ta, tb, tc, nullptr, a, at::cuda::getCurrentCUDAStream());
+    return;
   }
   launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
                                                    at::cuda::getCurrentCUDAStream(),
@@ -652,6 +935,10 @@ void gemm_tn_acc(torch::Tensor A, torch::Tensor B, torch::Tensor C) {
     // C += tile through TMA add-reductions (the read-modify-write happens in L2)
     tc = make_tmap_2d_f32(C.data_ptr(), M, N, C.stride(0), 32, 32);
     a.tma_epi = 1;
+  }
+  if (a.tma_epi && use_pair(M, N)) {  // ta / tb: 64 x 64 boxes, the same for both kernels
+    launch_gemm_pair<true, true, kEpiAccF32>(ta, tb, tc, nullptr, a, at::cuda::getCurrentCUDAStream());
+    return;
   }
   launch_gemm<kBN, kStages, true, true, kEpiAccF32>(ta, tb, a, cdiv(M, GBM) * cdiv(N, kBN),
                                                     at::cuda::getCurrentCUDAStream(),

@@ -11,10 +11,10 @@ again and reports, per parameter, whether the two updates are bit-identical
 and the largest difference.
 
 Expected nondeterminism is narrow and bounded: the attention backward adds
-the dQ partials of different key blocks with TMA bulk add-reductions and the
-embedding backward scatters rows with fp32 atomics, so those sums can round
-differently from run to run (relative differences around 1e-7 on the
-gradients before Adam).  Everything else is deterministic: the forward pass,
+the dQ partials of different key blocks with TMA bulk add-reductions, the
+embedding backward scatters rows with fp32 atomics and the cross-entropy adds
+its per-row losses with atomics, so those sums can round differently from run
+to run (relative differences around 1e-7).  Everything else is deterministic: the forward pass,
 the GEMMs (one CTA owns each output tile, fixed K order) and the optimizer.
 """
 

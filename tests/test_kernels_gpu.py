@@ -105,6 +105,38 @@ def test_gemm_tma_epilogue_matches_register_epilogue(E, M, N, K):
     assert rel_err(c_tma, c0 + At.float().t() @ Bk.float()) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(2048, 4096, 512), (4096, 2048, 2048), (1000, 9000, 1032)])
+def test_gemm_pair_kernels_match_one_sm(E, M, N, K):
+    """The CTA-pair kernels (tcgen05.mma.cta_group::2, 256 x 256 tiles) write
+    the same bits as the one-SM kernels for NT, NN, the SwiGLU epilogue and
+    fp32 accumulation (same K order per output), and match fp32."""
+    torch.manual_seed(6)
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    Bk = torch.randn(K, N, device=DEV).bfloat16()
+    W = (torch.randn(N // 256 * 256, K, device=DEV) / math.sqrt(K)).bfloat16()
+    At = torch.randn(K, M, device=DEV).bfloat16()
+    Bt = torch.randn(K, N // 8 * 8, device=DEV).bfloat16()
+    c0 = torch.randn(M, N // 8 * 8, device=DEV)
+    outs = {}
+    before = E.gemm_pair_mode(-1)
+    try:
+        for mode in (1, 0):
+            E.gemm_pair_mode(mode)
+            c = c0.clone()
+            E.gemm_tn_acc(At, Bt, c)
+            outs[mode] = (E.gemm_nt(A, B), E.gemm_nn(A, Bk), E.gemm_nt_swiglu(A, W), c)
+    finally:
+        E.gemm_pair_mode(before)
+    p, o = outs[1], outs[0]
+    assert torch.equal(p[0], o[0]) and torch.equal(p[1], o[1])
+    assert torch.equal(p[2][0], o[2][0]) and torch.equal(p[2][1], o[2][1])
+    assert rel_err(p[3], o[3]) < 1e-6
+    assert rel_err(p[0], A.float() @ B.float().t()) < 1e-2
+    assert rel_err(p[1], A.float() @ Bk.float()) < 1e-2
+    assert rel_err(p[3], c0 + At.float().t() @ Bt.float()) < 1e-2
+
+
 def _grouped_inputs(G, R_per, K, seed=3):
     torch.manual_seed(seed)
     sizes = [R_per[g] for g in range(G)]

@@ -137,7 +137,9 @@ def test_replay_determinism_on_gpu():
     assert replay_forward(eng.model, ids)
     eng.train_step([{"input_ids": ids, "labels": ids}])
     r = replay_step(eng, [{"input_ids": ids, "labels": ids}])
-    assert r["loss_equal"], r["loss"]
+    # the loss is a sum of per-row terms added with atomics: equal up to rounding
+    a, b = r["loss"]
+    assert abs(a - b) <= 1e-6 * abs(a), r["loss"]
     # Adam's normalised step bounds any difference by a few learning rates
     assert all(d < 5e-3 for d in r["differs"].values()), r["differs"]
     assert ext().error_flag_read() == 0
