@@ -12,8 +12,10 @@ std::vector<torch::Tensor> gemm_nt_swiglu(torch::Tensor A, torch::Tensor B);
 torch::Tensor gemm_nn(torch::Tensor A, torch::Tensor B);
 void gemm_nn_out(torch::Tensor A, torch::Tensor B, torch::Tensor C);
 void gemm_tn_acc(torch::Tensor A, torch::Tensor B, torch::Tensor C);
-torch::Tensor grouped_gemm_nt(torch::Tensor X, torch::Tensor W, torch::Tensor offsets);
-torch::Tensor grouped_gemm_nn(torch::Tensor dY, torch::Tensor W, torch::Tensor offsets);
+torch::Tensor grouped_gemm_nt(torch::Tensor X, torch::Tensor W, torch::Tensor offsets, int64_t, int64_t, int64_t,
+                              int64_t, int64_t, int64_t);
+torch::Tensor grouped_gemm_nn(torch::Tensor dY, torch::Tensor W, torch::Tensor offsets, int64_t, int64_t, int64_t,
+                              int64_t, int64_t, int64_t);
 void grouped_gemm_tn_acc(torch::Tensor dY, torch::Tensor X, torch::Tensor dW, torch::Tensor offsets);
 // norm.cu
 std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor, c10::optional<torch::Tensor>, torch::Tensor, double);
@@ -124,8 +126,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_nn", &nq::gemm_nn, "C = A @ B (bf16, tcgen05)");
   m.def("gemm_nn_out", &nq::gemm_nn_out);
   m.def("gemm_tn_acc", &nq::gemm_tn_acc, "C(fp32) += A^T @ B (tcgen05)");
-  m.def("grouped_gemm_nt", &nq::grouped_gemm_nt);
-  m.def("grouped_gemm_nn", &nq::grouped_gemm_nn);
+  m.def("grouped_gemm_nt", &nq::grouped_gemm_nt,
+        "rows grouped by expert segments: C[r] = X[r] @ W[g(r)]^T; ep_*: wait per source rank for "
+        "expert-parallel dispatch flags before loading a tile's rows",
+        py::arg("X"), py::arg("W"), py::arg("offsets"), py::arg("ep_counts") = 0, py::arg("ep_flags") = 0,
+        py::arg("ep_seq") = 0, py::arg("ep_world") = 0, py::arg("ep_E") = 0, py::arg("ep_expert0") = 0);
+  m.def("grouped_gemm_nn", &nq::grouped_gemm_nn,
+        "rows grouped by expert segments: C[r] = dY[r] @ W[g(r)]; ep_*: as grouped_gemm_nt",
+        py::arg("dY"), py::arg("W"), py::arg("offsets"), py::arg("ep_counts") = 0, py::arg("ep_flags") = 0,
+        py::arg("ep_seq") = 0, py::arg("ep_world") = 0, py::arg("ep_E") = 0, py::arg("ep_expert0") = 0);
   m.def("grouped_gemm_tn_acc", &nq::grouped_gemm_tn_acc);
   m.def("add_rmsnorm_fwd", &nq::add_rmsnorm_fwd);
   m.def("add_rmsnorm_bwd", &nq::add_rmsnorm_bwd);

@@ -1023,7 +1023,25 @@ int64_t gemm_rs(torch::Tensor A, torch::Tensor B, bool nn, std::vector<int64_t> 
 // ------------------------------------------------------------- grouped GEMMs
 // X [R, K] rows grouped by `offsets` (multiples of 128), W [G, N, K]:
 //   out[r, :] = X[r, :] @ W[g(r)]^T
-torch::Tensor grouped_gemm_nt(torch::Tensor X, torch::Tensor W, torch::Tensor offsets) {
+// Expert-parallel wait arguments of the grouped GEMMs (see GemmArgs): the
+// local copy of every source's per-expert counts, this rank's flag slots of
+// the exchange channel, the sequence number, the world, E and the first
+// local expert.  counts == 0: no wait.
+static void set_ep_wait(GemmArgs& a, int64_t counts, int64_t flags, int64_t seq, int64_t world, int64_t E,
+                        int64_t expert0) {
+  if (counts == 0) return;
+  TORCH_CHECK(flags != 0 && world >= 1 && world <= 8 && E > 0, "grouped GEMM: expert-parallel wait arguments");
+  a.ep_counts = reinterpret_cast<const int*>(counts);
+  a.ep_flags = reinterpret_cast<const unsigned*>(flags);
+  a.ep_seq = static_cast<unsigned>(seq);
+  a.ep_world = static_cast<int>(world);
+  a.ep_E = static_cast<int>(E);
+  a.ep_expert0 = static_cast<int>(expert0);
+}
+
+torch::Tensor grouped_gemm_nt(torch::Tensor X, torch::Tensor W, torch::Tensor offsets, int64_t ep_counts,
+                              int64_t ep_flags, int64_t ep_seq, int64_t ep_world, int64_t ep_E,
+                              int64_t ep_expert0) {
   check_bf16(X, "X"); check_bf16(W, "W");
   TORCH_CHECK(W.dim() == 3 && X.size(1) == W.size(2) && W.is_contiguous() && X.is_contiguous(), "grouped_gemm_nt: shapes");
   TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() == W.size(0) + 1, "offsets");
@@ -1036,13 +1054,16 @@ torch::Tensor grouped_gemm_nt(torch::Tensor X, torch::Tensor W, torch::Tensor of
   auto tb = make_tmap_2d_bf16(W.data_ptr(), static_cast<int64_t>(G) * N, K, K, 64, kBN);
   auto a = base_args(R, N, K, C.data_ptr(), N);
   a.group_mode = kGroupM; a.num_groups = G; a.offsets = offsets.data_ptr<int>(); a.b_group_rows = N;
+  set_ep_wait(a, ep_counts, ep_flags, ep_seq, ep_world, ep_E, ep_expert0);
   launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, cdiv(R, GBM) * cdiv(N, kBN),
                                                     at::cuda::getCurrentCUDAStream());
   return C;
 }
 
 // dY [R, N] grouped rows, W [G, N, K]: out[r, :] = dY[r, :] @ W[g(r)]   ([R, K])
-torch::Tensor grouped_gemm_nn(torch::Tensor dY, torch::Tensor W, torch::Tensor offsets) {
+torch::Tensor grouped_gemm_nn(torch::Tensor dY, torch::Tensor W, torch::Tensor offsets, int64_t ep_counts,
+                              int64_t ep_flags, int64_t ep_seq, int64_t ep_world, int64_t ep_E,
+                              int64_t ep_expert0) {
   check_bf16(dY, "dY"); check_bf16(W, "W");
   TORCH_CHECK(W.dim() == 3 && dY.size(1) == W.size(1) && W.is_contiguous() && dY.is_contiguous(), "grouped_gemm_nn: shapes");
   const int G = W.size(0), N = W.size(1), K = W.size(2), R = dY.size(0);
@@ -1054,6 +1075,7 @@ torch::Tensor grouped_gemm_nn(torch::Tensor dY, torch::Tensor W, torch::Tensor o
   auto tb = make_tmap_2d_bf16(W.data_ptr(), static_cast<int64_t>(G) * N, K, K, 64, 64);
   auto a = base_args(R, K, N, C.data_ptr(), K);
   a.group_mode = kGroupM; a.num_groups = G; a.offsets = offsets.data_ptr<int>(); a.b_group_rows = N;
+  set_ep_wait(a, ep_counts, ep_flags, ep_seq, ep_world, ep_E, ep_expert0);
   launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, cdiv(R, GBM) * cdiv(K, kBN),
                                                    at::cuda::getCurrentCUDAStream());
   return C;

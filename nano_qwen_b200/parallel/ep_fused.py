@@ -11,8 +11,10 @@ Forward of one MoE layer on rank r (experts [r*El, (r+1)*El)):
 2. ``ep_dispatch``: each pair's token row is stored straight into the owner's
    receive buffer (P2P stores; the permutation and the all-to-all are one
    pass); padding rows of the own buffer are zeroed.
-3. After a bounded wait for every source, the grouped gate|up GEMM, SwiGLU and
-   the grouped down GEMM run on the receive buffer (tcgen05 grouped GEMMs).
+3. The grouped gate|up GEMM (tcgen05) consumes the receive buffer directly:
+   before loading a tile of an expert segment its TMA producer waits for the
+   dispatch flags of the source ranks whose rows the tile covers, so tiles
+   start as their rows land; SwiGLU and the grouped down GEMM follow.
 4. ``ep_combine``: each source pulls its pairs' output rows from the owners
    (P2P loads) and forms the weighted top-k sum.
 
@@ -81,6 +83,12 @@ class EPComm:
         self.seq[ch] += 1
         return self.seq[ch]
 
+    def ep_wait_args(self, ch: int, seq: int) -> dict:
+        """Arguments that make a grouped GEMM wait per tile for channel
+        ``ch``'s flags (this rank's slots, one per source) to reach ``seq``."""
+        return dict(ep_counts=self.counts.data_ptr(), ep_flags=self.flags.data_ptr() + ch * 8 * 4,
+                    ep_seq=seq, ep_world=self.world, ep_E=self.E, ep_expert0=self.rank * self.El)
+
     def advance(self, grid: int) -> int:
         before = self.count
         self.count += int(grid)
@@ -118,10 +126,12 @@ class _EPMoE(torch.autograd.Function):
         grid = E.ep_dispatch(comm.p_flags, comm.p_counts, recv_ptrs, comm.rank, x, idx, slot_of, loc_off,
                              dest_base, seg_off, seg_used, dest_row, El, comm.cap, s1, comm.counter, before)
         comm.advance(grid)
-        E.ep_wait(comm.p_flags, comm.p_counts, comm.rank, CH_DISPATCH, s1)
         Wgu = w_gu.compute.view(El, 2 * inter, H)
         Wd = w_d.compute.view(El, H, inter)
-        gu = E.grouped_gemm_nt(recv, Wgu, seg_off)
+        # the gate|up GEMM consumes the receive buffer as rows land: its TMA
+        # producer waits, per tile, for the dispatch flags of the sources
+        # whose rows the tile covers (no separate wait for all sources)
+        gu = E.grouped_gemm_nt(recv, Wgu, seg_off, **comm.ep_wait_args(CH_DISPATCH, s1))
         h = E.swiglu_fwd(gu)
         y = E.grouped_gemm_nt(h, Wd, seg_off)
         yo, yo_ptrs = comm.y_out
@@ -153,12 +163,14 @@ class _EPMoE(torch.autograd.Function):
         grid = E.ep_combine_bwd(comm.p_flags, comm.p_counts, dyr_ptrs, comm.rank, idx, dest_row, w32, dout,
                                 y_pulled, dw, El, s3, comm.counter, before)
         comm.advance(grid)
-        E.ep_wait(comm.p_flags, comm.p_counts, comm.rank, CH_DOUT, s3)
         Wgu = w_gu.compute.view(El, 2 * inter, H)
         Wd = w_d.compute.view(El, H, inter)
+        # the down-projection dgrad consumes the pushed output gradients as
+        # they land (per-tile waits on the sources' flags); the weight
+        # gradient runs after it in stream order, on complete data
+        dh = E.grouped_gemm_nn(dyr, Wd, seg_off, **comm.ep_wait_args(CH_DOUT, s3))
         if w_d.requires_grad:
             E.grouped_gemm_tn_acc(dyr, h, _grad_view(w_d, (El, H, inter)), seg_off)
-        dh = E.grouped_gemm_nn(dyr, Wd, seg_off)
         dgu = E.swiglu_bwd(dh, gu)
         if w_gu.requires_grad:
             E.grouped_gemm_tn_acc(dgu, recv, _grad_view(w_gu, (El, 2 * inter, H)), seg_off)
