@@ -106,7 +106,13 @@ class MoELayer(nn.Module):
         weights, idx, counts, prob_sum = self.router(x)
         gcounts, gtokens = None, None
         if self.global_stats_fn is not None:
-            gcounts, gtokens = self.global_stats_fn(counts, N)
+            grp = getattr(self, "global_stats_group", None)
+            if self.ep is not None and hasattr(self.ep, "covers") and self.ep.covers(grp, x):
+                # the fused expert-parallel counts exchange already spans the
+                # balancing group: no separate all-reduce in the forward
+                gcounts, gtokens = self.ep.global_stats(x, counts, idx.shape[1])
+            else:
+                gcounts, gtokens = self.global_stats_fn(counts, N)
         aux = ops.aux_loss_from_stats(counts, prob_sum, N, self.top_k, self.num_experts,
                                       gcounts, gtokens)
         if self.router.grad_scale != 1.0:

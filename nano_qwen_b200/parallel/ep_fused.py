@@ -101,9 +101,24 @@ def _grad_view(wref, shape):
     return wref.grad.view(shape)
 
 
+def ep_layout(comm: EPComm, counts: torch.Tensor):
+    """Counts exchange + receive layout of one MoE layer (``ep_layout``): every
+    rank's per-expert counts land in every rank's table; returns
+    (dest_base [E], seg_off [El+1], seg_used [El])."""
+    E = ext()
+    dev = counts.device
+    dest_base = torch.empty(comm.E, dtype=torch.int32, device=dev)
+    seg_off = torch.empty(comm.El + 1, dtype=torch.int32, device=dev)
+    seg_used = torch.empty(comm.El, dtype=torch.int32, device=dev)
+    s0 = comm.next(CH_COUNTS)
+    E.ep_layout(comm.p_flags, comm.p_counts, comm.rank, counts.float().contiguous(), comm.E, comm.El, s0,
+                dest_base, seg_off, seg_used, comm.cap)
+    return dest_base, seg_off, seg_used
+
+
 class _EPMoE(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weights, idx, counts, w_gu, w_d, comm: EPComm, layer: int, inter: int,
+    def forward(ctx, x, weights, idx, counts, w_gu, w_d, comm: EPComm, layer: int, inter: int, layout,
                 *anchors):
         E = ext()
         N, H = x.shape
@@ -112,12 +127,8 @@ class _EPMoE(torch.autograd.Function):
         El = comm.El
         idx = idx.to(torch.int32).contiguous()
         x = x.contiguous()
-        dest_base = torch.empty(comm.E, dtype=torch.int32, device=dev)
-        seg_off = torch.empty(El + 1, dtype=torch.int32, device=dev)
-        seg_used = torch.empty(El, dtype=torch.int32, device=dev)
-        s0 = comm.next(CH_COUNTS)
-        E.ep_layout(comm.p_flags, comm.p_counts, comm.rank, counts.float().contiguous(), comm.E, El, s0,
-                    dest_base, seg_off, seg_used, comm.cap)
+        # the layout may already have run (global load-balancing statistics)
+        dest_base, seg_off, seg_used = layout if layout is not None else ep_layout(comm, counts)
         slot_of, loc_off, _ = E.moe_plan(idx, comm.E, -1, 1)  # pad 1: unpadded order
         recv, recv_ptrs = comm.recv_buf(layer)
         dest_row = torch.empty(N, K, dtype=torch.int32, device=dev)
@@ -181,10 +192,10 @@ class _EPMoE(torch.autograd.Function):
         E.ep_signal(comm.p_flags, comm.p_counts, comm.rank, CH_DX, s4)
         dx = torch.empty(N, H, dtype=torch.bfloat16, device=dout.device)
         E.ep_dispatch_bwd(comm.p_flags, comm.p_counts, dxo_ptrs, comm.rank, idx, dest_row, dx, El, s4)
-        return (dx, dw, None, None, None, None, None, None, None) + (None,) * n_anchor
+        return (dx, dw, None, None, None, None, None, None, None, None) + (None,) * n_anchor
 
 
-def ep_moe(moe, x, weights, idx, counts, comm: EPComm, layer: int) -> torch.Tensor:
+def ep_moe(moe, x, weights, idx, counts, comm: EPComm, layer: int, layout=None) -> torch.Tensor:
     w_gu, w_d = moe.expert_weight_refs(x.dtype)
-    return _EPMoE.apply(x, weights, idx, counts, w_gu, w_d, comm, layer, moe.inter,
+    return _EPMoE.apply(x, weights, idx, counts, w_gu, w_d, comm, layer, moe.inter, layout,
                         *w_gu.anchors, *w_d.anchors)

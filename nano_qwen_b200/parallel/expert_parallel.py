@@ -82,19 +82,45 @@ class ExpertParallel:
         self.shared = shared if shared is not None else {}
         self.layer = layer
 
+    def _comm(self, x: torch.Tensor, top_k: int):
+        from .ep_fused import EPComm
+        N, H = x.shape
+        key = (N, H, top_k)
+        comm = self.shared.get(key)
+        if comm is None:
+            comm = self.shared[key] = EPComm(self.group, self.num_experts, H, N, top_k, x.device)
+        return comm
+
+    def covers(self, group, x: torch.Tensor) -> bool:
+        """True when the fused exchange's counts already span ``group`` (the
+        group the load-balancing statistics are summed over)."""
+        if not (self.fused and x.is_cuda):
+            return False
+        mine = dist.get_process_group_ranks(self.group)
+        other = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+        return sorted(mine) == sorted(other)
+
+    def global_stats(self, x: torch.Tensor, counts: torch.Tensor, top_k: int):
+        """Global-batch routing statistics from the fused counts exchange: runs
+        this layer's layout exchange now (the dispatch reuses it) and sums every
+        source's per-expert counts on the device, so the load-balancing loss
+        needs no separate all-reduce.  Returns (counts per expert, tokens)."""
+        from .ep_fused import ep_layout
+        comm = self._comm(x, top_k)
+        self._layout = ep_layout(comm, counts)
+        tab = comm.counts.view(comm.world, comm.E).float()
+        g = tab.sum(0)
+        return g, g.sum() / top_k
+
     def __call__(self, moe, x: torch.Tensor, weights: torch.Tensor, idx: torch.Tensor,
                  counts=None) -> torch.Tensor:
         if self.fused and x.is_cuda:
-            from .ep_fused import EPComm, ep_moe
-            N, H = x.shape
-            key = (N, H, idx.shape[1])
-            comm = self.shared.get(key)
-            if comm is None:
-                comm = self.shared[key] = EPComm(self.group, self.num_experts, H, N, idx.shape[1],
-                                                 x.device)
+            from .ep_fused import ep_moe
+            comm = self._comm(x, idx.shape[1])
             if counts is None:
                 counts = torch.bincount(idx.reshape(-1).long(), minlength=self.num_experts).float()
-            return ep_moe(moe, x, weights, idx, counts, comm, self.layer)
+            layout, self._layout = getattr(self, "_layout", None), None
+            return ep_moe(moe, x, weights, idx, counts, comm, self.layer, layout)
         return self._nccl(moe, x, weights, idx)
 
     def _nccl(self, moe, x: torch.Tensor, weights: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:

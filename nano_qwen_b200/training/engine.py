@@ -27,8 +27,11 @@ def set_global_batch_balance(model: nn.Module, group) -> int:
     """Route every MoE layer's routing fractions f_i through an all-reduce over
     the data-parallel group, so the load-balancing loss is the global-batch
     one (E * sum_i f_i p_i with f_i counted over every rank's tokens; the
-    probabilities p_i and the gradient stay local).  The reference describes
-    this balancing but never wires it (reference: model/moe.py:201-249).
+    probabilities p_i and the gradient stay local).  Under fused expert
+    parallelism over the same ranks the counts come from the dispatch's own
+    counts exchange instead (``ExpertParallel.global_stats``).  The reference
+    describes this balancing but never wires it (reference:
+    model/moe.py:201-249).
     Returns the number of MoE layers configured."""
     import torch.distributed as dist
     from ..models.moe import MoELayer
@@ -43,6 +46,7 @@ def set_global_batch_balance(model: nn.Module, group) -> int:
     for m in model.modules():
         if isinstance(m, MoELayer):
             m.global_stats_fn = stats
+            m.global_stats_group = group
             k += 1
     return k
 

@@ -212,6 +212,20 @@ def ep_fused_worker(rank, world, port):
                 rn = f"{pre}.experts.{int(e) + rank * e_loc}.{tail}"
             err = ((gr - ref_g[rn]).norm() / (ref_g[rn].norm() + 1e-12)).item()
             assert err < 2e-2, (fused, n, err)
+    # global-batch load balancing: the fused path takes the counts from its
+    # own exchange, the NCCL path all-reduces them; both give the same loss
+    from nano_qwen_b200.training.engine import set_global_batch_balance
+    aux = {}
+    for fused in (True, False):
+        m = build(True, fused)
+        set_global_batch_balance(m, grp)
+        o = m(ids, labels=ids)
+        o["loss"].backward()
+        torch.cuda.synchronize()
+        aux[fused] = (float(o["loss"]), float(o["aux_loss"]))
+    assert ext().error_flag_read() == 0
+    assert abs(aux[True][1] - aux[False][1]) < 1e-4 * abs(aux[False][1]), aux
+    assert abs(aux[True][0] - aux[False][0]) < 2e-3 * aux[False][0], aux
     dist.barrier()
     dist.destroy_process_group()
 
