@@ -83,10 +83,12 @@ class EPComm:
         self.seq[ch] += 1
         return self.seq[ch]
 
-    def ep_wait_args(self, ch: int, seq: int) -> dict:
+    def ep_wait_args(self, ch: int, seq: int, counts: torch.Tensor) -> dict:
         """Arguments that make a grouped GEMM wait per tile for channel
-        ``ch``'s flags (this rank's slots, one per source) to reach ``seq``."""
-        return dict(ep_counts=self.counts.data_ptr(), ep_flags=self.flags.data_ptr() + ch * 8 * 4,
+        ``ch``'s flags (this rank's slots, one per source) to reach ``seq``;
+        ``counts`` is the [ranks x experts] table of the layer whose rows
+        arrive (the live table belongs to the most recent layout)."""
+        return dict(ep_counts=counts.data_ptr(), ep_flags=self.flags.data_ptr() + ch * 8 * 4,
                     ep_seq=seq, ep_world=self.world, ep_E=self.E, ep_expert0=self.rank * self.El)
 
     def advance(self, grid: int) -> int:
@@ -129,6 +131,12 @@ class _EPMoE(torch.autograd.Function):
         x = x.contiguous()
         # the layout may already have run (global load-balancing statistics)
         dest_base, seg_off, seg_used = layout if layout is not None else ep_layout(comm, counts)
+        # this layer's [ranks x experts] counts: the shared table is rewritten
+        # by every later layer's layout, and the backward's row waits need
+        # this layer's (copied before any peer can start the next layout:
+        # a peer's next layout follows its combine, which waits for this
+        # rank's expert outputs, which follow this copy in stream order)
+        cnt = comm.counts.clone()
         slot_of, loc_off, _ = E.moe_plan(idx, comm.E, -1, 1)  # pad 1: unpadded order
         recv, recv_ptrs = comm.recv_buf(layer)
         dest_row = torch.empty(N, K, dtype=torch.int32, device=dev)
@@ -142,7 +150,7 @@ class _EPMoE(torch.autograd.Function):
         # the gate|up GEMM consumes the receive buffer as rows land: its TMA
         # producer waits, per tile, for the dispatch flags of the sources
         # whose rows the tile covers (no separate wait for all sources)
-        gu = E.grouped_gemm_nt(recv, Wgu, seg_off, **comm.ep_wait_args(CH_DISPATCH, s1))
+        gu = E.grouped_gemm_nt(recv, Wgu, seg_off, **comm.ep_wait_args(CH_DISPATCH, s1, cnt))
         h = E.swiglu_fwd(gu)
         y = E.grouped_gemm_nt(h, Wd, seg_off)
         yo, yo_ptrs = comm.y_out
@@ -154,13 +162,13 @@ class _EPMoE(torch.autograd.Function):
         w32 = weights.float().contiguous()
         E.ep_combine(comm.p_flags, comm.p_counts, yo_ptrs, comm.rank, idx, dest_row, w32, out, y_pulled,
                      El, s2)
-        ctx.save_for_backward(idx, dest_row, w32, y_pulled, seg_off, recv, gu, h)
+        ctx.save_for_backward(idx, dest_row, w32, y_pulled, seg_off, recv, gu, h, cnt)
         ctx.comm, ctx.w, ctx.meta = comm, (w_gu, w_d), (El, inter, H, len(w_gu.anchors) + len(w_d.anchors))
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        idx, dest_row, w32, y_pulled, seg_off, recv, gu, h = ctx.saved_tensors
+        idx, dest_row, w32, y_pulled, seg_off, recv, gu, h, cnt = ctx.saved_tensors
         comm: EPComm = ctx.comm
         w_gu, w_d = ctx.w
         El, inter, H, n_anchor = ctx.meta
@@ -179,7 +187,7 @@ class _EPMoE(torch.autograd.Function):
         # the down-projection dgrad consumes the pushed output gradients as
         # they land (per-tile waits on the sources' flags); the weight
         # gradient runs after it in stream order, on complete data
-        dh = E.grouped_gemm_nn(dyr, Wd, seg_off, **comm.ep_wait_args(CH_DOUT, s3))
+        dh = E.grouped_gemm_nn(dyr, Wd, seg_off, **comm.ep_wait_args(CH_DOUT, s3, cnt))
         if w_d.requires_grad:
             E.grouped_gemm_tn_acc(dyr, h, _grad_view(w_d, (El, H, inter)), seg_off)
         dgu = E.swiglu_bwd(dh, gu)
