@@ -1,6 +1,7 @@
 """Roofline benchmark of the peer-memory data-parallel kernels against NCCL.
 
     torchrun --nproc-per-node N -m nano_qwen_b200.utils.comm_bench [--numel 1.7e9]
+    torchrun --nproc-per-node N -m nano_qwen_b200.utils.comm_bench --path ep
 
 For a flat fp32 gradient of ``numel`` elements (default: the Qwen3-1.7B
 store) it times, with CUDA events and the max over ranks:
@@ -46,15 +47,70 @@ def _timed(fn, iters: int, warmup: int = 3) -> float:
     return float(t)
 
 
+def ep_layer(iters: int, world: int, rank: int) -> None:
+    """One expert-parallel MoE layer (BASELINE debug_moe shape: hidden 512, 64
+    experts, top-8, expert FFN 256, 8 x 2048 tokens per rank), forward +
+    backward, fused peer-memory path vs NCCL all-to-all.  Roofline: the slower
+    of the expert GEMM FLOPs at the measured sustained bf16 peak and the token
+    rows that must cross NVLink (dispatch + combine, and again in the
+    backward: 4 x N*k*(W-1)/W rows of H bf16 per rank) at the link bandwidth."""
+    from ..config import ModelConfig
+    from ..models.moe import MoELayer
+    from ..parallel.expert_parallel import apply_expert_parallel
+    from ..training.optimizer import attach_param_store
+    from .flops import measured_peaks
+    cfg = ModelConfig(hidden_size=512, num_hidden_layers=1, num_attention_heads=8, num_key_value_heads=2,
+                      head_dim=64, intermediate_size=1408, vocab_size=32000, num_experts=64,
+                      num_experts_per_tok=8, moe_intermediate_size=256)
+    N, H, K, I = 8 * 2048, 512, 8, 256
+    grp = dist.new_group(list(range(world)))
+    g = torch.Generator(device="cuda").manual_seed(3 + rank)
+    x = torch.randn(N, H, device="cuda", generator=g).bfloat16()
+    dy = torch.randn(N, H, device="cuda", generator=g).bfloat16()
+    peak = measured_peaks().get("bf16_tflops_sustained", 1392.0) * 1e12
+    flops = 3 * 2.0 * N * K * H * 2 * I + 3 * 2.0 * N * K * I * H  # gate|up and down, fwd + 2x bwd
+    link = 4 * N * K * (world - 1) / world * H * 2
+    for fused in (True, False):
+        torch.manual_seed(0)
+
+        class Wrap(torch.nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.moe = MoELayer(cfg)
+
+        m = Wrap().cuda()
+        apply_expert_parallel(m, grp, fused=fused)
+        attach_param_store(m)
+        xr = x.clone().requires_grad_(True)
+
+        def step():
+            out, aux = m.moe(xr)
+            out.backward(dy)
+
+        t = _timed(step, iters)
+        if rank == 0:
+            t_roof = max(flops / peak, link / (LINK_GBS * 1e9))
+            print(json.dumps({"path": "ep moe layer fwd+bwd (" + ("fused peer-memory" if fused else "nccl") + ")",
+                              "n_gpus": world, "tokens_per_rank": N, "ms": round(t * 1e3, 3),
+                              "roofline_ms": round(t_roof * 1e3, 3), "frac_of_roofline": round(t_roof / t, 3)}),
+                  flush=True)
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--numel", type=float, default=1.72e9)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--path", default="dp", choices=["dp", "ep"])
     a = ap.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     world, rank = dist.get_world_size(), dist.get_rank()
+    if a.path == "ep":
+        ep_layer(a.iters, world, rank)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     from ..ops._ext import ext
     from ..parallel.data_parallel import shard_bounds
     from ..parallel.peer_dp import SymmetricAllocator
