@@ -111,6 +111,16 @@ class PreTrainer:
         from ..utils.tracing import step_profiler_from_config
         self.step_profiler = step_profiler_from_config(training_config.get("profiling"),
                                                        rank=self.rank)
+        # optional failure detection between steps (training YAML ``fault``:
+        # ``step_gate_timeout_s``): every rank announces each step in the c10d
+        # store and a rank that left is named before the next collective
+        self.step_gate = None
+        gate_s = (training_config.get("fault", {}) or {}).get("step_gate_timeout_s")
+        if gate_s and self.world_size > 1:
+            import torch.distributed as dist
+            from ..utils.fault import HeartbeatMonitor
+            self.step_gate = HeartbeatMonitor(dist.distributed_c10d._get_default_store(), self.rank,
+                                              self.world_size, timeout_s=float(gate_s), prefix="nq_gate")
 
     def train(self, dataloader, total_steps: int, start_step: int = 0, sampler=None):
         step = start_step
@@ -133,6 +143,8 @@ class PreTrainer:
             if cuda:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
+            if self.step_gate is not None:
+                self.step_gate.gate(step)
             t0 = time.perf_counter()
             if self.step_profiler is not None:
                 with self.step_profiler.step(step):

@@ -90,6 +90,13 @@ class HeartbeatMonitor:
         their next collective or peer-memory wait."""
         if not self.silent:
             self.store.set(f"{self.prefix}/step/{step}/{self.rank}", "1")
+            # every peer passed its gate of step - 2 before announcing step - 1,
+            # which this rank saw at its previous gate: that key is no longer read
+            if step >= 2:
+                try:
+                    self.store.delete_key(f"{self.prefix}/step/{step - 2}/{self.rank}")
+                except Exception:
+                    pass
         peers = [r for r in range(self.world) if r != self.rank]
         keys = [f"{self.prefix}/step/{step}/{r}" for r in peers]
         try:
