@@ -9,6 +9,7 @@ train.py:36-146), so existing launch scripts work unchanged:
     python train.py grpo --model-config configs/model/debug.yaml
     python train.py dpo --model-config configs/model/debug.yaml
     python train.py eval --model-config configs/model/debug.yaml --checkpoint ckpt/checkpoint.pt
+    python train.py --nproc 8 pretrain --model-config configs/model/small.yaml   # one process per GPU
 
 Differences: ``--stage`` reaches the pretrainer (stage 3 enables YARN
 long-context scaling; the reference dropped the flag), ``--max-steps`` caps a
@@ -82,7 +83,34 @@ def load_model_for_eval(model_config: str, checkpoint: str):
     return model
 
 
+def relaunch_argv(argv: List[str]) -> Optional[List[str]]:
+    """``--nproc N`` (N > 1) before the sub-command: the command line that
+    runs the same sub-command with one process per GPU through
+    ``torch.distributed.run`` on this node (what the reference's
+    scripts/*.sh wrappers did with torchrun).  None when no relaunch is
+    needed (single process, or already inside a distributed launch)."""
+    if "--nproc" not in argv:
+        return None
+    i = argv.index("--nproc")
+    n = int(argv[i + 1])
+    rest = argv[:i] + argv[i + 2:]
+    if n <= 1 or "LOCAL_RANK" in __import__("os").environ:
+        return None
+    import os
+    script = os.path.abspath(sys.argv[0]) if sys.argv and sys.argv[0].endswith(".py") else "train.py"
+    return [sys.executable, "-m", "torch.distributed.run", "--standalone", "--nnodes=1",
+            f"--nproc-per-node={n}", "--local-addr", "127.0.0.1", script] + rest
+
+
 def main(argv: Optional[List[str]] = None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    cmd = relaunch_argv(argv)
+    if cmd is not None:
+        import subprocess
+        return subprocess.call(cmd)
+    if "--nproc" in argv:  # a single process, or already launched per GPU
+        i = argv.index("--nproc")
+        argv = argv[:i] + argv[i + 2:]
     args = build_parser().parse_args(argv)
     if args.command != "eval" and args.training_config is None:
         args.training_config = DEFAULT_TRAINING_CONFIGS[args.command]

@@ -167,3 +167,21 @@ def test_replay_step_is_bitwise_on_cpu():
     eng.train_step([{"input_ids": ids, "labels": ids}])
     r = replay_step(eng, [{"input_ids": ids, "labels": ids}])
     assert r["loss_equal"] and not r["differs"], r
+
+
+def test_cli_nproc_relaunch_command():
+    """``--nproc N`` turns the command into a one-process-per-GPU launch on
+    this node (the reference's torchrun shell wrappers)."""
+    import os
+    from nano_qwen_b200.cli import relaunch_argv
+    assert relaunch_argv(["pretrain", "--model-config", "m.yaml"]) is None
+    assert relaunch_argv(["--nproc", "1", "pretrain", "--model-config", "m.yaml"]) is None
+    cmd = relaunch_argv(["--nproc", "4", "sft", "--model-config", "m.yaml", "--variant", "fusion"])
+    assert cmd[1:4] == ["-m", "torch.distributed.run", "--standalone"]
+    assert "--nproc-per-node=4" in cmd and "127.0.0.1" in cmd
+    assert cmd[-5:] == ["sft", "--model-config", "m.yaml", "--variant", "fusion"]
+    os.environ["LOCAL_RANK"] = "0"
+    try:
+        assert relaunch_argv(["--nproc", "4", "pretrain"]) is None
+    finally:
+        del os.environ["LOCAL_RANK"]
