@@ -4,6 +4,7 @@
 // grouped GEMMs need lives in device memory (offsets), and the permuted buffer
 // has the static capacity N*k + E*pad.
 #include "common.cuh"
+#include "sm100.cuh"
 #include "tmap.h"
 
 namespace nq {
@@ -15,7 +16,7 @@ constexpr int kMaxK = 16;
 template <typename TL>
 __global__ void router_fwd_kernel(const TL* __restrict__ logits, int N, int E, int K, int norm,
                                   float* __restrict__ w_out, int* __restrict__ idx_out,
-                                  float* __restrict__ counts, float* __restrict__ psum) {
+                                  float* __restrict__ counts, float* __restrict__ psum, int* err) {
   __shared__ float s_cnt[kMaxE], s_psum[kMaxE];
   for (int e = threadIdx.x; e < E; e += blockDim.x) { s_cnt[e] = 0.f; s_psum[e] = 0.f; }
   __syncthreads();
@@ -40,11 +41,20 @@ __global__ void router_fwd_kernel(const TL* __restrict__ logits, int N, int E, i
     }
     sum = warp_sum(sum);
     const float inv = 1.f / sum;
+    // A non-finite logit makes the row's probabilities NaN; the top-k below
+    // must still pick K distinct experts in [0, E), so such a row routes on
+    // zero probabilities (lowest expert ids) and the error word records it.
+    bool bad = false;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       p[i] *= inv;
+      if (!(p[i] >= 0.f)) {  // NaN
+        bad |= (lane + 32 * i < E);
+        p[i] = 0.f;
+      }
       if (lane + 32 * i < E) atomicAdd(&s_psum[lane + 32 * i], p[i]);
     }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicCAS(err, 0, kErrBadArg);
     // top-k by repeated warp argmax (ties -> lower expert id)
     float selv[kMaxK];
     int seli[kMaxK];
@@ -66,13 +76,20 @@ __global__ void router_fwd_kernel(const TL* __restrict__ logits, int N, int E, i
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
       }
-      if ((bi & 31) == lane) taken[bi >> 5] = true;
+      if (bi >= E) {  // cannot happen with finite probabilities and K <= E
+        if (lane == 0) atomicCAS(err, 0, kErrBadArg);
+        bi = 0;
+        bv = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        if (lane + 32 * i == bi) taken[i] = true;
       selv[j] = bv;
       seli[j] = bi;
       selsum += bv;
     }
     if (lane == 0) {
-      const float rn = norm ? 1.f / selsum : 1.f;
+      const float rn = norm && selsum > 0.f ? 1.f / selsum : 1.f;
       for (int j = 0; j < K; ++j) {
         w_out[static_cast<int64_t>(t) * K + j] = selv[j] * rn;
         idx_out[static_cast<int64_t>(t) * K + j] = seli[j];
@@ -162,11 +179,11 @@ std::vector<torch::Tensor> router_fwd(torch::Tensor logits, int64_t K, bool norm
   if (logits.scalar_type() == torch::kBFloat16)
     router_fwd_kernel<__nv_bfloat16><<<warp_grid(N), 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), N, E, K, norm, w.data_ptr<float>(),
-        idx.data_ptr<int>(), counts.data_ptr<float>(), psum.data_ptr<float>());
+        idx.data_ptr<int>(), counts.data_ptr<float>(), psum.data_ptr<float>(), error_flag_ptr());
   else
     router_fwd_kernel<float><<<warp_grid(N), 256, 0, st>>>(
         logits.data_ptr<float>(), N, E, K, norm, w.data_ptr<float>(), idx.data_ptr<int>(),
-        counts.data_ptr<float>(), psum.data_ptr<float>());
+        counts.data_ptr<float>(), psum.data_ptr<float>(), error_flag_ptr());
   NQ_CHECK_CUDA(cudaGetLastError());
   return {w, idx, counts, psum};
 }

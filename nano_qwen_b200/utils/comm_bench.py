@@ -78,7 +78,11 @@ def ep_layer(iters: int, world: int, rank: int) -> None:
                 super().__init__()
                 self.moe = MoELayer(cfg)
 
-        m = Wrap().cuda()
+        m = Wrap()
+        with torch.no_grad():  # the module leaves its weights uninitialised; the model's init
+            for p in m.parameters():
+                p.normal_(0.0, 0.02)
+        m = m.cuda()
         apply_expert_parallel(m, grp, fused=fused)
         attach_param_store(m)
         xr = x.clone().requires_grad_(True)

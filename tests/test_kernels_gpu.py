@@ -481,6 +481,29 @@ def test_adamw_flat_shard_state(E):
 
 
 # ------------------------------------------------------------------- MoE
+def test_router_nonfinite_logits_stay_in_range(E):
+    """A row with a non-finite logit still routes to K distinct experts in
+    [0, E) (no out-of-range index reaches the dispatch) and the error word
+    records kErrBadArg; finite rows are unaffected."""
+    torch.manual_seed(15)
+    N, Ex, k = 64, 64, 8
+    logits = torch.randn(N, Ex, device=DEV)
+    logits[3, 5] = float("nan")
+    logits[7, :] = float("inf")
+    E.error_flag_clear()
+    w, idx, counts, psum = E.router_fwd(logits.bfloat16(), k, True)
+    torch.cuda.synchronize()
+    assert E.error_flag_read() == 7
+    E.error_flag_clear()
+    assert int(idx.min()) >= 0 and int(idx.max()) < Ex
+    for r in range(N):
+        assert len(set(idx[r].tolist())) == k
+    assert int(counts.sum()) == N * k
+    ok = [r for r in range(N) if r not in (3, 7)]
+    ref_idx = torch.topk(torch.softmax(logits.bfloat16().float()[ok], -1), k, -1).indices
+    assert torch.equal(idx[ok].long().sort(-1).values, ref_idx.sort(-1).values)
+
+
 def test_router_and_plan(E):
     from nano_qwen_b200.ops import reference as R
     torch.manual_seed(13)
