@@ -40,7 +40,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 
 DP_LABEL = {"p2p": "ZeRO-2, fused peer-memory reduce-scatter + sharded AdamW + all-gather kernels",
             "shard": "ZeRO-2 over NCCL reduce-scatter / all-gather",
-            "replicate": "NCCL all-reduce"}
+            "replicate": "NCCL all-reduce",
+            "fsdp": "fully sharded: per-block bf16 all-gather / fp32 reduce-scatter over NCCL"}
 
 BASELINE_METRIC = "train tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; MFU"
 # the only measured reference number: its CPU fp32 debug step (BASELINE config #1)
@@ -111,8 +112,9 @@ def parse():
                    help="ours, dp p2p: reduce-scatter per block during the backward instead of after it")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="ours, tp/ep configs: peer-memory fused kernels or NCCL collectives")
-    p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate"],
-                   help="ours, N>1: peer-memory fused ZeRO step (p2p) or NCCL ZeRO-2 / all-reduce")
+    p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate", "fsdp"],
+                   help="ours, N>1: peer-memory fused ZeRO step (p2p), NCCL ZeRO-2 / all-reduce, "
+                        "or fully sharded parameters (fsdp)")
     p.add_argument("--device", default="cuda", choices=["cuda", "cpu"],
                    help="cpu: fp32 on the host, world size 1 (BASELINE config #1 with --config debug)")
     return p.parse_args()

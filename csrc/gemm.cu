@@ -88,6 +88,14 @@ struct GemmArgs {
 // shared-memory stores are free of bank conflicts.
 constexpr int kEpiWarpBytes = 6144;
 
+// Reduce-scatter destinations as tensor maps (one per owner rank): the
+// tensor-parallel epilogue writes each finished row tile into its owner's
+// partial buffer with TMA stores (64-byte row pieces) instead of 16-byte
+// register stores across NVLink.  Plain stores, no multicast.
+struct RsMaps {
+  CUtensorMap m[8];
+};
+
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr int kABytes = GBM * GBK * 2;
@@ -227,7 +235,7 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH,
-                const GemmArgs args) {
+                const __grid_constant__ RsMaps rsm, const GemmArgs args) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -443,7 +451,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m_limit = (args.group_mode == kGroupM) ? s_off[args.num_groups] : args.M;
       const bool row_ok = row < m_limit;
       const bool has_acc = ke > kb;
-      if (args.tma_epi) {
+      if (args.tma_epi && args.rs) {
+        // reduce-scatter: the tile's rows belong to one owner (tp_rows % 128 == 0)
+        const int owner = m0 / args.tp_rows;
+        epilogue_tma<BN, EPI>(smem + L::kEpiOff + quarter * kEpiWarpBytes,
+                              tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN,
+                              m0 - owner * args.tp_rows + quarter * 32, n0, args, &rsm.m[owner], &tmH,
+                              has_acc, lane, stg_half);
+      } else if (args.tma_epi) {
         epilogue_tma<BN, EPI>(smem + L::kEpiOff + quarter * kEpiWarpBytes,
                               tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN,
                               m0 + quarter * 32, n0, args, &tmC, &tmH, has_acc, lane, stg_half);
@@ -537,8 +552,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
-    // TMA stores complete before the CTA's shared memory goes away
-    if (args.tma_epi && lane == 0) bulk_wait_all();
+    // TMA stores complete before the CTA's shared memory goes away (and, for
+    // the reduce-scatter, before the grid's completion flag is published)
+    if (args.tma_epi && lane == 0) {
+      bulk_wait_all();
+      if (args.rs) asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
   }
 
   tc_fence_before();
@@ -746,7 +765,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) __cluster_dims__(2, 1, 1)
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                         int max_tiles, cudaStream_t stream, const CUtensorMap* tc = nullptr,
-                        const CUtensorMap* th = nullptr) {
+                        const CUtensorMap* th = nullptr, const RsMaps* rsm = nullptr) {
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kBytes <= 232448, "GEMM shared memory budget");
   auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
@@ -754,7 +773,10 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   int grid = std::min(num_sms(), std::max(1, max_tiles));
   CUtensorMap none;
   std::memset(&none, 0, sizeof(none));
-  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, tc ? *tc : none, th ? *th : none, a);
+  RsMaps no_rs;
+  std::memset(&no_rs, 0, sizeof(no_rs));
+  kern<<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, tc ? *tc : none, th ? *th : none,
+                                                  rsm ? *rsm : no_rs, a);
   NQ_CHECK_CUDA(cudaGetLastError());
 }
 
@@ -779,6 +801,14 @@ int64_t gemm_pair_mode(int64_t mode) {
   const int before = pair_enabled() ? 1 : 0;
   if (mode >= 0) g_pair_mode.store(mode ? 1 : 0, std::memory_order_relaxed);
   return before;
+}
+
+static bool rs_tma_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("NQ_RS_TMA");
+    return e != nullptr && std::string(e) == "1";
+  }();
+  return on;
 }
 
 static bool use_pair(int M, int N) {
@@ -1010,12 +1040,25 @@ int64_t gemm_rs(torch::Tensor A, torch::Tensor B, bool nn, std::vector<int64_t> 
   a.rs_target = static_cast<unsigned>(counter_before + grid);
   auto st = at::cuda::getCurrentCUDAStream();
   if (K == 0) TORCH_CHECK(false, "gemm_rs: K must be positive");
+  // With NQ_RS_TMA=1 each owner's plane [tp_rows, N] (ld N) becomes a TMA
+  // store destination (64-byte row pieces per request instead of 16-byte
+  // register stores); the register epilogue is the default.
+  RsMaps rsm;
+  std::memset(&rsm, 0, sizeof(rsm));
+  const RsMaps* rsp = nullptr;
+  if (rs_tma_enabled()) {
+    for (int r = 0; r < world; ++r)
+      rsm.m[r] = make_tmap_2d_bf16(reinterpret_cast<const void*>(rs_dst[r]), tp_rows, N, N, 32, 32,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    a.tma_epi = 1;
+    rsp = &rsm;
+  }
   if (nn) {
     auto tb = make_tmap_2d_bf16(B.data_ptr(), K, N, N, 64, 64);
-    launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, tiles, st);
+    launch_gemm<kBN, kStages, false, true, kEpiBF16>(ta, tb, a, tiles, st, nullptr, nullptr, rsp);
   } else {
     auto tb = make_tmap_2d_bf16(B.data_ptr(), N, K, K, 64, kBN);
-    launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, tiles, st);
+    launch_gemm<kBN, kStages, false, false, kEpiBF16>(ta, tb, a, tiles, st, nullptr, nullptr, rsp);
   }
   return grid;
 }

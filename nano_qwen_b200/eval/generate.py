@@ -17,6 +17,8 @@ enable_thinking, thinking_budget, stop_tokens, stream_callback)`` and
 
 from __future__ import annotations
 
+import contextlib
+
 from typing import Callable, List, Optional, Tuple
 
 import torch
@@ -143,6 +145,14 @@ class GraphedDecoder:
         return self.out
 
 
+def full_params(model):
+    """Context in which a fully sharded model's weights are all gathered and
+    kept (the decode step reads the layers' weights directly, and a captured
+    CUDA graph needs them at fixed addresses); a no-op otherwise."""
+    summon = getattr(getattr(model, "param_store", None), "summon_full_params", None)
+    return summon() if summon is not None else contextlib.nullcontext()
+
+
 class TextGenerator:
     def __init__(self, model, tokenizer, device: torch.device = torch.device("cpu"),
                  max_len: int = 4096, use_graph: Optional[bool] = None):
@@ -166,6 +176,13 @@ class TextGenerator:
                  enable_thinking: bool = False, thinking_budget: Optional[int] = None,
                  stop_tokens: Optional[List[int]] = None,
                  stream_callback: Optional[Callable[[str], None]] = None) -> str:
+        with full_params(self.model):
+            return self._generate(prompt, max_new_tokens, temperature, top_k, top_p,
+                                  repetition_penalty, enable_thinking, thinking_budget,
+                                  stop_tokens, stream_callback)
+
+    def _generate(self, prompt, max_new_tokens, temperature, top_k, top_p, repetition_penalty,
+                  enable_thinking, thinking_budget, stop_tokens, stream_callback) -> str:
         if enable_thinking:
             prompt = prompt + "<think>\n"
         ids = torch.tensor([self.tokenizer.encode(prompt, allowed_special="all")],
@@ -225,6 +242,12 @@ class TextGenerator:
         Returns (tokens [B, T], logprobs [B, T] under the sampling distribution,
         mask [B, T] of tokens before and including the first EOS).
         """
+        with full_params(self.model):
+            return self._sample_batch(prompt_ids, max_new_tokens, temperature, top_k, top_p,
+                                      eos_id, check_every)
+
+    def _sample_batch(self, prompt_ids, max_new_tokens, temperature, top_k, top_p, eos_id,
+                      check_every):
         B, P = prompt_ids.shape
         if P >= self.max_len:
             raise ValueError(f"prompt length {P} leaves no room below the {self.max_len}-position limit")

@@ -68,11 +68,17 @@ class TransformerBlock(nn.Module):
         self.feed_forward = MoELayer(config) if self._use_moe else build_ffn(config)
         # set by data parallelism to overlap gradient reduction with the backward
         self.grad_ready_hook = None
+        # set by fully sharded data parallelism: gathers this block's weights
+        # before it runs and releases them after (``parallel.fsdp.ParamUnit``)
+        self.param_unit = None
 
     def forward_fused(self, resid: torch.Tensor, delta: Optional[torch.Tensor],
                       position_ids=None, attention_mask=None, kv_cache=None, rope=None):
         """(resid, pending delta) -> (resid, new delta, aux).  resid is fp32."""
         eps = self.config.rms_norm_eps
+        unit = self.param_unit
+        if unit is not None:
+            resid, delta = unit.enter(resid, delta)
         if self.grad_ready_hook is not None and resid.requires_grad:
             # the gradient of the block input is produced after every weight
             # gradient of the block: the hook may start reducing them
@@ -86,6 +92,8 @@ class TransformerBlock(nn.Module):
                 f, aux = self.feed_forward(x)
             else:
                 f, aux = self.feed_forward(x), None
+        if unit is not None:
+            resid, f, aux = unit.leave(resid, f, aux)
         return resid, f, aux
 
     def forward(self, hidden_states, position_ids=None, attention_mask=None, kv_cache=None):
@@ -153,6 +161,9 @@ class Qwen3Model(nn.Module):
     def hidden(self, input_ids: torch.Tensor, position_ids=None, attention_mask=None,
                kv_caches: Optional[List[KVCache]] = None, inputs_embeds=None, rope=None):
         """Runs embed + blocks + final norm; returns (normed hidden [B,S,H], aux_total, n_moe)."""
+        gather = getattr(self, "param_gather", None)
+        if gather is not None:  # fully sharded: embedding / lm_head / norms gathered
+            gather()
         if self.sp_group is not None:
             # sequence parallel: this rank's slice only (embedding rows are looked
             # up for the local tokens, so their gradient is partial over TP)

@@ -9,8 +9,13 @@ def grad_buffer(p: torch.Tensor) -> torch.Tensor:
     """fp32 gradient buffer of a parameter, created (zeroed) on first use.
 
     Parameters placed in a ``FlatParamStore`` already carry a view into the
-    store's flat gradient buffer; kernels accumulate into it in place.
+    store's flat gradient buffer; kernels accumulate into it in place.  A
+    fully sharded store hands out the view of its gathered gradient buffer
+    (its parameters may be bf16 while their gradients are fp32).
     """
+    store = getattr(p, "_nq_store", None)
+    if store is not None and hasattr(store, "grad_of"):
+        return store.grad_of(p)
     if p.grad is None:
         p.grad = torch.zeros(p.shape, dtype=torch.float32, device=p.device)
     return p.grad

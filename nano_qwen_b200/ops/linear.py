@@ -26,18 +26,26 @@ class WeightRef:
 
     ``compute``: tensor used in the forward GEMM (bf16 on CUDA).
     ``grad``: fp32 [N, K] buffer the weight-gradient GEMM accumulates into, or
-    None when the rows belong to separate gradient tensors (``parts``).
+    None when the rows belong to separate gradient tensors (``parts``).  It
+    may be given as a zero-argument callable that returns the buffer, so a
+    slice of a gradient buffer that only exists during the backward (fully
+    sharded parameters) is taken when the backward needs it.
     ``anchors``: the leaf Parameters, passed through autograd so that outputs
     require grad; their autograd gradient is always None.
     """
 
-    __slots__ = ("compute", "grad", "anchors", "parts")
+    __slots__ = ("compute", "_grad", "anchors", "parts")
 
     def __init__(self, compute, grad, anchors, parts=None):
         self.compute = compute
-        self.grad = grad
+        self._grad = grad
         self.anchors = tuple(anchors)
         self.parts = parts
+
+    @property
+    def grad(self):
+        g = self._grad
+        return g() if callable(g) else g
 
     @property
     def requires_grad(self) -> bool:

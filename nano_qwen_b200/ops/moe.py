@@ -183,5 +183,7 @@ def _expert_ref(wref: WeightRef, stacked: torch.Tensor, e: int) -> WeightRef:
     anchors = wref.anchors[e * per:(e + 1) * per]
     grad = None
     if wref.grad is not None:
-        grad = wref.grad.view(stacked.shape)[e]
+        # sliced when the backward runs (the buffer may not be allocated yet)
+        def grad():
+            return wref.grad.view(stacked.shape)[e]
     return WeightRef(stacked[e], grad, anchors, parts=None if grad is not None else True)

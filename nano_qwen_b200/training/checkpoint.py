@@ -179,14 +179,29 @@ class CheckpointManager:
                 return {}
         d = Path(checkpoint_dir)
         shard = d / f"shard_{get_rank():05d}.pt"
+        # full-shape parameters / moments to load into while the file is read
+        # (a fully sharded store binds its parameters to full fp32 tensors)
+        full = getattr(optimizer, "gather_full_state", None)
         if shard.exists():
             st = torch.load(shard, map_location="cpu", weights_only=False)
-            model.load_state_dict(st["model"])
-            if optimizer is not None and "optimizer" in st:
-                optimizer.load_state_dict(st["optimizer"])
+            if full is not None:
+                full()
+            try:
+                model.load_state_dict(st["model"])
+                if optimizer is not None and "optimizer" in st:
+                    optimizer.load_state_dict(st["optimizer"])
+            finally:
+                if full is not None:
+                    optimizer.release_full_state(scatter=True)
             out = {}
         elif (d / "checkpoint.pt").exists() and not (d / ".metadata").exists():
-            out = self._load_plain(d, model, optimizer, scheduler)
+            if full is not None:
+                full()
+            try:
+                out = self._load_plain(d, model, optimizer, scheduler)
+            finally:
+                if full is not None:
+                    optimizer.release_full_state(scatter=True)
         else:
             self._load_logical(d, model, optimizer)
             out = {}

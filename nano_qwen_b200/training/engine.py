@@ -72,7 +72,15 @@ class TrainEngine:
         world = get_world_size(dp_group)
         dist_cfg = training_config.get("distributed", {}) or {}
         if dp_mode is None:
-            dp_mode = "shard" if dist_cfg.get("fsdp_enabled", True) else "replicate"
+            if dist_cfg.get("shard_params", False):
+                dp_mode = "fsdp"
+            else:
+                dp_mode = "shard" if dist_cfg.get("fsdp_enabled", True) else "replicate"
+        opt = training_config.get("optimizer", {}) or {}
+        if dp_mode == "fsdp":
+            self._init_fsdp(dp_group, parallel, dist_cfg, opt)
+            self._init_tail(training_config, opt, dp_group, world)
+            return
         alloc = None
         if dp_mode == "p2p" and parallel is not None:
             dp_mode = "shard"
@@ -97,17 +105,35 @@ class TrainEngine:
                                     expert_group=expert_group) if world > 1 else None)
         if self.dp is not None:
             self.dp.broadcast_params(0)
-        self._dups = self._duplicated_params()
-        moe_cfg = training_config.get("moe", {}) or {}
-        if world > 1 and moe_cfg.get("global_batch_balance", True):
-            set_global_batch_balance(self.model, dp_group)
-        opt = training_config.get("optimizer", {}) or {}
         self.optimizer = build_optimizer(
             self.model, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),
             beta1=opt.get("beta1", 0.9), beta2=opt.get("beta2", 0.95), eps=opt.get("eps", 1e-8),
             fused=True, store=self.store, shard=self.dp.shard if self.dp is not None else None)
         if self.dp is not None and hasattr(self.optimizer, "state_gather"):
             self.optimizer.state_gather = self.dp.gather_flat_
+        self._init_tail(training_config, opt, dp_group, world)
+
+    def _init_fsdp(self, dp_group, parallel, dist_cfg: dict, opt: dict) -> None:
+        """Fully sharded data parallelism (``distributed.shard_params``):
+        weights, gradients and Adam moments sharded, block weights gathered
+        per use (``parallel.fsdp``)."""
+        from ..parallel.fsdp import FullyShardedStore, build_fsdp_optimizer
+        if parallel is not None and any(int(getattr(parallel.config, k, 1)) > 1
+                                        for k in ("tp_size", "pp_size", "ep_size", "cp_size")):
+            raise ValueError("shard_params runs over plain data parallelism (tp/pp/ep/cp = 1)")
+        self.store = FullyShardedStore(self.model, group=dp_group,
+                                       reshard_after_forward=dist_cfg.get("reshard_after_forward",
+                                                                          True))
+        self.dp = self.store
+        self.optimizer = build_fsdp_optimizer(
+            self.store, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),
+            beta1=opt.get("beta1", 0.9), beta2=opt.get("beta2", 0.95), eps=opt.get("eps", 1e-8))
+
+    def _init_tail(self, training_config: dict, opt: dict, dp_group, world: int) -> None:
+        self._dups = self._duplicated_params()
+        moe_cfg = training_config.get("moe", {}) or {}
+        if world > 1 and moe_cfg.get("global_batch_balance", True):
+            set_global_batch_balance(self.model, dp_group)
         sch = training_config.get("scheduler", {}) or {}
         self.scheduler = build_scheduler(self.optimizer, scheduler_type=sch.get("type", "cosine"),
                                          warmup_steps=sch.get("warmup_steps", 2000),
@@ -153,6 +179,8 @@ class TrainEngine:
                     l, a = loss.detach(), None
                 else:
                     l, a = self.forward_backward(mb, 1.0 / n)
+                if hasattr(self.dp, "finish_backward"):
+                    self.dp.finish_backward()
                 loss_sum += l.float()
                 if a is not None:
                     aux_sum = a.float() if aux_sum is None else aux_sum + a.float()

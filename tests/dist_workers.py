@@ -489,3 +489,95 @@ def pp_checkpoint_worker(rank, world, port, tmp):
         assert torch.equal(p, full[n]), n
         assert torch.equal(e1.optimizer.state[p]["exp_avg"], e2.optimizer.state[full[n]]["exp_avg"]), n
     dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ FSDP
+def fsdp_worker(rank, world, port, moe, ckpt):
+    """Fully sharded data parallelism (parameters, gradients and moments
+    sharded; block weights gathered per use) against the ZeRO shard mode on
+    the same ranks and data (itself checked against single-process
+    accumulation), over three steps of two micro-batches, with and without
+    activation checkpointing."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.fsdp import _FREE
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg(moe, gradient_checkpointing=ckpt)
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_mode="shard")
+    fs = TrainEngine(build(cfg), dict(tcfg, distributed={"shard_params": True}), torch.device("cpu"))
+    st = fs.store
+    assert st.mode == "fsdp" and fs.dp is st
+    total = sum(p.numel() for p in fs.model.parameters())
+    # every per-rank buffer holds about 1/world of the parameters
+    assert st.master.numel() == fs.optimizer.exp_avg.numel() == st.grad.numel()
+    assert st.master.numel() <= total / world + 64 * len(st.units), (st.master.numel(), total)
+    for step in range(3):
+        ids = batch(cfg, 2 * world, 16, seed=100 + step)
+        mine = [{"input_ids": ids[2 * rank + i:2 * rank + i + 1],
+                 "labels": ids[2 * rank + i:2 * rank + i + 1]} for i in range(2)]
+        r = ref.train_step(mine)
+        f = fs.train_step(mine)
+        close(f["loss"], r["loss"], 1e-5, "loss")
+        close(f["grad_norm"], r["grad_norm"], 1e-4, "grad norm")
+        if moe:
+            close(f["aux_loss"], r["aux_loss"], 1e-5, "aux loss")
+        # block weights are released between steps
+        assert all(u.state == _FREE for u in st.block_units[:-1])
+        assert not any(u.grad_live for u in st.units)
+    ref.state_for_save()
+    fs.state_for_save()
+    for (n, p), (_, q) in zip(fs.model.named_parameters(), ref.model.named_parameters()):
+        assert p.dtype == torch.float32 and p.shape == q.shape, n
+        close(p, q, 1e-5, n)
+    fs.optimizer.release_full_state()
+    dist.destroy_process_group()
+
+
+def fsdp_checkpoint_worker(rank, world, port, tmp):
+    """A fully sharded run saves the single-process state (DCP): a fresh
+    fully sharded engine resumes it exactly, and a 1-rank engine loads the
+    same weights and moments."""
+    init(rank, world, port)
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg()
+    tc = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+          "scheduler": {"warmup_steps": 1, "total_steps": 20},
+          "distributed": {"shard_params": True}}
+
+    def engine(**kw):
+        return TrainEngine(build(cfg, seed=kw.pop("seed", 0)), tc, torch.device("cpu"), **kw)
+
+    a = engine()
+    data = [batch(cfg, 2, 16, seed=10 * s + rank) for s in range(4)]
+    for s in range(3):
+        a.train_step([{"input_ids": data[s], "labels": data[s]}])
+    mgr = CheckpointManager(save_dir=tmp, async_save=False)
+    d = mgr.save(3, *a.state_for_save())
+    p0 = next(iter(a.model.parameters()))
+    assert p0.dtype == torch.float32 and "exp_avg" not in a.optimizer.state[p0]  # released
+    b = engine(seed=3)
+    mgr.load(b.model, b.optimizer, b.scheduler, checkpoint_dir=str(d))
+    assert b.optimizer.step_count == a.optimizer.step_count
+    assert torch.equal(b.store.master, a.store.master)
+    assert torch.equal(b.optimizer.exp_avg, a.optimizer.exp_avg)
+    assert torch.equal(b.optimizer.exp_avg_sq, a.optimizer.exp_avg_sq)
+    ra = a.train_step([{"input_ids": data[3], "labels": data[3]}])
+    rb = b.train_step([{"input_ids": data[3], "labels": data[3]}])
+    assert torch.equal(ra["loss"], rb["loss"]), (ra["loss"], rb["loss"])
+    # the 1-rank (unsharded) layout reads the same checkpoint
+    singles = [dist.new_group([r]) for r in range(world)]
+    c = TrainEngine(build(cfg, seed=9), dict(tc, distributed={}), torch.device("cpu"),
+                    dp_group=singles[rank])
+    mgr.load(c.model, c.optimizer, c.scheduler, checkpoint_dir=str(d))
+    a2 = engine(seed=4)
+    mgr.load(a2.model, a2.optimizer, a2.scheduler, checkpoint_dir=str(d))
+    a2.state_for_save()
+    full = dict(c.model.named_parameters())
+    for n, p in a2.model.named_parameters():
+        assert torch.equal(p, full[n]), n
+        assert torch.equal(a2.optimizer.state[p]["exp_avg"], c.optimizer.state[full[n]]["exp_avg"]), n
+    a2.optimizer.release_full_state()
+    dist.barrier()
+    dist.destroy_process_group()

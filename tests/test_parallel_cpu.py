@@ -76,3 +76,12 @@ def test_zero_shard_checkpoint_resumes_exactly(tmp_path):
 
 def test_pipeline_parallel_checkpoint_loads_single_layout(tmp_path):
     _run(W.pp_checkpoint_worker, 2, str(tmp_path))
+
+
+@pytest.mark.parametrize("moe,ckpt", [(False, False), (False, True), (True, False)])
+def test_fully_sharded_matches_zero(moe, ckpt):
+    _run(W.fsdp_worker, 2, moe, ckpt)
+
+
+def test_fully_sharded_checkpoint_resumes_and_reshards(tmp_path):
+    _run(W.fsdp_checkpoint_worker, 2, str(tmp_path))
