@@ -115,6 +115,8 @@ def parse():
     p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate", "fsdp"],
                    help="ours, N>1: peer-memory fused ZeRO step (p2p), NCCL ZeRO-2 / all-reduce, "
                         "or fully sharded parameters (fsdp)")
+    p.add_argument("--cp-mode", default="allgather", choices=["allgather", "ring"],
+                   help="ours, cp configs: gathered k|v (peer-memory kernels) or the k|v ring")
     p.add_argument("--device", default="cuda", choices=["cuda", "cpu"],
                    help="cpu: fp32 on the host, world size 1 (BASELINE config #1 with --config debug)")
     return p.parse_args()
@@ -312,6 +314,7 @@ def run_ours(args, world, rank, local):
         pm = ParallelismManager(ParallelConfig(tp_size=world if par == "tp" else 1,
                                                ep_size=world if par == "ep" else 1,
                                                cp_size=world if par == "cp" else 1,
+                                               cp_mode=args.cp_mode,
                                                tp_fused=fused, ep_fused=fused))
         model = pm.apply_parallelism(model)
     eng = TrainEngine(model, tcfg, dev, dp_mode=args.dp_mode if world > 1 else None, parallel=pm)
@@ -342,6 +345,8 @@ def run_ours(args, world, rank, local):
     if par == "ep" and world > 1:
         eps = [m.ep for m in eng.model.modules() if getattr(m, "ep", None) is not None]
         mode = "ep-fused" if eps and all(e.fused for e in eps) else "ep-nccl"
+    if par == "cp" and world > 1:
+        mode = "cp-" + args.cp_mode
     return ms, clocks, {"kernel_error_flag": err, "gpu_launches_per_step": launches,
                         "dp_mode": mode}, e2e
 
@@ -535,6 +540,8 @@ def parallel_label(par, world, impl, mode):
         return f"tp{world}+sp (" + ("all-gather / reduce-scatter fused into the norm and GEMM kernels over peer memory"
                                     if mode == "tp-fused" else "NCCL collectives") + ")"
     if par == "cp":
+        if mode == "cp-ring":
+            return f"cp{world} (zigzag; k|v ring over NCCL send/recv, flash kernels per chunk pair)"
         return f"cp{world} (zigzag; K/V exchange by P2P stores consumed by the attention kernels)"
     if par == "ep":
         return f"ep{world} x dp{world} (" + ("dispatch/combine kernels over peer memory" if mode == "ep-fused"

@@ -93,6 +93,11 @@ class Attention(nn.Module):
         """Context-parallel attention: local queries against the group's keys
         (``parallel.context_parallel.cp_attention``); positions are global."""
         from ..parallel.context_parallel import cp_attention, cp_attention_kernel, kernel_usable
+        if getattr(self, "cp_mode", "allgather") == "ring":
+            # k|v blocks passed around the ring: two blocks per rank in memory
+            from ..parallel.ring_attention import ring_attention_qkv
+            pos = position_ids.expand(B, S)
+            return ring_attention_qkv(qkv, qw, kw, cos, sin, pos, group, Hq, Hk, D, eps)
         if qkv.is_cuda and kernel_usable(S):
             pos = position_ids.expand(B, S).to(torch.int64)
             return cp_attention_kernel(qkv, qw, kw, cos, sin, pos, group, Hq, Hk, D, eps,

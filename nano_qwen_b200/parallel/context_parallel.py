@@ -261,14 +261,22 @@ def kernel_usable(S_local: int) -> bool:
     return torch.cuda.is_available() and S_local % 512 == 0
 
 
-def apply_context_parallel(model: nn.Module, cp_group, cp_ranks=None) -> nn.Module:
-    """Mark a Qwen3Model (or the LM of a VL model) for context parallelism."""
+def apply_context_parallel(model: nn.Module, cp_group, cp_ranks=None,
+                           mode: str = "allgather") -> nn.Module:
+    """Mark a Qwen3Model (or the LM of a VL model) for context parallelism.
+    ``mode``: "allgather" (every rank gathers the group's k|v: one exchange
+    per layer, peer-memory kernels on GPUs) or "ring" (k|v blocks passed
+    around the group, ``parallel.ring_attention``: two blocks per rank in
+    memory, for sequences whose gathered k|v would not fit)."""
     from ..models.attention import Attention
+    if mode not in ("allgather", "ring"):
+        raise ValueError(f"cp mode {mode!r}: allgather or ring")
     lm = getattr(model, "language_model", model)
     lm.cp_group = cp_group
     for m in lm.modules():
         if isinstance(m, Attention):
             m.cp_group = cp_group
+            m.cp_mode = mode
     return model
 
 

@@ -34,6 +34,8 @@ class ParallelConfig:
     pp_size: int = 1
     ep_size: int = 1
     cp_size: int = 1
+    # context-parallel attention: "allgather" (gathered k|v) or "ring"
+    cp_mode: str = "allgather"
     fsdp_enabled: bool = True
     dtype: str = "bfloat16"
     reshard_after_forward: bool = True
@@ -151,7 +153,7 @@ class ParallelismManager:
             apply_expert_parallel(model, self.groups["ep"], fused=c.ep_fused)
         if c.cp_size > 1:
             from .context_parallel import apply_context_parallel
-            apply_context_parallel(model, self.groups["cp"], self.ranks["cp"])
+            apply_context_parallel(model, self.groups["cp"], self.ranks["cp"], mode=c.cp_mode)
         if c.pp_size > 1:
             from .pipeline_parallel import apply_pipeline_parallel
             model = apply_pipeline_parallel(model, self.groups["pp"], self.ranks["pp"],

@@ -64,7 +64,8 @@ def build_parallel(training_config: dict, world_size: int):
     pc = ParallelConfig(dp_size=int(d.get("dp_size", -1) or -1), **sizes,
                         fsdp_enabled=bool(d.get("fsdp_enabled", True)),
                         sequence_parallel=bool(d.get("sequence_parallel", True)),
-                        pp_microbatches=int(d.get("pp_microbatches", 4)))
+                        pp_microbatches=int(d.get("pp_microbatches", 4)),
+                        cp_mode=str(d.get("cp_mode", "allgather")))
     return ParallelismManager(pc)
 
 

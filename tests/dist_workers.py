@@ -154,7 +154,7 @@ def ep_worker(rank, world, port):
 
 
 # ------------------------------------------------------------------ CP
-def cp_worker(rank, world, port, moe):
+def cp_worker(rank, world, port, moe, mode="allgather"):
     init(rank, world, port)
     from nano_qwen_b200.parallel.context_parallel import apply_context_parallel
     from nano_qwen_b200.parallel.data_parallel import DataParallel
@@ -165,7 +165,7 @@ def cp_worker(rank, world, port, moe):
     ref, ref_loss, ref_g = _full_grads(cfg, ids)
     m = build(cfg)
     grp = dist.new_group(list(range(world)))
-    apply_context_parallel(m, grp)
+    apply_context_parallel(m, grp, mode=mode)
     store = attach_param_store(m, torch.float32, torch.device("cpu"))
     dp = DataParallel(store, mode="replicate", group=grp)
     out = m(ids, labels=ids)

@@ -230,9 +230,10 @@ def ep_fused_worker(rank, world, port):
     dist.destroy_process_group()
 
 
-def cp_kernel_worker(rank, world, port):
+def cp_kernel_worker(rank, world, port, mode="allgather"):
     """Context parallelism on the attention kernels (zigzag over the ranks) against
-    the single-GPU model on the full sequence: loss and gradients."""
+    the single-GPU model on the full sequence: loss and gradients.  ``mode``:
+    gathered k|v (peer-memory kernels) or the k|v ring."""
     init(rank, world, port)
     from nano_qwen_b200.models import Qwen3Model
     from nano_qwen_b200.ops import ext
@@ -254,7 +255,7 @@ def cp_kernel_worker(rank, world, port):
                 if p.ndim >= 2:
                     p.normal_(0.0, 0.05)
         if cp:
-            apply_context_parallel(m, grp)
+            apply_context_parallel(m, grp, mode=mode)
         attach_param_store(m)
         return m
 

@@ -55,6 +55,13 @@ def test_context_parallel_kernels_match_single_gpu(world):
 
 
 @pytest.mark.parametrize("world", [2, 4])
+def test_ring_context_parallel_matches_single_gpu(world):
+    _need(world)
+    import multi_gpu_workers as W
+    mp.spawn(W.cp_kernel_worker, args=(world, _port(), "ring"), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 4])
 def test_rank_leaving_between_steps_is_detected(world):
     _need(world)
     import multi_gpu_workers as W

@@ -41,6 +41,13 @@ def test_context_parallel_matches_single(moe):
     _run(W.cp_worker, 2, moe)
 
 
+@pytest.mark.parametrize("world,moe", [(2, False), (4, False), (2, True)])
+def test_ring_context_parallel_matches_single(world, moe):
+    """k|v blocks passed around the ring (two blocks per rank in memory)
+    give the single-process loss, logits and every gradient."""
+    _run(W.cp_worker, world, moe, "ring")
+
+
 @pytest.mark.parametrize("tied,micro", [(False, 2), (True, 4)])
 def test_pipeline_parallel_matches_accumulation(tied, micro):
     _run(W.pp_worker, 2, tied, micro)
