@@ -283,6 +283,40 @@ def cp_kernel_worker(rank, world, port, mode="allgather"):
     dist.destroy_process_group()
 
 
+def fsdp_worker(rank, world, port):
+    """Fully sharded parameters over NCCL (per-block bf16 all-gathers with
+    prefetch, fp32 reduce-scatters on a side stream) against the NCCL ZeRO-2
+    step on the same ranks and data: losses, norms and final weights."""
+    init(rank, world, port)
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.parallel.fsdp import _FREE
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 4096, (4 * world, 128), generator=g).cuda()
+    mine = [{"input_ids": ids[4 * rank + i:4 * rank + i + 2],
+             "labels": ids[4 * rank + i:4 * rank + i + 2]} for i in (0, 2)]
+    zero = _engine("shard", None)
+    fs = _engine("fsdp", None)
+    assert fs.store.mode == "fsdp" and fs.store.nccl
+    total = sum(p.numel() for p in zero.model.parameters())
+    assert fs.store.master.numel() < total // world + 64 * len(fs.store.units)
+    for _ in range(3):
+        a = zero.train_step(mine)
+        b = fs.train_step(mine)
+        assert abs(float(a["loss"]) - float(b["loss"])) < 1e-4 * abs(float(a["loss"])), (a, b)
+        assert abs(float(a["grad_norm"]) - float(b["grad_norm"])) < 1e-3 * float(a["grad_norm"])
+        assert all(u.state == _FREE for u in fs.store.block_units[:-1])
+    torch.cuda.synchronize()
+    assert ext().error_flag_read() == 0, "kernel error word set"
+    zero.state_for_save()
+    fs.state_for_save()
+    for (n, p), q in zip(zero.model.named_parameters(), fs.model.parameters()):
+        err = ((p - q).norm() / (p.norm() + 1e-12)).item()
+        assert err < 1e-3, (n, err)
+    fs.optimizer.release_full_state()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def rank_leave_worker(rank, world, port):
     """One process per GPU trains with NCCL data parallelism; the last rank
     leaves between steps (synchronised, then exits without a word).  The
