@@ -617,7 +617,15 @@ class FSDPAdamW(FusedAdamW):
             self.state[p] = {"step": torch.zeros((), dtype=torch.float32)}
 
     @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float, norm_sq_reduce=None) -> torch.Tensor:
+        self.store.finish_backward()
+        return super().clip_grad_norm_(max_norm, norm_sq_reduce or self.store.norm_sq_reduce)
+
+    @torch.no_grad()
     def step(self, closure=None, update=None):
+        # gradients still in full buffers (a loop without the training
+        # engine's per-micro-batch hook) are reduced into the shards first
+        self.store.finish_backward()
         out = super().step(closure, update)
         self.store.after_step()
         return out
@@ -656,3 +664,49 @@ class FSDPAdamW(FusedAdamW):
 def build_fsdp_optimizer(store: FullyShardedStore, lr: float = 3e-4, weight_decay: float = 0.1,
                          beta1: float = 0.9, beta2: float = 0.95, eps: float = 1e-8):
     return FSDPAdamW(store, lr=lr, betas=(beta1, beta2), eps=eps, weight_decay=weight_decay)
+
+
+# ---------------------------------------------------------------- reference API
+class MixedPrecisionPolicy:
+    """Gathered-parameter dtype and gradient-reduction dtype (the fields of
+    FSDP2's policy; reference: distributed/fsdp.py:36-41)."""
+
+    def __init__(self, param_dtype: torch.dtype = torch.bfloat16,
+                 reduce_dtype: torch.dtype = torch.float32):
+        self.param_dtype = param_dtype
+        self.reduce_dtype = reduce_dtype
+
+
+def get_mixed_precision_policy(dtype: str = "bfloat16") -> MixedPrecisionPolicy:
+    return MixedPrecisionPolicy(param_dtype=getattr(torch, dtype, torch.bfloat16),
+                                reduce_dtype=torch.float32)
+
+
+def apply_fsdp2(model: nn.Module, mesh=None, mp_policy: Optional[MixedPrecisionPolicy] = None,
+                reshard_after_forward: bool = True) -> nn.Module:
+    """Shard ``model`` per transformer block plus a root unit (the call the
+    reference makes, reference: distributed/fsdp.py:44-75).  ``mesh``: a
+    process group, a 1-D ``DeviceMesh`` or None (the default group).  The
+    gathered weights use ``mp_policy.param_dtype`` on the GPU; gradients are
+    reduced in fp32.  ``build_optimizer(model)`` then returns ``FSDPAdamW``."""
+    group = mesh.get_group() if hasattr(mesh, "get_group") else mesh
+    dev = next(model.parameters()).device
+    dtype = None
+    if mp_policy is not None and dev.type == "cuda":
+        dtype = mp_policy.param_dtype
+    FullyShardedStore(model, group=group, compute_dtype=dtype,
+                      reshard_after_forward=reshard_after_forward)
+    return model
+
+
+def apply_fsdp1(model: nn.Module, dtype: str = "bfloat16", cpu_offload: bool = False,
+                sharding_strategy: str = "FULL_SHARD") -> nn.Module:
+    """The reference's FSDP1 fallback (reference: distributed/fsdp.py:78-101)
+    maps to the same sharding; CPU offload is not provided (180 GB of HBM per
+    GPU holds the shards of every configuration here)."""
+    if cpu_offload:
+        raise NotImplementedError("CPU offload of parameter shards")
+    if sharding_strategy not in ("FULL_SHARD", "SHARD_GRAD_OP"):
+        raise ValueError(f"sharding strategy {sharding_strategy!r}")
+    return apply_fsdp2(model, None, get_mixed_precision_policy(dtype),
+                       reshard_after_forward=sharding_strategy == "FULL_SHARD")

@@ -236,6 +236,9 @@ def build_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.
                     fused: bool = True, store: Optional[FlatParamStore] = None,
                     shard: Optional[Tuple[int, int]] = None) -> torch.optim.Optimizer:
     store = store or getattr(model, "param_store", None)
+    if store is not None and getattr(store, "mode", None) == "fsdp":
+        from ..parallel.fsdp import FSDPAdamW
+        return FSDPAdamW(store, lr=lr, betas=(beta1, beta2), eps=eps, weight_decay=weight_decay)
     if store is not None and fused:
         return FusedAdamW(store, lr=lr, betas=(beta1, beta2), eps=eps,
                           weight_decay=weight_decay, shard=shard)

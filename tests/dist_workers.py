@@ -534,6 +534,38 @@ def fsdp_worker(rank, world, port, moe, ckpt):
     dist.destroy_process_group()
 
 
+def fsdp_api_worker(rank, world, port):
+    """The reference's calls (``apply_fsdp2`` per block + root, then a plain
+    loop: forward, backward, clip, step) on the fully sharded store give the
+    ZeRO engine's losses and weights."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.fsdp import FSDPAdamW, apply_fsdp2, get_mixed_precision_policy
+    from nano_qwen_b200.training.engine import TrainEngine
+    from nano_qwen_b200.training.optimizer import build_optimizer
+    cfg = tiny_cfg()
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0, "weight_decay": 0.1},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_mode="shard")
+    model = apply_fsdp2(build(cfg), None, get_mixed_precision_policy("bfloat16"))
+    opt = build_optimizer(model, lr=1e-2, weight_decay=0.1)
+    assert isinstance(opt, FSDPAdamW)
+    for step in range(3):
+        ids = batch(cfg, 2 * world, 16, seed=200 + step)
+        mine = ids[2 * rank:2 * rank + 2]
+        lrs = [g["lr"] for g in ref.optimizer.param_groups]   # what the engine's step uses
+        r = ref.train_step([{"input_ids": mine, "labels": mine}])
+        loss = model(mine, labels=mine)["loss"]
+        loss.backward()
+        norm = opt.clip_grad_norm_(1.0)
+        for g, lr in zip(opt.param_groups, lrs):
+            g["lr"] = lr
+        opt.step()
+        opt.zero_grad()
+        close(loss.detach(), r["loss"], 1e-5, "loss")
+        close(norm, r["grad_norm"], 1e-4, "grad norm")
+    dist.destroy_process_group()
+
+
 def fsdp_checkpoint_worker(rank, world, port, tmp):
     """A fully sharded run saves the single-process state (DCP): a fresh
     fully sharded engine resumes it exactly, and a 1-rank engine loads the

@@ -92,3 +92,7 @@ def test_fully_sharded_matches_zero(moe, ckpt):
 
 def test_fully_sharded_checkpoint_resumes_and_reshards(tmp_path):
     _run(W.fsdp_checkpoint_worker, 2, str(tmp_path))
+
+
+def test_fully_sharded_reference_api_loop():
+    _run(W.fsdp_api_worker, 2)
