@@ -588,6 +588,10 @@ class FSDPAdamW(FusedAdamW):
     ``gather_full_state`` exposes full fp32 parameters and moments under
     the single-process names for a checkpoint save or load."""
 
+    # ``gather_full_state`` rebinds the parameters (checkpoint saves of this
+    # optimizer run synchronously)
+    full_state_rebinds_params = True
+
     def __init__(self, store: FullyShardedStore, lr: float = 3e-4, betas=(0.9, 0.95),
                  eps: float = 1e-8, weight_decay: float = 0.1):
         self.store = store

@@ -92,6 +92,11 @@ class CheckpointManager:
         self._release = getattr(optimizer, "release_full_state", None)
         if self._release is not None:
             optimizer.gather_full_state()
+        # a fully sharded optimizer points the parameters themselves at the
+        # gathered tensors while they are saved, so its saves complete before
+        # training resumes (no background write of tensors in use)
+        self._async_now = self.async_save and not getattr(optimizer, "full_state_rebinds_params",
+                                                          False)
         groups = None
         if optimizer is not None:
             groups = [{k: v for k, v in g.items() if k != "params" and isinstance(v, (int, float, list, tuple))}
@@ -131,7 +136,7 @@ class CheckpointManager:
         (the optimizer's hyper-parameters go to ``meta.json``)."""
         from .dcp_state import model_parallel_state
         sd = model_parallel_state(model, optimizer)
-        if self.async_save and torch.distributed.is_initialized():
+        if self._async_now and torch.distributed.is_initialized():
             self._pending = dcp.async_save(sd, checkpoint_id=str(d))
         else:
             dcp.save(sd, checkpoint_id=str(d))
@@ -140,7 +145,7 @@ class CheckpointManager:
         sd = {"model": get_model_state_dict(model)}
         if optimizer is not None:
             sd["optimizer"] = get_optimizer_state_dict(model, optimizer)
-        if self.async_save and torch.distributed.is_initialized():
+        if self._async_now and torch.distributed.is_initialized():
             self._pending = dcp.async_save(sd, checkpoint_id=str(d))
         else:
             dcp.save(sd, checkpoint_id=str(d))

@@ -585,8 +585,13 @@ def fsdp_checkpoint_worker(rank, world, port, tmp):
     data = [batch(cfg, 2, 16, seed=10 * s + rank) for s in range(4)]
     for s in range(3):
         a.train_step([{"input_ids": data[s], "labels": data[s]}])
-    mgr = CheckpointManager(save_dir=tmp, async_save=False)
+    mgr = CheckpointManager(save_dir=tmp, async_save=True)
     d = mgr.save(3, *a.state_for_save())
+    # the save completed in the call (the parameters were bound to the gathered
+    # tensors) and the parameters are views of the gathered units again
+    assert a.optimizer._full is None and mgr._pending is None
+    for p in a.model.parameters():
+        assert p.data_ptr() == a.store._pviews[id(p)].data_ptr()
     p0 = next(iter(a.model.parameters()))
     assert p0.dtype == torch.float32 and "exp_avg" not in a.optimizer.state[p0]  # released
     b = engine(seed=3)
