@@ -73,14 +73,25 @@ def _set_storage(t: torch.Tensor, numel: int) -> None:
 
 
 class ParamUnit:
-    """One flat buffer of parameters gathered and released together."""
+    """One flat buffer of parameters gathered and released together, sharded
+    over its own process group (the data-parallel group; for expert-parallel
+    experts the group of ranks that hold the same experts)."""
 
     def __init__(self, name: str, groups, dtype: torch.dtype, persistent: bool, decay: bool,
-                 world: int):
+                 group=None, grad_scale: float = 1.0, local: bool = False):
+        """``local``: not sharded (this rank alone holds these parameters)."""
         self.name = name
         self.dtype = dtype
         self.persistent = persistent
         self.decay = decay
+        self.group = group
+        self.world = 1 if local else get_world_size(group)
+        self.rank = 0 if local else get_rank(group)
+        self.distributed = is_dist() and self.world > 1
+        self.nccl = self.distributed and dist.get_backend(group) == "nccl"
+        # multiplies the mean over ``group`` of the gradient (experts: the
+        # data-parallel mean is the sum over the group / data-parallel world)
+        self.grad_scale = grad_scale
         self.params: List[nn.Parameter] = []
         self.names: List[str] = []
         self.local: Dict[int, int] = {}
@@ -95,9 +106,9 @@ class ParamUnit:
                 self.names.append(n)
                 off += p.numel()
         self.numel = off
-        chunk = ALIGN * world
+        chunk = ALIGN * self.world
         self.padded = max(chunk, (off + chunk - 1) // chunk * chunk)
-        self.per = self.padded // world
+        self.per = self.padded // self.world
         self.soff = 0      # offset of this rank's shard in the store's shard buffers
         self.voff = 0      # offset of the unit in the full (virtual) flat layout
         self.full: Optional[torch.Tensor] = None    # gathered weights, compute dtype
@@ -106,19 +117,41 @@ class ParamUnit:
         self.work = None
         self.stale = True
         self.grad_live = False
-        self.in_backward = False
-        self.prev: Optional["ParamUnit"] = None
-        self.next: Optional["ParamUnit"] = None
-        self.store: Optional["FullyShardedStore"] = None
 
-    # ------------------------------------------------------------ block hooks
+    def src(self) -> int:
+        """Global rank whose initial values every member starts from."""
+        return dist.get_global_rank(self.group, 0) if self.group is not None else 0
+
+
+class BlockUnits:
+    """The units of one transformer block (its dense matrices; under expert
+    parallelism also its local experts), gathered before the block and
+    released after it in the forward and again in the backward."""
+
+    def __init__(self, store: "FullyShardedStore", parts: List[ParamUnit]):
+        self.store = store
+        self.parts = parts
+        self.persistent = all(u.persistent for u in parts)
+        self.in_backward = False
+        self.prev: Optional["BlockUnits"] = None
+        self.next: Optional["BlockUnits"] = None
+
+    def _gather(self, wait: bool = True) -> None:
+        for u in self.parts:
+            self.store.gather(u, wait=wait)
+
+    def _release(self) -> None:
+        for u in self.parts:
+            if not u.persistent:
+                self.store.release(u)
+
     def enter(self, resid: torch.Tensor, delta: Optional[torch.Tensor]):
         """Block pre-forward: gather, prefetch the next block, and arm the
         post-backward hook on the block's inputs."""
         st = self.store
-        st.gather(self)
+        self._gather()
         if not self.in_backward and self.next is not None and not st.pinned:
-            st.gather(self.next, wait=False)
+            self.next._gather(wait=False)
         if torch.is_grad_enabled() and resid.requires_grad and not self.in_backward:
             if delta is not None and delta.requires_grad:
                 resid, delta = _Hook.apply(self._post_backward, resid, delta)
@@ -140,26 +173,26 @@ class ParamUnit:
                 resid, out = _Hook.apply(self._pre_backward, resid, out)
         # the last block's weights are needed again at once by the backward
         keep = self.next is None and torch.is_grad_enabled() and resid.requires_grad
-        if not self.in_backward and not self.persistent and not st.pinned and not keep:
-            st.release(self)
+        if not self.in_backward and not st.pinned and not keep:
+            self._release()
         return resid, out, aux
 
     def _pre_backward(self) -> None:
-        st = self.store
         self.in_backward = True
-        st.gather(self)
-        st.alloc_grad(self)
+        self._gather()
+        for u in self.parts:
+            self.store.alloc_grad(u)
         if self.prev is not None:
-            st.gather(self.prev, wait=False)
+            self.prev._gather(wait=False)
 
     def _post_backward(self) -> None:
-        st = self.store
         if not self.in_backward:
             return
         self.in_backward = False
-        st.reduce_grad(self)
-        if not self.persistent and not st.pinned:
-            st.release(self)
+        for u in self.parts:
+            self.store.reduce_grad(u)
+        if not self.store.pinned:
+            self._release()
 
 
 class _Hook(torch.autograd.Function):
@@ -187,7 +220,11 @@ class FullyShardedStore:
     mode = "fsdp"
 
     def __init__(self, model: nn.Module, group=None, compute_dtype: Optional[torch.dtype] = None,
-                 device: Optional[torch.device] = None, reshard_after_forward: bool = True):
+                 device: Optional[torch.device] = None, reshard_after_forward: bool = True,
+                 expert_group=None):
+        """``expert_group``: under expert parallelism, the ranks that hold the
+        same experts (one per expert-parallel block); each block's local
+        experts form a unit sharded over it."""
         from ..models.transformer import TransformerBlock
         self.model = model
         self.group = group
@@ -210,47 +247,66 @@ class FullyShardedStore:
             for p in blk.parameters():
                 owner.setdefault(id(p), bi)
         per_block: List[list] = [[] for _ in blocks]
+        per_block_experts: List[list] = [[] for _ in blocks]
         rest_decay, rest_nodecay, small = [], [], []
         for grp in groups:
             # a fusion group is homogeneous in rank and decay; split it if not
-            kinds = {(p.ndim <= 1, no_decay_rule(n, p)) for n, p in grp}
+            kinds = {(p.ndim <= 1, no_decay_rule(n, p), bool(getattr(p, "_ep_local", False)))
+                     for n, p in grp}
             parts = [grp] if len(kinds) == 1 else [[item] for item in grp]
             for part in parts:
                 n0, p0 = part[0]
+                expert = bool(getattr(p0, "_ep_local", False))
+                if expert and (p0.ndim <= 1 or no_decay_rule(n0, p0) or id(p0) not in owner):
+                    raise NotImplementedError(f"expert-parallel parameter {n0} outside the "
+                                              "blocks' expert matrices")
                 if p0.ndim <= 1:
                     small.append(part)
                 elif no_decay_rule(n0, p0):
                     rest_nodecay.append(part)
+                elif expert:
+                    per_block_experts[owner[id(p0)]].append(part)
                 elif id(p0) in owner:
                     per_block[owner[id(p0)]].append(part)
                 else:
                     rest_decay.append(part)
+        # the expert gradient's data-parallel mean: summed over the ranks
+        # holding the same experts, divided by the data-parallel world
+        # (no group: every expert set exists once, on this rank)
+        e_local = expert_group is None
+        e_scale = (1 if e_local else get_world_size(expert_group)) / max(1, self.world)
+        keep = not reshard_after_forward
         units: List[ParamUnit] = []
-        block_units: List[ParamUnit] = []
-        for bi, gs in enumerate(per_block):
-            if not gs:
+        self.blocks: List[BlockUnits] = []
+        for bi in range(len(blocks)):
+            parts = []
+            if per_block[bi]:
+                parts.append(ParamUnit(f"layers.{bi}", per_block[bi], compute_dtype, keep, True,
+                                       group))
+            if per_block_experts[bi]:
+                parts.append(ParamUnit(f"layers.{bi}.experts", per_block_experts[bi], compute_dtype,
+                                       keep, True, expert_group, grad_scale=e_scale,
+                                       local=e_local))
+            if not parts:
                 continue
-            u = ParamUnit(f"layers.{bi}", gs, compute_dtype, not reshard_after_forward, True,
-                          self.world)
-            blocks[bi].param_unit = u
-            units.append(u)
-            block_units.append(u)
-        for a, b in zip(block_units, block_units[1:]):
+            units += parts
+            sched = BlockUnits(self, parts)
+            blocks[bi].param_unit = sched
+            self.blocks.append(sched)
+        for a, b in zip(self.blocks, self.blocks[1:]):
             a.next, b.prev = b, a
+        self.block_units = [u for b in self.blocks for u in b.parts]
         if rest_decay:
-            units.append(ParamUnit("root_decay", rest_decay, compute_dtype, True, True, self.world))
+            units.append(ParamUnit("root_decay", rest_decay, compute_dtype, True, True, group))
         if rest_nodecay:
-            units.append(ParamUnit("root_nodecay", rest_nodecay, compute_dtype, True, False,
-                                   self.world))
+            units.append(ParamUnit("root_nodecay", rest_nodecay, compute_dtype, True, False, group))
         if small:
-            units.append(ParamUnit("fp32_1d", small, torch.float32, True, False, self.world))
+            units.append(ParamUnit("fp32_1d", small, torch.float32, True, False, group))
         self.units = units
-        self.block_units = block_units
 
         soff = voff = 0
         self.decay_end = 0
         for u in units:
-            u.store = self
             u.soff, u.voff = soff, voff
             soff += u.per
             voff += u.padded
@@ -272,7 +328,8 @@ class FullyShardedStore:
         self._pviews: Dict[int, torch.Tensor] = {}
         self._gviews: Dict[int, torch.Tensor] = {}
         self._fviews: Dict[tuple, Tuple[torch.Tensor, torch.Tensor]] = {}
-        self._rs_stream = torch.cuda.Stream(device=dev) if self.nccl else None
+        self._rs_stream = (torch.cuda.Stream(device=dev)
+                           if any(u.nccl for u in units) else None)
         with torch.no_grad():
             for u in units:
                 self._init_unit(u)
@@ -284,9 +341,6 @@ class FullyShardedStore:
         self._hook = model.register_forward_pre_hook(lambda m, a: self.gather_root())
 
     # ------------------------------------------------------------ set-up
-    def _src(self) -> int:
-        return dist.get_global_rank(self.group, 0) if self.group is not None else 0
-
     def _init_unit(self, u: ParamUnit) -> None:
         """Shard the unit's initial values (rank 0's, broadcast), build the
         gathered / gradient buffers and every view of them, then release
@@ -296,9 +350,9 @@ class FullyShardedStore:
         for p in u.params:
             o = u.local[id(p)]
             tmp[o:o + p.numel()].copy_(p.detach().reshape(-1).to(dev, torch.float32))
-        if self.distributed:
-            dist.broadcast(tmp, src=self._src(), group=self.group)
-        mine = tmp[self.rank * u.per:(self.rank + 1) * u.per]
+        if u.distributed:
+            dist.broadcast(tmp, src=u.src(), group=u.group)
+        mine = tmp[u.rank * u.per:(u.rank + 1) * u.per]
         self.master[u.soff:u.soff + u.per].copy_(mine)
         if self.compute is not None:
             self.compute[u.soff:u.soff + u.per].copy_(mine)
@@ -383,14 +437,14 @@ class FullyShardedStore:
             return
         _set_storage(u.full, u.padded)
         src = self._source(u)
-        if not self.distributed:
+        if not u.distributed:
             u.full.copy_(src)
             u.state = _READY
-        elif self.nccl:
-            u.work = dist.all_gather_into_tensor(u.full, src, group=self.group, async_op=True)
+        elif u.nccl:
+            u.work = dist.all_gather_into_tensor(u.full, src, group=u.group, async_op=True)
             u.state = _GATHERING
         else:
-            all_gather_flat_(u.full, src, self.group)
+            all_gather_flat_(u.full, src, u.group)
             u.state = _READY
         u.stale = False
         if wait:
@@ -440,20 +494,20 @@ class FullyShardedStore:
         if not u.grad_live:
             return
         g = self.grad[u.soff:u.soff + u.per]
-        if not self.distributed:
-            g.add_(u.gfull)
-        elif self.nccl:
+        if not u.distributed:
+            g.add_(u.gfull, alpha=u.grad_scale)
+        elif u.nccl:
             side = self._rs_stream
             side.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(side):
                 tmp = torch.empty(u.per, dtype=torch.float32, device=self.device)
-                dist.reduce_scatter_tensor(tmp, u.gfull, op=dist.ReduceOp.AVG, group=self.group)
-                g.add_(tmp)
+                dist.reduce_scatter_tensor(tmp, u.gfull, op=dist.ReduceOp.AVG, group=u.group)
+                g.add_(tmp, alpha=u.grad_scale)
             u.gfull.record_stream(side)
         else:
             tmp = torch.empty(u.per, dtype=torch.float32, device=self.device)
-            reduce_scatter_avg_(tmp, u.gfull, self.group)
-            g.add_(tmp)
+            reduce_scatter_avg_(tmp, u.gfull, u.group)
+            g.add_(tmp, alpha=u.grad_scale)
         for p in u.params:
             p.grad = None
         _set_storage(u.gfull, 0)
@@ -468,18 +522,19 @@ class FullyShardedStore:
         """After a micro-batch's backward: reduce what no hook reduced (a
         block whose input needed no gradient) and, after the last
         micro-batch, the persistent units' accumulated gradients."""
-        for u in self.block_units:
-            if u.in_backward:
-                u._post_backward()
-            elif u.grad_live:
-                self.reduce_grad(u)
-                if not u.persistent and not self.pinned:
-                    self.release(u)
+        for b in self.blocks:
+            if b.in_backward:
+                b._post_backward()
+            elif any(u.grad_live for u in b.parts):
+                for u in b.parts:
+                    self.reduce_grad(u)
+                if not self.pinned:
+                    b._release()
         if self.final_micro:
             for u in self.units:
                 if u.persistent and u.grad_live:
                     self.reduce_grad(u)
-        if self.nccl:
+        if self._rs_stream is not None:
             torch.cuda.current_stream(self.device).wait_stream(self._rs_stream)
 
     def sync_grads(self) -> None:
@@ -534,9 +589,9 @@ class FullyShardedStore:
         finally:
             self.pinned = prev
             if not prev:
-                for u in self.units:
-                    if not u.persistent and not u.in_backward:
-                        self.release(u)
+                for b in self.blocks:
+                    if not b.in_backward:
+                        b._release()
 
     # --------------------------------------------- full (virtual) buffers
     @torch.no_grad()
@@ -547,8 +602,8 @@ class FullyShardedStore:
         for u in self.units:
             dst = out[u.voff:u.voff + u.padded]
             src = shard_buf[u.soff:u.soff + u.per].contiguous()
-            if self.distributed:
-                all_gather_flat_(dst, src, self.group)
+            if u.distributed:
+                all_gather_flat_(dst, src, u.group)
             else:
                 dst.copy_(src)
         return out
@@ -557,7 +612,7 @@ class FullyShardedStore:
     def scatter_virtual(self, full: torch.Tensor, shard_buf: torch.Tensor) -> None:
         """This rank's part of a full-layout buffer back into shard layout."""
         for u in self.units:
-            a = u.voff + self.rank * u.per
+            a = u.voff + u.rank * u.per
             shard_buf[u.soff:u.soff + u.per].copy_(full[a:a + u.per])
 
     def bind_full(self, full: torch.Tensor) -> None:

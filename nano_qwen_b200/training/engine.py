@@ -119,9 +119,10 @@ class TrainEngine:
         per use (``parallel.fsdp``)."""
         from ..parallel.fsdp import FullyShardedStore, build_fsdp_optimizer
         if parallel is not None and any(int(getattr(parallel.config, k, 1)) > 1
-                                        for k in ("tp_size", "pp_size", "ep_size", "cp_size")):
-            raise ValueError("shard_params runs over plain data parallelism (tp/pp/ep/cp = 1)")
-        self.store = FullyShardedStore(self.model, group=dp_group,
+                                        for k in ("tp_size", "pp_size", "cp_size")):
+            raise ValueError("shard_params runs over data (and expert) parallelism: tp/pp/cp = 1")
+        expert_group = parallel.groups.get("edp") if parallel is not None else None
+        self.store = FullyShardedStore(self.model, group=dp_group, expert_group=expert_group,
                                        reshard_after_forward=dist_cfg.get("reshard_after_forward",
                                                                           True))
         self.dp = self.store

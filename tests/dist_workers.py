@@ -534,6 +534,43 @@ def fsdp_worker(rank, world, port, moe, ckpt):
     dist.destroy_process_group()
 
 
+def fsdp_ep_worker(rank, world, port, ep):
+    """Fully sharded parameters with expert parallelism: dense matrices
+    sharded over the data-parallel group, each block's local experts over
+    the ranks that hold the same experts; against the replicated EP engine
+    (itself checked against the single-process model) on the same layout."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg(moe=True)
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+
+    def engine(shard):
+        pm = ParallelismManager(ParallelConfig(ep_size=ep, ep_fused=False))
+        m = pm.apply_parallelism(build(cfg))
+        return TrainEngine(m, dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"),
+                           parallel=pm)
+
+    ref, fs = engine(False), engine(True)
+    assert fs.store.mode == "fsdp"
+    xu = [u for u in fs.store.units if u.name.endswith(".experts")]
+    assert xu and all(u.world == world // ep for u in xu), [(u.name, u.world) for u in xu]
+    for step in range(3):
+        ids = batch(cfg, 2 * world, 16, seed=300 + step)
+        mine = [{"input_ids": ids[2 * rank:2 * rank + 2], "labels": ids[2 * rank:2 * rank + 2]}]
+        r = ref.train_step(mine)
+        f = fs.train_step(mine)
+        close(f["loss"], r["loss"], 1e-5, "loss")
+        close(f["grad_norm"], r["grad_norm"], 1e-4, "grad norm")
+    ref.state_for_save()
+    fs.state_for_save()
+    for (n, p), (_, q) in zip(fs.model.named_parameters(), ref.model.named_parameters()):
+        close(p, q, 1e-5, n)
+    fs.optimizer.release_full_state()
+    dist.destroy_process_group()
+
+
 def fsdp_api_worker(rank, world, port):
     """The reference's calls (``apply_fsdp2`` per block + root, then a plain
     loop: forward, backward, clip, step) on the fully sharded store give the

@@ -96,3 +96,8 @@ def test_fully_sharded_checkpoint_resumes_and_reshards(tmp_path):
 
 def test_fully_sharded_reference_api_loop():
     _run(W.fsdp_api_worker, 2)
+
+
+@pytest.mark.parametrize("world,ep", [(2, 2), (4, 2)])
+def test_fully_sharded_with_expert_parallel(world, ep):
+    _run(W.fsdp_ep_worker, world, ep)
