@@ -44,57 +44,25 @@ DP_LABEL = {"p2p": "ZeRO-2, fused peer-memory reduce-scatter + sharded AdamW + a
             "fsdp": "fully sharded: per-block bf16 all-gather / fp32 reduce-scatter over NCCL"}
 
 BASELINE_METRIC = "train tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; MFU"
-# the only measured reference number: its CPU fp32 debug step (BASELINE config #1)
+# the reference's only published measurement: its CPU fp32 step of the debug model
 CPU_BASELINE_TOKS = 1169.0
 
-CONFIGS = {
-    # name: (model kwargs, per-GPU micro batch, seq, parallel label)
-    "qwen3-1.7b": (dict(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16,
-                        num_key_value_heads=8, head_dim=128, intermediate_size=6144,
-                        vocab_size=151936, max_position_embeddings=4096, rope_theta=1e6,
-                        qk_norm=True, tie_word_embeddings=True), 4, 4096, "dp"),
-    "debug": (dict(hidden_size=512, num_hidden_layers=8, num_attention_heads=8, num_key_value_heads=2,
-                   head_dim=64, intermediate_size=1408, vocab_size=32000, max_position_embeddings=2048,
-                   rope_theta=1e6, qk_norm=True, tie_word_embeddings=True), 4, 256, "dp"),
-    "debug-moe": (dict(hidden_size=512, num_hidden_layers=8, num_attention_heads=8, num_key_value_heads=2,
-                       head_dim=64, intermediate_size=1408, vocab_size=32000,
-                       max_position_embeddings=2048, rope_theta=1e6, qk_norm=True,
-                       tie_word_embeddings=True, num_experts=64, num_experts_per_tok=8,
-                       moe_intermediate_size=256, router_aux_loss_coef=0.001), 8, 2048, "dp"),
-    # BASELINE config 2 with expert parallelism over all ranks (per-GPU batch 8 x 2048)
-    "debug-moe-ep": (dict(hidden_size=512, num_hidden_layers=8, num_attention_heads=8,
-                          num_key_value_heads=2, head_dim=64, intermediate_size=1408,
-                          vocab_size=32000, max_position_embeddings=2048, rope_theta=1e6,
-                          qk_norm=True, tie_word_embeddings=True, num_experts=64,
-                          num_experts_per_tok=8, moe_intermediate_size=256,
-                          router_aux_loss_coef=0.001), 8, 2048, "ep"),
-    # Qwen3-235B-A22B layer shape truncated to 12 layers, expert
-    # parallelism over all ranks (per-GPU batch 2 x 4096)
-    "qwen3-235b-l12-ep": (dict(hidden_size=4096, num_hidden_layers=12, num_attention_heads=64,
-                               num_key_value_heads=4, head_dim=128, intermediate_size=12288,
-                               vocab_size=151936, max_position_embeddings=4096, rope_theta=1e6,
-                               qk_norm=True, tie_word_embeddings=False, num_experts=128,
-                               num_experts_per_tok=8, moe_intermediate_size=1536,
-                               router_aux_loss_coef=0.001), 2, 4096, "ep"),
-    # Qwen3-1.7B shape under tensor + sequence parallelism (global batch 4 x 4096): a
-    # smaller tp configuration for comparing the fused and NCCL paths
-    "qwen3-1.7b-tp": (dict(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16,
-                           num_key_value_heads=8, head_dim=128, intermediate_size=6144,
-                           vocab_size=151936, max_position_embeddings=4096, rope_theta=1e6,
-                           qk_norm=True, tie_word_embeddings=True), 4, 4096, "tp"),
-    # long context: Qwen3-1.7B shape, one 32768-token sequence split over the ranks by
-    # context parallelism (zigzag), strong scaling
-    "qwen3-1.7b-cp32k": (dict(hidden_size=2048, num_hidden_layers=28, num_attention_heads=16,
-                              num_key_value_heads=8, head_dim=128, intermediate_size=6144,
-                              vocab_size=151936, max_position_embeddings=32768, rope_theta=1e6,
-                              qk_norm=True, tie_word_embeddings=True), 1, 32768, "cp"),
-    # Qwen3-8B shape, tensor + sequence parallel over all ranks,
-    # global batch 8 x 8192 (the same tokens on every rank: strong scaling)
-    "qwen3-8b-tp": (dict(hidden_size=4096, num_hidden_layers=36, num_attention_heads=32,
-                         num_key_value_heads=8, head_dim=128, intermediate_size=12288,
-                         vocab_size=151936, max_position_embeddings=8192, rope_theta=1e6,
-                         qk_norm=True, tie_word_embeddings=False), 8, 8192, "tp"),
-}
+def load_configs(directory=None):
+    """Benchmark configurations from ``configs/bench/*.yaml``:
+    name -> (model kwargs, per-GPU micro batch, sequence length, parallel
+    label: dp / tp / ep / cp)."""
+    import glob
+    import yaml
+    directory = directory or os.path.join(os.path.dirname(os.path.abspath(__file__)), "configs", "bench")
+    out = {}
+    for path in sorted(glob.glob(os.path.join(directory, "*.yaml"))):
+        with open(path) as f:
+            d = yaml.safe_load(f)
+        out[d["name"]] = (dict(d["model"]), int(d["micro_batch"]), int(d["seq_len"]), d["parallel"])
+    return out
+
+
+CONFIGS = load_configs()
 
 
 def parse():
@@ -118,7 +86,7 @@ def parse():
     p.add_argument("--cp-mode", default="allgather", choices=["allgather", "ring"],
                    help="ours, cp configs: gathered k|v (peer-memory kernels) or the k|v ring")
     p.add_argument("--device", default="cuda", choices=["cuda", "cpu"],
-                   help="cpu: fp32 on the host, world size 1 (BASELINE config #1 with --config debug)")
+                   help="cpu: fp32 on the host, world size 1 (the reference's CPU debug step with --config debug)")
     return p.parse_args()
 
 
@@ -508,7 +476,7 @@ def run_reference(args, world, rank, local):
 
 
 def run_reference_cpu(args, mk, B, S):
-    """BASELINE config #1: the reference's Qwen3Model + build_optimizer (unfused
+    """The CPU debug step: the reference's Qwen3Model + build_optimizer (unfused
     AdamW on the CPU) + clip_grad_norm_, fp32, one process, host-timed."""
     import torch
     import torch.nn as nn

@@ -10,7 +10,7 @@ packing copies):
   rank owns 1/N of the flat buffer, the fused AdamW kernel updates only that
   shard, and the updated bf16 compute copy is all-gathered.  This is ZeRO-2:
   with 180 GB of HBM per B200 the bf16 working copy of every model in the
-  BASELINE configs fits, so the forward needs no per-layer parameter
+  benchmark configurations fits, so the forward needs no per-layer parameter
   all-gather at all; the fp32 master/Adam state (16 B/param) is what gets
   sharded.
 

@@ -10,8 +10,8 @@ and returns the model; data parallelism / FSDP-style sharding is applied by the
 training engine on the flat parameter store (``parallel.data_parallel``).
 
 Differences from the reference: every axis is functional (its TP crashed on a
-head-count view, EP exchanged only counts, PP/CP were never used; SURVEY of
-distributed/*), the world-size check includes ep and cp, and SFT/GRPO/DPO take
+head-count view, EP exchanged only counts, PP/CP were never used; reference:
+distributed/*.py), the world-size check includes ep and cp, and SFT/GRPO/DPO take
 the same config as pretraining.
 """
 

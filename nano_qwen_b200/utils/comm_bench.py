@@ -48,7 +48,7 @@ def _timed(fn, iters: int, warmup: int = 3) -> float:
 
 
 def ep_layer(iters: int, world: int, rank: int) -> None:
-    """One expert-parallel MoE layer (BASELINE debug_moe shape: hidden 512, 64
+    """One expert-parallel MoE layer (the debug_moe shape: hidden 512, 64
     experts, top-8, expert FFN 256, 8 x 2048 tokens per rank), forward +
     backward, fused peer-memory path vs NCCL all-to-all.  Roofline: the slower
     of the expert GEMM FLOPs at the measured sustained bf16 peak and the token
