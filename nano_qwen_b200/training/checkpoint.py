@@ -67,6 +67,30 @@ def model_parallel(model: nn.Module) -> bool:
                for p in model.parameters())
 
 
+def manager_from_config(training_config: dict, default_dir: str = "checkpoints") -> "CheckpointManager":
+    """The checkpoint manager a training YAML's ``checkpoint`` section asks for."""
+    ck = training_config.get("checkpoint", {}) or {}
+    return CheckpointManager(save_dir=ck.get("save_dir", default_dir),
+                             save_interval=ck.get("save_interval", 1000),
+                             max_checkpoints=ck.get("max_checkpoints", 5),
+                             async_save=ck.get("async_save", True))
+
+
+def resolve_resume(resume_from: Optional[str], training_config: dict,
+                   manager: Optional["CheckpointManager"] = None) -> Optional[str]:
+    """The checkpoint directory (or file) to resume from: the command line's
+    value, else the training YAML's ``checkpoint.resume_from`` (which the
+    reference reads but never uses); ``latest`` / ``auto`` mean the newest
+    ``step_*`` directory under the manager's save directory (None when there
+    is none yet, i.e. a fresh start)."""
+    value = resume_from or ((training_config.get("checkpoint", {}) or {}).get("resume_from"))
+    if value in (None, "", "none", "null"):
+        return None
+    if str(value).lower() in ("latest", "auto"):
+        return manager.latest() if manager is not None else None
+    return str(value)
+
+
 class CheckpointManager:
     def __init__(self, save_dir: str = "checkpoints", save_interval: int = 1000,
                  max_checkpoints: int = 5, async_save: bool = True, use_dcp: bool = True):

@@ -20,6 +20,7 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..models.transformer import shift_targets
+from .checkpoint import manager_from_config, resolve_resume
 from .engine import TrainEngine
 
 
@@ -170,10 +171,16 @@ def run_dpo(model_config_path: str, training_config_path: str, resume_from: Opti
     loader = DataLoader(ds, batch_size=(tcfg.get("batch", {}) or {}).get("micro_batch_size", 2),
                         sampler=sampler, num_workers=0)
     trainer = DPOTrainer(policy, ref, tcfg, device)
+    mgr = manager_from_config(tcfg, "checkpoints/dpo")
+    start = 0
+    resume_from = resolve_resume(resume_from, tcfg, mgr)
+    if resume_from:
+        start = int(mgr.load(trainer.policy, trainer.optimizer, trainer.scheduler, resume_from,
+                             sampler=sampler).get("step", 0))
     logger = TrainingLogger(log_interval=1)
     total = max_steps or (tcfg.get("scheduler", {}) or {}).get("total_steps", 2000)
     it = iter(loader)
-    for step in range(1, total + 1):
+    for step in range(start + 1, total + 1):
         try:
             b = next(it)
         except StopIteration:
@@ -182,5 +189,9 @@ def run_dpo(model_config_path: str, training_config_path: str, resume_from: Opti
         m = trainer.train_step(b["chosen_ids"], b["rejected_ids"], b["chosen_labels"], b["rejected_labels"])
         logger.log_step(step=step, loss=m["loss"], lr=trainer.scheduler.get_last_lr()[0],
                         grad_norm=m["grad_norm"], extra={f"dpo/{k}": v for k, v in m.items()})
+        if mgr.should_save(step):
+            mdl, opt, sch = trainer.engine.state_for_save()
+            mgr.save(step, mdl, opt, sch, extra_state={"step": step}, sampler=sampler)
+    mgr.wait()
     logger.finish()
     return trainer

@@ -143,7 +143,13 @@ class TrainEngine:
                                          stable_steps=sch.get("stable_steps",
                                                               int(0.8 * sch.get("total_steps", 100000))))
         self.grad_clip = opt.get("grad_clip", 1.0)
-        self.dtype = getattr(torch, (training_config.get("precision", {}) or {}).get("dtype", "bfloat16"))
+        prec = training_config.get("precision", {}) or {}
+        self.dtype = getattr(torch, prec.get("dtype", "bfloat16"))
+        if prec.get("grad_scaler", False) and self.dtype == torch.float16:
+            # the reference's key (always false in its YAMLs): a loss scaler
+            # only matters for fp16, whose compute path is not provided here
+            raise NotImplementedError("precision.grad_scaler with float16: the kernels compute in "
+                                      "bfloat16, which needs no loss scaling")
 
     # ----------------------------------------------------------------- step
     def forward_backward(self, batch: Dict[str, torch.Tensor], scale: float):

@@ -23,6 +23,7 @@ from typing import Callable, Dict, List, Optional, Tuple
 import torch
 
 from .. import ops
+from .checkpoint import manager_from_config, resolve_resume
 from .engine import TrainEngine
 
 
@@ -100,10 +101,13 @@ class GRPO:
                        "advantages_mean": advantages.mean()}
 
     def train_step(self, prompt_ids: torch.Tensor, reward_fn: Callable,
-                   ground_truth: Optional[str] = None) -> dict:
+                   ground_truth: Optional[str] = None, prompt: Optional[str] = None) -> dict:
         seqs, old_lp, mask = self.generate_responses(prompt_ids, self.group_size)
         P = prompt_ids.shape[1]
         texts = [self.tokenizer.decode(s[P:][m].tolist()) for s, m in zip(seqs, mask)]
+        if hasattr(reward_fn, "set_prompt"):
+            reward_fn.set_prompt(prompt if prompt is not None else self.tokenizer.decode(
+                prompt_ids[0].tolist()))
         rewards = reward_fn(texts, ground_truth)
         rewards = torch.as_tensor(rewards, dtype=torch.float32, device=self.device)
         adv = self.compute_advantages(rewards)
@@ -119,15 +123,24 @@ class GRPO:
                        total_loss=float(out["loss"]), grad_norm=float(out["grad_norm"]))
         return metrics
 
-    def train(self, queries: List[dict], reward_fn: Callable, total_steps: int):
+    def train(self, queries: List[dict], reward_fn: Callable, total_steps: int, start_step: int = 0,
+              ckpt_mgr=None):
+        """Steps ``start_step + 1 .. total_steps`` (one prompt each, cycling
+        through ``queries``); checkpoints every ``save_interval`` steps when a
+        manager is given."""
         from .logger import TrainingLogger
         logger = TrainingLogger(log_interval=1)
-        for step in range(total_steps):
+        for step in range(start_step, total_steps):
             q = queries[step % len(queries)]
             ids = torch.tensor(self.tokenizer.encode(q["prompt"]), dtype=torch.long).unsqueeze(0)
-            m = self.train_step(ids, reward_fn, q.get("answer"))
+            m = self.train_step(ids, reward_fn, q.get("answer"), q["prompt"])
             logger.log_step(step=step + 1, loss=m["total_loss"], lr=self.scheduler.get_last_lr()[0],
                             grad_norm=m["grad_norm"], extra={f"rl/{k}": v for k, v in m.items()})
+            if ckpt_mgr is not None and ckpt_mgr.should_save(step + 1):
+                mdl, opt, sch = self.engine.state_for_save()
+                ckpt_mgr.save(step + 1, mdl, opt, sch, extra_state={"step": step + 1})
+        if ckpt_mgr is not None:
+            ckpt_mgr.wait()
         logger.finish()
 
 
@@ -158,6 +171,80 @@ def _math_reward_fn(responses: List[str], ground_truth: Optional[str]) -> List[f
     return out
 
 
+class CombinedReward:
+    """Weighted sum of the reward sources a training YAML's
+    ``grpo.reward_types`` names (the reference lists them but always uses
+    the math reward):
+
+    * ``verifiable``: 1.0 when the final answer matches the ground truth;
+    * ``model``: a trained ``RewardModel`` (``grpo.reward_model_checkpoint``,
+      a ``checkpoint.pt`` with its state dict; model shape from the policy's
+      config) scoring prompt + response.
+
+    ``grpo.reward_weights`` (same order, default 1.0 each) weights them."""
+
+    def __init__(self, fns: List[Tuple[str, Callable, float]]):
+        self.fns = fns
+        self.prompt = ""
+
+    def set_prompt(self, prompt: str) -> None:
+        self.prompt = prompt
+
+    def __call__(self, responses: List[str], ground_truth: Optional[str]) -> List[float]:
+        total = [0.0] * len(responses)
+        for _, fn, w in self.fns:
+            vals = fn(responses, ground_truth, self.prompt)
+            total = [t + w * float(v) for t, v in zip(total, vals)]
+        return total
+
+
+def build_reward_fn(training_config: dict, model_config=None, tokenizer=None,
+                    device: torch.device = torch.device("cpu")) -> CombinedReward:
+    g = training_config.get("grpo", {}) or {}
+    types = list(g.get("reward_types") or ["verifiable"])
+    weights = list(g.get("reward_weights") or [1.0] * len(types))
+    if len(weights) != len(types):
+        raise ValueError("grpo.reward_weights needs one weight per reward type")
+    fns: List[Tuple[str, Callable, float]] = []
+    for kind, w in zip(types, weights):
+        if kind == "verifiable":
+            fns.append((kind, lambda r, gt, prompt: _math_reward_fn(r, gt), float(w)))
+        elif kind == "model":
+            path = g.get("reward_model_checkpoint")
+            if not path:
+                from ..parallel.comm import is_main_process
+                if is_main_process():
+                    print("grpo.reward_types lists 'model' but grpo.reward_model_checkpoint is "
+                          "not set: the model reward is skipped")
+                continue
+            fns.append((kind, _model_reward(path, model_config, tokenizer, device), float(w)))
+        else:
+            raise ValueError(f"unknown reward type {kind!r} (verifiable, model)")
+    if not fns:
+        raise ValueError("no usable reward in grpo.reward_types")
+    return CombinedReward(fns)
+
+
+def _model_reward(path: str, model_config, tokenizer, device):
+    from .reward_model import RewardModel
+    rm = RewardModel(model_config)
+    st = torch.load(path, map_location="cpu", weights_only=False)
+    rm.load_state_dict(st.get("model", st))
+    rm = rm.to(device).eval()
+
+    @torch.no_grad()
+    def score(responses, ground_truth, prompt):
+        seqs = [tokenizer.encode(prompt + r) for r in responses]
+        L = max(len(x) for x in seqs)
+        ids = torch.zeros(len(seqs), L, dtype=torch.long)
+        mask = torch.zeros(len(seqs), L, dtype=torch.long)
+        for i, x in enumerate(seqs):
+            ids[i, :len(x)] = torch.tensor(x, dtype=torch.long)
+            mask[i, :len(x)] = 1
+        return rm(ids.to(device), mask.to(device)).float().cpu().tolist()
+    return score
+
+
 def run_grpo(model_config_path: str, training_config_path: str, resume_from: Optional[str] = None,
              max_samples: Optional[int] = None, max_steps: Optional[int] = None):
     import yaml
@@ -186,6 +273,13 @@ def run_grpo(model_config_path: str, training_config_path: str, resume_from: Opt
         queries = [{"prompt": "What is 15 + 27?", "answer": "42"},
                    {"prompt": "What is 100 - 37?", "answer": "63"}] * 50
     trainer = GRPO(policy, ref, tok, tcfg, device)
+    mgr = manager_from_config(tcfg, "checkpoints/rl")
+    start = 0
+    resume_from = resolve_resume(resume_from, tcfg, mgr)
+    if resume_from:
+        start = int(mgr.load(trainer.policy, trainer.optimizer, trainer.scheduler,
+                             resume_from).get("step", 0))
     total = max_steps or (tcfg.get("scheduler", {}) or {}).get("total_steps", 2000)
-    trainer.train(queries, _math_reward_fn, total)
+    reward = build_reward_fn(tcfg, mcfg, tok, device)
+    trainer.train(queries, reward, total, start, mgr)
     return trainer

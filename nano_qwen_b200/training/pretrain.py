@@ -26,7 +26,7 @@ from ..models.transformer import Qwen3Model
 from ..parallel.comm import (get_local_rank, get_world_size, init_distributed, is_main_process,
                              max_over_ranks)
 from ..utils.flops import mfu
-from .checkpoint import CheckpointManager
+from .checkpoint import CheckpointManager, resolve_resume
 from .engine import TrainEngine
 from .logger import TrainingLogger
 
@@ -201,6 +201,7 @@ def run_pretraining(model_config_path: str, training_config_path: str,
                         num_workers=data_cfg.get("num_workers", 4),
                         pin_memory=torch.cuda.is_available())
     start = 0
+    resume_from = resolve_resume(resume_from, tcfg, trainer.ckpt_mgr)
     if resume_from:
         extra = trainer.ckpt_mgr.load(trainer.model, trainer.optimizer, trainer.scheduler,
                                       resume_from, sampler=sampler)

@@ -29,7 +29,7 @@ from ..data.sampler import DistributedSampler
 from ..data.tokenizer import Tokenizer
 from ..models.transformer import Qwen3Model
 from ..parallel.comm import init_distributed, is_main_process
-from .checkpoint import CheckpointManager
+from .checkpoint import CheckpointManager, resolve_resume
 from .engine import TrainEngine
 from .logger import TrainingLogger
 from .pretrain import pick_device
@@ -215,6 +215,7 @@ def run_sft(model_config_path: str, training_config_path: str, variant: str = "c
                         collate_fn=TextCollator(), num_workers=0)
     trainer = SFTTrainer(model, tcfg, device)
     start = 0
+    resume_from = resolve_resume(resume_from, tcfg, trainer.ckpt_mgr)
     if resume_from:
         start = int(trainer.ckpt_mgr.load(trainer.model, trainer.optimizer, trainer.scheduler,
                                           resume_from).get("step", 0))

@@ -99,10 +99,35 @@ def test_cli_pretrain_and_resume(cfgs):
 
 @pytest.mark.parametrize("cmd", ["sft", "dpo", "grpo"])
 def test_cli_post_training_phases(cfgs, cmd):
+    """Each phase runs, checkpoints every ``save_interval`` steps, and resumes
+    from the newest checkpoint when the YAML says ``resume_from: latest``."""
     from nano_qwen_b200.cli import main
     m, t = cfgs
     assert main([cmd, "--model-config", m, "--training-config", t, "--max-steps", "2",
                  "--max-samples", "8"]) == 0
+    assert os.path.isdir("ck/step_00000002")
+    cfg = yaml.safe_load(open(t))
+    cfg["checkpoint"]["resume_from"] = "latest"
+    with open(t, "w") as f:
+        yaml.safe_dump(cfg, f)
+    assert main([cmd, "--model-config", m, "--training-config", t, "--max-steps", "4",
+                 "--max-samples", "8"]) == 0
+    assert os.path.isdir("ck/step_00000004")
+    meta = json.load(open("ck/step_00000004/meta.json"))
+    assert meta["step"] == 4
+
+
+def test_grpo_reward_types_combine():
+    """``grpo.reward_types`` / ``reward_weights`` select and weight reward
+    sources; a model reward without a checkpoint is skipped."""
+    from nano_qwen_b200.training.grpo import build_reward_fn
+    fn = build_reward_fn({"grpo": {"reward_types": ["verifiable", "model"],
+                                   "reward_weights": [2.0, 1.0]}})
+    assert [k for k, _, _ in fn.fns] == ["verifiable"]
+    fn.set_prompt("What is 6 * 7?")
+    assert fn(["It is 42.", "\\boxed{41}"], "42") == [2.0, 0.0]
+    with pytest.raises(ValueError):
+        build_reward_fn({"grpo": {"reward_types": ["nonsense"]}})
 
 
 def test_cli_eval_multiple_choice(cfgs, tmp_path):
