@@ -11,8 +11,9 @@ training engine on the flat parameter store (``parallel.data_parallel``).
 
 Differences from the reference: every axis is functional (its TP crashed on a
 head-count view, EP exchanged only counts, PP/CP were never used; reference:
-distributed/*.py), the world-size check includes ep and cp, and SFT/GRPO/DPO take
-the same config as pretraining.
+distributed/*.py), the world-size check includes ep and cp, and SFT takes the same
+config as pretraining (GRPO and DPO run data parallel, optionally fully
+sharded: their rollouts and reference-model passes are per rank).
 """
 
 from __future__ import annotations

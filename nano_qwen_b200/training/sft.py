@@ -109,10 +109,13 @@ class SFTDataset(Dataset):
 
 
 class SFTTrainer:
-    def __init__(self, model, training_config: dict, device: torch.device):
+    def __init__(self, model, training_config: dict, device: torch.device, parallel=None):
+        """``parallel``: the ``ParallelismManager`` the model went through
+        (tensor / pipeline / expert / context parallelism from the training
+        YAML's ``distributed`` section, as in pretraining)."""
         self.cfg = training_config
         self.device = device
-        self.engine = TrainEngine(model, training_config, device)
+        self.engine = TrainEngine(model, training_config, device, parallel=parallel)
         self.model = self.engine.model
         self.optimizer = self.engine.optimizer
         self.scheduler = self.engine.scheduler
@@ -210,10 +213,18 @@ def run_sft(model_config_path: str, training_config_path: str, variant: str = "c
         if is_main_process():
             print(f"HF dataset load failed ({type(exc).__name__}), falling back to dummy data")
         ds = SFTDataset(DUMMY_SFT * 100, tok, S, **kw)
-    sampler = DistributedSampler(ds, num_replicas=world, rank=rank)
+    # the same model-parallel layouts as pretraining; one data shard per
+    # data-parallel rank
+    from .pretrain import build_parallel
+    parallel = build_parallel(tcfg, world)
+    dp_rank, dp_size = rank, world
+    if parallel is not None:
+        model = parallel.apply_parallelism(model.to(device))
+        dp_rank, dp_size = parallel.coords["dp"], parallel.config.dp_size
+    sampler = DistributedSampler(ds, num_replicas=dp_size, rank=dp_rank)
     loader = DataLoader(ds, batch_size=bcfg.get("micro_batch_size", 2), sampler=sampler,
                         collate_fn=TextCollator(), num_workers=0)
-    trainer = SFTTrainer(model, tcfg, device)
+    trainer = SFTTrainer(model, tcfg, device, parallel=parallel)
     start = 0
     resume_from = resolve_resume(resume_from, tcfg, trainer.ckpt_mgr)
     if resume_from:

@@ -655,3 +655,37 @@ def fsdp_checkpoint_worker(rank, world, port, tmp):
     a2.optimizer.release_full_state()
     dist.barrier()
     dist.destroy_process_group()
+
+
+def sft_parallel_worker(rank, world, port, tmp, axis):
+    """The SFT phase through the CLI with a model-parallel layout from the
+    training YAML (as pretraining takes it): two steps and a checkpoint."""
+    import yaml
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    torch.set_num_threads(1)
+    os.chdir(tmp)
+    from nano_qwen_b200.cli import main
+    model = dict(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                 head_dim=16, intermediate_size=128, vocab_size=300, max_position_embeddings=256,
+                 tie_word_embeddings=True)
+    train = {"optimizer": {"lr": 1e-3}, "scheduler": {"warmup_steps": 1, "total_steps": 4},
+             "batch": {"micro_batch_size": 2, "gradient_accumulation_steps": 1, "max_seq_len": 64},
+             "checkpoint": {"save_interval": 2, "save_dir": "ck", "async_save": False},
+             "logging": {"log_interval": 1, "tensorboard_enabled": False},
+             "distributed": {axis: world}}
+    if rank == 0:
+        with open("m.yaml", "w") as f:
+            yaml.safe_dump(model, f)
+        with open("t.yaml", "w") as f:
+            yaml.safe_dump(train, f)
+    else:
+        import time
+        while not os.path.exists("t.yaml"):
+            time.sleep(0.05)
+        time.sleep(0.2)
+    assert main(["sft", "--model-config", "m.yaml", "--training-config", "t.yaml",
+                 "--max-steps", "2", "--max-samples", "8"]) == 0
+    assert os.path.isdir("ck/step_00000002")
+    if dist.is_initialized():
+        dist.destroy_process_group()

@@ -101,3 +101,8 @@ def test_fully_sharded_reference_api_loop():
 @pytest.mark.parametrize("world,ep", [(2, 2), (4, 2)])
 def test_fully_sharded_with_expert_parallel(world, ep):
     _run(W.fsdp_ep_worker, world, ep)
+
+
+@pytest.mark.parametrize("axis", ["tp_size", "cp_size"])
+def test_sft_takes_model_parallel_layouts(tmp_path, axis):
+    _run(W.sft_parallel_worker, 2, str(tmp_path), axis)
