@@ -1,0 +1,211 @@
+"""Flag protocols of the peer-memory kernels, checked on an emulated
+flag/counter model (``protocol_sim``) under many random interleavings of the
+ranks: no rank reads a buffer before its producer's data is there or after a
+later producer has overwritten it, and no schedule deadlocks.
+
+Each model restates, per rank, the order of kernel launches, flag channels,
+sequence numbers and buffer choices that the host code issues
+(``parallel/peer_dp.py`` for the ZeRO step, ``parallel/tp_fused.py`` for
+tensor + sequence parallelism, whose sequence bookkeeping is the real
+``TPComm.next_seq`` / ``parts_index``), and the loads and stores each kernel
+makes (``csrc/zero_comm.cu``, ``csrc/tp_comm.cu``, ``csrc/gemm.cu``).  A
+variant with a protocol step removed must be caught.
+"""
+
+import pytest
+
+from protocol_sim import ProtocolError, explore
+
+# ------------------------------------------------------------------ ZeRO step
+
+
+def zero_rank(r: int, W: int, steps: int, publish: bool = True):
+    """One rank of the fused data-parallel step over ``steps`` steps: the
+    forward/backward reads every shard of the local bf16 compute copy and
+    writes every shard of the local fp32 gradient; ``zero_rs`` (flag slot 0)
+    reads shard r of every peer's gradient and writes the mean into the local
+    shard; after the norm all-reduce ``zero_adamw_ag`` stores the updated
+    shard r into every peer's compute copy; ``zero_publish`` (slot 1) is the
+    barrier before anyone's next forward."""
+    for t in range(1, steps + 1):
+        for s in range(W):
+            yield ("read", ("comp", s), ("w", t - 1))          # forward / backward
+        for s in range(W):
+            yield ("write", r, ("grad", s), ("g", r, t))
+        for p in range(W):                                    # zero_rs: signal, wait
+            yield ("signal", p, "zero0", r, t)
+        yield ("wait", "zero0", range(W), t)
+        for p in range(W):
+            yield ("read_peer", p, ("grad", r), ("g", p, t))
+        yield ("write", r, ("grad", r), ("mean", t))
+        yield ("collective", f"norm{t}")                      # squared norm all-reduce
+        yield ("read", ("grad", r), ("mean", t))              # zero_adamw_ag
+        for p in range(W):
+            yield ("write", p, ("comp", r), ("w", t))
+        if publish:                                           # zero_publish
+            for p in range(W):
+                yield ("signal", p, "zero1", r, t)
+            yield ("wait", "zero1", range(W), t)
+
+
+def _zero_ranks(W, steps, publish=True):
+    def make():
+        ranks = [zero_rank(r, W, steps, publish) for r in range(W)]
+        return ranks
+
+    return make
+
+
+def _init_zero(W):
+    # initial compute copy: version 0 everywhere (written before the first step)
+    def gen(r):
+        for s in range(W):
+            yield ("write", r, ("comp", s), ("w", 0))
+        yield ("collective", "init")
+    return gen
+
+
+def _with_init(W, body):
+    init = _init_zero(W)
+
+    def make():
+        out = []
+        for r, g in enumerate(body()):
+            def chain(r=r, g=g):
+                yield from init(r)
+                yield from g
+            out.append(chain())
+        return out
+    return make
+
+
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_zero_step_protocol(W):
+    explore(_with_init(W, _zero_ranks(W, 3)), schedules=150)
+
+
+def test_zero_step_without_publish_barrier_races():
+    """Without the publish barrier a fast rank's next forward reads a compute
+    shard that a slow peer has not stored yet."""
+    with pytest.raises(ProtocolError):
+        explore(_with_init(4, _zero_ranks(4, 3, publish=False)), schedules=150)
+
+
+# -------------------------------------------------------- tensor parallel
+
+AG_FWD, RS_FWD, AG_BWD, RS_BWD = 0, 1, 2, 3
+
+
+def _comm(W, r):
+    from nano_qwen_b200.parallel.tp_fused import TPComm
+    c = object.__new__(TPComm)
+    c.world, c.rank, c.seq, c.count = W, r, [0, 0, 0, 0], 0
+    return c
+
+
+def tp_rank(r: int, W: int, layers: int, steps: int, ping_pong: int = 2, norm_waits: bool = True,
+            close_step: bool = True):
+    """One rank of fused TP+SP training (``block_forward`` and the autograd
+    backward of its functions) over ``steps`` steps.  Buffers: x_full per
+    (layer, norm) (persistent, read again by the weight-gradient GEMMs),
+    ``parts_fwd`` / ``parts_bwd`` / ``dy_full`` rotating over ``ping_pong``
+    copies chosen by sequence number, planes indexed by the writing rank."""
+    from nano_qwen_b200.parallel.tp_fused import parts_index
+    comm = _comm(W, r)
+
+    def signal_all(ch, seq):
+        for p in range(W):
+            yield ("signal", p, ch, r, seq)
+
+    def rs_write(kind, ch):            # gemm_rs: row tiles to their owners, then the grid flag
+        seq = comm.next_seq(ch)
+        for q in range(W):
+            yield ("write", q, (kind, seq % ping_pong, r), (kind, r, seq))
+        yield from signal_all(ch, seq)
+
+    def rs_read(kind, ch, seq):        # tp_norm: wait for every source, read every plane
+        if norm_waits:
+            yield ("wait", ch, range(W), seq)
+        for p in range(W):
+            yield ("read", (kind, seq % ping_pong, p), (kind, p, seq))
+
+    def ag_write(key, ch, seq):        # tp_norm: this rank's rows into every rank's buffer
+        for q in range(W):
+            yield ("write", q, key + (r,), (key, r, seq))
+        yield from signal_all(ch, seq)
+
+    def ag_read(key, ch, seq):         # gemm_ag: producer waits per owner, reads all rows
+        yield ("wait", ch, range(W), seq)
+        for p in range(W):
+            yield ("read", key + (p,), (key, p, seq))
+
+    for t in range(steps):
+        ag_seqs = {}
+        # ---- forward
+        have_parts = False
+        for layer in range(layers):
+            for n in (0, 1):
+                if have_parts:
+                    _, pseq = parts_index(comm)
+                    yield from rs_read("pf", RS_FWD, pseq)
+                s = comm.next_seq(AG_FWD)
+                key = ("x", layer, n)
+                ag_seqs[(layer, n)] = s
+                yield from ag_write(key, AG_FWD, s)
+                yield from ag_read(key, AG_FWD, comm.seq[AG_FWD])   # q|k|v or gate|up
+                yield from rs_write("pf", RS_FWD)                    # o_proj or down_proj
+                have_parts = True
+        _, pseq = parts_index(comm)
+        yield from rs_read("pf", RS_FWD, pseq)                       # final norm
+        # ---- backward: final norm (gathers dy for the last down_proj)
+        s = comm.next_seq(AG_BWD)
+        yield from ag_write(("dy", s % ping_pong), AG_BWD, s)
+        for layer in reversed(range(layers)):
+            for n in (1, 0):
+                s = comm.seq[AG_BWD]                                 # row-parallel dgrad/wgrad
+                yield from ag_read(("dy", s % ping_pong), AG_BWD, s)
+                yield from rs_write("pb", RS_BWD)                    # column-parallel dgrad
+                key = ("x", layer, n)                                # its weight gradient
+                for p in range(W):
+                    yield ("read", key + (p,), (key, p, ag_seqs[(layer, n)]))
+                yield from rs_read("pb", RS_BWD, comm.seq[RS_BWD])   # norm backward
+                if not (layer == 0 and n == 0):                      # fed by partials: gather dy
+                    s = comm.next_seq(AG_BWD)
+                    yield from ag_write(("dy", s % ping_pong), AG_BWD, s)
+        # replicated-gradient all-reduce and the norm all-reduce close the step
+        if close_step:
+            yield ("collective", f"grads{t}")
+
+
+def _tp_ranks(W, layers, steps, ping_pong=2, norm_waits=True, close_step=True):
+    return lambda: [tp_rank(r, W, layers, steps, ping_pong, norm_waits, close_step)
+                    for r in range(W)]
+
+
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_tensor_parallel_protocol(W):
+    explore(_tp_ranks(W, layers=3, steps=2), schedules=60)
+
+
+def test_tensor_parallel_single_buffer_is_also_ordered():
+    """The partial / gradient buffers alternate between two copies, but the
+    protocol does not depend on it: a rank's next reduce-scatter store comes
+    after its all-gather wait on every rank's norm, which has finished
+    reading the previous partials.  (The second copy is kept as slack.)"""
+    explore(_tp_ranks(4, layers=3, steps=2, ping_pong=1), schedules=60)
+
+
+def test_tensor_parallel_norm_without_wait_races():
+    """A norm that sums the partials without waiting for every source's
+    reduce-scatter flag reads a plane that is not there yet."""
+    with pytest.raises(ProtocolError):
+        explore(_tp_ranks(4, layers=3, steps=2, norm_waits=False), schedules=60)
+
+
+def test_tensor_parallel_steps_are_ordered_by_the_gradient_all_reduce():
+    """The gathered activations of a layer are read again by its
+    weight-gradient GEMM; the next step's all-gather into them is held back
+    only by the collectives that close a step (replicated-gradient and norm
+    all-reduces).  Without them a fast rank overwrites a slow rank's x_full."""
+    with pytest.raises(ProtocolError):
+        explore(_tp_ranks(4, layers=2, steps=3, close_step=False), schedules=100)
