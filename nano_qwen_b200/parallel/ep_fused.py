@@ -62,7 +62,11 @@ class EPComm:
         self.p_counts = self.alloc.peer_ptrs(self.counts)
         self.y_out = self._buf()
         self.dy_recv = self._buf()
-        self.dx_recv = self._buf()
+        # two input-gradient staging buffers, by MoE-layer parity: an owner
+        # whose dgrad waits for no rows of some source (that source routed
+        # nothing to it in this layer) could otherwise overwrite the buffer
+        # while that source still pulls the previous layer's rows from it
+        self.dx_recv = [self._buf(), self._buf()]
         self.recv: Dict[int, Tuple[torch.Tensor, List[int]]] = {}
         self.counter = torch.zeros(1, dtype=torch.int32, device=device)
         self.count = 0
@@ -164,6 +168,7 @@ class _EPMoE(torch.autograd.Function):
                      El, s2)
         ctx.save_for_backward(idx, dest_row, w32, y_pulled, seg_off, recv, gu, h, cnt)
         ctx.comm, ctx.w, ctx.meta = comm, (w_gu, w_d), (El, inter, H, len(w_gu.anchors) + len(w_d.anchors))
+        ctx.layer = layer
         return out
 
     @staticmethod
@@ -194,7 +199,7 @@ class _EPMoE(torch.autograd.Function):
         if w_gu.requires_grad:
             E.grouped_gemm_tn_acc(dgu, recv, _grad_view(w_gu, (El, 2 * inter, H)), seg_off)
         dxr = E.grouped_gemm_nn(dgu, Wgu, seg_off)
-        dxo, dxo_ptrs = comm.dx_recv
+        dxo, dxo_ptrs = comm.dx_recv[ctx.layer % 2]
         dxo.copy_(dxr)
         s4 = comm.next(CH_DX)
         E.ep_signal(comm.p_flags, comm.p_counts, comm.rank, CH_DX, s4)

@@ -209,3 +209,109 @@ def test_tensor_parallel_steps_are_ordered_by_the_gradient_all_reduce():
     all-reduces).  Without them a fast rank overwrites a slow rank's x_full."""
     with pytest.raises(ProtocolError):
         explore(_tp_ranks(4, layers=2, steps=3, close_step=False), schedules=100)
+
+
+# -------------------------------------------------------- expert parallel
+
+CH_COUNTS, CH_DISPATCH, CH_OUT, CH_DOUT, CH_DX = 0, 1, 2, 3, 4
+
+
+def ep_rank(r: int, W: int, routes, steps: int, dx_buffers: int = 2):
+    """One rank of fused expert parallelism (``parallel/ep_fused.py``) over
+    ``steps`` steps of len(routes) MoE layers; ``routes[l][s][q]`` is True
+    when source s has (token, expert) pairs on owner q's experts in layer l.
+    Per layer: the counts exchange (every rank's table, all-rank wait), the
+    dispatch (P2P stores into the owners' per-layer receive buffers, then the
+    grid flag to every rank), the gate|up GEMM whose tiles wait only for the
+    sources whose rows they read, the outputs in the shared ``y_out`` buffer
+    pulled by the sources' combine (all-rank wait).  Backward: the weighted
+    output gradient pushed into the owners' shared ``dy_recv``, the dgrad
+    GEMM's per-source waits, the weight gradients re-reading ``dy_recv`` and
+    the receive buffer, the input gradient staged in ``dx_recv`` (one copy
+    per layer parity) and pulled by the sources (all-rank wait)."""
+    seq = [0] * 5
+    L = len(routes)
+
+    def nxt(ch):
+        seq[ch] += 1
+        return seq[ch]
+
+    def signal_all(ch, s):
+        for p in range(W):
+            yield ("signal", p, ch, r, s)
+
+    for t in range(steps):
+        for layer in range(L):
+            rt = routes[layer]
+            s0 = nxt(CH_COUNTS)
+            for p in range(W):
+                yield ("write", p, ("counts", r), ("cnt", layer, r, t))
+            yield from signal_all(CH_COUNTS, s0)
+            yield ("wait", CH_COUNTS, range(W), s0)
+            for p in range(W):
+                yield ("read", ("counts", p), ("cnt", layer, p, t))   # layout + table copy
+            s1 = nxt(CH_DISPATCH)
+            for q in range(W):
+                if rt[r][q]:
+                    yield ("write", q, ("recv", layer, r), ("x", layer, r, t))
+            yield from signal_all(CH_DISPATCH, s1)
+            senders = [s for s in range(W) if rt[s][r]]
+            if senders:
+                yield ("wait", CH_DISPATCH, senders, s1)
+            for s in senders:
+                yield ("read", ("recv", layer, s), ("x", layer, s, t))
+            s2 = nxt(CH_OUT)
+            yield ("write", r, ("yout",), ("y", layer, r, t))
+            yield from signal_all(CH_OUT, s2)
+            yield ("wait", CH_OUT, range(W), s2)
+            for q in range(W):
+                if rt[r][q]:
+                    yield ("read_peer", q, ("yout",), ("y", layer, q, t))
+        for layer in reversed(range(L)):
+            rt = routes[layer]
+            s3 = nxt(CH_DOUT)
+            for q in range(W):
+                if rt[r][q]:
+                    yield ("write", q, ("dyr", r), ("dy", layer, r, t))
+            yield from signal_all(CH_DOUT, s3)
+            senders = [s for s in range(W) if rt[s][r]]
+            if senders:
+                yield ("wait", CH_DOUT, senders, s3)
+            for s in senders:
+                yield ("read", ("dyr", s), ("dy", layer, s, t))        # dgrad, then weight grads
+                yield ("read", ("recv", layer, s), ("x", layer, s, t))
+            s4 = nxt(CH_DX)
+            slot = layer % dx_buffers
+            yield ("write", r, ("dxr", slot), ("dx", layer, r, t))
+            yield from signal_all(CH_DX, s4)
+            yield ("wait", CH_DX, range(W), s4)
+            for q in range(W):
+                if rt[r][q]:
+                    yield ("read_peer", q, ("dxr", slot), ("dx", layer, q, t))
+        yield ("collective", f"grads{t}")      # dense-gradient all-reduce closes the step
+
+
+def _routes(W, L, seed, density=0.5):
+    import random
+    g = random.Random(seed)
+    return [[[g.random() < density for _ in range(W)] for _ in range(W)] for _ in range(L)]
+
+
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_expert_parallel_protocol(W):
+    for k in range(6):
+        routes = _routes(W, 4, k, density=0.3 + 0.1 * k)
+        explore(lambda: [ep_rank(r, W, routes, 2) for r in range(W)], schedules=40)
+
+
+def test_expert_parallel_single_dx_buffer_races():
+    """With one ``dx_recv`` buffer an owner that no source waits on can
+    overwrite it with the next (earlier) layer's input gradient while a
+    source still pulls the current layer's rows: source 0 routes to owner 1
+    in layer 1 but not in layer 0, so owner 1's layer-0 dgrad does not wait
+    for it."""
+    routes = [[[True, False], [True, True]],      # layer 0: 0 -> 0 only; 1 -> both
+              [[True, True], [True, True]]]       # layer 1: everyone -> everyone
+    with pytest.raises(ProtocolError):
+        explore(lambda: [ep_rank(r, 2, routes, 1, dx_buffers=1) for r in range(2)], schedules=200)
+    explore(lambda: [ep_rank(r, 2, routes, 1, dx_buffers=2) for r in range(2)], schedules=200)
