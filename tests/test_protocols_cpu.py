@@ -7,9 +7,12 @@ Each model restates, per rank, the order of kernel launches, flag channels,
 sequence numbers and buffer choices that the host code issues
 (``parallel/peer_dp.py`` for the ZeRO step, ``parallel/tp_fused.py`` for
 tensor + sequence parallelism, whose sequence bookkeeping is the real
-``TPComm.next_seq`` / ``parts_index``), and the loads and stores each kernel
-makes (``csrc/zero_comm.cu``, ``csrc/tp_comm.cu``, ``csrc/gemm.cu``).  A
-variant with a protocol step removed must be caught.
+``TPComm.next_seq`` / ``parts_index``, ``parallel/ep_fused.py`` for expert
+parallelism, ``parallel/context_parallel.py`` for context parallelism), and
+the loads and stores each kernel makes (``csrc/zero_comm.cu``,
+``csrc/tp_comm.cu``, ``csrc/gemm.cu``, ``csrc/ep_comm.cu``,
+``csrc/cp_comm.cu``).  A variant with a protocol step removed must be
+caught.
 """
 
 import pytest
@@ -315,3 +318,56 @@ def test_expert_parallel_single_dx_buffer_races():
     with pytest.raises(ProtocolError):
         explore(lambda: [ep_rank(r, 2, routes, 1, dx_buffers=1) for r in range(2)], schedules=200)
     explore(lambda: [ep_rank(r, 2, routes, 1, dx_buffers=2) for r in range(2)], schedules=200)
+
+
+# -------------------------------------------------------- context parallel
+
+
+def cp_rank(r: int, W: int, layers: int, steps: int, dkv_buffers: int = 2):
+    """One rank of context parallelism on the peer-memory kernels
+    (``parallel/context_parallel.py``, ``csrc/cp_comm.cu``): per layer the
+    rank stores its k|v rows into every rank's per-layer gathered buffer and
+    releases channel 0; its attention waits, per key block, for the owner's
+    flag (with the zigzag split every rank's later chunk sees every owner).
+    Backward: the rank's fp32 dk|dv partial for every key goes into its own
+    buffer (alternating by sequence number), channel 1 is released, and the
+    gather waits for every rank before summing the rows of its own tokens
+    from every rank's partial; the backward also re-reads the gathered k|v."""
+    seq = [0, 0]
+    for t in range(steps):
+        for layer in range(layers):
+            seq[0] += 1
+            s0 = seq[0]
+            for q in range(W):
+                yield ("write", q, ("kv", layer, r), ("kv", layer, r, t))
+            for q in range(W):
+                yield ("signal", q, 0, r, s0)
+            for o in range(W):
+                yield ("wait", 0, [o], s0)
+                yield ("read", ("kv", layer, o), ("kv", layer, o, t))
+        for layer in reversed(range(layers)):
+            for o in range(W):
+                yield ("read", ("kv", layer, o), ("kv", layer, o, t))
+            seq[1] += 1
+            s1 = seq[1]
+            slot = s1 % dkv_buffers
+            yield ("write", r, ("dkv", slot), ("dkv", layer, r, t))
+            for q in range(W):
+                yield ("signal", q, 1, r, s1)
+            yield ("wait", 1, range(W), s1)
+            for q in range(W):
+                yield ("read_peer", q, ("dkv", slot), ("dkv", layer, q, t))
+        yield ("collective", f"grads{t}")
+
+
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_context_parallel_protocol(W):
+    explore(lambda: [cp_rank(r, W, 3, 2) for r in range(W)], schedules=80)
+
+
+def test_context_parallel_single_dkv_buffer_races():
+    """The dk|dv partial buffers must alternate: with one buffer a fast rank
+    writes the next layer's partial while a slow rank still sums this
+    layer's rows from it."""
+    with pytest.raises(ProtocolError):
+        explore(lambda: [cp_rank(r, 4, 3, 2, dkv_buffers=1) for r in range(4)], schedules=150)
