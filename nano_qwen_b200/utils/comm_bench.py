@@ -2,6 +2,7 @@
 
     torchrun --nproc-per-node N -m nano_qwen_b200.utils.comm_bench [--numel 1.7e9]
     torchrun --nproc-per-node N -m nano_qwen_b200.utils.comm_bench --path ep
+    torchrun --nproc-per-node N -m nano_qwen_b200.utils.comm_bench --path tp   # or cp
 
 For a flat fp32 gradient of ``numel`` elements (default: the Qwen3-1.7B
 store) it times, with CUDA events and the max over ranks:
@@ -100,18 +101,110 @@ def ep_layer(iters: int, world: int, rank: int) -> None:
                   flush=True)
 
 
+def _one_layer_model(cfg, seed: int = 0):
+    from ..models import Qwen3Model
+    torch.manual_seed(seed)
+    with torch.device("cuda"):
+        m = Qwen3Model(cfg)
+    return m
+
+
+def tp_block(iters: int, world: int, rank: int, tokens: int = 65536, seq: int = 8192) -> None:
+    """One Qwen3-8B-shaped transformer block (vocabulary cut to 4096 so the
+    block dominates) under tensor + sequence parallelism over every rank,
+    forward + backward of ``tokens`` global tokens: the fused path (norms
+    all-gathering into peer memory, GEMMs waiting per row tile, reduce-scatter
+    epilogues) vs NCCL collectives.  Roofline: the slower of the block's
+    training FLOPs / world at the measured sustained bf16 peak and the NVLink
+    bytes into each GPU (two all-gathers and two reduce-scatters of the
+    [tokens, hidden] bf16 stream forward, the same backward:
+    8 x (W-1)/W x tokens x hidden x 2 bytes) at the link bandwidth."""
+    from ..config import ModelConfig
+    from ..parallel.manager import ParallelConfig, ParallelismManager
+    from ..training.optimizer import attach_param_store
+    from .flops import measured_peaks
+    cfg = ModelConfig(hidden_size=4096, num_hidden_layers=1, num_attention_heads=32,
+                      num_key_value_heads=8, head_dim=128, intermediate_size=12288, vocab_size=4096,
+                      max_position_embeddings=seq, rope_theta=1e6, tie_word_embeddings=True)
+    B = tokens // seq
+    peak = measured_peaks().get("bf16_tflops_sustained", 1392.0) * 1e12
+    flops = tokens * cfg.train_flops_per_token(seq) / world
+    link = 8 * (world - 1) / world * tokens * cfg.hidden_size * 2
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, cfg.vocab_size, (B, seq), generator=g).cuda()
+    for fused in (True, False):
+        pm = ParallelismManager(ParallelConfig(tp_size=world, tp_fused=None if fused else False))
+        m = pm.apply_parallelism(_one_layer_model(cfg))
+        attach_param_store(m)
+
+        def step():
+            out = m(ids, labels=ids)
+            out["loss"].backward()
+
+        t = _timed(step, iters)
+        if rank == 0:
+            t_roof = max(flops / peak, link / (LINK_GBS * 1e9))
+            print(json.dumps({"path": "tp block fwd+bwd (" + ("fused peer-memory" if getattr(m, "tp_fused", False)
+                                                              else "nccl") + ")",
+                              "n_gpus": world, "tokens": tokens, "ms": round(t * 1e3, 3),
+                              "roofline_ms": round(t_roof * 1e3, 3), "frac_of_roofline": round(t_roof / t, 3)}),
+                  flush=True)
+        del m
+        torch.cuda.empty_cache()
+
+
+def cp_layer(iters: int, world: int, rank: int, seq: int = 32768) -> None:
+    """One Qwen3-1.7B-shaped layer (vocabulary cut to 4096) over one
+    ``seq``-token sequence split by context parallelism over every rank,
+    forward + backward: gathered k|v by peer-memory stores (allgather) vs the
+    k|v ring.  Roofline: the slower of the training FLOPs / world at the
+    measured sustained bf16 peak and the NVLink bytes into each GPU (the
+    other ranks' k|v rows in bf16 forward, their fp32 dk|dv partials of this
+    rank's rows backward)."""
+    from ..config import ModelConfig
+    from ..parallel.manager import ParallelConfig, ParallelismManager
+    from ..training.optimizer import attach_param_store
+    from .flops import measured_peaks
+    cfg = ModelConfig(hidden_size=2048, num_hidden_layers=1, num_attention_heads=16,
+                      num_key_value_heads=8, head_dim=128, intermediate_size=6144, vocab_size=4096,
+                      max_position_embeddings=seq, rope_theta=1e6, tie_word_embeddings=True)
+    peak = measured_peaks().get("bf16_tflops_sustained", 1392.0) * 1e12
+    flops = seq * cfg.train_flops_per_token(seq) / world
+    kv_row = 2 * cfg.num_key_value_heads * cfg.head_dim
+    link = (world - 1) / world * seq * kv_row * (2 + 4)
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, cfg.vocab_size, (1, seq), generator=g).cuda()
+    for mode in ("allgather", "ring"):
+        pm = ParallelismManager(ParallelConfig(cp_size=world, cp_mode=mode))
+        m = pm.apply_parallelism(_one_layer_model(cfg))
+        attach_param_store(m)
+
+        def step():
+            out = m(ids, labels=ids)
+            out["loss"].backward()
+
+        t = _timed(step, iters)
+        if rank == 0:
+            t_roof = max(flops / peak, link / (LINK_GBS * 1e9))
+            print(json.dumps({"path": f"cp layer fwd+bwd ({mode})", "n_gpus": world, "seq": seq,
+                              "ms": round(t * 1e3, 3), "roofline_ms": round(t_roof * 1e3, 3),
+                              "frac_of_roofline": round(t_roof / t, 3)}), flush=True)
+        del m
+        torch.cuda.empty_cache()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--numel", type=float, default=1.72e9)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--path", default="dp", choices=["dp", "ep"])
+    ap.add_argument("--path", default="dp", choices=["dp", "ep", "tp", "cp"])
     a = ap.parse_args(argv)
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     world, rank = dist.get_world_size(), dist.get_rank()
-    if a.path == "ep":
-        ep_layer(a.iters, world, rank)
+    if a.path in ("ep", "tp", "cp"):
+        {"ep": ep_layer, "tp": tp_block, "cp": cp_layer}[a.path](a.iters, world, rank)
         dist.barrier()
         dist.destroy_process_group()
         return
