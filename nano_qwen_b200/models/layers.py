@@ -7,7 +7,6 @@ CPU tensors).
 
 from __future__ import annotations
 
-import math
 from typing import Optional, Sequence
 
 import torch

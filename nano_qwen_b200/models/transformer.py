@@ -14,7 +14,7 @@ caller asks for them (``return_logits`` / ``logits_to_keep``).
 
 from __future__ import annotations
 
-from typing import List, Optional, Tuple
+from typing import List, Optional
 
 import torch
 import torch.nn as nn
@@ -26,7 +26,7 @@ from ..utils.tracing import nvtx_range
 from .attention import Attention
 from .ffn import build_ffn
 from .kv_cache import KVCache
-from .layers import Linear, RMSNorm, fused_linear
+from .layers import Linear, RMSNorm
 from .moe import MoELayer
 
 

@@ -14,7 +14,7 @@ training/pretrain.py:172).
 
 from __future__ import annotations
 
-from typing import List, Optional, Sequence
+from typing import Optional, Sequence
 
 import torch
 

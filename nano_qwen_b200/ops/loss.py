@@ -16,13 +16,12 @@ materialised softmax and one-hot [BT, V]).
 
 from __future__ import annotations
 
-from typing import Optional
 
 import torch
 import torch.nn.functional as F
 
 from ._ext import ext
-from .common import grad_buffer, rows
+from .common import rows
 from .linear import WeightRef
 
 DEFAULT_CHUNK_ROWS = 8192

@@ -20,14 +20,13 @@ Replaces reference: model/moe.py:23-198 (a Python loop over experts with a
 
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import Optional
 
 import torch
 import torch.nn.functional as F
 
 from . import reference as ref
 from ._ext import ext
-from .common import grad_buffer
 from .linear import WeightRef
 
 PAD = 128

@@ -17,7 +17,7 @@ import torch.nn.functional as F
 
 from ._ext import ext
 from .common import grad_buffer, rows
-from .linear import WeightRef, linear
+from .linear import linear
 
 
 class _LayerNormFn(torch.autograd.Function):

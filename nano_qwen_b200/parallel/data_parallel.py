@@ -22,13 +22,13 @@ save.
 
 from __future__ import annotations
 
-from typing import List, Optional, Tuple
+from typing import Tuple
 
 import torch
 import torch.distributed as dist
 
 from ..runtime.flat_params import ALIGN, FlatParamStore
-from .comm import (all_gather_flat_, all_reduce_avg_, get_rank, get_world_size, is_dist,
+from .comm import (all_gather_flat_, all_reduce_avg_, get_rank, get_world_size,
                    reduce_scatter_avg_)
 
 

@@ -25,7 +25,7 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
-from .comm import get_rank, get_world_size, init_distributed, is_dist
+from .comm import init_distributed, is_dist
 
 
 @dataclass

@@ -24,15 +24,15 @@ ranks on one NVSwitch domain.
 from __future__ import annotations
 
 import importlib
-from typing import List, Optional
+from typing import List
 
 import torch
 import torch.distributed as dist
 
 from ..ops._ext import ext
 from ..runtime.flat_params import ALIGN, FlatParamStore
-from .comm import get_rank, get_world_size
-from .data_parallel import DataParallel, shard_bounds
+from .comm import get_world_size
+from .data_parallel import DataParallel
 
 
 def symmetric_available(group=None) -> bool:

@@ -29,14 +29,12 @@ from typing import Any, Dict, Optional
 import torch
 import torch.nn as nn
 
-from ..parallel.comm import barrier, get_rank, get_world_size, is_main_process
+from ..parallel.comm import barrier, get_rank, is_main_process
 
 try:
     import torch.distributed.checkpoint as dcp
     from torch.distributed.checkpoint.state_dict import (get_model_state_dict,
-                                                         get_optimizer_state_dict,
-                                                         set_model_state_dict,
-                                                         set_optimizer_state_dict)
+                                                         get_optimizer_state_dict)
     HAS_DCP = True
 except ImportError:  # pragma: no cover
     HAS_DCP = False

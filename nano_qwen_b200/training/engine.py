@@ -10,7 +10,7 @@ training/sft.py:197-240), which called ``loss.item()`` every micro-step.
 
 from __future__ import annotations
 
-from typing import Dict, Iterable, List, Optional
+from typing import Dict, List, Optional
 
 import torch
 import torch.nn as nn

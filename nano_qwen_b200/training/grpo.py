@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import copy
 import re
-from typing import Callable, Dict, List, Optional, Tuple
+from typing import Callable, List, Optional, Tuple
 
 import torch
 

@@ -12,7 +12,6 @@ Otherwise it falls back to ``torch.optim.AdamW``.
 
 from __future__ import annotations
 
-import math
 from typing import Optional, Tuple
 
 import torch

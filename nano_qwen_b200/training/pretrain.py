@@ -23,7 +23,7 @@ from ..data.collator import TextCollator
 from ..data.dataset import PackedTextDataset
 from ..data.sampler import DistributedSampler
 from ..models.transformer import Qwen3Model
-from ..parallel.comm import (get_local_rank, get_world_size, init_distributed, is_main_process,
+from ..parallel.comm import (get_local_rank, init_distributed, is_main_process,
                              max_over_ranks)
 from ..utils.flops import mfu
 from .checkpoint import CheckpointManager, resolve_resume

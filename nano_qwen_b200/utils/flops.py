@@ -3,7 +3,6 @@
 from __future__ import annotations
 
 import json
-import os
 from pathlib import Path
 
 # Nominal dense bf16 peak of one B200; used only when no measurement exists.
