@@ -24,6 +24,7 @@ ranks on one NVSwitch domain.
 from __future__ import annotations
 
 import importlib
+import os
 from typing import List
 
 import torch
@@ -35,10 +36,25 @@ from .comm import get_world_size
 from .data_parallel import DataParallel
 
 
+def same_node(ranks: List[int], local_world_size: int) -> bool:
+    """True when every global rank in ``ranks`` runs on one node, with
+    ``local_world_size`` consecutive ranks per node (torchrun's layout); an
+    unknown size (0) means a single-node launch."""
+    if local_world_size <= 0:
+        return True
+    return len({r // local_world_size for r in ranks}) == 1
+
+
 def symmetric_available(group=None) -> bool:
+    """Peer-memory kernels need NCCL ranks of one NVLink domain: 2, 4 or 8
+    ranks on the same node (a group that spans nodes falls back to NCCL)."""
     if not (torch.cuda.is_available() and dist.is_initialized()):
         return False
     if dist.get_backend(group) != "nccl" or get_world_size(group) not in (2, 4, 8):
+        return False
+    ranks = (dist.get_process_group_ranks(group) if group is not None
+             else list(range(dist.get_world_size())))
+    if not same_node(ranks, int(os.environ.get("LOCAL_WORLD_SIZE", "0") or 0)):
         return False
     try:
         importlib.import_module("torch.distributed._symmetric_memory")

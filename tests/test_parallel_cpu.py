@@ -106,3 +106,13 @@ def test_fully_sharded_with_expert_parallel(world, ep):
 @pytest.mark.parametrize("axis", ["tp_size", "cp_size"])
 def test_sft_takes_model_parallel_layouts(tmp_path, axis):
     _run(W.sft_parallel_worker, 2, str(tmp_path), axis)
+
+
+def test_peer_memory_groups_stay_on_one_node():
+    """Groups that span nodes (torchrun's consecutive local ranks) are not
+    given the peer-memory kernels."""
+    from nano_qwen_b200.parallel.peer_dp import same_node
+    assert same_node([0, 1, 2, 3], 8) and same_node([8, 9, 15], 8)
+    assert not same_node([6, 7, 8, 9], 8)
+    assert not same_node([0, 8], 8)       # an expert-data-parallel pair across nodes
+    assert same_node([0, 8, 16], 0)       # size unknown: single-node launch
