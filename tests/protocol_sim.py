@@ -13,7 +13,9 @@ interleaving (one operation of one runnable rank at a time):
 * ``("wait", channel, slots, seq)``: block until this rank's flags
   (channel, s) have reached ``seq`` for every s in ``slots``;
 * ``("collective", name)``: block until every rank has arrived (an NCCL
-  collective such as the gradient-norm all-reduce).
+  collective such as the gradient-norm all-reduce);
+* ``("record", name)`` / ``("wait_event", name)``: a CUDA event recorded on
+  one of the rank's streams and waited for on another.
 
 A kernel's stores are visible to a peer once the peer has observed the flag
 the kernel released after them, which is what the release/acquire pairs of
@@ -31,50 +33,62 @@ class ProtocolError(AssertionError):
     pass
 
 
-def run(ranks: List[Iterator], seed: int, max_ops: int = 1_000_000) -> Dict[str, int]:
+def run(actors: List, seed: int, max_ops: int = 1_000_000) -> Dict[str, int]:
+    """``actors``: one operation generator per rank, or (rank, generator)
+    pairs when a rank has several CUDA streams (each stream is an actor of
+    that rank; they share its memory, flags and events)."""
     rng = random.Random(seed)
-    world = len(ranks)
+    items = [a if isinstance(a, tuple) else (i, a) for i, a in enumerate(actors)]
+    rank_of = [rk for rk, _ in items]
+    gens = [g for _, g in items]
+    n = len(items)
+    world = len(set(rank_of))
     mem: Dict[Tuple[int, object], object] = {}
     flags: Dict[Tuple[int, object, int], int] = {}
+    events: set = set()
     arrived: Dict[str, set] = {}
-    pending: List[object] = [None] * world
-    done = [False] * world
+    pending: List[object] = [None] * n
+    done = [False] * n
     stats = {"ops": 0, "waits_blocked": 0}
 
-    def runnable(r: int) -> bool:
-        op = pending[r]
+    def runnable(i: int) -> bool:
+        op = pending[i]
         if op is None:
             return True
-        kind = op[0]
+        kind, r = op[0], rank_of[i]
         if kind == "wait":
             _, ch, slots, seq = op
             return all(flags.get((r, ch, s), 0) >= seq for s in slots)
         if kind == "collective":
             return len(arrived.get(op[1], ())) == world
+        if kind == "wait_event":
+            return (r, op[1]) in events
         return True
 
     for _ in range(max_ops):
-        live = [r for r in range(world) if not done[r]]
+        live = [i for i in range(n) if not done[i]]
         if not live:
             return stats
-        ready = [r for r in live if runnable(r)]
+        ready = [i for i in live if runnable(i)]
         if not ready:
-            raise ProtocolError("deadlock: " + ", ".join(f"rank {r} at {pending[r]}" for r in live))
-        r = rng.choice(ready)
-        op = pending[r]
+            raise ProtocolError("deadlock: " + ", ".join(
+                f"rank {rank_of[i]} (actor {i}) at {pending[i]}" for i in live))
+        i = rng.choice(ready)
+        r = rank_of[i]
+        op = pending[i]
         if op is None:
             try:
-                op = next(ranks[r])
+                op = next(gens[i])
             except StopIteration:
-                done[r] = True
+                done[i] = True
                 continue
-            pending[r] = op
+            pending[i] = op
             if op[0] == "collective":
                 arrived.setdefault(op[1], set()).add(r)
-            if not runnable(r):
+            if not runnable(i):
                 stats["waits_blocked"] += 1
                 continue
-        pending[r] = None
+        pending[i] = None
         stats["ops"] += 1
         kind = op[0]
         if kind == "write":
@@ -90,7 +104,9 @@ def run(ranks: List[Iterator], seed: int, max_ops: int = 1_000_000) -> Dict[str,
             _, dst, ch, slot, seq = op
             key = (dst, ch, slot)
             flags[key] = max(flags.get(key, 0), seq)
-        elif kind in ("wait", "collective"):
+        elif kind == "record":
+            events.add((r, op[1]))
+        elif kind in ("wait", "collective", "wait_event"):
             pass
         else:
             raise ValueError(op)

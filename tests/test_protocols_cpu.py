@@ -371,3 +371,103 @@ def test_context_parallel_single_dkv_buffer_races():
     layer's rows from it."""
     with pytest.raises(ProtocolError):
         explore(lambda: [cp_rank(r, 4, 3, 2, dkv_buffers=1) for r in range(4)], schedules=150)
+
+
+# ------------------------------------------- ZeRO step with overlapped RS
+
+
+def zero_overlap_rank(r: int, W: int, spans: int, steps: int, side_waits_block: bool = True):
+    """``PeerDataParallel.attach_overlap``: as each block's backward ends, the
+    main stream records an event and the side (communication) stream runs
+    ``zero_rs`` over that block's gradient span (flag slot 0, the sequence
+    number of the call, the same order on every rank); after the backward the
+    main stream waits for the side stream, reduces what remains (span
+    ``spans``: embedding, norms) itself, and runs the norm all-reduce,
+    ``zero_adamw_ag`` and ``zero_publish`` as in the plain step.  Returns the
+    (rank, main) and (rank, side) actors."""
+    calls = {"n": 0}
+    shared = {"epoch": 0}
+
+    def rs(span, seq):
+        for p in range(W):
+            yield ("signal", p, "zero0", r, seq)
+        yield ("wait", "zero0", range(W), seq)
+        for p in range(W):
+            yield ("read_peer", p, ("grad", span, r), ("g", p, span, shared["t"]))
+        yield ("write", r, ("grad", span, r), ("mean", span, shared["t"]))
+
+    def main():
+        for t in range(1, steps + 1):
+            shared["t"] = t
+            for sp in range(spans + 1):
+                for s in range(W):
+                    yield ("read", ("comp", sp, s), ("w", t - 1))     # forward
+            for sp in reversed(range(spans + 1)):                      # backward, last block first
+                for s in range(W):
+                    yield ("write", r, ("grad", sp, s), ("g", r, sp, t))
+                if sp < spans:
+                    yield ("record", ("block", t, sp))
+            yield ("wait_event", ("side_done", t))
+            base = shared["epoch"]
+            yield from rs(spans, base + spans + 1)                    # the remainder, on main
+            shared["epoch"] = base + spans + 1
+            yield ("collective", f"norm{t}")
+            for sp in range(spans + 1):
+                yield ("read", ("grad", sp, r), ("mean", sp, t))
+                for p in range(W):
+                    yield ("write", p, ("comp", sp, r), ("w", t))
+            for p in range(W):
+                yield ("signal", p, "zero1", r, t)
+            yield ("wait", "zero1", range(W), t)
+
+    def side():
+        for t in range(1, steps + 1):
+            base = (t - 1) * (spans + 1)
+            for k, sp in enumerate(reversed(range(spans))):           # hooks fire in backward order
+                if side_waits_block:
+                    yield ("wait_event", ("block", t, sp))
+                yield from rs(sp, base + k + 1)
+            yield ("record", ("side_done", t))
+
+    return [(r, main()), (r, side())]
+
+
+def _overlap(W, spans, steps, side_waits_block=True):
+    def make():
+        init = _init_zero_spans(W, spans)
+        out = []
+        for r in range(W):
+            (rm, m), (rs_, sd) = zero_overlap_rank(r, W, spans, steps, side_waits_block)
+
+            def chain(r=r, m=m):
+                yield from init(r)
+                yield from m
+
+            def side_after_init(r=r, sd=sd):
+                yield ("wait_event", "init")
+                yield from sd
+            out += [(r, chain()), (r, side_after_init())]
+        return out
+    return make
+
+
+def _init_zero_spans(W, spans):
+    def gen(r):
+        for sp in range(spans + 1):
+            for s in range(W):
+                yield ("write", r, ("comp", sp, s), ("w", 0))
+        yield ("collective", "init")
+        yield ("record", "init")
+    return gen
+
+
+@pytest.mark.parametrize("W", [2, 4])
+def test_zero_step_overlapped_reduce_scatter_protocol(W):
+    explore(_overlap(W, spans=3, steps=2), schedules=150)
+
+
+def test_overlapped_reduce_scatter_needs_the_block_event():
+    """A side-stream reduce-scatter that does not wait for its block's
+    backward reads a peer's gradient before the peer has written it."""
+    with pytest.raises(ProtocolError):
+        explore(_overlap(4, spans=3, steps=2, side_waits_block=False), schedules=150)
