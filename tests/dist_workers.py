@@ -689,3 +689,66 @@ def sft_parallel_worker(rank, world, port, tmp, axis):
     assert os.path.isdir("ck/step_00000002")
     if dist.is_initialized():
         dist.destroy_process_group()
+
+
+# ----------------------------------------------- peer-memory ZeRO host code
+def peer_dp_fake_worker(rank, world, port, tmp):
+    """The host code of the fused data-parallel step (``PeerDataParallel``:
+    epochs, shard bounds, the sharded moments, ``fused_step``, checkpointing)
+    on Gloo CPU ranks over a file-backed stand-in for symmetric memory and
+    restated kernels (``fake_peer``).  Against the NCCL-style ZeRO shard
+    engine on the same data: losses, norms and weights for three steps, then
+    a checkpoint that a fresh peer engine resumes exactly."""
+    init(rank, world, port)
+    import fake_peer
+    from nano_qwen_b200.parallel import peer_dp
+    from nano_qwen_b200.training import engine as engine_mod
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    from nano_qwen_b200.training.optimizer import attach_param_store
+
+    cur = {}
+
+    def make_alloc(group=None):
+        d = os.path.join(tmp, f"peer{len(cur)}")
+        os.makedirs(d, exist_ok=True)
+        a = fake_peer.FakeSymmetricAllocator(d, group)
+        cur["alloc"] = a
+        return a
+
+    peer_dp.symmetric_available = lambda group=None: True
+    peer_dp.SymmetricAllocator = make_alloc
+    peer_dp.ext = lambda: fake_peer.FakeZeroExt(cur["alloc"])
+    torch.cuda.synchronize = lambda *a, **k: None
+    cfg = tiny_cfg()
+    tc = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+          "scheduler": {"warmup_steps": 1, "total_steps": 20}}
+    ref = TrainEngine(build(cfg), tc, torch.device("cpu"), dp_mode="shard")
+    # the peer engines get a bf16 compute copy, as on the GPU (the CPU forward
+    # itself reads the fp32 master)
+    engine_mod.attach_param_store = lambda m, **kw: attach_param_store(m, torch.bfloat16, **kw)
+    a = TrainEngine(build(cfg), tc, torch.device("cpu"), dp_mode="p2p")
+    assert isinstance(a.dp, peer_dp.PeerDataParallel) and a.optimizer.sharded
+    data = [batch(cfg, 2, 16, seed=10 * s + rank) for s in range(5)]
+    for s in range(3):
+        r = ref.train_step([{"input_ids": data[s], "labels": data[s]}])
+        o = a.train_step([{"input_ids": data[s], "labels": data[s]}])
+        close(o["loss"], r["loss"], 1e-5, "loss")
+        close(o["grad_norm"], r["grad_norm"], 1e-5, "grad norm")
+        # the CPU forward reads the fp32 master, which the step updates only in
+        # this rank's shard (the GPU forward reads the all-gathered bf16 copy)
+        a.dp.gather_master()
+        close(a.store.master, ref.store.master, 1e-5, "master")
+        comp = a.store.compute.float()
+        assert torch.equal(comp, a.store.master.to(torch.bfloat16).float()), "compute copy"
+    mgr = CheckpointManager(save_dir=os.path.join(tmp, "ck"), async_save=False)
+    d = mgr.save(3, *a.state_for_save())
+    b = TrainEngine(build(cfg, seed=4), tc, torch.device("cpu"), dp_mode="p2p")
+    mgr.load(b.model, b.optimizer, b.scheduler, checkpoint_dir=str(d))
+    assert torch.equal(b.optimizer.exp_avg, a.optimizer.exp_avg)
+    assert torch.equal(b.optimizer.exp_avg_sq, a.optimizer.exp_avg_sq)
+    ra = a.train_step([{"input_ids": data[3], "labels": data[3]}])
+    rb = b.train_step([{"input_ids": data[3], "labels": data[3]}])
+    assert torch.equal(ra["loss"], rb["loss"]), (ra["loss"], rb["loss"])
+    dist.barrier()
+    dist.destroy_process_group()

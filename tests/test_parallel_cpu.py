@@ -116,3 +116,8 @@ def test_peer_memory_groups_stay_on_one_node():
     assert not same_node([6, 7, 8, 9], 8)
     assert not same_node([0, 8], 8)       # an expert-data-parallel pair across nodes
     assert same_node([0, 8, 16], 0)       # size unknown: single-node launch
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_memory_zero_host_code_on_fake_transport(tmp_path, world):
+    _run(W.peer_dp_fake_worker, world, str(tmp_path))
