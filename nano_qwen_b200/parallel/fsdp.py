@@ -72,21 +72,61 @@ def _set_storage(t: torch.Tensor, numel: int) -> None:
         st.resize_(nbytes)
 
 
+def partition(model: nn.Module):
+    """Group the trainable parameters into units: (blocks, per-block dense
+    fusion groups, per-block expert fusion groups, other decayed matrices,
+    non-decayed matrices, 1-D parameters)."""
+    from ..models.transformer import TransformerBlock
+    groups = [g for g in default_groups(model) if all(p.requires_grad for _, p in g)]
+    blocks = [m for m in model.modules() if isinstance(m, TransformerBlock)]
+    owner: Dict[int, int] = {}
+    for bi, blk in enumerate(blocks):
+        for p in blk.parameters():
+            owner.setdefault(id(p), bi)
+    per_block: List[list] = [[] for _ in blocks]
+    per_block_experts: List[list] = [[] for _ in blocks]
+    rest_decay, rest_nodecay, small = [], [], []
+    for grp in groups:
+        # a fusion group is homogeneous in rank and decay; split it if not
+        kinds = {(p.ndim <= 1, no_decay_rule(n, p), bool(getattr(p, "_ep_local", False)))
+                 for n, p in grp}
+        parts = [grp] if len(kinds) == 1 else [[item] for item in grp]
+        for part in parts:
+            n0, p0 = part[0]
+            expert = bool(getattr(p0, "_ep_local", False))
+            if expert and (p0.ndim <= 1 or no_decay_rule(n0, p0) or id(p0) not in owner):
+                raise NotImplementedError(f"expert-parallel parameter {n0} outside the "
+                                          "blocks' expert matrices")
+            if p0.ndim <= 1:
+                small.append(part)
+            elif no_decay_rule(n0, p0):
+                rest_nodecay.append(part)
+            elif expert:
+                per_block_experts[owner[id(p0)]].append(part)
+            elif id(p0) in owner:
+                per_block[owner[id(p0)]].append(part)
+            else:
+                rest_decay.append(part)
+    return blocks, per_block, per_block_experts, rest_decay, rest_nodecay, small
+
+
 class ParamUnit:
     """One flat buffer of parameters gathered and released together, sharded
     over its own process group (the data-parallel group; for expert-parallel
     experts the group of ranks that hold the same experts)."""
 
     def __init__(self, name: str, groups, dtype: torch.dtype, persistent: bool, decay: bool,
-                 group=None, grad_scale: float = 1.0, local: bool = False):
-        """``local``: not sharded (this rank alone holds these parameters)."""
+                 group=None, grad_scale: float = 1.0, local: bool = False,
+                 world: Optional[int] = None):
+        """``local``: not sharded (this rank alone holds these parameters).
+        ``world``: shard count to plan with, without a process group."""
         self.name = name
         self.dtype = dtype
         self.persistent = persistent
         self.decay = decay
         self.group = group
-        self.world = 1 if local else get_world_size(group)
-        self.rank = 0 if local else get_rank(group)
+        self.world = 1 if local else (world if world is not None else get_world_size(group))
+        self.rank = 0 if local else (0 if world is not None else get_rank(group))
         self.distributed = is_dist() and self.world > 1
         self.nccl = self.distributed and dist.get_backend(group) == "nccl"
         # multiplies the mean over ``group`` of the gradient (experts: the
@@ -225,7 +265,6 @@ class FullyShardedStore:
         """``expert_group``: under expert parallelism, the ranks that hold the
         same experts (one per expert-parallel block); each block's local
         experts form a unit sharded over it."""
-        from ..models.transformer import TransformerBlock
         self.model = model
         self.group = group
         self.world = get_world_size(group)
@@ -240,36 +279,7 @@ class FullyShardedStore:
         self.pinned = False
         self.final_micro = True
 
-        groups = [g for g in default_groups(model) if all(p.requires_grad for _, p in g)]
-        blocks = [m for m in model.modules() if isinstance(m, TransformerBlock)]
-        owner: Dict[int, int] = {}
-        for bi, blk in enumerate(blocks):
-            for p in blk.parameters():
-                owner.setdefault(id(p), bi)
-        per_block: List[list] = [[] for _ in blocks]
-        per_block_experts: List[list] = [[] for _ in blocks]
-        rest_decay, rest_nodecay, small = [], [], []
-        for grp in groups:
-            # a fusion group is homogeneous in rank and decay; split it if not
-            kinds = {(p.ndim <= 1, no_decay_rule(n, p), bool(getattr(p, "_ep_local", False)))
-                     for n, p in grp}
-            parts = [grp] if len(kinds) == 1 else [[item] for item in grp]
-            for part in parts:
-                n0, p0 = part[0]
-                expert = bool(getattr(p0, "_ep_local", False))
-                if expert and (p0.ndim <= 1 or no_decay_rule(n0, p0) or id(p0) not in owner):
-                    raise NotImplementedError(f"expert-parallel parameter {n0} outside the "
-                                              "blocks' expert matrices")
-                if p0.ndim <= 1:
-                    small.append(part)
-                elif no_decay_rule(n0, p0):
-                    rest_nodecay.append(part)
-                elif expert:
-                    per_block_experts[owner[id(p0)]].append(part)
-                elif id(p0) in owner:
-                    per_block[owner[id(p0)]].append(part)
-                else:
-                    rest_decay.append(part)
+        blocks, per_block, per_block_experts, rest_decay, rest_nodecay, small = partition(model)
         # the expert gradient's data-parallel mean: summed over the ranks
         # holding the same experts, divided by the data-parallel world
         # (no group: every expert set exists once, on this rank)
@@ -634,6 +644,41 @@ class FullyShardedStore:
         persistent = sum(u.padded * (u.full.element_size() + 4) for u in self.units if u.persistent)
         largest = max((u.padded * (u.full.element_size() + 4) for u in self.block_units), default=0)
         return {"shards": shard, "persistent_units": persistent, "largest_block_unit": largest}
+
+
+def memory_plan(model: nn.Module, world: int, compute_bytes: int = 2) -> Dict[str, float]:
+    """Bytes per rank of ``model`` (a meta-device model will do: nothing is
+    allocated) fully sharded over ``world`` ranks, next to the flat ZeRO-2
+    layout of ``FlatParamStore`` + ``FusedAdamW``:
+
+    * ``fsdp_state``: the shards (fp32 master and gradient, the compute copy
+      and the two fp32 Adam moments, 18 B per element with bf16);
+    * ``fsdp_persistent``: embedding / lm_head / 1-D units, gathered for a
+      step with their fp32 gradients;
+    * ``fsdp_blocks_peak``: two gathered block units (the running block and
+      the prefetched one) and one block's fp32 gradient;
+    * ``zero2_state``: full fp32 master, gradient and compute copy on every
+      rank, moments sharded."""
+    _, pb, pbe, rd, rn, small = partition(model)
+    units = []
+    for gs in pb + pbe:
+        if gs:
+            units.append(("block", ParamUnit("b", gs, torch.bfloat16, False, True, world=world)))
+    for kind, gs, fp32 in (("root", rd, False), ("root", rn, False), ("root", small, True)):
+        if gs:
+            units.append((kind, ParamUnit(kind, gs, torch.float32 if fp32 else torch.bfloat16, True,
+                                          True, world=world)))
+    shard = sum(u.per for _, u in units)
+    state = shard * (4 + 4 + compute_bytes + 8)
+    persistent = sum(u.padded * ((4 if u.dtype == torch.float32 else compute_bytes) + 4)
+                     for k, u in units if k == "root")
+    biggest = max((u.padded for k, u in units if k == "block"), default=0)
+    peak_blocks = biggest * (2 * compute_bytes + 4)
+    numel = sum(p.numel() for p in model.parameters() if p.requires_grad)
+    zero2 = numel * (4 + 4 + compute_bytes) + numel * 8 / world
+    return {"params": float(numel), "fsdp_state": float(state), "fsdp_persistent": float(persistent),
+            "fsdp_blocks_peak": float(peak_blocks),
+            "fsdp_total": float(state + persistent + peak_blocks), "zero2_state": float(zero2)}
 
 
 class FSDPAdamW(FusedAdamW):

@@ -260,3 +260,20 @@ def test_fully_sharded_single_process_matches_flat_store():
     fs.optimizer.release_full_state()
     mem = fs.store.memory_bytes()
     assert mem["shards"] > 0 and mem["largest_block_unit"] > 0
+
+
+def test_fully_sharded_memory_plan():
+    """The memory plan of the fully sharded layout (a meta-device model, no
+    allocation): the per-rank state falls with the world size (18 B per
+    element over the ranks, up to unit padding), below ZeRO-2's."""
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.parallel.fsdp import memory_plan
+    with torch.device("meta"):
+        m = Qwen3Model(ModelConfig(**dict(MODEL, hidden_size=256, intermediate_size=512,
+                                          vocab_size=4096, num_hidden_layers=4)))
+    one, eight = memory_plan(m, 1), memory_plan(m, 8)
+    n = one["params"]
+    assert abs(one["fsdp_state"] - 18 * n) < 0.05 * 18 * n
+    assert eight["fsdp_state"] < one["fsdp_state"] / 7
+    assert eight["fsdp_total"] < eight["zero2_state"]
