@@ -231,7 +231,7 @@ def heartbeat_worker(rank, world, port, dead_rank):
     init(rank, world, port)
     from nano_qwen_b200.utils.fault import HeartbeatMonitor, PeerFailure
     store = dist.distributed_c10d._get_default_store()
-    mon = HeartbeatMonitor(store, rank, world, interval_s=0.1, timeout_s=1.0)
+    mon = HeartbeatMonitor(store, rank, world, interval_s=0.1, timeout_s=2.0)
     mon.beat()
     if rank == dead_rank:
         return  # leaves between steps without further heartbeats (no collective in flight)
@@ -395,12 +395,15 @@ def rank_leave_worker(rank, world, port):
     from nano_qwen_b200.training.engine import TrainEngine
     from nano_qwen_b200.utils.fault import HeartbeatMonitor, PeerFailure
     store = dist.distributed_c10d._get_default_store()
-    hb = HeartbeatMonitor(store, rank, world, timeout_s=2.0, prefix="leave")
+    # the limit covers start-up skew between live ranks on a loaded machine
+    # (a live rank that misses it would be reported as departed)
+    hb = HeartbeatMonitor(store, rank, world, timeout_s=8.0, prefix="leave")
     cfg = tiny_cfg()
     eng = TrainEngine(build(cfg), {"optimizer": {"lr": 1e-3}, "scheduler": {"warmup_steps": 0}},
                       torch.device("cpu"), dp_mode="shard")
     ids = batch(cfg, 2, 16, seed=rank)
     leaver = world - 1
+    dist.barrier()
     for step in range(4):
         if rank == leaver and step == 2:
             os._exit(0)  # between steps: nothing in flight, no goodbye
