@@ -261,14 +261,22 @@ class FullyShardedStore:
 
     def __init__(self, model: nn.Module, group=None, compute_dtype: Optional[torch.dtype] = None,
                  device: Optional[torch.device] = None, reshard_after_forward: bool = True,
-                 expert_group=None):
+                 expert_group=None, tp_group=None, local: bool = False):
         """``expert_group``: under expert parallelism, the ranks that hold the
         same experts (one per expert-parallel block); each block's local
-        experts form a unit sharded over it."""
+        experts form a unit sharded over it.  ``tp_group``: under tensor
+        parallelism the units hold this rank's tensor shards (sharded again
+        over ``group``, the data-parallel ranks of the same tensor shard), and
+        the gradients of replicated parameters that are partial per tensor
+        rank (``_tp_reduce == "sum"``) are summed over ``tp_group`` before
+        each unit's reduce-scatter.  ``local``: one data-parallel replica (no
+        sharding of the dense units; ``group`` is ignored)."""
         self.model = model
+        self.tp_group = tp_group if (tp_group is not None and is_dist()
+                                     and get_world_size(tp_group) > 1) else None
         self.group = group
-        self.world = get_world_size(group)
-        self.rank = get_rank(group)
+        self.world = 1 if local else get_world_size(group)
+        self.rank = 0 if local else get_rank(group)
         dev = device or next(model.parameters()).device
         self.device = dev
         if compute_dtype is None:
@@ -292,7 +300,7 @@ class FullyShardedStore:
             parts = []
             if per_block[bi]:
                 parts.append(ParamUnit(f"layers.{bi}", per_block[bi], compute_dtype, keep, True,
-                                       group))
+                                       group, local=local))
             if per_block_experts[bi]:
                 parts.append(ParamUnit(f"layers.{bi}.experts", per_block_experts[bi], compute_dtype,
                                        keep, True, expert_group, grad_scale=e_scale,
@@ -307,12 +315,19 @@ class FullyShardedStore:
             a.next, b.prev = b, a
         self.block_units = [u for b in self.blocks for u in b.parts]
         if rest_decay:
-            units.append(ParamUnit("root_decay", rest_decay, compute_dtype, True, True, group))
+            units.append(ParamUnit("root_decay", rest_decay, compute_dtype, True, True, group,
+                                   local=local))
         if rest_nodecay:
-            units.append(ParamUnit("root_nodecay", rest_nodecay, compute_dtype, True, False, group))
+            units.append(ParamUnit("root_nodecay", rest_nodecay, compute_dtype, True, False, group,
+                                   local=local))
         if small:
-            units.append(ParamUnit("fp32_1d", small, torch.float32, True, False, group))
+            units.append(ParamUnit("fp32_1d", small, torch.float32, True, False, group,
+                                   local=local))
         self.units = units
+        for u in units:
+            u.tp_sum = ([(u.local[id(p)], p.numel()) for p in u.params
+                         if getattr(p, "_tp_reduce", "none") == "sum"]
+                        if self.tp_group is not None else [])
 
         soff = voff = 0
         self.decay_end = 0
@@ -505,16 +520,19 @@ class FullyShardedStore:
             return
         g = self.grad[u.soff:u.soff + u.per]
         if not u.distributed:
+            self._tp_sum(u)
             g.add_(u.gfull, alpha=u.grad_scale)
         elif u.nccl:
             side = self._rs_stream
             side.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(side):
+                self._tp_sum(u)
                 tmp = torch.empty(u.per, dtype=torch.float32, device=self.device)
                 dist.reduce_scatter_tensor(tmp, u.gfull, op=dist.ReduceOp.AVG, group=u.group)
                 g.add_(tmp, alpha=u.grad_scale)
             u.gfull.record_stream(side)
         else:
+            self._tp_sum(u)
             tmp = torch.empty(u.per, dtype=torch.float32, device=self.device)
             reduce_scatter_avg_(tmp, u.gfull, u.group)
             g.add_(tmp, alpha=u.grad_scale)
@@ -522,6 +540,27 @@ class FullyShardedStore:
             p.grad = None
         _set_storage(u.gfull, 0)
         u.grad_live = False
+
+    def _tp_sum(self, u: ParamUnit) -> None:
+        """Sum the partial gradients of tensor-replicated parameters over the
+        tensor-parallel group (one all-reduce per unit)."""
+        if not u.tp_sum:
+            return
+        flat = torch.cat([u.gfull[o:o + n] for o, n in u.tp_sum])
+        dist.all_reduce(flat, group=self.tp_group)
+        k = 0
+        for o, n in u.tp_sum:
+            u.gfull[o:o + n].copy_(flat[k:k + n])
+            k += n
+
+    def shard_slices(self, p: torch.Tensor) -> List[Tuple[int, int]]:
+        """Ranges of this rank's shard buffers that hold elements of ``p``."""
+        u = self.unit_of[id(p)]
+        v0 = u.local[id(p)]
+        v1 = v0 + p.numel()
+        a, b = u.rank * u.per, (u.rank + 1) * u.per
+        lo, hi = max(v0, a), min(v1, b)
+        return [(u.soff + lo - a, u.soff + hi - a)] if hi > lo else []
 
     # ------------------------------------------------- engine-facing hooks
     def begin_step(self, final_micro: bool) -> None:

@@ -69,7 +69,12 @@ class TrainEngine:
             self.tp_group = parallel.groups.get("tp")
             self.pp_group = parallel.groups.get("pp")
             expert_group = parallel.groups.get("edp")
-        world = get_world_size(dp_group)
+            # the manager leaves size-1 axes without a group: a None data-
+            # parallel group then means one replica, not the default group
+            world = len(parallel.ranks.get("dp_cp") or parallel.ranks.get("dp") or [0])
+        else:
+            world = get_world_size(dp_group)
+        self._dp_world = world
         dist_cfg = training_config.get("distributed", {}) or {}
         if dp_mode is None:
             if dist_cfg.get("shard_params", False):
@@ -119,10 +124,17 @@ class TrainEngine:
         per use (``parallel.fsdp``)."""
         from ..parallel.fsdp import FullyShardedStore, build_fsdp_optimizer
         if parallel is not None and any(int(getattr(parallel.config, k, 1)) > 1
-                                        for k in ("tp_size", "pp_size", "cp_size")):
-            raise ValueError("shard_params runs over data (and expert) parallelism: tp/pp/cp = 1")
+                                        for k in ("pp_size", "cp_size")):
+            raise ValueError("shard_params runs over data, expert and tensor parallelism: pp/cp = 1")
         expert_group = parallel.groups.get("edp") if parallel is not None else None
+        lm = getattr(self.model, "language_model", self.model)
+        if getattr(lm, "tp_fused", False):
+            # the fused TP kernels run their own block schedule over peer
+            # buffers; sharded blocks are gathered around the module path,
+            # whose TP collectives are NCCL's
+            lm.tp_fused = False
         self.store = FullyShardedStore(self.model, group=dp_group, expert_group=expert_group,
+                                       tp_group=self.tp_group, local=self._dp_world == 1,
                                        reshard_after_forward=dist_cfg.get("reshard_after_forward",
                                                                           True))
         self.dp = self.store
@@ -232,10 +244,14 @@ class TrainEngine:
         if self._dups:
             b, e = self.optimizer.shard
             for p in self._dups:
-                o = self.store.offsets[id(p)]
-                lo, hi = max(b, o), min(e, o + p.numel())
-                if hi > lo:
-                    sq = sq - self.store.grad[lo:hi].double().pow(2).sum().float()
+                if getattr(self.store, "mode", None) == "fsdp":
+                    ranges = self.store.shard_slices(p)
+                else:
+                    o = self.store.offsets[id(p)]
+                    ranges = [(max(b, o), min(e, o + p.numel()))]
+                for lo, hi in ranges:
+                    if hi > lo:
+                        sq = sq - self.store.grad[lo:hi].double().pow(2).sum().float()
         if self.dp is not None:
             sq = self.dp.norm_sq_reduce(sq)
         for g in (self.tp_group, self.pp_group):

@@ -755,3 +755,65 @@ def peer_dp_fake_worker(rank, world, port, tmp):
     assert torch.equal(ra["loss"], rb["loss"]), (ra["loss"], rb["loss"])
     dist.barrier()
     dist.destroy_process_group()
+
+
+def fsdp_tp_worker(rank, world, port, tp, moe):
+    """Fully sharded parameters with tensor (+ sequence) parallelism: the
+    tensor shards sharded again over the data-parallel ranks, partial
+    replicated gradients summed over the tensor group before each unit's
+    reduce-scatter, duplicates left out of the gradient norm; against the
+    ZeRO engine on the same tp x dp layout."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg(moe)
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+
+    def engine(shard):
+        pm = ParallelismManager(ParallelConfig(tp_size=tp, tp_fused=False))
+        m = pm.apply_parallelism(build(cfg))
+        return TrainEngine(m, dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"),
+                           parallel=pm), pm
+
+    (ref, pm), (fs, _) = engine(False), engine(True)
+    assert fs.store.mode == "fsdp" and fs.store.tp_group is not None
+    d = pm.coords["dp"]
+    for step in range(3):
+        ids = batch(cfg, 2 * (world // tp), 16, seed=400 + step)
+        mine = [{"input_ids": ids[2 * d:2 * d + 2], "labels": ids[2 * d:2 * d + 2]}]
+        r = ref.train_step(mine)
+        f = fs.train_step(mine)
+        close(f["loss"], r["loss"], 1e-5, "loss")
+        close(f["grad_norm"], r["grad_norm"], 1e-4, "grad norm")
+    ref.state_for_save()
+    fs.state_for_save()
+    for (n, p), (_, q) in zip(fs.model.named_parameters(), ref.model.named_parameters()):
+        close(p, q, 1e-5, n)
+    fs.optimizer.release_full_state()
+    dist.destroy_process_group()
+
+
+def tp_engine_worker(rank, world, port):
+    """A training engine under tensor parallelism over every rank (one data-
+    parallel replica): no data-parallel reduction runs (the manager has no
+    group for a size-1 axis, which must not mean the default group), and
+    three steps match the single-process engine on the same batch."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = tiny_cfg()
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    singles = [dist.new_group([r]) for r in range(world)]
+    ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_group=singles[rank])
+    pm = ParallelismManager(ParallelConfig(tp_size=world, tp_fused=False))
+    eng = TrainEngine(pm.apply_parallelism(build(cfg)), tcfg, torch.device("cpu"), parallel=pm)
+    assert eng.dp is None
+    for step in range(3):
+        ids = batch(cfg, 2, 16, seed=500 + step)
+        r = ref.train_step([{"input_ids": ids, "labels": ids}])
+        o = eng.train_step([{"input_ids": ids, "labels": ids}])
+        close(o["loss"], r["loss"], 1e-5, "loss")
+        close(o["grad_norm"], r["grad_norm"], 1e-4, "grad norm")
+    dist.destroy_process_group()

@@ -121,3 +121,12 @@ def test_peer_memory_groups_stay_on_one_node():
 @pytest.mark.parametrize("world", [2, 4])
 def test_peer_memory_zero_host_code_on_fake_transport(tmp_path, world):
     _run(W.peer_dp_fake_worker, world, str(tmp_path))
+
+
+@pytest.mark.parametrize("world,tp,moe", [(4, 2, False), (2, 2, False), (4, 2, True)])
+def test_fully_sharded_with_tensor_parallel(world, tp, moe):
+    _run(W.fsdp_tp_worker, world, tp, moe)
+
+
+def test_engine_under_pure_tensor_parallelism_matches_single():
+    _run(W.tp_engine_worker, 2)
