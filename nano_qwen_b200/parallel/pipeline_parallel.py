@@ -123,7 +123,16 @@ class PipelineParallel(nn.Module):
     # ------------------------------------------------------------- compute
     def _stage_forward(self, x_in: torch.Tensor, pos):
         m = self.model
-        resid = m.embed(x_in) if self.first else x_in
+        sp = getattr(m, "sp_group", None)
+        if self.first:
+            # under sequence parallelism a stage holds its TP rank's slice of
+            # the sequence, as ``Qwen3Model.hidden`` does
+            if sp is not None:
+                from .tensor_parallel import split_dim
+                x_in = split_dim(x_in, 1, sp)
+            resid = m.embed(x_in)
+        else:
+            resid = x_in
         delta, aux_total = None, None
         for layer in m.layers:
             resid, delta, aux = layer.forward_fused(resid, delta, pos, None, None, None)
@@ -151,6 +160,9 @@ class PipelineParallel(nn.Module):
         coef = self.config.router_aux_loss_coef / max(1, self.n_moe_total)
         dev = mbs[0]["input_ids"].device
         B, S = mbs[0]["input_ids"].shape
+        sp = getattr(self.model, "sp_group", None)
+        if sp is not None:  # activations between stages are the TP rank's sequence slice
+            S //= dist.get_world_size(sp)
         act_like = torch.empty(B, S, self.config.hidden_size, dtype=torch.float32, device=dev)
         saved_in: List[Optional[torch.Tensor]] = [None] * m
         saved_out: List = [None] * m
@@ -165,7 +177,11 @@ class PipelineParallel(nn.Module):
                 aux_sum.add_(aux.detach().float() * w)
             if self.last:
                 t = shift_targets(mbs[i]["labels"])
-                loss = ops.linear_cross_entropy(out, self.model.lm_head_ref(out.dtype), t) * w
+                if sp is not None:
+                    from ..models.transformer import _sp_loss
+                    loss = _sp_loss(out, self.model.lm_head_ref(out.dtype), t, sp) * w
+                else:
+                    loss = ops.linear_cross_entropy(out, self.model.lm_head_ref(out.dtype), t) * w
                 loss_sum.add_(loss.detach().float())
                 saved_out[i] = (loss if extra is None else loss + extra, None)
                 out = None

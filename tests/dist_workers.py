@@ -817,3 +817,41 @@ def tp_engine_worker(rank, world, port):
         close(o["loss"], r["loss"], 1e-5, "loss")
         close(o["grad_norm"], r["grad_norm"], 1e-4, "grad norm")
     dist.destroy_process_group()
+
+
+def layout_worker(rank, world, port, layout):
+    """The training engine on one parallel layout built by the
+    ``ParallelismManager`` (``layout``: ParallelConfig fields plus ``moe``
+    and ``shard_params``), three steps against the single-process engine on
+    the same global batch (the data-parallel ranks' slices as its
+    micro-batches): losses and gradient norms agree."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    layout = dict(layout)
+    moe = layout.pop("moe", False)
+    shard = layout.pop("shard_params", False)
+    # routing statistics are per rank under some layouts: compare without the aux term
+    cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4)
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}, "moe": {"global_batch_balance": False}}
+    singles = [dist.new_group([r]) for r in range(world)]
+    ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_group=singles[rank])
+    pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
+    eng = TrainEngine(pm.apply_parallelism(build(cfg)),
+                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"), parallel=pm)
+    dp = pm.config.dp_size
+    d = pm.coords["dp"]
+    B = 4
+    for step in range(3):
+        ids = batch(cfg, B * dp, 16, seed=600 + step)
+        full = [{"input_ids": ids[B * i:B * (i + 1)], "labels": ids[B * i:B * (i + 1)]} for i in range(dp)]
+        r = ref.train_step(full)
+        o = eng.train_step([full[d]])
+        # the engine reports its replica's loss; the mean over the replicas
+        # (every rank of a replica reports the same value) is the global one
+        loss = o["loss"].detach().clone()
+        dist.all_reduce(loss)
+        close(loss / world, r["loss"], 1e-5, f"loss step {step}")
+        close(o["grad_norm"], r["grad_norm"], 1e-4, f"grad norm step {step}")
+    dist.destroy_process_group()

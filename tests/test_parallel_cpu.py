@@ -130,3 +130,30 @@ def test_fully_sharded_with_tensor_parallel(world, tp, moe):
 
 def test_engine_under_pure_tensor_parallelism_matches_single():
     _run(W.tp_engine_worker, 2)
+
+
+LAYOUTS = {
+    "dp2": (2, {}),
+    "tp2": (2, {"tp_size": 2}),
+    "pp2": (2, {"pp_size": 2, "pp_microbatches": 2}),
+    "cp2": (2, {"cp_size": 2}),
+    "ep2-moe": (2, {"ep_size": 2, "moe": True}),
+    "tp2xdp2": (4, {"tp_size": 2}),
+    "pp2xdp2": (4, {"pp_size": 2, "pp_microbatches": 2}),
+    "tp2xdp2-fsdp": (4, {"tp_size": 2, "shard_params": True}),
+    "dp2-fsdp-moe": (2, {"moe": True, "shard_params": True}),
+    "cp2xdp2": (4, {"cp_size": 2}),
+    "cp2-ring": (2, {"cp_size": 2, "cp_mode": "ring"}),
+    "ep2xdp2-moe": (4, {"ep_size": 2, "moe": True}),
+    "ep2-fsdp-moe": (4, {"ep_size": 2, "moe": True, "shard_params": True}),
+    "tp2xpp2": (4, {"tp_size": 2, "pp_size": 2, "pp_microbatches": 2}),
+    "tp2xpp2-nosp": (4, {"tp_size": 2, "pp_size": 2, "pp_microbatches": 2, "sequence_parallel": False}),
+}
+
+
+@pytest.mark.parametrize("name", sorted(LAYOUTS))
+def test_engine_layouts_match_single_process(name):
+    """Every layout the manager builds trains like one process: the engine's
+    loss and gradient norm over three steps."""
+    world, layout = LAYOUTS[name]
+    _run(W.layout_worker, world, layout)
