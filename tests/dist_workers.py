@@ -831,6 +831,7 @@ def layout_worker(rank, world, port, layout):
     layout = dict(layout)
     moe = layout.pop("moe", False)
     shard = layout.pop("shard_params", False)
+    accum = layout.pop("accum", 1)
     # routing statistics are per rank under some layouts: compare without the aux term
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
@@ -845,9 +846,11 @@ def layout_worker(rank, world, port, layout):
     B = 4
     for step in range(3):
         ids = batch(cfg, B * dp, 16, seed=600 + step)
-        full = [{"input_ids": ids[B * i:B * (i + 1)], "labels": ids[B * i:B * (i + 1)]} for i in range(dp)]
+        c = B // accum
+        full = [{"input_ids": ids[c * i:c * (i + 1)], "labels": ids[c * i:c * (i + 1)]}
+                for i in range(dp * accum)]
         r = ref.train_step(full)
-        o = eng.train_step([full[d]])
+        o = eng.train_step(full[d * accum:(d + 1) * accum])
         # the engine reports its replica's loss; the mean over the replicas
         # (every rank of a replica reports the same value) is the global one
         loss = o["loss"].detach().clone()

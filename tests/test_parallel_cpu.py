@@ -148,6 +148,16 @@ LAYOUTS = {
     "ep2-fsdp-moe": (4, {"ep_size": 2, "moe": True, "shard_params": True}),
     "tp2xpp2": (4, {"tp_size": 2, "pp_size": 2, "pp_microbatches": 2}),
     "tp2xpp2-nosp": (4, {"tp_size": 2, "pp_size": 2, "pp_microbatches": 2, "sequence_parallel": False}),
+    "tp2xcp2-nosp": (4, {"tp_size": 2, "cp_size": 2, "sequence_parallel": False}),
+    "cp2-moe": (2, {"cp_size": 2, "moe": True}),
+    "pp2-moe": (2, {"pp_size": 2, "pp_microbatches": 2, "moe": True}),
+    "pp2xep2-moe": (4, {"pp_size": 2, "pp_microbatches": 2, "ep_size": 2, "moe": True}),
+    "tp2-moe": (2, {"tp_size": 2, "moe": True}),
+    "tp2xep2-moe": (4, {"tp_size": 2, "ep_size": 2, "moe": True, "sequence_parallel": False}),
+    "dp2-accum2": (2, {"accum": 2}),
+    "tp2xdp2-fsdp-accum2": (4, {"tp_size": 2, "shard_params": True, "accum": 2}),
+    "ep2-fsdp-moe-accum2": (2, {"ep_size": 2, "moe": True, "shard_params": True, "accum": 2}),
+    "cp2xdp2-accum2": (4, {"cp_size": 2, "accum": 2}),
 }
 
 
