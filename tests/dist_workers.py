@@ -858,3 +858,55 @@ def layout_worker(rank, world, port, layout):
         close(loss / world, r["loss"], 1e-5, f"loss step {step}")
         close(o["grad_norm"], r["grad_norm"], 1e-4, f"grad norm step {step}")
     dist.destroy_process_group()
+
+
+def layout_ckpt_worker(rank, world, port, layout, tmp, from_single=False):
+    """A checkpoint written by an engine on any manager layout loads into the
+    single-process engine, which then continues exactly like the layout
+    engine: two more steps with equal losses and gradient norms (weights,
+    Adam moments and step counts all carried over)."""
+    init(rank, world, port)
+    from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+    from nano_qwen_b200.training.checkpoint import CheckpointManager
+    from nano_qwen_b200.training.engine import TrainEngine
+    layout = dict(layout)
+    moe = layout.pop("moe", False)
+    shard = layout.pop("shard_params", False)
+    cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4)
+    tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+            "scheduler": {"warmup_steps": 0, "total_steps": 10}, "moe": {"global_batch_balance": False}}
+    singles = [dist.new_group([r]) for r in range(world)]
+    pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
+    eng = TrainEngine(pm.apply_parallelism(build(cfg)),
+                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"), parallel=pm)
+    dp, d, B = pm.config.dp_size, pm.coords["dp"], 4
+
+    def data(step):
+        ids = batch(cfg, B * dp, 16, seed=700 + step)
+        return [{"input_ids": ids[B * i:B * (i + 1)], "labels": ids[B * i:B * (i + 1)]} for i in range(dp)]
+
+    one = TrainEngine(build(cfg, seed=11), tcfg, torch.device("cpu"), dp_group=singles[rank])
+    mgr = CheckpointManager(save_dir=os.path.join(tmp, "ck"), async_save=False)
+    if from_single:   # the other direction: one process writes, the layout reads
+        for step in range(2):
+            one.train_step(data(step))
+        # every rank holds the same single-process state; DCP writes it once
+        path = mgr.save(2, *one.state_for_save(), extra_state={"step": 2})
+        mgr.load(eng.model, eng.optimizer, eng.scheduler, str(path))
+        assert eng.optimizer.step_count == 2
+    else:
+        for step in range(2):
+            eng.train_step([data(step)[d]])
+        path = mgr.save(2, *eng.state_for_save(), extra_state={"step": 2})
+        mgr.load(one.model, one.optimizer, one.scheduler, str(path))
+        assert one.optimizer.step_count == 2
+    for step in (2, 3):
+        full = data(step)
+        r = one.train_step(full)
+        o = eng.train_step([full[d]])
+        loss = o["loss"].detach().clone()
+        dist.all_reduce(loss)
+        close(loss / world, r["loss"], 1e-5, f"loss step {step}")
+        close(o["grad_norm"], r["grad_norm"], 1e-4, f"grad norm step {step}")
+    dist.barrier()
+    dist.destroy_process_group()

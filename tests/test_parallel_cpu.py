@@ -167,3 +167,18 @@ def test_engine_layouts_match_single_process(name):
     loss and gradient norm over three steps."""
     world, layout = LAYOUTS[name]
     _run(W.layout_worker, world, layout)
+
+
+CKPT_LAYOUTS = ["dp2", "tp2", "pp2", "ep2-moe", "tp2xdp2-fsdp", "ep2-fsdp-moe", "tp2xpp2", "cp2"]
+
+
+@pytest.mark.parametrize("name", CKPT_LAYOUTS)
+def test_layout_checkpoints_resume_in_one_process(tmp_path, name):
+    world, layout = LAYOUTS[name]
+    _run(W.layout_ckpt_worker, world, layout, str(tmp_path))
+
+
+@pytest.mark.parametrize("name", CKPT_LAYOUTS)
+def test_single_process_checkpoint_resumes_in_layouts(tmp_path, name):
+    world, layout = LAYOUTS[name]
+    _run(W.layout_ckpt_worker, world, layout, str(tmp_path), True)
