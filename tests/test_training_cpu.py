@@ -277,3 +277,32 @@ def test_fully_sharded_memory_plan():
     assert abs(one["fsdp_state"] - 18 * n) < 0.05 * 18 * n
     assert eight["fsdp_state"] < one["fsdp_state"] / 7
     assert eight["fsdp_total"] < eight["zero2_state"]
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_cached_generation_paths_match_full_forward_on_cpu(moe):
+    """The three inference paths agree with one full forward (fp32, CPU):
+    the model with a growing KV cache, and the static-cache decode step the
+    generator uses (prefill, then one token at a time at the right
+    positions), batch of two."""
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.eval.generate import DecodeState, decode_step, prefill
+    from nano_qwen_b200.models import KVCache, Qwen3Model
+    torch.manual_seed(0)
+    extra = dict(num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32) if moe else {}
+    cfg = ModelConfig(**dict(MODEL, **extra))
+    m = Qwen3Model(cfg).eval()
+    ids = torch.randint(0, cfg.vocab_size, (2, 24))
+    with torch.no_grad():
+        full = m(ids, return_logits=True)["logits"]
+        caches = [KVCache() for _ in range(cfg.num_hidden_layers)]
+        steps = [m(ids[:, :16], kv_caches=caches, return_logits=True)["logits"][:, -1]]
+        for t in range(16, 23):
+            steps.append(m(ids[:, t:t + 1], kv_caches=caches, return_logits=True)["logits"][:, -1])
+        torch.testing.assert_close(torch.stack(steps, 1), full[:, 15:23], rtol=1e-4, atol=1e-4)
+        st = DecodeState(m, 2, 32, torch.device("cpu"), torch.float32)
+        got = [prefill(m, st, ids[:, :16])]
+        for t in range(16, 23):
+            st.ids.copy_(ids[:, t:t + 1])
+            got.append(decode_step(m, st))
+        torch.testing.assert_close(torch.stack(got, 1), full[:, 15:23].float(), rtol=1e-4, atol=1e-4)
