@@ -272,3 +272,58 @@ def test_dpo_loss_matches_reference(dcfg):
     r_lab[:, :6] = -100
     lm, _ = b.dpo_loss(c_ids, r_ids, c_lab, r_lab)
     assert torch.isfinite(lm)
+
+
+@pytest.mark.skipif(not HAS_REF, reason="reference copy not present")
+def test_evaluator_and_reward_model_match_reference():
+    """Perplexity, multiple-choice scoring and the reward model's
+    Bradley-Terry loss against the reference's on the same weights."""
+    RC, RM = _ref_import()
+    from eval.evaluate import Evaluator as RefEval
+    from training.reward_model import RewardModel as RefRM
+
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.data.tokenizer import Tokenizer
+    from nano_qwen_b200.eval.evaluate import Evaluator
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.reward_model import RewardModel
+    torch.manual_seed(0)
+    cfg = dict(TINY, vocab_size=300)
+    ref = RM(RC(**cfg)).eval()
+    ours = Qwen3Model(ModelConfig(**cfg)).eval()
+    ours.load_state_dict(ref.state_dict())
+    tok = Tokenizer(backend="bytes")
+    g = torch.Generator().manual_seed(2)
+    batches = []
+    for _ in range(3):
+        ids = torch.randint(0, 256, (2, 20), generator=g)
+        lab = ids.clone()
+        lab[:, :3] = -100
+        batches.append({"input_ids": ids, "labels": lab})
+    dev = torch.device("cpu")
+    with torch.no_grad():
+        pa = RefEval(ref, tok, dev).compute_perplexity(batches)
+        pb = Evaluator(ours, tok, dev).compute_perplexity(batches)
+    assert abs(pa - pb) < 1e-3 * pa, (pa, pb)
+    qs = [{"prompt": f"question {i}?", "choices": ["alpha", "beta", "gamma", "delta"], "answer": i % 4}
+          for i in range(4)]
+    ra = RefEval(ref, tok, dev).eval_multiple_choice(qs)
+    rb = Evaluator(ours, tok, dev).eval_multiple_choice(qs)
+    assert ra["correct"] == rb["correct"] and ra["total"] == rb["total"], (ra, rb)
+    rr = RefRM(RC(**cfg))
+    rm = RewardModel(ModelConfig(**cfg))
+    missing, unexpected = rm.load_state_dict(rr.state_dict(), strict=False)
+    assert not unexpected and all("lm_head" in k for k in missing), (missing, unexpected)
+    c, r = torch.randint(0, 256, (3, 16), generator=g), torch.randint(0, 256, (3, 16), generator=g)
+    # (the reference's attention cannot take a [B, S] padding mask, so the
+    # comparison pools the last position of unpadded rows)
+    la = rr.compute_preference_loss(c, r)["loss"]
+    lb = rm.compute_preference_loss(c, r)["loss"]
+    assert torch.allclose(la, lb, atol=1e-5, rtol=1e-5), (float(la), float(lb))
+    # ours takes right-padded rows: the last real token is pooled
+    mask = torch.ones(3, 16, dtype=torch.long)
+    mask[0, 12:] = 0
+    padded = rm.compute_preference_loss(c, r, mask, mask)
+    trimmed = rm(c[:1, :12])
+    assert torch.allclose(rm(c, mask)[0], trimmed[0], atol=1e-5), "pooling of a padded row"
+    assert torch.isfinite(padded["loss"])
