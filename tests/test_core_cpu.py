@@ -327,3 +327,20 @@ def test_evaluator_and_reward_model_match_reference():
     trimmed = rm(c[:1, :12])
     assert torch.allclose(rm(c, mask)[0], trimmed[0], atol=1e-5), "pooling of a padded row"
     assert torch.isfinite(padded["loss"])
+
+
+@pytest.mark.skipif(not HAS_REF, reason="reference copy not present")
+def test_grpo_reward_and_advantages_match_reference():
+    """The verifiable math reward (\\boxed{}, '####', last number) and the
+    group-normalised advantages against the reference's."""
+    _ref_import()
+    from training.grpo import GRPO as RefGRPO, _math_reward_fn as ref_reward
+
+    from nano_qwen_b200.training.grpo import GRPO, _math_reward_fn
+    responses = ["so the answer is \\\\boxed{42}", "#### 41", "I think 42.0", "no idea", "x = -3",
+                 "\\\\boxed{forty-two}", "12 then 42", ""]
+    for gt in ("42", "#### 42", "\\\\boxed{-3}", "forty-two", None):
+        assert _math_reward_fn(responses, gt) == ref_reward(responses, gt), gt
+    rewards = torch.tensor([1.0, 0.0, 1.0, 0.0, 0.0, 1.0])
+    ref_adv = RefGRPO.compute_advantages(None, rewards)   # a method that uses no state
+    assert torch.allclose(GRPO.compute_advantages(rewards), ref_adv, atol=1e-6)
