@@ -344,3 +344,18 @@ def test_grpo_reward_and_advantages_match_reference():
     rewards = torch.tensor([1.0, 0.0, 1.0, 0.0, 0.0, 1.0])
     ref_adv = RefGRPO.compute_advantages(None, rewards)   # a method that uses no state
     assert torch.allclose(GRPO.compute_advantages(rewards), ref_adv, atol=1e-6)
+
+
+@pytest.mark.skipif(not HAS_REF, reason="reference copy not present")
+def test_chat_format_matches_reference():
+    """The SFT chat template (thinking, empty thinking, plain) is the
+    reference's text exactly: checkpoints trained on either format the same
+    prompts."""
+    _ref_import()
+    from training.sft import format_conversation as ref_fmt
+
+    from nano_qwen_b200.training.sft import format_conversation
+    for reasoning in ("step 1\nstep 2", None):
+        for think in (True, False):
+            args = ("be brief", "What is 2+2?", "4", reasoning, think)
+            assert format_conversation(*args) == ref_fmt(*args)
