@@ -123,9 +123,9 @@ class TrainEngine:
         weights, gradients and Adam moments sharded, block weights gathered
         per use (``parallel.fsdp``)."""
         from ..parallel.fsdp import FullyShardedStore, build_fsdp_optimizer
-        if parallel is not None and any(int(getattr(parallel.config, k, 1)) > 1
-                                        for k in ("pp_size", "cp_size")):
-            raise ValueError("shard_params runs over data, expert and tensor parallelism: pp/cp = 1")
+        if parallel is not None and int(getattr(parallel.config, "pp_size", 1)) > 1:
+            raise ValueError("shard_params runs over data, expert, tensor and context "
+                             "parallelism: pp = 1")
         expert_group = parallel.groups.get("edp") if parallel is not None else None
         lm = getattr(self.model, "language_model", self.model)
         if getattr(lm, "tp_fused", False):

@@ -158,6 +158,9 @@ LAYOUTS = {
     "tp2xdp2-fsdp-accum2": (4, {"tp_size": 2, "shard_params": True, "accum": 2}),
     "ep2-fsdp-moe-accum2": (2, {"ep_size": 2, "moe": True, "shard_params": True, "accum": 2}),
     "cp2xdp2-accum2": (4, {"cp_size": 2, "accum": 2}),
+    "cp2-fsdp": (2, {"cp_size": 2, "shard_params": True}),
+    "cp2xdp2-fsdp": (4, {"cp_size": 2, "shard_params": True}),
+    "cp2-ring-fsdp-moe": (2, {"cp_size": 2, "cp_mode": "ring", "shard_params": True, "moe": True}),
 }
 
 
@@ -169,7 +172,8 @@ def test_engine_layouts_match_single_process(name):
     _run(W.layout_worker, world, layout)
 
 
-CKPT_LAYOUTS = ["dp2", "tp2", "pp2", "ep2-moe", "tp2xdp2-fsdp", "ep2-fsdp-moe", "tp2xpp2", "cp2"]
+CKPT_LAYOUTS = ["dp2", "tp2", "pp2", "ep2-moe", "tp2xdp2-fsdp", "ep2-fsdp-moe", "tp2xpp2", "cp2",
+                "cp2-fsdp"]
 
 
 @pytest.mark.parametrize("name", CKPT_LAYOUTS)
