@@ -62,6 +62,9 @@ class PipelineParallel(nn.Module):
             # own copy of the shared matrix on the last stage (the first stage's
             # values arrive with the initial broadcast below)
             model.lm_head.weight = nn.Parameter(model.embed.embed_tokens.weight.detach().clone())
+            # the copy follows the embedding's optimizer rule (no weight
+            # decay), or the two stages' copies drift apart
+            model.lm_head.weight._no_decay = True
         if not self.first:
             model.embed = None
         if not self.last:
@@ -117,12 +120,17 @@ class PipelineParallel(nn.Module):
             else:
                 p.data.copy_(self._p2p(recv_like=p.data, recv_from=peer))
             return
-        other = self._p2p(send=p.grad, send_to=peer, recv_like=p.grad, recv_from=peer)
-        p.grad.add_(other)
+        store = getattr(p, "_nq_store", None)
+        g = store.grad_of(p) if hasattr(store, "grad_of") else p.grad
+        other = self._p2p(send=g, send_to=peer, recv_like=g, recv_from=peer)
+        g.add_(other)
 
     # ------------------------------------------------------------- compute
     def _stage_forward(self, x_in: torch.Tensor, pos):
         m = self.model
+        gather = getattr(self, "param_gather", None) or getattr(m, "param_gather", None)
+        if gather is not None:  # fully sharded: embedding / lm_head / norms gathered
+            gather()
         sp = getattr(m, "sp_group", None)
         if self.first:
             # under sequence parallelism a stage holds its TP rank's slice of

@@ -31,8 +31,11 @@ ALIGN = 64
 
 
 def no_decay_rule(name: str, p: torch.Tensor) -> bool:
-    """The reference's no-decay rule (training/optimizer.py:40-43)."""
-    return p.ndim <= 1 or "norm" in name or "bias" in name or "embed" in name
+    """The reference's no-decay rule (training/optimizer.py:40-43); a
+    parameter may also be marked ``_no_decay`` (the last pipeline stage's
+    copy of a tied embedding)."""
+    return (p.ndim <= 1 or "norm" in name or "bias" in name or "embed" in name
+            or bool(getattr(p, "_no_decay", False)))
 
 
 def default_groups(model: nn.Module) -> List[List[Tuple[str, nn.Parameter]]]:

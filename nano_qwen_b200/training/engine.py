@@ -123,9 +123,6 @@ class TrainEngine:
         weights, gradients and Adam moments sharded, block weights gathered
         per use (``parallel.fsdp``)."""
         from ..parallel.fsdp import FullyShardedStore, build_fsdp_optimizer
-        if parallel is not None and int(getattr(parallel.config, "pp_size", 1)) > 1:
-            raise ValueError("shard_params runs over data, expert, tensor and context "
-                             "parallelism: pp = 1")
         expert_group = parallel.groups.get("edp") if parallel is not None else None
         lm = getattr(self.model, "language_model", self.model)
         if getattr(lm, "tp_fused", False):
@@ -188,6 +185,8 @@ class TrainEngine:
         aux_sum = None
         if hasattr(self.model, "pipeline_forward_backward") and loss_fn is None:
             loss_sum, aux_sum = self.model.pipeline_forward_backward(micro_batches)
+            if hasattr(self.dp, "finish_backward"):
+                self.dp.finish_backward()
         else:
             for i, mb in enumerate(micro_batches):
                 if hasattr(self.dp, "begin_step"):

@@ -832,8 +832,9 @@ def layout_worker(rank, world, port, layout):
     moe = layout.pop("moe", False)
     shard = layout.pop("shard_params", False)
     accum = layout.pop("accum", 1)
+    tied = layout.pop("tied", False)
     # routing statistics are per rank under some layouts: compare without the aux term
-    cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4)
+    cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4, tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
             "scheduler": {"warmup_steps": 0, "total_steps": 10}, "moe": {"global_batch_balance": False}}
     singles = [dist.new_group([r]) for r in range(world)]

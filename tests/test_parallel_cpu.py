@@ -161,6 +161,12 @@ LAYOUTS = {
     "cp2-fsdp": (2, {"cp_size": 2, "shard_params": True}),
     "cp2xdp2-fsdp": (4, {"cp_size": 2, "shard_params": True}),
     "cp2-ring-fsdp-moe": (2, {"cp_size": 2, "cp_mode": "ring", "shard_params": True, "moe": True}),
+    "pp2-fsdp": (2, {"pp_size": 2, "pp_microbatches": 2, "shard_params": True}),
+    "pp2xdp2-fsdp": (4, {"pp_size": 2, "pp_microbatches": 2, "shard_params": True}),
+    "pp2-tied": (2, {"pp_size": 2, "pp_microbatches": 2, "tied": True}),
+    "pp2-fsdp-tied": (2, {"pp_size": 2, "pp_microbatches": 2, "shard_params": True, "tied": True}),
+    "dp2-fsdp-tied": (2, {"shard_params": True, "tied": True}),
+    "tp2-tied": (2, {"tp_size": 2, "tied": True}),
 }
 
 
