@@ -833,10 +833,15 @@ def layout_worker(rank, world, port, layout):
     shard = layout.pop("shard_params", False)
     accum = layout.pop("accum", 1)
     tied = layout.pop("tied", False)
-    # routing statistics are per rank under some layouts: compare without the aux term
-    cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4, tie_word_embeddings=tied)
+    # routing statistics are per rank under most layouts: compare without the
+    # aux term, except for the global-batch balance, whose statistics are the
+    # full batch's (then the reference runs the full batch as one micro-batch)
+    balance = layout.pop("balance", False)
+    cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=4,
+                   tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
-            "scheduler": {"warmup_steps": 0, "total_steps": 10}, "moe": {"global_batch_balance": False}}
+            "scheduler": {"warmup_steps": 0, "total_steps": 10},
+            "moe": {"global_batch_balance": balance}}
     singles = [dist.new_group([r]) for r in range(world)]
     ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_group=singles[rank])
     pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
@@ -850,7 +855,10 @@ def layout_worker(rank, world, port, layout):
         c = B // accum
         full = [{"input_ids": ids[c * i:c * (i + 1)], "labels": ids[c * i:c * (i + 1)]}
                 for i in range(dp * accum)]
-        r = ref.train_step(full)
+        if balance:
+            r = ref.train_step([{"input_ids": ids, "labels": ids}])
+        else:
+            r = ref.train_step(full)
         o = eng.train_step(full[d * accum:(d + 1) * accum])
         # the engine reports its replica's loss; the mean over the replicas
         # (every rank of a replica reports the same value) is the global one

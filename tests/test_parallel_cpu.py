@@ -167,6 +167,9 @@ LAYOUTS = {
     "pp2-fsdp-tied": (2, {"pp_size": 2, "pp_microbatches": 2, "shard_params": True, "tied": True}),
     "dp2-fsdp-tied": (2, {"shard_params": True, "tied": True}),
     "tp2-tied": (2, {"tp_size": 2, "tied": True}),
+    "dp2-moe-balance": (2, {"moe": True, "balance": True}),
+    "ep2-moe-balance": (2, {"ep_size": 2, "moe": True, "balance": True}),
+    "dp2-fsdp-moe-balance": (2, {"moe": True, "balance": True, "shard_params": True}),
 }
 
 
