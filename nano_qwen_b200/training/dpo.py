@@ -34,7 +34,8 @@ def sequence_logprobs(model, ids: torch.Tensor, labels: torch.Tensor) -> torch.T
 
 
 class DPOTrainer:
-    def __init__(self, policy_model, ref_model, config: dict, device: torch.device):
+    def __init__(self, policy_model, ref_model, config: dict, device: torch.device, dp_group=None):
+        """``dp_group``: the data-parallel ranks (default: every rank)."""
         dcfg = config.get("dpo", {}) or {}
         self.beta = dcfg.get("beta", 0.1)
         self.label_smoothing = dcfg.get("label_smoothing", 0.0)
@@ -46,7 +47,7 @@ class DPOTrainer:
         sch.setdefault("warmup_steps", 50)
         sch.setdefault("total_steps", 2000)
         cfg["scheduler"] = sch
-        self.engine = TrainEngine(policy_model, cfg, device)
+        self.engine = TrainEngine(policy_model, cfg, device, dp_group=dp_group)
         self.policy = self.engine.model
         self.optimizer = self.engine.optimizer
         self.scheduler = self.engine.scheduler

@@ -919,3 +919,30 @@ def layout_ckpt_worker(rank, world, port, layout, tmp, from_single=False):
         close(o["grad_norm"], r["grad_norm"], 1e-4, f"grad norm step {step}")
     dist.barrier()
     dist.destroy_process_group()
+
+
+def dpo_layout_worker(rank, world, port, shard):
+    """DPO over two data-parallel ranks (ZeRO or fully sharded) against one
+    process on all pairs: per-step gradient norms and the replica-mean
+    loss."""
+    init(rank, world, port)
+    from nano_qwen_b200.training.dpo import DPOTrainer
+    cfg = tiny_cfg()
+    tc = {"dpo": {"beta": 0.3}, "optimizer": {"lr": 1e-2, "grad_clip": 1.0},
+          "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    singles = [dist.new_group([r]) for r in range(world)]
+    one = DPOTrainer(build(cfg), build(cfg, seed=5), tc, torch.device("cpu"), dp_group=singles[rank])
+    two = DPOTrainer(build(cfg), build(cfg, seed=5), dict(tc, distributed={"shard_params": shard}),
+                     torch.device("cpu"))
+    for step in range(3):
+        g = torch.Generator().manual_seed(800 + step)
+        c = torch.randint(0, cfg.vocab_size, (2 * world, 12), generator=g)
+        r = torch.randint(0, cfg.vocab_size, (2 * world, 12), generator=g)
+        a = one.train_step(c, r, c.clone(), r.clone())
+        sl = slice(2 * rank, 2 * rank + 2)
+        b = two.train_step(c[sl], r[sl], c[sl].clone(), r[sl].clone())
+        loss = torch.tensor(b["loss"])
+        dist.all_reduce(loss)
+        assert abs(float(loss) / world - a["loss"]) < 1e-5 * max(1.0, abs(a["loss"])), (loss, a)
+        assert abs(b["grad_norm"] - a["grad_norm"]) < 1e-4 * a["grad_norm"], (b, a)
+    dist.destroy_process_group()

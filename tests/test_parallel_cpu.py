@@ -195,3 +195,8 @@ def test_layout_checkpoints_resume_in_one_process(tmp_path, name):
 def test_single_process_checkpoint_resumes_in_layouts(tmp_path, name):
     world, layout = LAYOUTS[name]
     _run(W.layout_ckpt_worker, world, layout, str(tmp_path), True)
+
+
+@pytest.mark.parametrize("shard", [False, True])
+def test_dpo_data_parallel_matches_single(shard):
+    _run(W.dpo_layout_worker, 2, shard)
