@@ -79,8 +79,12 @@ class TrainEngine:
         if dp_mode is None:
             if dist_cfg.get("shard_params", False):
                 dp_mode = "fsdp"
+            elif not dist_cfg.get("fsdp_enabled", True):
+                dp_mode = "replicate"
             else:
-                dp_mode = "shard" if dist_cfg.get("fsdp_enabled", True) else "replicate"
+                # the peer-memory step where symmetric memory is available
+                # (it falls back to the NCCL ZeRO step otherwise)
+                dp_mode = "p2p" if dist_cfg.get("dp_comm", "p2p") == "p2p" else "shard"
         opt = training_config.get("optimizer", {}) or {}
         if dp_mode == "fsdp":
             self._init_fsdp(dp_group, parallel, dist_cfg, opt)
