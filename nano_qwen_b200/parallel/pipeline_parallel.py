@@ -126,7 +126,7 @@ class PipelineParallel(nn.Module):
         g.add_(other)
 
     # ------------------------------------------------------------- compute
-    def _stage_forward(self, x_in: torch.Tensor, pos):
+    def _stage_forward(self, x_in: torch.Tensor, pos, mask=None):
         m = self.model
         gather = getattr(self, "param_gather", None) or getattr(m, "param_gather", None)
         if gather is not None:  # fully sharded: embedding / lm_head / norms gathered
@@ -143,7 +143,7 @@ class PipelineParallel(nn.Module):
             resid = x_in
         delta, aux_total = None, None
         for layer in m.layers:
-            resid, delta, aux = layer.forward_fused(resid, delta, pos, None, None, None)
+            resid, delta, aux = layer.forward_fused(resid, delta, pos, mask, None, None)
             if aux is not None:
                 aux_total = aux if aux_total is None else aux_total + aux
         if self.last:
@@ -157,12 +157,15 @@ class PipelineParallel(nn.Module):
         """Runs forward and backward of every micro-batch with the 1F1B order;
         returns (loss, aux) summed over micro-batches (each scaled by 1/m), the
         same on every stage."""
-        from ..models.transformer import shift_targets
+        from ..models.transformer import key_range_mask, shift_targets
         mbs = micro_batches
         if len(mbs) == 1 and self.n_micro > 1 and mbs[0]["input_ids"].shape[0] >= self.n_micro:
+            # split every per-row field (ids, labels, document ids, masks)
             b = mbs[0]
-            mbs = [dict(input_ids=i, labels=l) for i, l in
-                   zip(b["input_ids"].chunk(self.n_micro), b["labels"].chunk(self.n_micro))]
+            keys = [k for k, v in b.items() if torch.is_tensor(v) and v.dim() >= 1
+                    and v.shape[0] == b["input_ids"].shape[0]]
+            parts = {k: b[k].chunk(self.n_micro) for k in keys}
+            mbs = [{k: parts[k][j] for k in keys} for j in range(len(parts["input_ids"]))]
         m = len(mbs)
         w = scale / m
         coef = self.config.router_aux_loss_coef / max(1, self.n_moe_total)
@@ -179,7 +182,10 @@ class PipelineParallel(nn.Module):
 
         def fwd(i, a):
             x_in = mbs[i]["input_ids"] if self.first else a.requires_grad_(True)
-            out, aux = self._stage_forward(x_in, None)
+            # packed documents / padding: the same key ranges as Qwen3Model.forward
+            docs = mbs[i].get("document_ids", mbs[i].get("doc_ids"))
+            mask = key_range_mask(mbs[i].get("attention_mask"), docs)
+            out, aux = self._stage_forward(x_in, None, mask)
             extra = coef * aux * w if aux is not None else None
             if aux is not None:
                 aux_sum.add_(aux.detach().float() * w)

@@ -837,6 +837,7 @@ def layout_worker(rank, world, port, layout):
     # aux term, except for the global-batch balance, whose statistics are the
     # full batch's (then the reference runs the full batch as one micro-batch)
     balance = layout.pop("balance", False)
+    docs = layout.pop("docs", False)
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=4,
                    tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
@@ -855,6 +856,13 @@ def layout_worker(rank, world, port, layout):
         c = B // accum
         full = [{"input_ids": ids[c * i:c * (i + 1)], "labels": ids[c * i:c * (i + 1)]}
                 for i in range(dp * accum)]
+        if docs:   # packed documents: each token attends within its own document
+            gd = torch.Generator().manual_seed(900 + step)
+            cuts = (torch.rand(ids.shape, generator=gd) < 0.2).long()
+            cuts[:, 0] = 0
+            dids = cuts.cumsum(1)
+            for i, mb in enumerate(full):
+                mb["doc_ids"] = dids[c * i:c * (i + 1)]
         if balance:
             r = ref.train_step([{"input_ids": ids, "labels": ids}])
         else:

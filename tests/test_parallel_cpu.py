@@ -170,6 +170,10 @@ LAYOUTS = {
     "dp2-moe-balance": (2, {"moe": True, "balance": True}),
     "ep2-moe-balance": (2, {"ep_size": 2, "moe": True, "balance": True}),
     "dp2-fsdp-moe-balance": (2, {"moe": True, "balance": True, "shard_params": True}),
+    "dp2-docs": (2, {"docs": True}),
+    "tp2-docs": (2, {"tp_size": 2, "docs": True}),
+    "pp2-docs": (2, {"pp_size": 2, "pp_microbatches": 2, "docs": True}),
+    "tp2xpp2-docs": (4, {"tp_size": 2, "pp_size": 2, "pp_microbatches": 2, "docs": True}),
 }
 
 
