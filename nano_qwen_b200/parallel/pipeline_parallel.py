@@ -155,11 +155,16 @@ class PipelineParallel(nn.Module):
     def pipeline_forward_backward(self, micro_batches: List[Dict[str, torch.Tensor]],
                                   scale: float = 1.0):
         """Runs forward and backward of every micro-batch with the 1F1B order;
-        returns (loss, aux) summed over micro-batches (each scaled by 1/m), the
-        same on every stage."""
+        returns (loss, aux) summed over micro-batches, the same on every stage.
+        Given several micro-batches, each loss is scaled by 1/m (the mean of
+        their means, as the training engine's gradient accumulation); a single
+        batch that the pipeline splits itself keeps its token mean (each
+        piece weighted by its share of the valid targets)."""
         from ..models.transformer import key_range_mask, shift_targets
         mbs = micro_batches
+        split = False
         if len(mbs) == 1 and self.n_micro > 1 and mbs[0]["input_ids"].shape[0] >= self.n_micro:
+            split = True
             # split every per-row field (ids, labels, document ids, masks)
             b = mbs[0]
             keys = [k for k, v in b.items() if torch.is_tensor(v) and v.dim() >= 1
@@ -168,6 +173,12 @@ class PipelineParallel(nn.Module):
             mbs = [{k: parts[k][j] for k in keys} for j in range(len(parts["input_ids"]))]
         m = len(mbs)
         w = scale / m
+        if split:
+            counts = [(shift_targets(mb["labels"]) != -100).sum().float() for mb in mbs]
+            total = torch.stack(counts).sum().clamp(min=1.0)
+            lw = [scale * c / total for c in counts]
+        else:
+            lw = [w] * m
         coef = self.config.router_aux_loss_coef / max(1, self.n_moe_total)
         dev = mbs[0]["input_ids"].device
         B, S = mbs[0]["input_ids"].shape
@@ -193,9 +204,9 @@ class PipelineParallel(nn.Module):
                 t = shift_targets(mbs[i]["labels"])
                 if sp is not None:
                     from ..models.transformer import _sp_loss
-                    loss = _sp_loss(out, self.model.lm_head_ref(out.dtype), t, sp) * w
+                    loss = _sp_loss(out, self.model.lm_head_ref(out.dtype), t, sp) * lw[i]
                 else:
-                    loss = ops.linear_cross_entropy(out, self.model.lm_head_ref(out.dtype), t) * w
+                    loss = ops.linear_cross_entropy(out, self.model.lm_head_ref(out.dtype), t) * lw[i]
                 loss_sum.add_(loss.detach().float())
                 saved_out[i] = (loss if extra is None else loss + extra, None)
                 out = None

@@ -838,6 +838,7 @@ def layout_worker(rank, world, port, layout):
     # full batch's (then the reference runs the full batch as one micro-batch)
     balance = layout.pop("balance", False)
     docs = layout.pop("docs", False)
+    pad = layout.pop("pad", False)
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=4,
                    tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
@@ -863,6 +864,14 @@ def layout_worker(rank, world, port, layout):
             dids = cuts.cumsum(1)
             for i, mb in enumerate(full):
                 mb["doc_ids"] = dids[c * i:c * (i + 1)]
+        if pad:    # right padding of uneven length: masked keys, ignored targets
+            gp = torch.Generator().manual_seed(950 + step)
+            lens = torch.randint(6, 17, (ids.shape[0],), generator=gp)
+            am = (torch.arange(ids.shape[1])[None, :] < lens[:, None]).long()
+            lab = torch.where(am.bool(), ids, torch.full_like(ids, -100))
+            for i, mb in enumerate(full):
+                mb["attention_mask"] = am[c * i:c * (i + 1)]
+                mb["labels"] = lab[c * i:c * (i + 1)]
         if balance:
             r = ref.train_step([{"input_ids": ids, "labels": ids}])
         else:

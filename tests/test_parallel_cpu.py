@@ -174,6 +174,9 @@ LAYOUTS = {
     "tp2-docs": (2, {"tp_size": 2, "docs": True}),
     "pp2-docs": (2, {"pp_size": 2, "pp_microbatches": 2, "docs": True}),
     "tp2xpp2-docs": (4, {"tp_size": 2, "pp_size": 2, "pp_microbatches": 2, "docs": True}),
+    "dp2-pad": (2, {"pad": True}),
+    "tp2-pad": (2, {"tp_size": 2, "pad": True}),
+    "pp2-pad": (2, {"pp_size": 2, "pp_microbatches": 2, "pad": True}),
 }
 
 
