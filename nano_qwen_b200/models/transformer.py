@@ -104,6 +104,18 @@ class TransformerBlock(nn.Module):
         return resid + f.to(resid.dtype), aux
 
 
+def _right_padding(mask) -> bool:
+    """True for a 2-D key-padding mask whose real tokens form a prefix of
+    every row (or None)."""
+    if mask is None:
+        return True
+    if not (torch.is_tensor(mask) and mask.dim() == 2):
+        return False
+    m = mask.bool()
+    # a prefix: once a row turns false it stays false
+    return bool((m[:, 1:] <= m[:, :-1]).all())
+
+
 def key_range_mask(attention_mask, document_ids=None, cached: bool = False):
     """The attention mask the layers receive: ``document_ids`` or a
     one-run-per-row 2-D padding mask become an ``ops.KeyRange`` (handled by
@@ -206,10 +218,18 @@ class Qwen3Model(nn.Module):
         packed rows; each token then attends only within its document.  A 2-D
         key-padding ``attention_mask`` with one run of real tokens per row
         (left or right padding) runs on the same masked kernels."""
+        if (getattr(self, "cp_group", None) is not None and kv_caches is None
+                and document_ids is None and _right_padding(attention_mask)):
+            # right padding under causal attention: a real token never sees a
+            # pad key and the pads' targets are ignored, so plain causal
+            # attention is exact for everything the loss reads
+            attention_mask = None
         attention_mask = key_range_mask(attention_mask, document_ids, kv_caches is not None)
         if getattr(self, "cp_group", None) is not None and kv_caches is None:
             if attention_mask is not None:
-                raise NotImplementedError("context parallelism runs plain causal attention")
+                raise NotImplementedError("context parallelism runs plain causal attention "
+                                          "(right-padded rows are accepted; packed documents "
+                                          "and left padding are not)")
             return self._forward_cp(input_ids, position_ids, labels, return_logits,
                                     logits_to_keep, inputs_embeds)
         if getattr(self, "tp_fused", False) and kv_caches is None and inputs_embeds is None \

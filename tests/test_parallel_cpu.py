@@ -177,6 +177,10 @@ LAYOUTS = {
     "dp2-pad": (2, {"pad": True}),
     "tp2-pad": (2, {"tp_size": 2, "pad": True}),
     "pp2-pad": (2, {"pp_size": 2, "pp_microbatches": 2, "pad": True}),
+    "ep2-moe-pad": (2, {"ep_size": 2, "moe": True, "pad": True}),
+    "dp2-fsdp-pad-accum2": (2, {"shard_params": True, "pad": True, "accum": 2}),
+    "tp2xdp2-pad": (4, {"tp_size": 2, "pad": True}),
+    "cp2-pad": (2, {"cp_size": 2, "pad": True}),
 }
 
 
