@@ -819,13 +819,30 @@ def tp_engine_worker(rank, world, port):
     dist.destroy_process_group()
 
 
+def layouts_worker(rank, world, port, layouts):
+    """Every (name, layout) in ``layouts`` in one spawned job (the process
+    group is set up once); a failure names its layout."""
+    init(rank, world, port)
+    for name, layout in layouts:
+        try:
+            _layout_case(rank, world, layout)
+        except AssertionError as e:
+            raise AssertionError(f"layout {name}: {e}") from e
+    dist.destroy_process_group()
+
+
 def layout_worker(rank, world, port, layout):
+    init(rank, world, port)
+    _layout_case(rank, world, layout)
+    dist.destroy_process_group()
+
+
+def _layout_case(rank, world, layout):
     """The training engine on one parallel layout built by the
     ``ParallelismManager`` (``layout``: ParallelConfig fields plus ``moe``
-    and ``shard_params``), three steps against the single-process engine on
+    and ``shard_params``), two steps against the single-process engine on
     the same global batch (the data-parallel ranks' slices as its
     micro-batches): losses and gradient norms agree."""
-    init(rank, world, port)
     from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
     from nano_qwen_b200.training.engine import TrainEngine
     layout = dict(layout)
@@ -839,7 +856,7 @@ def layout_worker(rank, world, port, layout):
     balance = layout.pop("balance", False)
     docs = layout.pop("docs", False)
     pad = layout.pop("pad", False)
-    cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=4,
+    cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=2,
                    tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
             "scheduler": {"warmup_steps": 0, "total_steps": 10},
@@ -852,7 +869,7 @@ def layout_worker(rank, world, port, layout):
     dp = pm.config.dp_size
     d = pm.coords["dp"]
     B = 4
-    for step in range(3):
+    for step in range(2):   # the second step checks the first update
         ids = batch(cfg, B * dp, 16, seed=600 + step)
         c = B // accum
         full = [{"input_ids": ids[c * i:c * (i + 1)], "labels": ids[c * i:c * (i + 1)]}
@@ -883,15 +900,25 @@ def layout_worker(rank, world, port, layout):
         dist.all_reduce(loss)
         close(loss / world, r["loss"], 1e-5, f"loss step {step}")
         close(o["grad_norm"], r["grad_norm"], 1e-4, f"grad norm step {step}")
+
+
+def layout_ckpts_worker(rank, world, port, cases, tmp):
+    """Every (name, layout, from_single) checkpoint case of one world size
+    in one spawned job; a failure names its case."""
+    init(rank, world, port)
+    for k, (name, layout, from_single) in enumerate(cases):
+        try:
+            _layout_ckpt_case(rank, world, layout, os.path.join(tmp, f"case{k}"), from_single)
+        except AssertionError as e:
+            raise AssertionError(f"layout {name} (from_single={from_single}): {e}") from e
     dist.destroy_process_group()
 
 
-def layout_ckpt_worker(rank, world, port, layout, tmp, from_single=False):
+def _layout_ckpt_case(rank, world, layout, tmp, from_single=False):
     """A checkpoint written by an engine on any manager layout loads into the
     single-process engine, which then continues exactly like the layout
     engine: two more steps with equal losses and gradient norms (weights,
     Adam moments and step counts all carried over)."""
-    init(rank, world, port)
     from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
     from nano_qwen_b200.training.checkpoint import CheckpointManager
     from nano_qwen_b200.training.engine import TrainEngine
@@ -935,7 +962,6 @@ def layout_ckpt_worker(rank, world, port, layout, tmp, from_single=False):
         close(loss / world, r["loss"], 1e-5, f"loss step {step}")
         close(o["grad_norm"], r["grad_norm"], 1e-4, f"grad norm step {step}")
     dist.barrier()
-    dist.destroy_process_group()
 
 
 def dpo_layout_worker(rank, world, port, shard):

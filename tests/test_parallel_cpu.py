@@ -184,28 +184,27 @@ LAYOUTS = {
 }
 
 
-@pytest.mark.parametrize("name", sorted(LAYOUTS))
-def test_engine_layouts_match_single_process(name):
+@pytest.mark.parametrize("world", [2, 4])
+def test_engine_layouts_match_single_process(world):
     """Every layout the manager builds trains like one process: the engine's
-    loss and gradient norm over three steps."""
-    world, layout = LAYOUTS[name]
-    _run(W.layout_worker, world, layout)
+    loss and gradient norm over two steps (all layouts of one world size in
+    one job; a failure names its layout)."""
+    cases = [(n, lay) for n, (w, lay) in sorted(LAYOUTS.items()) if w == world]
+    _run(W.layouts_worker, world, cases)
 
 
 CKPT_LAYOUTS = ["dp2", "tp2", "pp2", "ep2-moe", "tp2xdp2-fsdp", "ep2-fsdp-moe", "tp2xpp2", "cp2",
                 "cp2-fsdp"]
 
 
-@pytest.mark.parametrize("name", CKPT_LAYOUTS)
-def test_layout_checkpoints_resume_in_one_process(tmp_path, name):
-    world, layout = LAYOUTS[name]
-    _run(W.layout_ckpt_worker, world, layout, str(tmp_path))
-
-
-@pytest.mark.parametrize("name", CKPT_LAYOUTS)
-def test_single_process_checkpoint_resumes_in_layouts(tmp_path, name):
-    world, layout = LAYOUTS[name]
-    _run(W.layout_ckpt_worker, world, layout, str(tmp_path), True)
+@pytest.mark.parametrize("world", [2, 4])
+def test_layout_checkpoints_move_to_and_from_one_process(tmp_path, world):
+    """A checkpoint of each layout resumes in one process, and one process's
+    checkpoint resumes in each layout, both continuing with equal losses and
+    gradient norms (all cases of one world size in one job)."""
+    cases = [(n, LAYOUTS[n][1], fs) for n in CKPT_LAYOUTS if LAYOUTS[n][0] == world
+             for fs in (False, True)]
+    _run(W.layout_ckpts_worker, world, cases, str(tmp_path))
 
 
 @pytest.mark.parametrize("shard", [False, True])
