@@ -80,8 +80,9 @@ def parse():
                    help="ours, dp p2p: reduce-scatter per block during the backward instead of after it")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="ours, tp/ep configs: peer-memory fused kernels or NCCL collectives")
-    p.add_argument("--dp-mode", default="p2p", choices=["p2p", "shard", "replicate", "fsdp"],
-                   help="ours, N>1: peer-memory fused ZeRO step (p2p), NCCL ZeRO-2 / all-reduce, "
+    p.add_argument("--dp-mode", default=None, choices=["p2p", "shard", "replicate", "fsdp"],
+                   help="ours, N>1: peer-memory fused ZeRO step (p2p; the default for plain data "
+                        "parallelism, opt-in under tp/ep/cp), NCCL ZeRO-2 / all-reduce, "
                         "or fully sharded parameters (fsdp)")
     p.add_argument("--cp-mode", default="allgather", choices=["allgather", "ring"],
                    help="ours, cp configs: gathered k|v (peer-memory kernels) or the k|v ring")

@@ -108,7 +108,7 @@ void ep_dispatch_bwd(std::vector<int64_t>, std::vector<int64_t>, std::vector<int
                      torch::Tensor, torch::Tensor, int64_t, int64_t);
 // zero_comm.cu
 void zero_rs(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t, int64_t,
-             torch::Tensor, int64_t, int64_t);
+             torch::Tensor, int64_t, int64_t, double);
 void zero_clip(torch::Tensor, double, torch::Tensor, torch::Tensor);
 void zero_adamw_ag(std::vector<int64_t>, std::vector<int64_t>, std::vector<int64_t>, int64_t, torch::Tensor,
                    torch::Tensor, torch::Tensor, torch::Tensor, int64_t, int64_t, int64_t, int64_t, double,

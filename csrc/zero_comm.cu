@@ -195,16 +195,18 @@ static ZeroPeers make_peers(const std::vector<int64_t>& grad, const std::vector<
 
 // Reduce-scatter of the mean gradient into this rank's shard, fused with the
 // squared-norm partial (added into sq_out).  grid_ctas = 0 picks 3 per SM.
+// scale multiplies the mean (expert spans: the sum over the ranks holding the
+// same experts divided by the whole data-parallel world).
 void zero_rs(std::vector<int64_t> grad, std::vector<int64_t> comp, std::vector<int64_t> flags,
              int64_t rank, int64_t begin, int64_t end, torch::Tensor sq_out, int64_t epoch,
-             int64_t grid_ctas) {
+             int64_t grid_ctas, double scale) {
   auto P = make_peers(grad, comp, flags, rank);
   TORCH_CHECK(begin % 4 == 0 && end % 4 == 0 && end >= begin, "zero_rs: 4-aligned shard");
   TORCH_CHECK(sq_out.scalar_type() == torch::kFloat32 && sq_out.is_cuda(), "zero_rs: sq_out fp32");
   auto st = at::cuda::getCurrentCUDAStream();
   const int grid = grid_ctas > 0 ? static_cast<int>(grid_ctas) : 3 * num_sms();
   NQ_W_DISPATCH(P.world, zero_rs_kernel<WW><<<grid, 256, 0, st>>>(
-      P, begin, end, 1.f / P.world, sq_out.data_ptr<float>(), static_cast<unsigned>(epoch),
+      P, begin, end, static_cast<float>(scale) / P.world, sq_out.data_ptr<float>(), static_cast<unsigned>(epoch),
       error_flag_ptr()));
   NQ_CHECK_CUDA(cudaGetLastError());
 }

@@ -19,6 +19,14 @@ is updated only in the shard (the rest is refreshed by ``gather_master``
 before a save).  Same interface as ``DataParallel``; the engine calls
 ``fused_step`` instead of sync + clip + step + gather.  Requires 1, 2, 4 or 8
 ranks on one NVSwitch domain.
+
+Under expert parallelism the store's expert span holds different experts on
+the ranks of different expert blocks, so it is reduced and updated only over
+the ranks that hold the same experts (``expert_group``, a subset of the
+data-parallel group): its own shard bounds, its own flag words and the
+subset of the peer pointers the data-parallel mapping already provides.  The
+dense shard skips the expert span (always as two reduce calls, possibly
+empty, so every rank issues the same sequence of flag epochs).
 """
 
 from __future__ import annotations
@@ -32,8 +40,8 @@ import torch.distributed as dist
 
 from ..ops._ext import ext
 from ..runtime.flat_params import ALIGN, FlatParamStore
-from .comm import get_world_size
-from .data_parallel import DataParallel
+from .comm import all_gather_flat_, get_world_size
+from .data_parallel import DataParallel, shard_bounds
 
 
 def same_node(ranks: List[int], local_world_size: int) -> bool:
@@ -92,21 +100,48 @@ class SymmetricAllocator:
         return [int(p) for p in h.buffer_ptrs]
 
 
+def _group_ranks(group) -> List[int]:
+    return (dist.get_process_group_ranks(group) if group is not None
+            else list(range(dist.get_world_size())))
+
+
 class PeerDataParallel(DataParallel):
     def __init__(self, store: FlatParamStore, allocator: SymmetricAllocator, group=None,
-                 rs_ctas: int = 0):
-        super().__init__(store, mode="shard", group=group)
-        if self.expert_span is not None:
-            raise ValueError("peer-memory data parallelism does not handle expert spans")
+                 rs_ctas: int = 0, expert_group=None):
+        super().__init__(store, mode="shard", group=group, expert_group=expert_group)
+        # DataParallel replicates a store with an expert span; this step
+        # shards both parts
+        self.mode = "shard"
+        self.shard = shard_bounds(store.numel, self.world, self.rank)
         self.alloc = allocator
         dev = store.master.device
         self.flags = allocator(2 * 8, torch.int32, dev)
+        self.xflags = allocator(2 * 8, torch.int32, dev) if self.expert_span is not None else None
         torch.cuda.synchronize()
         self.p_grad = allocator.peer_ptrs(store.grad)
         self.p_comp = allocator.peer_ptrs(store.compute)
         self.p_flags = allocator.peer_ptrs(self.flags)
+        self.x_shard = None
+        if self.xflags is not None:
+            p_xflags = allocator.peer_ptrs(self.xflags)
+            dp_ranks = _group_ranks(group)
+            me = dist.get_rank()
+            members = _group_ranks(expert_group) if expert_group is not None else [me]
+            idx = [dp_ranks.index(r) for r in members]
+            self.x_rank, self.x_world = members.index(me), len(members)
+            self.x_grad = [self.p_grad[i] for i in idx]
+            self.x_comp = [self.p_comp[i] for i in idx]
+            self.x_flags = [p_xflags[i] for i in idx]
+            xb, xe = self.expert_span
+            lo, hi = shard_bounds(xe - xb, self.x_world, self.x_rank)
+            self.x_shard = (xb + lo, xb + hi)
+            self.x_per = shard_bounds(xe - xb, self.x_world, 0)[1]
+            fb, fe = getattr(store, "fp32_span", (0, 0))
+            if fe > fb and fb < xe and xb < fe:
+                raise ValueError("the fp32 span overlaps the expert span")
         dist.barrier(group=group)
         self.epoch = 0
+        self.x_epoch = 0
         self.rs_ctas = rs_ctas
         self.sq = torch.zeros(1, dtype=torch.float32, device=dev)
         self.norm = torch.zeros((), dtype=torch.float32, device=dev)
@@ -118,6 +153,8 @@ class PeerDataParallel(DataParallel):
         soon as the block's backward is done (last micro-batch only), with a
         small grid that shares the SMs with the backward kernels."""
         from ..models.transformer import TransformerBlock
+        if self.expert_span is not None:
+            return  # expert spans are reduced after the backward
         st = self.store
         spans = []
         for blk in model.modules():
@@ -180,7 +217,22 @@ class PeerDataParallel(DataParallel):
             hi = lo
         self._calls += 1
         ext().zero_rs(self.p_grad, self.p_comp, self.p_flags, self.rank, lo, hi, self.sq,
-                      self.epoch + self._calls, ctas)
+                      self.epoch + self._calls, ctas, 1.0)
+
+    def dense_pieces(self, lo: int, hi: int):
+        """[lo, hi) without the expert span: two ranges, either possibly empty."""
+        if self.expert_span is None:
+            return [(lo, hi)]
+        xb, xe = self.expert_span
+        return [(lo, min(hi, xb)), (max(lo, xe), hi)]
+
+    def owned_ranges(self):
+        """The flat ranges this rank reduces and updates."""
+        b, e = self.shard
+        out = [(lo, hi) for lo, hi in self.dense_pieces(b, e) if hi > lo]
+        if self.x_shard is not None and self.x_shard[1] > self.x_shard[0]:
+            out.append(self.x_shard)
+        return out
 
     def sync_grads(self) -> None:
         """Reduce-scatter whatever the overlapped block reductions did not
@@ -188,7 +240,16 @@ class PeerDataParallel(DataParallel):
         if getattr(self, "spans", None) is None:
             self._calls = 0
             self.sq.zero_()
-            self._rs(0, self.store.numel, self.rs_ctas)
+            for lo, hi in self.dense_pieces(0, self.store.numel):
+                self._rs(lo, hi, self.rs_ctas)
+            if self.x_shard is not None:
+                self.x_epoch += 1
+                xb, xe = self.x_shard
+                # each expert's gradient already sums the tokens its EP block
+                # routed to it: sum over the ranks holding the same experts and
+                # divide by the data-parallel world (x_world / world x mean)
+                ext().zero_rs(self.x_grad, self.x_comp, self.x_flags, self.x_rank, xb, xe,
+                              self.sq, self.x_epoch, self.rs_ctas, self.x_world / self.world)
         else:
             torch.cuda.current_stream().wait_stream(self.comm_stream)
             if not self.final_micro:  # no backward ran with the hooks armed
@@ -217,10 +278,18 @@ class PeerDataParallel(DataParallel):
 
         def update(hp):
             lr_d, lr_n, b1, b2, eps, wd, bc1, bc2 = hp
-            E.zero_adamw_ag(self.p_grad, self.p_comp, self.p_flags, self.rank, self.store.master,
-                            optimizer.exp_avg, optimizer.exp_avg_sq, self.clip, b, e,
-                            optimizer.state_base, self.store.decay_end, lr_d, lr_n, b1, b2, eps, wd,
-                            bc1, bc2)
+            for lo, hi in self.dense_pieces(b, e):
+                if hi > lo:
+                    E.zero_adamw_ag(self.p_grad, self.p_comp, self.p_flags, self.rank,
+                                    self.store.master, optimizer.exp_avg, optimizer.exp_avg_sq,
+                                    self.clip, lo, hi, optimizer.state_base, self.store.decay_end,
+                                    lr_d, lr_n, b1, b2, eps, wd, bc1, bc2)
+            if self.x_shard is not None and self.x_shard[1] > self.x_shard[0]:
+                xb, xe = self.x_shard
+                E.zero_adamw_ag(self.x_grad, self.x_comp, self.x_flags, self.x_rank,
+                                self.store.master, optimizer.x_exp_avg, optimizer.x_exp_avg_sq,
+                                self.clip, xb, xe, xb, self.store.decay_end,
+                                lr_d, lr_n, b1, b2, eps, wd, bc1, bc2)
 
         optimizer.step(update=update)
         E.zero_publish(self.p_grad, self.p_comp, self.p_flags, self.rank, self.epoch)
@@ -230,3 +299,24 @@ class PeerDataParallel(DataParallel):
     def gather_params(self) -> None:
         """The fused step already wrote every peer's compute copy."""
         return
+
+    @torch.no_grad()
+    def gather_flat_(self, buf: torch.Tensor) -> None:
+        """Complete a store-sized fp32 buffer of which this rank holds its
+        owned ranges: the dense shards over the data-parallel group, then the
+        expert span over the ranks holding the same experts."""
+        if self.x_shard is None:
+            return super().gather_flat_(buf)
+        xb, xe = self.x_shard
+        mine = buf[xb:xe].clone()
+        super().gather_flat_(buf)
+        sb = self.expert_span[0]
+        full = torch.zeros(self.x_per * self.x_world, dtype=buf.dtype, device=buf.device)
+        if self.x_world > 1:
+            part = torch.zeros(self.x_per, dtype=buf.dtype, device=buf.device)
+            part[:xe - xb].copy_(mine)
+            all_gather_flat_(full, part, self.expert_group)
+        else:
+            full[:xe - xb].copy_(mine)
+        n = self.expert_span[1] - sb
+        buf[sb:sb + n].copy_(full[:n])

@@ -76,6 +76,9 @@ class TrainEngine:
             world = get_world_size(dp_group)
         self._dp_world = world
         dist_cfg = training_config.get("distributed", {}) or {}
+        if dp_mode is None and dist_cfg.get("dp_mode"):
+            dp_mode = dist_cfg["dp_mode"]   # named in the config: taken as asked
+        explicit_mode = dp_mode is not None
         if dp_mode is None:
             if dist_cfg.get("shard_params", False):
                 dp_mode = "fsdp"
@@ -91,18 +94,21 @@ class TrainEngine:
             self._init_tail(training_config, opt, dp_group, world)
             return
         alloc = None
-        if dp_mode == "p2p" and parallel is not None:
+        if dp_mode == "p2p" and parallel is not None and not explicit_mode:
+            # under model parallelism the peer-memory step is taken only when
+            # asked for by name (dp_mode="p2p"); the configured default keeps
+            # the NCCL ZeRO step there
             dp_mode = "shard"
         if dp_mode == "p2p":
             from ..parallel.peer_dp import SymmetricAllocator, symmetric_available
-            if symmetric_available(dp_group) and expert_group is None:
+            if world > 1 and symmetric_available(dp_group):
                 alloc = SymmetricAllocator(dp_group)
             else:
                 dp_mode = "shard"
         self.store = attach_param_store(self.model, pad_multiple=ALIGN * max(1, world), alloc=alloc)
         if world > 1 and alloc is not None:
             from ..parallel.peer_dp import PeerDataParallel
-            self.dp = PeerDataParallel(self.store, alloc, group=dp_group)
+            self.dp = PeerDataParallel(self.store, alloc, group=dp_group, expert_group=expert_group)
             # Off by default: the per-block reduce-scatter kernels wait on every
             # rank's block, and with 4 ranks their spinning CTAs held SMs that the
             # persistent GEMM / attention grids needed (Qwen3-1.7B dp4: 371 ms/step
@@ -117,7 +123,8 @@ class TrainEngine:
         self.optimizer = build_optimizer(
             self.model, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),
             beta1=opt.get("beta1", 0.9), beta2=opt.get("beta2", 0.95), eps=opt.get("eps", 1e-8),
-            fused=True, store=self.store, shard=self.dp.shard if self.dp is not None else None)
+            fused=True, store=self.store, shard=self.dp.shard if self.dp is not None else None,
+            expert_shard=getattr(self.dp, "x_shard", None))
         if self.dp is not None and hasattr(self.optimizer, "state_gather"):
             self.optimizer.state_gather = self.dp.gather_flat_
         self._init_tail(training_config, opt, dp_group, world)
@@ -211,7 +218,8 @@ class TrainEngine:
             sync_replicated_grads(self.model, self.tp_group)
         with nvtx_range("optimizer_step"):
             if hasattr(self.dp, "fused_step"):
-                gnorm = self.dp.fused_step(self.optimizer, self.grad_clip)
+                gnorm = self.dp.fused_step(self.optimizer, self.grad_clip,
+                                           extra_sq=lambda sq: self._norm_sq_reduce(sq, dp=False))
                 self.scheduler.step()
                 return {"loss": loss_sum, "grad_norm": gnorm, "aux_loss": aux_sum}
             if self.dp is not None:
@@ -242,20 +250,25 @@ class TrainEngine:
                 out.append(p)
         return out
 
-    def _norm_sq_reduce(self, sq: torch.Tensor) -> torch.Tensor:
+    def _norm_sq_reduce(self, sq: torch.Tensor, dp: bool = True) -> torch.Tensor:
+        """This rank's squared-norm part -> the global squared norm: remove
+        the duplicated parameters' share, then sum over the data-parallel
+        group (``dp``; the peer-memory step does that itself) and the TP / PP
+        groups."""
         import torch.distributed as dist
         if self._dups:
-            b, e = self.optimizer.shard
+            owned = (self.dp.owned_ranges() if hasattr(self.dp, "owned_ranges")
+                     else [self.optimizer.shard])
             for p in self._dups:
                 if getattr(self.store, "mode", None) == "fsdp":
                     ranges = self.store.shard_slices(p)
                 else:
                     o = self.store.offsets[id(p)]
-                    ranges = [(max(b, o), min(e, o + p.numel()))]
+                    ranges = [(max(b, o), min(e, o + p.numel())) for b, e in owned]
                 for lo, hi in ranges:
                     if hi > lo:
                         sq = sq - self.store.grad[lo:hi].double().pow(2).sum().float()
-        if self.dp is not None:
+        if self.dp is not None and dp:
             sq = self.dp.norm_sq_reduce(sq)
         for g in (self.tp_group, self.pp_group):
             if g is not None and dist.get_world_size(g) > 1:

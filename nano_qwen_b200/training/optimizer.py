@@ -32,11 +32,20 @@ class FusedAdamW(torch.optim.Optimizer):
     Full-shape per-parameter views of the moments (what ``state_dict`` and DCP
     see) then exist only between ``gather_full_state`` and
     ``release_full_state``, which checkpointing calls around a save or load.
+
+    ``expert_shard`` = (begin, end): a second slice, inside the store's expert
+    span, that this rank also updates (expert parallelism shards the expert
+    span over the ranks holding the same experts, not over the whole
+    data-parallel group); its moments live in ``x_exp_avg`` /
+    ``x_exp_avg_sq``.  The caller performs that update (``step(update=...)``).
     """
+
+    x_shard: Optional[Tuple[int, int]] = None
 
     def __init__(self, store: FlatParamStore, lr: float = 3e-4, betas=(0.9, 0.95),
                  eps: float = 1e-8, weight_decay: float = 0.1,
-                 shard: Optional[Tuple[int, int]] = None):
+                 shard: Optional[Tuple[int, int]] = None,
+                 expert_shard: Optional[Tuple[int, int]] = None):
         self.store = store
         decay = [p for p in store.params if store.offset(p) < store.decay_end]
         nodecay = [p for p in store.params if store.offset(p) >= store.decay_end]
@@ -49,12 +58,16 @@ class FusedAdamW(torch.optim.Optimizer):
         dev = store.master.device
         self.shard = shard or (0, store.numel)
         b, e = self.shard
-        self.sharded = (b, e) != (0, store.numel)
+        self.x_shard = expert_shard
+        self.sharded = (b, e) != (0, store.numel) or expert_shard is not None
         # flat index of element 0 of exp_avg / exp_avg_sq
         self.state_base = b if self.sharded else 0
         n = e - b if self.sharded else store.numel
         self.exp_avg = torch.zeros(n, dtype=torch.float32, device=dev)
         self.exp_avg_sq = torch.zeros(n, dtype=torch.float32, device=dev)
+        xn = expert_shard[1] - expert_shard[0] if expert_shard is not None else 0
+        self.x_exp_avg = torch.zeros(xn, dtype=torch.float32, device=dev)
+        self.x_exp_avg_sq = torch.zeros(xn, dtype=torch.float32, device=dev)
         self._full = None
         # completes a full-size buffer across the data-parallel group (set by
         # the training engine; ``gather_full_state`` uses it by default)
@@ -85,9 +98,11 @@ class FusedAdamW(torch.optim.Optimizer):
         b, e = self.shard
         gather = gather or self.state_gather
         full = []
-        for shard in (self.exp_avg, self.exp_avg_sq):
+        for shard, xshard in ((self.exp_avg, self.x_exp_avg), (self.exp_avg_sq, self.x_exp_avg_sq)):
             buf = torch.zeros(self.store.numel, dtype=torch.float32, device=shard.device)
             buf[b:e].copy_(shard)
+            if self.x_shard is not None:
+                buf[self.x_shard[0]:self.x_shard[1]].copy_(xshard)
             if gather is not None:
                 gather(buf)
             full.append(buf)
@@ -105,6 +120,10 @@ class FusedAdamW(torch.optim.Optimizer):
             b, e = self.shard
             self.exp_avg.copy_(self._full[0][b:e])
             self.exp_avg_sq.copy_(self._full[1][b:e])
+            if self.x_shard is not None:
+                xb, xe = self.x_shard
+                self.x_exp_avg.copy_(self._full[0][xb:xe])
+                self.x_exp_avg_sq.copy_(self._full[1][xb:xe])
         for p in self.store.params:
             self.state[p].pop("exp_avg", None)
             self.state[p].pop("exp_avg_sq", None)
@@ -159,6 +178,8 @@ class FusedAdamW(torch.optim.Optimizer):
         if update is not None:
             update(hp)
             return loss
+        if self.x_shard is not None:
+            raise RuntimeError("an expert shard is updated by the caller (step(update=...))")
         lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2 = hp
         if st.master.is_cuda:
             comp = st.compute if st.compute is not None else torch.empty(0, device=st.master.device)
@@ -233,14 +254,15 @@ class FusedAdamW(torch.optim.Optimizer):
 def build_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.1,
                     beta1: float = 0.9, beta2: float = 0.95, eps: float = 1e-8,
                     fused: bool = True, store: Optional[FlatParamStore] = None,
-                    shard: Optional[Tuple[int, int]] = None) -> torch.optim.Optimizer:
+                    shard: Optional[Tuple[int, int]] = None,
+                    expert_shard: Optional[Tuple[int, int]] = None) -> torch.optim.Optimizer:
     store = store or getattr(model, "param_store", None)
     if store is not None and getattr(store, "mode", None) == "fsdp":
         from ..parallel.fsdp import FSDPAdamW
         return FSDPAdamW(store, lr=lr, betas=(beta1, beta2), eps=eps, weight_decay=weight_decay)
     if store is not None and fused:
         return FusedAdamW(store, lr=lr, betas=(beta1, beta2), eps=eps,
-                          weight_decay=weight_decay, shard=shard)
+                          weight_decay=weight_decay, shard=shard, expert_shard=expert_shard)
     decay, nodecay = [], []
     for name, p in model.named_parameters():
         if not p.requires_grad:

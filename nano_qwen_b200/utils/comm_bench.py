@@ -227,7 +227,7 @@ def main(argv=None) -> None:
 
     def rs():
         epoch[0] += 1
-        E.zero_rs(pg, pc, pf, rank, b, e, sq, epoch[0], 0)
+        E.zero_rs(pg, pc, pf, rank, b, e, sq, epoch[0], 0, 1.0)
 
     master = torch.randn(n, device=dev)
     m = torch.zeros(n, device=dev)

@@ -695,6 +695,34 @@ def sft_parallel_worker(rank, world, port, tmp, axis):
 
 
 # ----------------------------------------------- peer-memory ZeRO host code
+def _install_fake_peer(tmp):
+    """Route ``parallel.peer_dp`` to the file-backed stand-in (``fake_peer``)."""
+    import fake_peer
+    from nano_qwen_b200.parallel import peer_dp
+    peer_dp.symmetric_available = lambda group=None: True
+    peer_dp.SymmetricAllocator = fake_peer.make_allocator_factory(tmp)
+    peer_dp.ext = lambda: fake_peer.FakeZeroExt()
+    torch.cuda.synchronize = lambda *a, **k: None
+    # the peer engines (their stores come from the symmetric allocator) get
+    # a bf16 compute copy, as on the GPU
+    from nano_qwen_b200.training import engine as engine_mod
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    engine_mod.attach_param_store = lambda m, **kw: attach_param_store(
+        m, torch.bfloat16 if kw.get("alloc") is not None else None, **kw)
+    # the CPU forward reads the fp32 master, which the step updates only in
+    # this rank's ranges (the GPU forward reads the all-gathered bf16 copy):
+    # complete it after each step
+    if not getattr(peer_dp.PeerDataParallel, "_fake_gathers", False):
+        step = peer_dp.PeerDataParallel.fused_step
+
+        def fused_step(self, *a, **k):
+            norm = step(self, *a, **k)
+            self.gather_master()
+            return norm
+        peer_dp.PeerDataParallel.fused_step = fused_step
+        peer_dp.PeerDataParallel._fake_gathers = True
+
+
 def peer_dp_fake_worker(rank, world, port, tmp):
     """The host code of the fused data-parallel step (``PeerDataParallel``:
     epochs, shard bounds, the sharded moments, ``fused_step``, checkpointing)
@@ -710,26 +738,11 @@ def peer_dp_fake_worker(rank, world, port, tmp):
     from nano_qwen_b200.training.engine import TrainEngine
     from nano_qwen_b200.training.optimizer import attach_param_store
 
-    cur = {}
-
-    def make_alloc(group=None):
-        d = os.path.join(tmp, f"peer{len(cur)}")
-        os.makedirs(d, exist_ok=True)
-        a = fake_peer.FakeSymmetricAllocator(d, group)
-        cur["alloc"] = a
-        return a
-
-    peer_dp.symmetric_available = lambda group=None: True
-    peer_dp.SymmetricAllocator = make_alloc
-    peer_dp.ext = lambda: fake_peer.FakeZeroExt(cur["alloc"])
-    torch.cuda.synchronize = lambda *a, **k: None
+    _install_fake_peer(tmp)
     cfg = tiny_cfg()
     tc = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
           "scheduler": {"warmup_steps": 1, "total_steps": 20}}
     ref = TrainEngine(build(cfg), tc, torch.device("cpu"), dp_mode="shard")
-    # the peer engines get a bf16 compute copy, as on the GPU (the CPU forward
-    # itself reads the fp32 master)
-    engine_mod.attach_param_store = lambda m, **kw: attach_param_store(m, torch.bfloat16, **kw)
     a = TrainEngine(build(cfg), tc, torch.device("cpu"), dp_mode="p2p")
     assert isinstance(a.dp, peer_dp.PeerDataParallel) and a.optimizer.sharded
     data = [batch(cfg, 2, 16, seed=10 * s + rank) for s in range(5)]
@@ -856,6 +869,7 @@ def _layout_case(rank, world, layout):
     balance = layout.pop("balance", False)
     docs = layout.pop("docs", False)
     pad = layout.pop("pad", False)
+    dp_mode = layout.pop("dp_mode", None)
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=2,
                    tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
@@ -865,7 +879,9 @@ def _layout_case(rank, world, layout):
     ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_group=singles[rank])
     pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
     eng = TrainEngine(pm.apply_parallelism(build(cfg)),
-                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"), parallel=pm)
+                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"),
+                      dp_mode=dp_mode, parallel=pm)
+    _check_peer_step(eng, dp_mode)
     dp = pm.config.dp_size
     d = pm.coords["dp"]
     B = 4
@@ -902,10 +918,33 @@ def _layout_case(rank, world, layout):
         close(o["grad_norm"], r["grad_norm"], 1e-4, f"grad norm step {step}")
 
 
+def _check_peer_step(eng, dp_mode):
+    """A layout that asks for the peer-memory step gets it."""
+    if dp_mode == "p2p":
+        from nano_qwen_b200.parallel.peer_dp import PeerDataParallel
+        assert isinstance(eng.dp, PeerDataParallel), type(eng.dp)
+        assert eng.optimizer.sharded
+
+
+def peer_layouts_worker(rank, world, port, cases, tmp):
+    """``layouts_worker`` with the peer-memory step's host code running over
+    the file-backed stand-in for symmetric memory (``fake_peer``)."""
+    init(rank, world, port)
+    _install_fake_peer(tmp)
+    for name, layout in cases:
+        try:
+            _layout_case(rank, world, layout)
+        except AssertionError as e:
+            raise AssertionError(f"layout {name}: {e}") from e
+    dist.destroy_process_group()
+
+
 def layout_ckpts_worker(rank, world, port, cases, tmp):
     """Every (name, layout, from_single) checkpoint case of one world size
     in one spawned job; a failure names its case."""
     init(rank, world, port)
+    if any(lay.get("dp_mode") == "p2p" for _, lay, _ in cases):
+        _install_fake_peer(os.path.join(tmp, "peer"))
     for k, (name, layout, from_single) in enumerate(cases):
         try:
             _layout_ckpt_case(rank, world, layout, os.path.join(tmp, f"case{k}"), from_single)
@@ -925,13 +964,16 @@ def _layout_ckpt_case(rank, world, layout, tmp, from_single=False):
     layout = dict(layout)
     moe = layout.pop("moe", False)
     shard = layout.pop("shard_params", False)
+    dp_mode = layout.pop("dp_mode", None)
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
             "scheduler": {"warmup_steps": 0, "total_steps": 10}, "moe": {"global_batch_balance": False}}
     singles = [dist.new_group([r]) for r in range(world)]
     pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
     eng = TrainEngine(pm.apply_parallelism(build(cfg)),
-                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"), parallel=pm)
+                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"),
+                      dp_mode=dp_mode, parallel=pm)
+    _check_peer_step(eng, dp_mode)
     dp, d, B = pm.config.dp_size, pm.coords["dp"], 4
 
     def data(step):

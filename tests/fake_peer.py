@@ -3,9 +3,12 @@ fused data-parallel step (``parallel/peer_dp.py``) runs on Gloo CPU ranks.
 
 * ``FakeSymmetricAllocator``: every allocation is a file-backed tensor under a
   shared directory, mapped by every rank (the role of symmetric memory); a
-  "pointer" is an integer naming (allocation, rank), resolved by the fake
-  kernels.  Allocations happen in the same order on every rank, as with the
-  real allocator.
+  "pointer" is an integer naming (allocator, allocation, rank), resolved by
+  the fake kernels.  Allocations happen in the same order on every rank, as
+  with the real allocator; ``make_allocator_factory`` gives each allocator a
+  directory named by its creation order and its group's ranks, so the groups
+  of one layout (the two data-parallel groups of tp2 x dp2, say) and several
+  engines in one process never share files.
 * ``FakeZeroExt``: the four kernels of the step, restated with tensor
   operations over the mapped buffers: the same flag slots and sequence
   numbers (bounded spin on the peers' flags), the same reads and writes
@@ -26,6 +29,28 @@ import torch
 _SLOTS = 8
 
 
+_ALLOCATORS: List["FakeSymmetricAllocator"] = []
+
+
+def resolve(key: int) -> torch.Tensor:
+    return _ALLOCATORS[int(key) >> 20].resolve(key)
+
+
+def make_allocator_factory(tmp: str):
+    """``SymmetricAllocator`` stand-in: ``factory(group)``."""
+    count = [0]
+
+    def factory(group=None):
+        import torch.distributed as dist
+        ranks = (dist.get_process_group_ranks(group) if group is not None
+                 else list(range(dist.get_world_size())))
+        d = os.path.join(tmp, f"peer{count[0]}_{'-'.join(map(str, ranks))}")
+        count[0] += 1
+        os.makedirs(d, exist_ok=True)
+        return FakeSymmetricAllocator(d, group)
+    return factory
+
+
 class FakeSymmetricAllocator:
     def __init__(self, directory: str, group=None):
         import torch.distributed as dist
@@ -35,6 +60,8 @@ class FakeSymmetricAllocator:
         self.rank = dist.get_rank(group)
         self.meta: List[Tuple[int, torch.dtype]] = []
         self.tensors: List[torch.Tensor] = []
+        self.id = len(_ALLOCATORS)
+        _ALLOCATORS.append(self)
 
     def path(self, i: int, r: int) -> str:
         return os.path.join(self.dir, f"buf_{i}_{r}")
@@ -49,10 +76,10 @@ class FakeSymmetricAllocator:
 
     def peer_ptrs(self, t: torch.Tensor) -> List[int]:
         i = next(k for k, x in enumerate(self.tensors) if x.data_ptr() == t.data_ptr())
-        return [i * 1024 + r for r in range(self.world)]
+        return [(self.id << 20) | (i << 10) | r for r in range(self.world)]
 
     def resolve(self, key: int) -> torch.Tensor:
-        i, r = divmod(int(key), 1024)
+        i, r = (int(key) >> 10) & 1023, int(key) & 1023
         if r == self.rank:
             return self.tensors[i]
         cache: Dict[int, torch.Tensor] = self.__dict__.setdefault("_peers", {})
@@ -62,9 +89,16 @@ class FakeSymmetricAllocator:
         return cache[key]
 
 
+class _Registry:
+    resolve = staticmethod(resolve)
+
+
 class FakeZeroExt:
-    def __init__(self, alloc: FakeSymmetricAllocator, timeout_s: float = 30.0):
-        self.a = alloc
+    """The step's kernels over any fake allocator's buffers (a pointer names
+    its allocator)."""
+
+    def __init__(self, alloc=None, timeout_s: float = 30.0):
+        self.a = _Registry()
         self.timeout = timeout_s
 
     def _flags(self, key: int) -> torch.Tensor:
@@ -84,12 +118,12 @@ class FakeZeroExt:
                 raise TimeoutError(f"peer flag slot {slot} did not reach {epoch}")
             time.sleep(0.001)
 
-    def zero_rs(self, p_grad, p_comp, p_flags, rank, lo, hi, sq, epoch, ctas):
+    def zero_rs(self, p_grad, p_comp, p_flags, rank, lo, hi, sq, epoch, ctas, scale):
         self._signal(p_flags, rank, 0, epoch)
         self._wait(p_flags, rank, 0, epoch)
         if hi > lo:
             parts = [self.a.resolve(k)[lo:hi] for k in p_grad]
-            mean = torch.stack(parts).sum(0) / len(parts)
+            mean = torch.stack(parts).sum(0) * (scale / len(parts))
             self.a.resolve(p_grad[rank])[lo:hi] = mean
             sq += mean.double().pow(2).sum().float()
 

@@ -406,3 +406,56 @@ def pp_worker(rank, world, port):
         assert err < 5e-2, (n, err)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def peer_dp_layout_worker(rank, world, port):
+    """The peer-memory data-parallel step under model-parallel layouts
+    (``dp_mode="p2p"`` with a ``ParallelismManager``): expert parallelism
+    (the expert span reduced over the ranks holding the same experts) and
+    tensor parallelism, against the NCCL ZeRO step on the same layout, three
+    steps: losses, gradient norms, then every weight."""
+    init(rank, world, port)
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.ops import ext
+    from nano_qwen_b200.parallel.manager import ParallelConfig, ParallelismManager
+    from nano_qwen_b200.parallel.peer_dp import PeerDataParallel
+    from nano_qwen_b200.training.engine import TrainEngine
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=64, intermediate_size=512, vocab_size=4096,
+                      max_position_embeddings=512, tie_word_embeddings=True, num_experts=8,
+                      num_experts_per_tok=2, moe_intermediate_size=128)
+    dev = torch.device("cuda", rank)
+    tc = {"optimizer": {"lr": 1e-3, "grad_clip": 0.5},
+          "scheduler": {"warmup_steps": 0, "total_steps": 10}}
+    layouts = [{"ep_size": 2}] + ([{"tp_size": 2}] if world >= 4 else [])
+    for layout in layouts:
+        engines = {}
+        for mode in ("p2p", "shard"):
+            torch.manual_seed(0)
+            pm = ParallelismManager(ParallelConfig(**layout))
+            m = Qwen3Model(cfg).to(dev)
+            engines[mode] = (TrainEngine(pm.apply_parallelism(m), tc, dev, dp_mode=mode, parallel=pm), pm)
+        p2p, pm = engines["p2p"]
+        nccl, _ = engines["shard"]
+        assert isinstance(p2p.dp, PeerDataParallel), "symmetric memory unavailable"
+        d = pm.coords["dp"]
+        g = torch.Generator().manual_seed(21)
+        for step in range(3):
+            ids = torch.randint(0, cfg.vocab_size, (2 * pm.config.dp_size, 128), generator=g).to(dev)
+            mb = [{"input_ids": ids[2 * d:2 * d + 2], "labels": ids[2 * d:2 * d + 2]}]
+            a = p2p.train_step(mb)
+            b = nccl.train_step(mb)
+            assert abs(float(a["loss"]) - float(b["loss"])) < 2e-3 * float(b["loss"]), (layout, step)
+            assert abs(float(a["grad_norm"]) - float(b["grad_norm"])) < 2e-3 * float(b["grad_norm"]), \
+                (layout, step, float(a["grad_norm"]), float(b["grad_norm"]))
+        torch.cuda.synchronize()
+        assert ext().error_flag_read() == 0, "kernel error word set"
+        p2p.state_for_save()
+        nccl.state_for_save()
+        for (n, q), s in zip(p2p.model.named_parameters(), nccl.model.parameters()):
+            err = ((q.float() - s.float()).norm() / (s.float().norm() + 1e-12)).item()
+            assert err < 2e-3, (layout, n, err)
+        dist.barrier()
+        del p2p, nccl, engines
+    dist.destroy_process_group()

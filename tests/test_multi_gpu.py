@@ -34,6 +34,13 @@ def test_peer_memory_zero_step_matches_single_process(world):
 
 
 @pytest.mark.parametrize("world", WORLDS)
+def test_peer_memory_step_under_model_parallel_layouts(world):
+    _need(world)
+    import multi_gpu_workers as W
+    mp.spawn(W.peer_dp_layout_worker, args=(world, _port()), nprocs=world, join=True)
+
+
+@pytest.mark.parametrize("world", WORLDS)
 def test_fully_sharded_matches_zero_step(world):
     _need(world)
     import multi_gpu_workers as W

@@ -193,8 +193,35 @@ def test_engine_layouts_match_single_process(world):
     _run(W.layouts_worker, world, cases)
 
 
+# the peer-memory data-parallel step (dp_mode="p2p") under model
+# parallelism, its kernels restated over file-backed shared buffers
+PEER_LAYOUTS = {
+    "cp2-p2p": (2, {"cp_size": 2, "dp_mode": "p2p"}),
+    "ep2-moe-p2p": (2, {"ep_size": 2, "moe": True, "dp_mode": "p2p"}),
+    "dp2-moe-p2p": (2, {"moe": True, "dp_mode": "p2p"}),
+    "tp2xdp2-p2p": (4, {"tp_size": 2, "dp_mode": "p2p"}),
+    "pp2xdp2-p2p": (4, {"pp_size": 2, "pp_microbatches": 2, "dp_mode": "p2p"}),
+    "cp2xdp2-p2p": (4, {"cp_size": 2, "dp_mode": "p2p"}),
+    "ep2xdp2-moe-p2p": (4, {"ep_size": 2, "moe": True, "dp_mode": "p2p"}),
+    "tp2xep2-moe-p2p": (4, {"tp_size": 2, "ep_size": 2, "moe": True, "sequence_parallel": False,
+                            "dp_mode": "p2p"}),
+    "pp2xep2-moe-p2p": (4, {"pp_size": 2, "pp_microbatches": 2, "ep_size": 2, "moe": True,
+                            "dp_mode": "p2p"}),
+    "ep2xdp2-moe-p2p-accum2": (4, {"ep_size": 2, "moe": True, "dp_mode": "p2p", "accum": 2}),
+}
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_step_layouts_match_single_process(tmp_path, world):
+    """The peer-memory step's host code (shard bounds, the expert span's own
+    shard over the ranks holding the same experts, flag epochs, the norm
+    over TP / PP) under each layout trains like one process."""
+    cases = [(n, lay) for n, (w, lay) in sorted(PEER_LAYOUTS.items()) if w == world]
+    _run(W.peer_layouts_worker, world, cases, str(tmp_path))
+
+
 CKPT_LAYOUTS = ["dp2", "tp2", "pp2", "ep2-moe", "tp2xdp2-fsdp", "ep2-fsdp-moe", "tp2xpp2", "cp2",
-                "cp2-fsdp"]
+                "cp2-fsdp", "ep2xdp2-moe-p2p", "tp2xdp2-p2p"]
 
 
 @pytest.mark.parametrize("world", [2, 4])
@@ -202,7 +229,8 @@ def test_layout_checkpoints_move_to_and_from_one_process(tmp_path, world):
     """A checkpoint of each layout resumes in one process, and one process's
     checkpoint resumes in each layout, both continuing with equal losses and
     gradient norms (all cases of one world size in one job)."""
-    cases = [(n, LAYOUTS[n][1], fs) for n in CKPT_LAYOUTS if LAYOUTS[n][0] == world
+    every = {**LAYOUTS, **PEER_LAYOUTS}
+    cases = [(n, every[n][1], fs) for n in CKPT_LAYOUTS if every[n][0] == world
              for fs in (False, True)]
     _run(W.layout_ckpts_worker, world, cases, str(tmp_path))
 

@@ -94,6 +94,82 @@ def test_zero_step_without_publish_barrier_races():
         explore(_with_init(4, _zero_ranks(4, 3, publish=False)), schedules=150)
 
 
+def zero_ep_rank(r: int, W: int, EP: int, steps: int, expert_peers_only: bool = True):
+    """One rank of the fused data-parallel step with an expert span
+    (``PeerDataParallel`` under expert parallelism): ranks r with the same
+    r % EP hold the same experts.  The dense shard is reduced in two calls
+    (the pieces before and after the expert span; flag epochs 2t-1 and 2t);
+    the expert span is sharded over the X = W / EP ranks holding the same
+    experts, with its own flag words (``xzero0``) and the subset of the peer
+    pointers, and its AdamW stores only into those ranks' compute copies
+    (``expert_peers_only``); one publish barrier over all W ranks."""
+    X = W // EP
+    blk = r % EP
+    members = [p for p in range(W) if p % EP == blk]
+    xr = members.index(r)
+    for t in range(1, steps + 1):
+        for s in range(W):
+            yield ("read", ("comp", s), ("w", t - 1))
+        for j in range(X):
+            yield ("read", ("xcomp", j), ("xw", blk, t - 1))
+        for s in range(W):
+            yield ("write", r, ("grad", s), ("g", r, t))
+        for j in range(X):
+            yield ("write", r, ("xgrad", j), ("xg", r, t))
+        for call in (2 * t - 1, 2 * t):                       # dense pieces
+            for p in range(W):
+                yield ("signal", p, "zero0", r, call)
+            yield ("wait", "zero0", range(W), call)
+            if call == 2 * t - 1:
+                for p in range(W):
+                    yield ("read_peer", p, ("grad", r), ("g", p, t))
+                yield ("write", r, ("grad", r), ("mean", t))
+        for p in members:                                     # expert span
+            yield ("signal", p, "xzero0", xr, t)
+        yield ("wait", "xzero0", range(X), t)
+        for p in members:
+            yield ("read_peer", p, ("xgrad", xr), ("xg", p, t))
+        yield ("write", r, ("xgrad", xr), ("xmean", t))
+        yield ("collective", f"norm{t}")
+        yield ("read", ("grad", r), ("mean", t))
+        for p in range(W):
+            yield ("write", p, ("comp", r), ("w", t))
+        yield ("read", ("xgrad", xr), ("xmean", t))
+        for p in (members if expert_peers_only else range(W)):
+            yield ("write", p, ("xcomp", xr), ("xw", blk, t))
+        for p in range(W):
+            yield ("signal", p, "zero1", r, t)
+        yield ("wait", "zero1", range(W), t)
+
+
+def _zero_ep(W, EP, steps, expert_peers_only=True):
+    def make():
+        out = []
+        for r in range(W):
+            def chain(r=r):
+                for s in range(W):
+                    yield ("write", r, ("comp", s), ("w", 0))
+                for j in range(W // EP):
+                    yield ("write", r, ("xcomp", j), ("xw", r % EP, 0))
+                yield ("collective", "init")
+                yield from zero_ep_rank(r, W, EP, steps, expert_peers_only)
+            out.append(chain())
+        return out
+    return make
+
+
+@pytest.mark.parametrize("W,EP", [(2, 2), (4, 2), (8, 2), (8, 4)])
+def test_zero_step_with_expert_span_protocol(W, EP):
+    explore(_zero_ep(W, EP, 3), schedules=120)
+
+
+def test_zero_step_expert_update_to_every_rank_is_caught():
+    """Storing the updated expert shard into every data-parallel rank, not
+    only the ranks holding the same experts, overwrites other experts."""
+    with pytest.raises(ProtocolError):
+        explore(_zero_ep(4, 2, 2, expert_peers_only=False), schedules=60)
+
+
 # -------------------------------------------------------- tensor parallel
 
 AG_FWD, RS_FWD, AG_BWD, RS_BWD = 0, 1, 2, 3
