@@ -266,7 +266,6 @@ class PeerDataParallel(DataParallel):
         """Reduce-scatter + norm, clip, sharded AdamW + all-gather, publish.
         Returns the global gradient norm (device tensor)."""
         E = ext()
-        b, e = self.shard
         self.sync_grads()
         sq = self.sq
         if extra_sq is not None:
@@ -278,18 +277,14 @@ class PeerDataParallel(DataParallel):
 
         def update(hp):
             lr_d, lr_n, b1, b2, eps, wd, bc1, bc2 = hp
-            for lo, hi in self.dense_pieces(b, e):
-                if hi > lo:
-                    E.zero_adamw_ag(self.p_grad, self.p_comp, self.p_flags, self.rank,
-                                    self.store.master, optimizer.exp_avg, optimizer.exp_avg_sq,
-                                    self.clip, lo, hi, optimizer.state_base, self.store.decay_end,
-                                    lr_d, lr_n, b1, b2, eps, wd, bc1, bc2)
-            if self.x_shard is not None and self.x_shard[1] > self.x_shard[0]:
-                xb, xe = self.x_shard
-                E.zero_adamw_ag(self.x_grad, self.x_comp, self.x_flags, self.x_rank,
-                                self.store.master, optimizer.x_exp_avg, optimizer.x_exp_avg_sq,
-                                self.clip, xb, xe, xb, self.store.decay_end,
-                                lr_d, lr_n, b1, b2, eps, wd, bc1, bc2)
+            # the optimizer's state is this rank's owned ranges back to back
+            for lo, hi, off in optimizer.pieces:
+                expert = self.x_shard is not None and (lo, hi) == self.x_shard
+                ptrs = ((self.x_grad, self.x_comp, self.x_flags, self.x_rank) if expert
+                        else (self.p_grad, self.p_comp, self.p_flags, self.rank))
+                E.zero_adamw_ag(*ptrs, self.store.master, optimizer.exp_avg[off:],
+                                optimizer.exp_avg_sq[off:], self.clip, lo, hi, lo,
+                                self.store.decay_end, lr_d, lr_n, b1, b2, eps, wd, bc1, bc2)
 
         optimizer.step(update=update)
         E.zero_publish(self.p_grad, self.p_comp, self.p_flags, self.rank, self.epoch)

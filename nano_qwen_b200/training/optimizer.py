@@ -12,7 +12,7 @@ Otherwise it falls back to ``torch.optim.AdamW``.
 
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import List, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -33,19 +33,20 @@ class FusedAdamW(torch.optim.Optimizer):
     see) then exist only between ``gather_full_state`` and
     ``release_full_state``, which checkpointing calls around a save or load.
 
-    ``expert_shard`` = (begin, end): a second slice, inside the store's expert
-    span, that this rank also updates (expert parallelism shards the expert
-    span over the ranks holding the same experts, not over the whole
-    data-parallel group); its moments live in ``x_exp_avg`` /
-    ``x_exp_avg_sq``.  The caller performs that update (``step(update=...)``).
+    ``pieces`` = [(begin, end), ...]: the flat ranges this rank updates when
+    they are not one slice (under expert parallelism the dense shard skips
+    the expert span, which is sharded over the ranks holding the same
+    experts); the moments are the pieces' elements back to back, and the
+    caller performs the update (``step(update=...)``, ``pieces`` then holds
+    (begin, end, offset into the moments)).
     """
 
-    x_shard: Optional[Tuple[int, int]] = None
+    pieces: Optional[List[Tuple[int, int, int]]] = None
 
     def __init__(self, store: FlatParamStore, lr: float = 3e-4, betas=(0.9, 0.95),
                  eps: float = 1e-8, weight_decay: float = 0.1,
                  shard: Optional[Tuple[int, int]] = None,
-                 expert_shard: Optional[Tuple[int, int]] = None):
+                 pieces: Optional[List[Tuple[int, int]]] = None):
         self.store = store
         decay = [p for p in store.params if store.offset(p) < store.decay_end]
         nodecay = [p for p in store.params if store.offset(p) >= store.decay_end]
@@ -58,16 +59,17 @@ class FusedAdamW(torch.optim.Optimizer):
         dev = store.master.device
         self.shard = shard or (0, store.numel)
         b, e = self.shard
-        self.x_shard = expert_shard
-        self.sharded = (b, e) != (0, store.numel) or expert_shard is not None
+        self.sharded = (b, e) != (0, store.numel) or pieces is not None
         # flat index of element 0 of exp_avg / exp_avg_sq
         self.state_base = b if self.sharded else 0
         n = e - b if self.sharded else store.numel
+        if pieces is not None:
+            self.pieces, n = [], 0
+            for lo, hi in pieces:
+                self.pieces.append((lo, hi, n))
+                n += hi - lo
         self.exp_avg = torch.zeros(n, dtype=torch.float32, device=dev)
         self.exp_avg_sq = torch.zeros(n, dtype=torch.float32, device=dev)
-        xn = expert_shard[1] - expert_shard[0] if expert_shard is not None else 0
-        self.x_exp_avg = torch.zeros(xn, dtype=torch.float32, device=dev)
-        self.x_exp_avg_sq = torch.zeros(xn, dtype=torch.float32, device=dev)
         self._full = None
         # completes a full-size buffer across the data-parallel group (set by
         # the training engine; ``gather_full_state`` uses it by default)
@@ -81,6 +83,12 @@ class FusedAdamW(torch.optim.Optimizer):
             self._bind_views(self.exp_avg, self.exp_avg_sq)
 
     # ------------------------------------------------------- moment views
+    def _ranges(self):
+        """(flat begin, flat end, offset into the moments) of this rank's state."""
+        if self.pieces is not None:
+            return self.pieces
+        return [(self.shard[0], self.shard[1], 0)]
+
     def _bind_views(self, m: torch.Tensor, v: torch.Tensor) -> None:
         for p in self.store.params:
             o = self.store.offset(p)
@@ -95,14 +103,12 @@ class FusedAdamW(torch.optim.Optimizer):
         them in ``self.state``.  No-op for unsharded state."""
         if not self.sharded or self._full is not None:
             return
-        b, e = self.shard
         gather = gather or self.state_gather
         full = []
-        for shard, xshard in ((self.exp_avg, self.x_exp_avg), (self.exp_avg_sq, self.x_exp_avg_sq)):
+        for shard in (self.exp_avg, self.exp_avg_sq):
             buf = torch.zeros(self.store.numel, dtype=torch.float32, device=shard.device)
-            buf[b:e].copy_(shard)
-            if self.x_shard is not None:
-                buf[self.x_shard[0]:self.x_shard[1]].copy_(xshard)
+            for lo, hi, off in self._ranges():
+                buf[lo:hi].copy_(shard[off:off + hi - lo])
             if gather is not None:
                 gather(buf)
             full.append(buf)
@@ -117,13 +123,9 @@ class FusedAdamW(torch.optim.Optimizer):
         if self._full is None:
             return
         if scatter:
-            b, e = self.shard
-            self.exp_avg.copy_(self._full[0][b:e])
-            self.exp_avg_sq.copy_(self._full[1][b:e])
-            if self.x_shard is not None:
-                xb, xe = self.x_shard
-                self.x_exp_avg.copy_(self._full[0][xb:xe])
-                self.x_exp_avg_sq.copy_(self._full[1][xb:xe])
+            for lo, hi, off in self._ranges():
+                self.exp_avg[off:off + hi - lo].copy_(self._full[0][lo:hi])
+                self.exp_avg_sq[off:off + hi - lo].copy_(self._full[1][lo:hi])
         for p in self.store.params:
             self.state[p].pop("exp_avg", None)
             self.state[p].pop("exp_avg_sq", None)
@@ -178,8 +180,8 @@ class FusedAdamW(torch.optim.Optimizer):
         if update is not None:
             update(hp)
             return loss
-        if self.x_shard is not None:
-            raise RuntimeError("an expert shard is updated by the caller (step(update=...))")
+        if self.pieces is not None:
+            raise RuntimeError("a state in pieces is updated by the caller (step(update=...))")
         lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2 = hp
         if st.master.is_cuda:
             comp = st.compute if st.compute is not None else torch.empty(0, device=st.master.device)
@@ -255,14 +257,14 @@ def build_optimizer(model: nn.Module, lr: float = 3e-4, weight_decay: float = 0.
                     beta1: float = 0.9, beta2: float = 0.95, eps: float = 1e-8,
                     fused: bool = True, store: Optional[FlatParamStore] = None,
                     shard: Optional[Tuple[int, int]] = None,
-                    expert_shard: Optional[Tuple[int, int]] = None) -> torch.optim.Optimizer:
+                    pieces: Optional[List[Tuple[int, int]]] = None) -> torch.optim.Optimizer:
     store = store or getattr(model, "param_store", None)
     if store is not None and getattr(store, "mode", None) == "fsdp":
         from ..parallel.fsdp import FSDPAdamW
         return FSDPAdamW(store, lr=lr, betas=(beta1, beta2), eps=eps, weight_decay=weight_decay)
     if store is not None and fused:
         return FusedAdamW(store, lr=lr, betas=(beta1, beta2), eps=eps,
-                          weight_decay=weight_decay, shard=shard, expert_shard=expert_shard)
+                          weight_decay=weight_decay, shard=shard, pieces=pieces)
     decay, nodecay = [], []
     for name, p in model.named_parameters():
         if not p.requires_grad:

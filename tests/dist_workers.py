@@ -924,6 +924,20 @@ def _check_peer_step(eng, dp_mode):
         from nano_qwen_b200.parallel.peer_dp import PeerDataParallel
         assert isinstance(eng.dp, PeerDataParallel), type(eng.dp)
         assert eng.optimizer.sharded
+        # the owned ranges partition the store: every dense element once over
+        # the data-parallel group, every expert element once per expert set;
+        # the Adam moments hold exactly the owned elements
+        dp, st = eng.dp, eng.store
+        own = dp.owned_ranges()
+        n_own = sum(hi - lo for lo, hi in own)
+        assert eng.optimizer.exp_avg.numel() == n_own
+        xb, xe = dp.expert_span or (0, 0)
+        for lo, hi in own:
+            assert (lo, hi) == dp.x_shard or hi <= xb or lo >= xe, (lo, hi, dp.expert_span)
+        tot = torch.tensor([n_own], dtype=torch.float64)
+        dist.all_reduce(tot, group=dp.group)
+        sets = dp.world // dp.x_world if dp.x_shard is not None else 1
+        assert int(tot) == st.numel - (xe - xb) + (xe - xb) * sets, (int(tot), st.numel, xe - xb)
 
 
 def peer_layouts_worker(rank, world, port, cases, tmp):
