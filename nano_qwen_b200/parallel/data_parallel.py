@@ -14,6 +14,13 @@ packing copies):
   all-gather at all; the fp32 master/Adam state (16 B/param) is what gets
   sharded.
 
+Under expert parallelism the store's expert span holds different experts on
+the ranks of different EP blocks: shard mode then splits the store into
+three pieces with equal shards each (the store pads the span's ends for
+that): the dense pieces before and after the span over this group, the span
+over the ranks that hold the same experts, and the optimizer keeps its
+moments for the owned ranges only.
+
 Shard boundaries are multiples of 64 elements.  The Adam moments exist only
 for the shard (see ``FusedAdamW``); ``gather_master`` / ``gather_flat_``
 all-gather the fp32 master weights and the moments before a full state-dict
@@ -51,8 +58,8 @@ class DataParallel:
     parallelism (one per EP block).  The store's expert span is summed over it
     and divided by the data-parallel world, which equals the data-parallel mean
     of the full-batch expert gradient (each EP rank's expert gradient already
-    sums the tokens of its whole EP block).  Expert parallelism uses the
-    replicate mode."""
+    sums the tokens of its whole EP block).  In shard mode the span is also
+    sharded over that group (three pieces, ``split``)."""
 
     def __init__(self, store: FlatParamStore, mode: str = "shard", group=None,
                  bucket_mb: float = 256.0, expert_group=None):
@@ -61,14 +68,26 @@ class DataParallel:
         xb, xe = getattr(store, "expert_span", (0, 0))
         self.expert_span = (xb, xe) if xe > xb else None
         self.expert_group = expert_group
-        if self.expert_span is not None and mode == "shard":
-            mode = "replicate"
         self.mode = mode
         self.world = get_world_size(group)
         self.rank = get_rank(group)
         self.per = shard_bounds(store.numel, self.world, 0)[1]
         self.padded = self.per * self.world
         self.shard = shard_bounds(store.numel, self.world, self.rank) if mode == "shard" else (0, store.numel)
+        # shard mode with an expert span: the dense pieces before and after
+        # the span are sharded over this group, the span over the ranks
+        # holding the same experts (each owner's expert gradient already sums
+        # its EP block's tokens: sum over those ranks, divide by this world)
+        self.split = None
+        if self.expert_span is not None and mode == "shard" and self.world > 1:
+            xg = expert_group if expert_group is not None and get_world_size(expert_group) > 1 else None
+            xw = get_world_size(xg) if xg is not None else 1
+            xr = get_rank(xg) if xg is not None else 0
+            self.split = [(0, xb, group, self.world, self.rank, 1.0),
+                          (xe, store.numel, group, self.world, self.rank, 1.0),
+                          (xb, xe, xg, xw, xr, xw / self.world)]
+        # the optimizer keeps its state for ``owned_ranges()`` back to back
+        self.piecewise = self.split is not None
         self.bucket_elems = max(ALIGN, int(bucket_mb * 1024 * 1024 / 4) // ALIGN * ALIGN)
         # Reduce-scatter / all-gather need equal chunks: pad the flat buffers' views.
         self._grad_pad = None
@@ -86,12 +105,62 @@ class DataParallel:
         cached[: buf.numel()].copy_(buf)
         return cached
 
+    # ---------------------------------------------------------------- pieces
+    @staticmethod
+    def _owned(lo, hi, w, r):
+        per = shard_bounds(hi - lo, w, 0)[1]
+        return lo + min(hi - lo, r * per), lo + min(hi - lo, (r + 1) * per), per
+
+    def owned_ranges(self):
+        """The flat ranges this rank reduces and updates."""
+        if self.split is None:
+            return [self.shard]
+        out = []
+        for lo, hi, _, w, r, _ in self.split:
+            b, e, _ = self._owned(lo, hi, w, r)
+            if e > b:
+                out.append((b, e))
+        return out
+
+    def _piece_rs(self, g, lo, hi, grp, w, r, scale) -> None:
+        """Mean over ``grp`` of g[lo:hi], this rank's share written in place."""
+        b, e, per = self._owned(lo, hi, w, r)
+        if w > 1 and hi > lo:
+            src = g[lo:hi]
+            if per * w != hi - lo:
+                src = torch.zeros(per * w, dtype=g.dtype, device=g.device)
+                src[:hi - lo].copy_(g[lo:hi])
+            out = src[r * per:(r + 1) * per]
+            reduce_scatter_avg_(out, src, grp)
+            if src.data_ptr() != g[lo:hi].data_ptr():
+                g[b:e].copy_(out[:e - b])
+        if scale != 1.0 and e > b:
+            g[b:e].mul_(scale)
+
+    def _piece_ag(self, buf, lo, hi, grp, w, r) -> None:
+        """Complete buf[lo:hi] over ``grp`` from each rank's share."""
+        if w == 1 or hi <= lo:
+            return
+        b, e, per = self._owned(lo, hi, w, r)
+        if per * w == hi - lo:
+            bp = buf[lo:hi]
+            all_gather_flat_(bp, bp[r * per:(r + 1) * per].clone(), grp)
+            return
+        bp = torch.zeros(per * w, dtype=buf.dtype, device=buf.device)
+        bp[r * per:r * per + (e - b)].copy_(buf[b:e])
+        all_gather_flat_(bp, bp[r * per:(r + 1) * per].clone(), grp)
+        buf[lo:hi].copy_(bp[:hi - lo])
+
     # ------------------------------------------------------------- gradients
     @torch.no_grad()
     def sync_grads(self) -> None:
         if self.world == 1:
             return
         g = self.store.grad
+        if self.split is not None:
+            for lo, hi, grp, w, r, scale in self.split:
+                self._piece_rs(g, lo, hi, grp, w, r, scale)
+            return
         if self.mode == "replicate":
             for b, e in self._dense_ranges(g.numel()):
                 for s in range(b, e, self.bucket_elems):
@@ -152,6 +221,12 @@ class DataParallel:
             return
         st = self.store
         buf = st.compute if st.compute is not None else st.master
+        if self.split is not None:
+            for lo, hi, grp, w, r, _ in self.split:
+                self._piece_ag(buf, lo, hi, grp, w, r)
+            if st.compute is not None:
+                self.sync_fp32_span()
+            return
         bp = self._padded(buf, "_comp_pad")
         mine = bp[self.rank * self.per:(self.rank + 1) * self.per]
         if bp.data_ptr() != buf.data_ptr():
@@ -176,10 +251,10 @@ class DataParallel:
         if buf is None or buf.numel() != hi - lo:
             buf = self._span_buf = torch.zeros(hi - lo, dtype=torch.float32, device=m.device)
         buf.zero_()
-        b, e = self.shard
-        ib, ie = max(lo, b), min(hi, e)
-        if ie > ib:
-            buf[ib - lo:ie - lo].copy_(m[ib:ie])
+        for b, e in self.owned_ranges():
+            ib, ie = max(lo, b), min(hi, e)
+            if ie > ib:
+                buf[ib - lo:ie - lo].copy_(m[ib:ie])
         dist.all_reduce(buf, group=self.group)
         m[lo:hi].copy_(buf)
 
@@ -193,6 +268,10 @@ class DataParallel:
         own shard [b, e) (in place): the master weights, or the Adam moments
         before a checkpoint save."""
         if self.world == 1 or self.mode != "shard":
+            return
+        if self.split is not None:
+            for lo, hi, grp, w, r, _ in self.split:
+                self._piece_ag(buf, lo, hi, grp, w, r)
             return
         bp = self._padded(buf, "_master_pad")
         mine = bp[self.rank * self.per:(self.rank + 1) * self.per].clone()

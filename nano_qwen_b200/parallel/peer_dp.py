@@ -109,10 +109,12 @@ class PeerDataParallel(DataParallel):
     def __init__(self, store: FlatParamStore, allocator: SymmetricAllocator, group=None,
                  rs_ctas: int = 0, expert_group=None):
         super().__init__(store, mode="shard", group=group, expert_group=expert_group)
-        # DataParallel replicates a store with an expert span; this step
-        # shards both parts
         self.mode = "shard"
         self.shard = shard_bounds(store.numel, self.world, self.rank)
+        # its own layout: the dense shard over the whole store, skipping the
+        # expert span, and the span's shard over the expert ranks
+        self.split = None
+        self.piecewise = True
         self.alloc = allocator
         dev = store.master.device
         self.flags = allocator(2 * 8, torch.int32, dev)

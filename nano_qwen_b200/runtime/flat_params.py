@@ -99,12 +99,18 @@ class FlatParamStore:
         self.decay_end = 0
         self.group_spans: List[Tuple[int, int]] = []
         self.expert_span = (0, 0)
+        # the expert span starts and ends on a multiple of pad_multiple (ALIGN
+        # x the data-parallel world), so the dense pieces before and after it
+        # and the span itself each split into equal shards
+        span_pad = max(ALIGN, int(pad_multiple))
         for gi, grp in enumerate(ordered):
             off = (off + ALIGN - 1) // ALIGN * ALIGN
             if gi == len(dense_decay) and expert_decay:
+                off = (off + span_pad - 1) // span_pad * span_pad
                 self.expert_span = (off, 0)
             if gi == len(decay):
                 if expert_decay:
+                    off = (off + span_pad - 1) // span_pad * span_pad
                     self.expert_span = (self.expert_span[0], off)
                 self.decay_end = off
             g0 = off
@@ -115,9 +121,10 @@ class FlatParamStore:
                 off += p.numel()
             self.group_spans.append((g0, off))
         if len(decay) == len(ordered):
-            self.decay_end = off
             if expert_decay:
+                off = (off + span_pad - 1) // span_pad * span_pad
                 self.expert_span = (self.expert_span[0], off)
+            self.decay_end = off
         # Padding to a multiple of (ALIGN * data-parallel world) lets reduce-scatter and
         # all-gather run on equal-size shards of the buffers themselves.
         pad = max(ALIGN, int(pad_multiple))

@@ -124,7 +124,7 @@ class TrainEngine:
             self.model, lr=opt.get("lr", 3e-4), weight_decay=opt.get("weight_decay", 0.1),
             beta1=opt.get("beta1", 0.9), beta2=opt.get("beta2", 0.95), eps=opt.get("eps", 1e-8),
             fused=True, store=self.store, shard=self.dp.shard if self.dp is not None else None,
-            pieces=self.dp.owned_ranges() if hasattr(self.dp, "owned_ranges") else None)
+            pieces=self.dp.owned_ranges() if getattr(self.dp, "piecewise", False) else None)
         if self.dp is not None and hasattr(self.optimizer, "state_gather"):
             self.optimizer.state_gather = self.dp.gather_flat_
         self._init_tail(training_config, opt, dp_group, world)

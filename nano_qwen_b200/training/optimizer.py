@@ -134,14 +134,17 @@ class FusedAdamW(torch.optim.Optimizer):
     # ----------------------------------------------------------- clipping
     @torch.no_grad()
     def clip_grad_norm_(self, max_norm: float, norm_sq_reduce=None) -> torch.Tensor:
-        """Global L2 norm of the flat gradient (this shard, optionally summed
-        over ranks by ``norm_sq_reduce``); sets the clip factor used by step()."""
-        b, e = self.shard
-        g = self.store.grad[b:e]
-        if g.is_cuda:
-            sq = ext().sum_squares(g)
-        else:
-            sq = torch.linalg.vector_norm(g).square().reshape(())
+        """Global L2 norm of the flat gradient (this rank's ranges, optionally
+        summed over ranks by ``norm_sq_reduce``); sets the clip factor used by
+        step()."""
+        sq = None
+        for lo, hi, _ in self._ranges():
+            g = self.store.grad[lo:hi]
+            part = (ext().sum_squares(g) if g.is_cuda
+                    else torch.linalg.vector_norm(g).square().reshape(()))
+            sq = part if sq is None else sq + part
+        if sq is None:
+            sq = torch.zeros((), dtype=torch.float32, device=self.store.grad.device)
         if norm_sq_reduce is not None:
             sq = norm_sq_reduce(sq)
         norm = sq.sqrt()
@@ -175,24 +178,25 @@ class FusedAdamW(torch.optim.Optimizer):
         through ``step`` keeps the LR scheduler's step bookkeeping intact."""
         loss = closure() if closure is not None else None
         st = self.store
-        b, e = self.shard
         hp = self.advance()
         if update is not None:
             update(hp)
             return loss
-        if self.pieces is not None:
-            raise RuntimeError("a state in pieces is updated by the caller (step(update=...))")
         lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2 = hp
-        if st.master.is_cuda:
-            comp = st.compute if st.compute is not None else torch.empty(0, device=st.master.device)
-            ext().adamw_flat(st.master, st.grad, self.exp_avg, self.exp_avg_sq, comp,
-                             self.clip_scale, b, e, self.state_base, st.decay_end, lr_decay,
-                             lr_nodecay, beta1, beta2, eps, wd, bc1, bc2)
-        else:
-            self._step_cpu(b, e, lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2)
+        for lo, hi, off in self._ranges():
+            if hi <= lo:
+                continue
+            m, v = self.exp_avg[off:], self.exp_avg_sq[off:]
+            if st.master.is_cuda:
+                comp = st.compute if st.compute is not None else torch.empty(0, device=st.master.device)
+                ext().adamw_flat(st.master, st.grad, m, v, comp, self.clip_scale, lo, hi, lo,
+                                 st.decay_end, lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2)
+            else:
+                self._step_cpu(lo, hi, m, v, lr_decay, lr_nodecay, beta1, beta2, eps, wd, bc1, bc2)
         return loss
 
-    def _step_cpu(self, b, e, lr_d, lr_n, beta1, beta2, eps, wd, bc1, bc2):
+    def _step_cpu(self, b, e, m_all, v_all, lr_d, lr_n, beta1, beta2, eps, wd, bc1, bc2):
+        """[b, e) of the store; element b's moments at m_all[0] / v_all[0]."""
         st = self.store
         for lo, hi, lr, w in ((b, min(e, st.decay_end), lr_d, wd),
                               (max(b, st.decay_end), e, lr_n, 0.0)):
@@ -200,9 +204,8 @@ class FusedAdamW(torch.optim.Optimizer):
                 continue
             p = st.master[lo:hi]
             g = st.grad[lo:hi] * self.clip_scale
-            sb = self.state_base
-            m = self.exp_avg[lo - sb:hi - sb]
-            v = self.exp_avg_sq[lo - sb:hi - sb]
+            m = m_all[lo - b:hi - b]
+            v = v_all[lo - b:hi - b]
             p.mul_(1 - lr * w)
             m.mul_(beta1).add_(g, alpha=1 - beta1)
             v.mul_(beta2).addcmul_(g, g, value=1 - beta2)

@@ -333,6 +333,9 @@ def ep_checkpoint_worker(rank, world, port, tmp):
     assert e2.optimizer.sharded
     mgr.load(e2.model, e2.optimizer, e2.scheduler, str(path))
     e2.optimizer.gather_full_state()
+    # the expert-parallel engine's moments are sharded too (the checkpoint
+    # manager released its full views after the save)
+    e1.state_for_save()
     full = dict(e2.model.named_parameters())
     e_loc = cfg.num_experts // world
     n_checked = 0
@@ -349,6 +352,7 @@ def ep_checkpoint_worker(rank, world, port, tmp):
             assert torch.equal(e1.optimizer.state[p]["exp_avg"], e2.optimizer.state[full[n]]["exp_avg"]), n
     assert n_checked > 0
     e2.optimizer.release_full_state()
+    e1.optimizer.release_full_state()
     dist.destroy_process_group()
 
 
@@ -919,11 +923,13 @@ def _layout_case(rank, world, layout):
 
 
 def _check_peer_step(eng, dp_mode):
-    """A layout that asks for the peer-memory step gets it."""
+    """A layout that asks for the peer-memory step gets it; a data-parallel
+    step that keeps its state in pieces owns a partition of the store."""
     if dp_mode == "p2p":
         from nano_qwen_b200.parallel.peer_dp import PeerDataParallel
         assert isinstance(eng.dp, PeerDataParallel), type(eng.dp)
         assert eng.optimizer.sharded
+    if getattr(eng.dp, "piecewise", False):
         # the owned ranges partition the store: every dense element once over
         # the data-parallel group, every expert element once per expert set;
         # the Adam moments hold exactly the owned elements
@@ -932,11 +938,13 @@ def _check_peer_step(eng, dp_mode):
         n_own = sum(hi - lo for lo, hi in own)
         assert eng.optimizer.exp_avg.numel() == n_own
         xb, xe = dp.expert_span or (0, 0)
+        x_world = (dp.split[2][3] if getattr(dp, "split", None) is not None
+                   else getattr(dp, "x_world", 1))
         for lo, hi in own:
-            assert (lo, hi) == dp.x_shard or hi <= xb or lo >= xe, (lo, hi, dp.expert_span)
+            assert hi <= xb or lo >= xe or (xb <= lo and hi <= xe), (lo, hi, dp.expert_span)
         tot = torch.tensor([n_own], dtype=torch.float64)
         dist.all_reduce(tot, group=dp.group)
-        sets = dp.world // dp.x_world if dp.x_shard is not None else 1
+        sets = dp.world // x_world if dp.expert_span is not None else 1
         assert int(tot) == st.numel - (xe - xb) + (xe - xb) * sets, (int(tot), st.numel, xe - xb)
 
 
