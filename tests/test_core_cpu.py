@@ -127,6 +127,69 @@ def test_fused_adamw_cpu_matches_torch():
         assert torch.allclose(p, bp[n], atol=1e-5, rtol=1e-4), n
 
 
+def test_fused_adamw_pieces_match_whole_store():
+    """Moments kept for a list of flat ranges (back to back): three
+    optimizers whose pieces cover the store between them update exactly like
+    one whole-store optimizer, and their gathered moments agree."""
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.optimizer import FusedAdamW, attach_param_store
+    torch.manual_seed(0)
+    cfg = ModelConfig(**TINY)
+    a = Qwen3Model(cfg)
+    store = attach_param_store(a, torch.float32, torch.device("cpu"))
+    n = store.numel
+    cut = [0, n // 64 // 3 * 64, 2 * n // 64 // 3 * 64, n]
+    whole = FusedAdamW(store, lr=1e-2, weight_decay=0.1)
+    parts = [[(cut[0], cut[1]), (cut[2], cut[3])], [(cut[1], cut[2])]]
+    opts = [FusedAdamW(store, lr=1e-2, weight_decay=0.1, pieces=pc) for pc in parts]
+    assert [o.exp_avg.numel() for o in opts] == [cut[1] + n - cut[2], cut[2] - cut[1]]
+    ids = torch.randint(0, 256, (2, 16))
+    start = store.master.clone()
+    store.zero_grad()
+    a(ids, labels=ids)["loss"].backward()
+    # the pieces' squared norms add up to the whole store's
+    sq = sum(float(o.clip_grad_norm_(0.0)) ** 2 for o in opts)
+    assert abs(sq - float(whole.clip_grad_norm_(0.0)) ** 2) < 1e-5 * sq
+    for _ in range(2):
+        whole.step()
+    ref = store.master.clone()
+    store.master.copy_(start)
+    for _ in range(2):
+        for o in opts:
+            o.step()
+    assert torch.allclose(store.master, ref, atol=1e-6, rtol=1e-5)
+    full = torch.zeros(n)
+    for o in opts:
+        o.gather_full_state()
+        for p in store.params:
+            full_view = o.state[p]["exp_avg"]
+            o_ = store.offset(p)
+            full[o_:o_ + p.numel()] += full_view.reshape(-1)
+    assert torch.allclose(full, whole.exp_avg, atol=1e-7)
+
+
+def test_flat_store_pads_expert_span_to_shard_multiple():
+    """The expert span starts and ends on a multiple of pad_multiple, so the
+    dense pieces around it and the span itself split into equal shards."""
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.training.optimizer import attach_param_store
+    torch.manual_seed(0)
+    cfg = ModelConfig(**dict(TINY, num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32))
+    m = Qwen3Model(cfg)
+    for n, p in m.named_parameters():
+        if ".experts." in n:
+            p._ep_local = True
+    store = attach_param_store(m, torch.float32, torch.device("cpu"), pad_multiple=64 * 8)
+    xb, xe = store.expert_span
+    assert xe > xb and xb % 512 == 0 and xe % 512 == 0 and store.numel % 512 == 0
+    for n, p in zip(store.names, store.params):
+        o = store.offset(p)
+        inside = xb <= o < xe
+        assert inside == (".experts." in n), n
+
+
 def test_grad_clip_norm():
     from nano_qwen_b200.config import ModelConfig
     from nano_qwen_b200.models import Qwen3Model
