@@ -685,7 +685,7 @@ class FullyShardedStore:
         return {"shards": shard, "persistent_units": persistent, "largest_block_unit": largest}
 
 
-def memory_plan(model: nn.Module, world: int, compute_bytes: int = 2) -> Dict[str, float]:
+def memory_plan(model: nn.Module, world: int, compute_bytes: int = 2, ep: int = 1) -> Dict[str, float]:
     """Bytes per rank of ``model`` (a meta-device model will do: nothing is
     allocated) fully sharded over ``world`` ranks, next to the flat ZeRO-2
     layout of ``FlatParamStore`` + ``FusedAdamW``:
@@ -697,7 +697,13 @@ def memory_plan(model: nn.Module, world: int, compute_bytes: int = 2) -> Dict[st
     * ``fsdp_blocks_peak``: two gathered block units (the running block and
       the prefetched one) and one block's fp32 gradient;
     * ``zero2_state``: full fp32 master, gradient and compute copy on every
-      rank, moments sharded."""
+      rank, moments sharded;
+    * with ``ep`` > 1 (``model`` holding every expert, ``.experts.`` in their
+      names): ``zero2_ep_state``, the ZeRO-2 state of one rank that holds
+      1/ep of the experts, its expert moments sharded over the world / ep
+      ranks holding the same experts, and ``zero2_ep_replicated_state``, the
+      same with every moment of the rank's parameters kept (what replicating
+      the gradients of expert-parallel runs costs)."""
     _, pb, pbe, rd, rn, small = partition(model)
     units = []
     for gs in pb + pbe:
@@ -715,9 +721,17 @@ def memory_plan(model: nn.Module, world: int, compute_bytes: int = 2) -> Dict[st
     peak_blocks = biggest * (2 * compute_bytes + 4)
     numel = sum(p.numel() for p in model.parameters() if p.requires_grad)
     zero2 = numel * (4 + 4 + compute_bytes) + numel * 8 / world
-    return {"params": float(numel), "fsdp_state": float(state), "fsdp_persistent": float(persistent),
-            "fsdp_blocks_peak": float(peak_blocks),
-            "fsdp_total": float(state + persistent + peak_blocks), "zero2_state": float(zero2)}
+    out = {"params": float(numel), "fsdp_state": float(state), "fsdp_persistent": float(persistent),
+           "fsdp_blocks_peak": float(peak_blocks),
+           "fsdp_total": float(state + persistent + peak_blocks), "zero2_state": float(zero2)}
+    if ep > 1:
+        expert = sum(p.numel() for n, p in model.named_parameters()
+                     if p.requires_grad and ".experts." in n)
+        dense, local = numel - expert, expert / ep
+        resident = (dense + local) * (4 + 4 + compute_bytes)
+        out["zero2_ep_state"] = float(resident + dense * 8 / world + local * 8 / (world / ep))
+        out["zero2_ep_replicated_state"] = float(resident + (dense + local) * 8)
+    return out
 
 
 class FSDPAdamW(FusedAdamW):

@@ -279,6 +279,28 @@ def test_fully_sharded_memory_plan():
     assert eight["fsdp_total"] < eight["zero2_state"]
 
 
+def test_expert_parallel_zero2_memory_plan():
+    """ZeRO-2 under expert parallelism: one rank holds 1/ep of the experts;
+    sharding their moments over the world / ep ranks holding the same
+    experts (and the dense moments over the world) against keeping every
+    moment of the rank's parameters, by the element counts."""
+    from nano_qwen_b200.config import ModelConfig
+    from nano_qwen_b200.models import Qwen3Model
+    from nano_qwen_b200.parallel.fsdp import memory_plan
+    with torch.device("meta"):
+        m = Qwen3Model(ModelConfig(**dict(MODEL, hidden_size=256, intermediate_size=512,
+                                          vocab_size=4096, num_hidden_layers=4, num_experts=8,
+                                          num_experts_per_tok=2, moe_intermediate_size=128)))
+    n = sum(p.numel() for p in m.parameters())
+    x = sum(p.numel() for k, p in m.named_parameters() if ".experts." in k)
+    plan = memory_plan(m, 8, ep=2)
+    local = (n - x) + x / 2
+    assert abs(plan["zero2_ep_replicated_state"] - local * 18) < 1
+    assert abs(plan["zero2_ep_state"] - (local * 10 + (n - x) * 8 / 8 + x / 2 * 8 / 4)) < 1
+    assert plan["zero2_ep_state"] < plan["zero2_ep_replicated_state"]
+    assert "zero2_ep_state" not in memory_plan(m, 8)
+
+
 @pytest.mark.parametrize("moe", [False, True])
 def test_cached_generation_paths_match_full_forward_on_cpu(moe):
     """The three inference paths agree with one full forward (fp32, CPU):
