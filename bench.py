@@ -309,6 +309,7 @@ def run_ours(args, world, rank, local):
     mode = None
     if eng.dp is not None:
         mode = "p2p" if hasattr(eng.dp, "fused_step") else eng.dp.mode
+    dp_step = mode
     if par == "tp" and world > 1:
         mode = "tp-fused" if getattr(eng.model, "tp_fused", False) else "tp-nccl"
     if par == "ep" and world > 1:
@@ -317,7 +318,7 @@ def run_ours(args, world, rank, local):
     if par == "cp" and world > 1:
         mode = "cp-" + args.cp_mode
     return ms, clocks, {"kernel_error_flag": err, "gpu_launches_per_step": launches,
-                        "dp_mode": mode}, e2e
+                        "dp_mode": mode, "dp_step": dp_step}, e2e
 
 
 def count_launches(step_fn, ids):
@@ -584,6 +585,9 @@ def main():
         line["gpu_launches"] = extra["gpu_launches_per_step"]["ours"] * args.steps
         line["launches_per_step"] = extra["gpu_launches_per_step"]
         line["kernel_error_flag"] = extra["kernel_error_flag"]
+        # the data-parallel optimizer step that ran: p2p (peer memory),
+        # shard (NCCL ZeRO-2), replicate, fsdp, or none (one replica)
+        line["dp_step"] = extra.get("dp_step")
     if e2e is not None:
         line["e2e"] = {"value": round(tokens_per_step / e2e["s_per_step"], 1), "unit": "tokens/s",
                        "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]}
