@@ -208,6 +208,9 @@ PEER_LAYOUTS = {
     "pp2xep2-moe-p2p": (4, {"pp_size": 2, "pp_microbatches": 2, "ep_size": 2, "moe": True,
                             "dp_mode": "p2p"}),
     "ep2xdp2-moe-p2p-accum2": (4, {"ep_size": 2, "moe": True, "dp_mode": "p2p", "accum": 2}),
+    "ep2-moe-balance-p2p": (2, {"ep_size": 2, "moe": True, "balance": True, "dp_mode": "p2p"}),
+    "cp2-moe-p2p": (2, {"cp_size": 2, "moe": True, "dp_mode": "p2p"}),
+    "tp2-moe-p2p-tied": (4, {"tp_size": 2, "moe": True, "tied": True, "dp_mode": "p2p"}),
 }
 
 
