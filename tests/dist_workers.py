@@ -874,6 +874,8 @@ def _layout_case(rank, world, layout):
     docs = layout.pop("docs", False)
     pad = layout.pop("pad", False)
     dp_mode = layout.pop("dp_mode", None)
+    cfg_mode = layout.pop("dp_mode_cfg", None)   # named in the training config instead
+    expect_nccl = layout.pop("expect_nccl", False)
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=2,
                    tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
@@ -882,10 +884,15 @@ def _layout_case(rank, world, layout):
     singles = [dist.new_group([r]) for r in range(world)]
     ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_group=singles[rank])
     pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
-    eng = TrainEngine(pm.apply_parallelism(build(cfg)),
-                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"),
-                      dp_mode=dp_mode, parallel=pm)
-    _check_peer_step(eng, dp_mode)
+    dcfg = {"shard_params": shard}
+    if cfg_mode:
+        dcfg["dp_mode"] = cfg_mode
+    eng = TrainEngine(pm.apply_parallelism(build(cfg)), dict(tcfg, distributed=dcfg),
+                      torch.device("cpu"), dp_mode=dp_mode, parallel=pm)
+    _check_peer_step(eng, dp_mode or cfg_mode)
+    if expect_nccl:   # the configured default (dp_comm: p2p) under model parallelism
+        from nano_qwen_b200.parallel.peer_dp import PeerDataParallel
+        assert eng.dp is not None and not isinstance(eng.dp, PeerDataParallel), type(eng.dp)
     dp = pm.config.dp_size
     d = pm.coords["dp"]
     B = 4

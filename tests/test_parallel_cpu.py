@@ -211,6 +211,8 @@ PEER_LAYOUTS = {
     "ep2-moe-balance-p2p": (2, {"ep_size": 2, "moe": True, "balance": True, "dp_mode": "p2p"}),
     "cp2-moe-p2p": (2, {"cp_size": 2, "moe": True, "dp_mode": "p2p"}),
     "tp2-moe-p2p-tied": (4, {"tp_size": 2, "moe": True, "tied": True, "dp_mode": "p2p"}),
+    "tp2xdp2-p2p-config": (4, {"tp_size": 2, "dp_mode_cfg": "p2p"}),
+    "tp2xdp2-default-nccl": (4, {"tp_size": 2, "expect_nccl": True}),
 }
 
 
