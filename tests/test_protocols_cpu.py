@@ -94,7 +94,8 @@ def test_zero_step_without_publish_barrier_races():
         explore(_with_init(4, _zero_ranks(4, 3, publish=False)), schedules=150)
 
 
-def zero_ep_rank(r: int, W: int, EP: int, steps: int, expert_peers_only: bool = True):
+def zero_ep_rank(r: int, W: int, EP: int, steps: int, expert_peers_only: bool = True,
+                 skip_empty: bool = False):
     """One rank of the fused data-parallel step with an expert span
     (``PeerDataParallel`` under expert parallelism): ranks r with the same
     r % EP hold the same experts.  The dense shard is reduced in two calls
@@ -102,7 +103,9 @@ def zero_ep_rank(r: int, W: int, EP: int, steps: int, expert_peers_only: bool = 
     the expert span is sharded over the X = W / EP ranks holding the same
     experts, with its own flag words (``xzero0``) and the subset of the peer
     pointers, and its AdamW stores only into those ranks' compute copies
-    (``expert_peers_only``); one publish barrier over all W ranks."""
+    (``expert_peers_only``); one publish barrier over all W ranks.
+    ``skip_empty``: rank 0 leaves out its second (empty) dense call, with
+    its own epoch count, which the peers' waits must expose."""
     X = W // EP
     blk = r % EP
     members = [p for p in range(W) if p % EP == blk]
@@ -116,11 +119,12 @@ def zero_ep_rank(r: int, W: int, EP: int, steps: int, expert_peers_only: bool = 
             yield ("write", r, ("grad", s), ("g", r, t))
         for j in range(X):
             yield ("write", r, ("xgrad", j), ("xg", r, t))
-        for call in (2 * t - 1, 2 * t):                       # dense pieces
+        calls = (t,) if (skip_empty and r == 0) else (2 * t - 1, 2 * t)
+        for call in calls:                                    # dense pieces
             for p in range(W):
                 yield ("signal", p, "zero0", r, call)
             yield ("wait", "zero0", range(W), call)
-            if call == 2 * t - 1:
+            if call == calls[0]:
                 for p in range(W):
                     yield ("read_peer", p, ("grad", r), ("g", p, t))
                 yield ("write", r, ("grad", r), ("mean", t))
@@ -142,7 +146,7 @@ def zero_ep_rank(r: int, W: int, EP: int, steps: int, expert_peers_only: bool = 
         yield ("wait", "zero1", range(W), t)
 
 
-def _zero_ep(W, EP, steps, expert_peers_only=True):
+def _zero_ep(W, EP, steps, expert_peers_only=True, skip_empty=False):
     def make():
         out = []
         for r in range(W):
@@ -152,7 +156,7 @@ def _zero_ep(W, EP, steps, expert_peers_only=True):
                 for j in range(W // EP):
                     yield ("write", r, ("xcomp", j), ("xw", r % EP, 0))
                 yield ("collective", "init")
-                yield from zero_ep_rank(r, W, EP, steps, expert_peers_only)
+                yield from zero_ep_rank(r, W, EP, steps, expert_peers_only, skip_empty)
             out.append(chain())
         return out
     return make
@@ -161,6 +165,13 @@ def _zero_ep(W, EP, steps, expert_peers_only=True):
 @pytest.mark.parametrize("W,EP", [(2, 2), (4, 2), (8, 2), (8, 4)])
 def test_zero_step_with_expert_span_protocol(W, EP):
     explore(_zero_ep(W, EP, 3), schedules=120)
+
+
+def test_zero_step_uneven_dense_calls_are_caught():
+    """A rank that skips its empty dense piece (and so counts its flag
+    epochs differently) leaves its peers waiting or reading early."""
+    with pytest.raises(ProtocolError):
+        explore(_zero_ep(4, 2, 3, skip_empty=True), schedules=60)
 
 
 def test_zero_step_expert_update_to_every_rank_is_caught():
