@@ -151,6 +151,77 @@ class DataParallel:
         all_gather_flat_(bp, bp[r * per:(r + 1) * per].clone(), grp)
         buf[lo:hi].copy_(bp[:hi - lo])
 
+    # --------------------------------------------------------------- overlap
+    def attach_overlap(self, model) -> None:
+        """Shard mode without an expert span: reduce-scatter each transformer
+        block's (decay) gradient span as soon as the block's backward is done
+        on the last micro-batch, on a side stream next to the rest of the
+        backward; the remaining ranges after the backward.  Ownership becomes
+        per span (each span split into equal shards), so this is attached
+        before the optimizer is built (``piecewise``)."""
+        if self.mode != "shard" or self.world == 1 or self.split is not None:
+            return
+        from ..models.transformer import TransformerBlock
+        st = self.store
+        spans = []
+        for blk in model.modules():
+            if not isinstance(blk, TransformerBlock):
+                continue
+            ps = [p for p in blk.parameters() if id(p) in st.offsets
+                  and st.offsets[id(p)] < st.decay_end]
+            if not ps:
+                continue
+            lo = min(st.offsets[id(p)] for p in ps) // ALIGN * ALIGN
+            hi = (max(st.offsets[id(p)] + p.numel() for p in ps) + ALIGN - 1) // ALIGN * ALIGN
+            mine = {id(p) for p in ps}
+            if any(id(q) not in mine and lo <= st.offsets[id(q)] < hi for q in st.params):
+                continue  # not contiguous: reduced with the rest
+            spans.append((lo, hi, blk))
+        spans.sort(key=lambda t: t[0])
+        pieces, hooks, pos = [], {}, 0
+        for lo, hi, blk in spans:
+            if lo < pos:
+                continue
+            if lo > pos:
+                pieces.append((pos, lo))
+            hooks[len(pieces)] = blk
+            pieces.append((lo, hi))
+            pos = hi
+        if pos < st.numel:
+            pieces.append((pos, st.numel))
+        self.split = [(lo, hi, self.group, self.world, self.rank, 1.0) for lo, hi in pieces]
+        self.piecewise = True
+        self._hooked = set(hooks)
+        self._issued, self._final = set(), False
+        self._stream = torch.cuda.Stream(device=st.grad.device) if st.grad.is_cuda else None
+        for k, blk in hooks.items():
+            blk.grad_ready_hook = self._make_hook(k)
+
+    def _make_hook(self, k: int):
+        def hook():
+            if not self._final or k in self._issued:
+                return
+            self._issued.add(k)
+            lo, hi, grp, w, r, scale = self.split[k]
+            if self._stream is None:
+                self._piece_rs(self.store.grad, lo, hi, grp, w, r, scale)
+                return
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream())
+            self._stream.wait_event(ev)
+            with torch.cuda.stream(self._stream):
+                self._piece_rs(self.store.grad, lo, hi, grp, w, r, scale)
+        return hook
+
+    def begin_step(self, final_micro: bool) -> None:
+        """Called by the engine before each micro-batch's backward: the
+        block hooks reduce only on the last one."""
+        if getattr(self, "_hooked", None) is None:
+            return
+        if final_micro and not self._final:
+            self._issued = set()
+        self._final = final_micro
+
     # ------------------------------------------------------------- gradients
     @torch.no_grad()
     def sync_grads(self) -> None:
@@ -158,8 +229,16 @@ class DataParallel:
             return
         g = self.store.grad
         if self.split is not None:
-            for lo, hi, grp, w, r, scale in self.split:
-                self._piece_rs(g, lo, hi, grp, w, r, scale)
+            hooked = getattr(self, "_hooked", None)
+            if hooked is not None and self._stream is not None:
+                torch.cuda.current_stream().wait_stream(self._stream)
+            issued = self._issued if (hooked is not None and self._final) else set()
+            self.last_overlapped = len(issued)   # spans reduced during the backward
+            for k, (lo, hi, grp, w, r, scale) in enumerate(self.split):
+                if k not in issued:
+                    self._piece_rs(g, lo, hi, grp, w, r, scale)
+            if hooked is not None:
+                self._issued, self._final = set(), False
             return
         if self.mode == "replicate":
             for b, e in self._dense_ranges(g.numel()):

@@ -118,6 +118,10 @@ class TrainEngine:
         else:
             self.dp = (DataParallel(self.store, mode=dp_mode, group=dp_group,
                                     expert_group=expert_group) if world > 1 else None)
+            if self.dp is not None and dist_cfg.get("overlap_grad_reduce", False):
+                # per-block NCCL reduce-scatter during the backward (opt-in;
+                # sets the ownership the optimizer is built for)
+                self.dp.attach_overlap(self.model)
         if self.dp is not None:
             self.dp.broadcast_params(0)
         self.optimizer = build_optimizer(

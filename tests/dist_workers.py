@@ -876,6 +876,7 @@ def _layout_case(rank, world, layout):
     dp_mode = layout.pop("dp_mode", None)
     cfg_mode = layout.pop("dp_mode_cfg", None)   # named in the training config instead
     expect_nccl = layout.pop("expect_nccl", False)
+    overlap = layout.pop("overlap", False)
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.05 if balance else 0.0, num_hidden_layers=2,
                    tie_word_embeddings=tied)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
@@ -884,7 +885,7 @@ def _layout_case(rank, world, layout):
     singles = [dist.new_group([r]) for r in range(world)]
     ref = TrainEngine(build(cfg), tcfg, torch.device("cpu"), dp_group=singles[rank])
     pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
-    dcfg = {"shard_params": shard}
+    dcfg = {"shard_params": shard, "overlap_grad_reduce": overlap}
     if cfg_mode:
         dcfg["dp_mode"] = cfg_mode
     eng = TrainEngine(pm.apply_parallelism(build(cfg)), dict(tcfg, distributed=dcfg),
@@ -921,6 +922,9 @@ def _layout_case(rank, world, layout):
         else:
             r = ref.train_step(full)
         o = eng.train_step(full[d * accum:(d + 1) * accum])
+        if overlap:   # every block's span was reduced during the backward
+            assert eng.dp.last_overlapped == len(eng.dp._hooked) > 0, \
+                (eng.dp.last_overlapped, len(eng.dp._hooked))
         # the engine reports its replica's loss; the mean over the replicas
         # (every rank of a replica reports the same value) is the global one
         loss = o["loss"].detach().clone()
@@ -994,13 +998,14 @@ def _layout_ckpt_case(rank, world, layout, tmp, from_single=False):
     moe = layout.pop("moe", False)
     shard = layout.pop("shard_params", False)
     dp_mode = layout.pop("dp_mode", None)
+    overlap = layout.pop("overlap", False)
     cfg = tiny_cfg(moe, router_aux_loss_coef=0.0, num_hidden_layers=4)
     tcfg = {"optimizer": {"lr": 1e-2, "grad_clip": 1.0},
             "scheduler": {"warmup_steps": 0, "total_steps": 10}, "moe": {"global_batch_balance": False}}
     singles = [dist.new_group([r]) for r in range(world)]
     pm = ParallelismManager(ParallelConfig(tp_fused=False, ep_fused=False, **layout))
     eng = TrainEngine(pm.apply_parallelism(build(cfg)),
-                      dict(tcfg, distributed={"shard_params": shard}), torch.device("cpu"),
+                      dict(tcfg, distributed={"shard_params": shard, "overlap_grad_reduce": overlap}), torch.device("cpu"),
                       dp_mode=dp_mode, parallel=pm)
     _check_peer_step(eng, dp_mode)
     dp, d, B = pm.config.dp_size, pm.coords["dp"], 4

@@ -155,6 +155,10 @@ LAYOUTS = {
     "tp2-moe": (2, {"tp_size": 2, "moe": True}),
     "tp2xep2-moe": (4, {"tp_size": 2, "ep_size": 2, "moe": True, "sequence_parallel": False}),
     "dp2-accum2": (2, {"accum": 2}),
+    "dp2-overlap": (2, {"overlap": True}),
+    "dp2-overlap-accum2": (2, {"overlap": True, "accum": 2}),
+    "tp2xdp2-overlap": (4, {"tp_size": 2, "overlap": True}),
+    "dp2-overlap-tied": (2, {"overlap": True, "tied": True}),
     "tp2xdp2-fsdp-accum2": (4, {"tp_size": 2, "shard_params": True, "accum": 2}),
     "ep2-fsdp-moe-accum2": (2, {"ep_size": 2, "moe": True, "shard_params": True, "accum": 2}),
     "cp2xdp2-accum2": (4, {"cp_size": 2, "accum": 2}),
@@ -226,7 +230,7 @@ def test_peer_step_layouts_match_single_process(tmp_path, world):
 
 
 CKPT_LAYOUTS = ["dp2", "tp2", "pp2", "ep2-moe", "tp2xdp2-fsdp", "ep2-fsdp-moe", "tp2xpp2", "cp2",
-                "cp2-fsdp", "ep2xdp2-moe-p2p", "tp2xdp2-p2p"]
+                "cp2-fsdp", "ep2xdp2-moe-p2p", "tp2xdp2-p2p", "dp2-overlap"]
 
 
 @pytest.mark.parametrize("world", [2, 4])
