@@ -77,7 +77,7 @@ def parse():
     p.add_argument("--kernel-table", default=None,
                    help="ours: write per-kernel device time of the profiled extra step (markdown) to this path")
     p.add_argument("--overlap", action="store_true",
-                   help="ours, dp p2p: reduce-scatter per block during the backward instead of after it")
+                   help="ours, dp p2p or shard: reduce-scatter per block during the backward instead of after it")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="ours, tp/ep configs: peer-memory fused kernels or NCCL collectives")
     p.add_argument("--dp-mode", default=None, choices=["p2p", "shard", "replicate", "fsdp"],
