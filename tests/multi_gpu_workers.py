@@ -52,29 +52,35 @@ def peer_dp_worker(rank, world, port):
     assert hasattr(p2p.dp, "fused_step"), "symmetric memory unavailable"
     nccl = _engine("shard", None)
     ovl = _engine("p2p", None, overlap=True)  # per-block reduce-scatter during the backward
+    novl = _engine("shard", None, overlap=True)  # the same with NCCL on a side stream
     log = []
     for _ in range(3):
         r = ref.train_step(full)
         a = p2p.train_step(mine)
         b = nccl.train_step(mine)
         c = ovl.train_step(mine)
-        log.append([float(x[k]) for x in (r, a, b, c) for k in ("loss", "grad_norm")])
+        d = novl.train_step(mine)
+        assert novl.dp.last_overlapped == len(novl.dp._hooked) > 0
+        log.append([float(x[k]) for x in (r, a, b, c, d) for k in ("loss", "grad_norm")])
     torch.cuda.synchronize()
     assert ext().error_flag_read() == 0, "kernel error word set"
-    for x in (a, b, c):
+    for x in (a, b, c, d):
         assert abs(float(x["grad_norm"]) - float(r["grad_norm"])) < 1e-3 * float(r["grad_norm"]), \
             f"rank {rank} (loss, norm) ref/p2p/nccl per step: {log}"
     p2p.state_for_save()
     ovl.state_for_save()
     nccl.state_for_save()
+    novl.state_for_save()
     def rel(a_, b_):
         return ((a_ - b_).norm() / (b_.norm() + 1e-12)).item()
 
-    for (n, p), q, s, o in zip(ref.model.named_parameters(), p2p.model.parameters(),
-                               nccl.model.parameters(), ovl.model.parameters()):
+    for (n, p), q, s, o, no in zip(ref.model.named_parameters(), p2p.model.parameters(),
+                                   nccl.model.parameters(), ovl.model.parameters(),
+                                   novl.model.parameters()):
         # the data-parallel paths reduce the same per-rank gradients
         assert rel(q, s) < 1e-3, (n, rel(q, s))
         assert rel(q, o) < 1e-3, (n, rel(q, o))
+        assert rel(s, no) < 1e-3, (n, rel(s, no))
         # against gradient accumulation in one process the fp32 summation order
         # differs, and Adam's m/sqrt(v) amplifies that on near-zero gradients
         assert rel(q, p) < 2e-3, (n, rel(q, p))
